@@ -1,0 +1,385 @@
+"""Benchmark of the early-exit hot path (router -> compaction -> scatter).
+
+Workload per GPU ("llama8b_prefill_checkpoints"): the checkpoint sweep of a
+Llama-3.1-8B-architecture prefill batch of 16 x 2048 tokens = 32768 rows of
+H = 4096 bf16 hidden states, routers at layers 8/12/16/20/24/28 (RMSNorm
+eps 1e-5, router 4096 -> 128 -> 1) with biases placed so that 5/10/15/20/
+20/30 % of the batch exits at each checkpoint (everything by layer 28).
+Each checkpoint reads its own synthetic hidden-state tensor (rows N(0,1),
+the hidden states of the still-active tokens at that layer), scores it,
+compacts survivors (rows, int64 positions, int32 KV slots) into a dense
+buffer and writes exits, final-normed, to their original positions.  Active
+counts chain on the device between checkpoints (no host sync).  One step =
+the six checkpoints.  Inputs (1.1 GiB per step) exceed the 126 MB L2, so no
+explicit flush is needed between steps.
+
+Multi-GPU: one process per GPU under torchrun; every rank processes its own
+batch (weak scaling, no data-path collective); timing is the max over ranks.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+THRESHOLD = 0.85
+LAYERS = [8, 12, 16, 20, 24, 28]
+EXIT_FRACTIONS = [0.05, 0.10, 0.15, 0.20, 0.20, 0.30]  # of the whole batch
+ROWS, HIDDEN, BOTTLENECK = 16 * 2048, 4096, 128
+WORKLOAD = "llama8b_prefill_checkpoints"
+
+
+def algorithmic_bytes(n: int, exits: int, h: int, e: int) -> int:
+    """Bytes a single pass must move for one checkpoint of n rows: read every
+    row and write it once (survivor to the dense buffer, exit to its
+    position), fp32 score + u8 decision + int32 source index per row, read
+    int64 position + int32 slot per row, write position + slot per survivor."""
+    return n * 2 * h * e + 21 * n + 12 * (n - exits)
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    def __init__(self, index: int, period: float = 0.02):
+        self.index, self.period = index, period
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        except Exception as exc:  # NVML missing: clocks reported as unknown
+            self._err = str(exc)
+        return self
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        names = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+                 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+                 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+        seen = set()
+        for _, r in self.samples:
+            for bit, name in names.items():
+                if r & bit:
+                    seen.add(name)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(seen), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------- setup
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(world, v: float) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class Workload:
+    """Device-resident inputs and buffers of one rank's checkpoint sweep."""
+
+    def __init__(self, rank: int, path: int):
+        from tide_b200 import workloads
+        from tide_b200.ops import CheckpointRunner, NormSpec, prepare_router
+        from tide_b200.capi import NORM_RMS
+
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        self.path = path
+        self.norm = NormSpec(NORM_RMS, torch.ones(HIDDEN, device=dev), None, 1e-5)
+        self.runner = CheckpointRunner(dev)
+        self.x, self.routers, self.active = [], [], []
+        active = ROWS
+        for k, layer in enumerate(LAYERS):
+            x = torch.randn(ROWS, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+            down = 0.02 * torch.randn(BOTTLENECK, HIDDEN, generator=g, device=dev)
+            up = 0.02 * torch.randn(1, BOTTLENECK, generator=g, device=dev)
+            z = workloads.prebias_logits_torch(x[:active], "rms", self.norm.weight, None, 1e-5,
+                                               down, up)
+            exits = int(round(EXIT_FRACTIONS[k] * ROWS)) if k < len(LAYERS) - 1 else active
+            bias = workloads.bias_for_exit_fraction(z, exits / active, THRESHOLD)
+            self.routers.append(prepare_router(down, up, bias, self.norm, torch.bfloat16))
+            self.x.append(x)
+            self.active.append(active)
+            active -= exits
+        self.positions0 = torch.arange(ROWS, device=dev, dtype=torch.int64)
+        self.slots0 = torch.arange(ROWS, device=dev, dtype=torch.int32)
+        self.count0 = torch.tensor([ROWS], dtype=torch.int32, device=dev)
+        self.out = torch.zeros(ROWS, HIDDEN, dtype=torch.bfloat16, device=dev)
+        self.compact = torch.empty(ROWS, HIDDEN, dtype=torch.bfloat16, device=dev)
+        self.pos = [torch.empty(ROWS, dtype=torch.int64, device=dev) for _ in range(2)]
+        self.slots = [torch.empty(ROWS, dtype=torch.int32, device=dev) for _ in range(2)]
+        self.counts = torch.zeros(len(LAYERS), 2, dtype=torch.int32, device=dev)
+
+    def step(self, events=None, xs=None):
+        """One sweep of the six checkpoints; `events` (a list of start/end
+        CUDA event pairs, one per checkpoint) brackets each checkpoint call."""
+        xs = xs if xs is not None else self.x
+        pos_in, slot_in, cnt = self.positions0, self.slots0, self.count0
+        for k in range(len(LAYERS)):
+            if events is not None:
+                events[k][0].record()
+            c = self.runner.run(xs[k], self.routers[k], self.norm, THRESHOLD,
+                                positions=pos_in, slots=slot_in, out_buffer=self.out,
+                                compact_out=self.compact, positions_out=self.pos[k % 2],
+                                slots_out=self.slots[k % 2],
+                                n_rows_dev=None if k == 0 else cnt,
+                                counts=self.counts[k], path=self.path)
+            if events is not None:
+                events[k][1].record()
+            pos_in, slot_in, cnt = self.pos[k % 2], self.slots[k % 2], c[:1]
+
+
+def launches_per_checkpoint(path_used: int) -> int:
+    from tide_b200.capi import PATH_TC
+
+    return 1 if path_used == PATH_TC else 2
+
+
+# ----------------------------------------------------------------- CPU leg
+def cpu_checkpoint_sample(x_bf16: np.ndarray, down: np.ndarray, up: np.ndarray, bias: float):
+    """The oracle on one checkpoint's rows (the reference's CPU path,
+    restated): returns seconds."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import tide_oracle as O
+
+    norm = {"kind": "rms", "weight": np.ones(x_bf16.shape[1], dtype=np.float32), "bias": None,
+            "eps": 1e-5}
+    out = np.zeros_like(x_bf16)
+    t0 = time.perf_counter()
+    O.checkpoint(x_bf16, O.BF16, norm, down, up, bias, THRESHOLD,
+                 positions=np.arange(x_bf16.shape[0], dtype=np.int64),
+                 slots=np.arange(x_bf16.shape[0], dtype=np.int32), out_buffer=out)
+    return time.perf_counter() - t0
+
+
+def cpu_sample_inputs(wl: "Workload", rows: int):
+    x = wl.x[0][:rows].contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    r = wl.routers[0]
+    down = r.down_t.T.contiguous().cpu().numpy()
+    up = r.up.cpu().numpy().reshape(1, -1)
+    return x, down, up, r.up_bias
+
+
+# ----------------------------------------------------------------- main
+def run_reference(args, world, rank):
+    """--impl reference: the CPU restatement of the reference path (the
+    reference is Python and cannot be built into a library), timed on the host
+    cores with every thread numpy's BLAS can use; rank 0 only."""
+    if rank != 0:
+        return
+    torch.cuda.set_device(0)
+    wl = Workload(rank, 0)
+    rows = 4096
+    x, down, up, bias = cpu_sample_inputs(wl, rows)
+    for _ in range(args.warmup):
+        cpu_checkpoint_sample(x, down, up, bias)
+    ts = [cpu_checkpoint_sample(x, down, up, bias) for _ in range(args.steps)]
+    t = sum(ts)
+    v = rows * args.steps / t
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": "router_compact_scatter_tokens_per_s", "value": v,
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * t / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample_rows_per_step": rows, "hidden": HIDDEN,
+                   "bottleneck": BOTTLENECK, "checkpoint": "layer 8 router, 5% exit"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"one checkpoint ({rows} rows x {HIDDEN} bf16) per step"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--path", default="auto", choices=["auto", "simt", "tc"])
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    from tide_b200.capi import PATH_AUTO, PATH_SIMT, PATH_TC
+
+    path = {"auto": PATH_AUTO, "simt": PATH_SIMT, "tc": PATH_TC}[args.path]
+    wl = Workload(rank, path)
+    for _ in range(max(args.warmup, 3)):
+        wl.step()
+    torch.cuda.synchronize()
+    path_used = wl.runner.last_path
+    counts = wl.counts.cpu()
+    rows_per_step = int(counts.sum().item())
+    exits_per_stage = counts[:, 1].tolist()
+    active = (counts[:, 0] + counts[:, 1]).tolist()
+    wl.runner.check_errors()
+
+    # timed region: device-resident inputs; every checkpoint call is also
+    # bracketed by CUDA events on the launching (current) stream
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in LAYERS] for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for i in range(args.steps):
+            wl.step(events=ev[i])
+        end.record()
+        torch.cuda.synchronize()
+    elapsed = start.elapsed_time(end) / 1000.0
+    per_ck = [sum(ev[i][k][0].elapsed_time(ev[i][k][1]) for i in range(args.steps)) / args.steps
+              for k in range(len(LAYERS))]
+    del ev
+    barrier(world)
+    elapsed = max_over_ranks(world, elapsed)
+    value = world * rows_per_step * args.steps / elapsed
+
+    e = 2
+    alg = [algorithmic_bytes(active[k], exits_per_stage[k], HIDDEN, e) for k in range(len(LAYERS))]
+    achieved = sum(alg) / (sum(per_ck) / 1000.0) / 1e9
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    peak = peaks.get("hbm_gbs", 6650.0)
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": None,
+                "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                "per_checkpoint_ms": per_ck, "algorithmic_bytes_per_step": sum(alg)}
+
+    # e2e through the public operator with host buffers: H2D of the step's
+    # hidden states from pinned memory, D2H of the step's counts
+    host_x = [x.cpu().pin_memory() for x in wl.x]
+    dev_x = [torch.empty_like(x) for x in wl.x]
+    host_counts = torch.empty_like(wl.counts, device="cpu").pin_memory()
+    barrier(world)
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(args.e2e_steps):
+        for k in range(len(LAYERS)):
+            dev_x[k].copy_(host_x[k], non_blocking=True)
+        wl.step(xs=dev_x)
+        host_counts.copy_(wl.counts, non_blocking=True)
+    e_end.record()
+    torch.cuda.synchronize()
+    e_el = max_over_ranks(world, e_start.elapsed_time(e_end) / 1000.0)
+    e2e = {"value": world * rows_per_step * args.e2e_steps / e_el, "unit": "tokens/s",
+           "h2d_bytes_per_step": int(sum(x.numel() * x.element_size() for x in host_x)),
+           "d2h_bytes_per_step": int(host_counts.numel() * 4), "steps": args.e2e_steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows = 4096
+        x, down, up, bias = cpu_sample_inputs(wl, rows)
+        cpu_checkpoint_sample(x, down, up, bias)
+        t = min(cpu_checkpoint_sample(x, down, up, bias) for _ in range(3))
+        cpu = {"value": rows / t, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"oracle, one checkpoint of {rows} rows x {HIDDEN} bf16 (layer-8 router), "
+                         f"best of 3"}
+
+    n_launch = launches_per_checkpoint(path_used) * len(LAYERS) * args.steps
+    if rank == 0:
+        line = {
+            "metric": "router_compact_scatter_tokens_per_s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "hidden": HIDDEN,
+                       "bottleneck": BOTTLENECK, "checkpoint_layers": LAYERS,
+                       "exit_fractions_of_batch": EXIT_FRACTIONS,
+                       "rows_routed_per_step": rows_per_step, "active_rows": active,
+                       "exits": exits_per_stage,
+                       "path": {0: "auto", 1: "simt", 2: "tc"}.get(path_used, path_used),
+                       "parallelism": f"dp{world} (row shards, no collective)",
+                       "l2": "inputs 1.1 GiB/step > 126 MB L2, no flush"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": n_launch, "clocks": clocks.summary(),
+            "prefill_tokens_per_s": world * ROWS * args.steps / elapsed,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,184 @@
+/*
+ * tide_b200.h -- C ABI of the B200 (sm_100a) early-exit hot path.
+ *
+ * Everything here takes plain device pointers, sizes and a CUDA stream
+ * handle; no framework types cross this boundary.  Every call enqueues work
+ * on `stream` (NULL = legacy default stream) and returns without waiting.
+ * Return value: TIDE_OK (0) or a TIDE_ERR_* code; tide_last_error() gives a
+ * message for the calling thread.  Faults the kernels detect on the device
+ * (an exit position outside the output buffer, a look-back wait that ran out)
+ * are reported through the optional `error_word` (device int32, bit mask of
+ * TIDE_DEVERR_*): the affected write is skipped, the kernel returns, and the
+ * word is read back by the caller at its next synchronisation point.
+ *
+ * Reference interfaces replaced (RightNow-AI/TIDE v0.2.1):
+ *   tide_fused_layernorm_route  <- torch.ops.tide.fused_layernorm_route
+ *                                  csrc/extensions/torch_bindings.cpp:77-134,298-299
+ *   tide_batch_compact          <- torch.ops.tide.batch_compact
+ *                                  csrc/extensions/torch_bindings.cpp:136-198,300
+ *   tide_exit_scatter           <- torch.ops.tide.exit_scatter
+ *                                  csrc/extensions/torch_bindings.cpp:200-243,301-302
+ *   tide_exit_projection        <- torch.ops.tide.exit_projection
+ *                                  csrc/extensions/torch_bindings.cpp:245-293,303-304
+ *   tide_checkpoint             <- one checkpoint of TIDERuntime.forward:
+ *                                  python/TIDE/runtime.py:168-180 (score, strict
+ *                                  '>' threshold, normed exit scatter) with the
+ *                                  compaction of SkipScheduler.process_exits,
+ *                                  python/TIDE/scheduler.py:63-102
+ *   tide_norm_scatter           <- final norm + scatter of the rows that never
+ *                                  exit: python/TIDE/runtime.py:183-187,
+ *                                  python/TIDE/scheduler.py:111-116
+ *   tide_router_fold            <- the per-call weight casts/transposes of
+ *                                  torch_bindings.cpp:101-103 and the
+ *                                  pre-transpose of runtime.py:85-87, done once
+ */
+#ifndef TIDE_B200_H
+#define TIDE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void *tide_stream_t; /* a cudaStream_t */
+
+enum tide_dtype { TIDE_DTYPE_F32 = 0, TIDE_DTYPE_F16 = 1, TIDE_DTYPE_BF16 = 2 };
+enum tide_norm { TIDE_NORM_RMS = 0, TIDE_NORM_LAYER = 1 };
+enum tide_path { TIDE_PATH_AUTO = 0, TIDE_PATH_SIMT = 1, TIDE_PATH_TC = 2 };
+
+enum tide_status {
+  TIDE_OK = 0,
+  TIDE_ERR_INVALID = 1,     /* bad argument (null pointer, size, dtype)   */
+  TIDE_ERR_UNSUPPORTED = 2, /* valid but not handled by the chosen path    */
+  TIDE_ERR_CUDA = 3,        /* a CUDA runtime call failed                  */
+  TIDE_ERR_WORKSPACE = 4,   /* workspace missing, too small or misaligned  */
+  TIDE_ERR_ALIGNMENT = 5    /* pointer/stride not 16-byte aligned          */
+};
+
+/* device-side error bits written to error_word */
+enum tide_device_error {
+  TIDE_DEVERR_POSITION = 1, /* exit position outside [0, n_total): row skipped */
+  TIDE_DEVERR_TIMEOUT = 2,  /* a bounded spin wait expired; results invalid  */
+  TIDE_DEVERR_COUNT = 4     /* device row count above the row capacity       */
+};
+
+int tide_abi_version(void);
+const char *tide_last_error(void);
+
+/* ---- reference operator set ------------------------------------------- */
+
+/* scores[i] = sigmoid(up . SiLU(down_t^T . (RMSNorm(input[i]) * norm_weight)))
+ * input [n_tokens, hidden_dim] of `dtype`; norm_weight [hidden_dim] fp32;
+ * down_weight_t [hidden_dim, bottleneck_dim] fp32 (the pre-transposed layout
+ * of runtime.py:85-87); up_weight_t [bottleneck_dim] fp32; scores [n] fp32.
+ * bottleneck_dim <= 256, as in fused_layernorm_route.cu:104-168. */
+int tide_fused_layernorm_route(int dtype, const void *input, const float *norm_weight,
+                               const float *down_weight_t, const float *up_weight_t,
+                               float eps, float *scores, int64_t n_tokens,
+                               int64_t hidden_dim, int64_t bottleneck_dim,
+                               tide_stream_t stream);
+
+/* Stable split of rows by exit_mask (non-zero = exit).  Rows with mask 0 go
+ * to compacted[0..num_remaining) with their source index in
+ * continue_indices; rows with mask != 0 go to exited[0..n-num_remaining)
+ * with their index in exit_indices.  Both orders are ascending source order.
+ * compacted/exited have room for n_tokens rows.  num_remaining: device int32. */
+size_t tide_batch_compact_workspace_size(int64_t n_tokens);
+int tide_batch_compact(int dtype, const void *input, const int32_t *exit_mask,
+                       void *compacted, void *exited, int32_t *continue_indices,
+                       int32_t *exit_indices, int32_t *num_remaining, int64_t n_tokens,
+                       int64_t hidden_dim, void *workspace, size_t workspace_bytes,
+                       int32_t *error_word, tide_stream_t stream);
+
+/* output_buffer[exit_positions[i]] = exited_states[i]  (bit copy) */
+int tide_exit_scatter(int dtype, const void *exited_states, const int32_t *exit_positions,
+                      void *output_buffer, int64_t n_exited, int64_t hidden_dim,
+                      int64_t n_total, int32_t *error_word, tide_stream_t stream);
+
+/* output_buffer[exit_positions[i]] = RMSNorm(exited_states[i]) * norm_weight,
+ * computed in fp32 and rounded to `dtype`. */
+int tide_exit_projection(int dtype, const void *exited_states, const float *norm_weight,
+                         const int32_t *exit_positions, void *output_buffer, float eps,
+                         int64_t n_exited, int64_t hidden_dim, int64_t n_total,
+                         int32_t *error_word, tide_stream_t stream);
+
+/* output_buffer[positions[i]] = final_norm(rows[i]) rounded to `dtype`, the
+ * final norm being RMSNorm (norm_bias ignored) or LayerNorm (norm_bias may be
+ * NULL), statistics in fp32.  The remaining-token step of TIDERuntime.forward,
+ * python/TIDE/runtime.py:183-187, and SkipScheduler.finalize,
+ * python/TIDE/scheduler.py:111-116. */
+int tide_norm_scatter(int dtype, int norm_type, const void *rows, const int64_t *positions,
+                      void *output_buffer, const float *norm_weight, const float *norm_bias,
+                      float eps, int64_t n_rows, int64_t hidden_dim, int64_t n_total,
+                      int32_t *error_word, tide_stream_t stream);
+
+/* ---- router preparation (once per router) ------------------------------ */
+
+/* From the router's down.weight [B, H] fp32 and the final norm's weight (and
+ * bias, LayerNorm only) [H] fp32, build:
+ *   down_t      [H, B] fp32             (SIMT path; may be NULL)
+ *   folded      [B, H] in fold_dtype    folded[b,i] = down[b,i] * norm_weight[i]
+ *                                       (tensor-core path; may be NULL)
+ *   colsum      [B] fp32                sum_i float(folded[b,i])   (may be NULL)
+ *   bias_proj   [B] fp32                sum_i norm_bias[i]*down[b,i] (may be NULL) */
+int tide_router_fold(int fold_dtype, const float *down, const float *norm_weight,
+                     const float *norm_bias, int64_t hidden_dim, int64_t bottleneck_dim,
+                     float *down_t, void *folded, float *colsum, float *bias_proj,
+                     tide_stream_t stream);
+
+/* ---- one checkpoint of the early-exit path ----------------------------- */
+
+typedef struct tide_checkpoint_args {
+  int32_t dtype;          /* element type of x, out_buffer, compact_out        */
+  int32_t norm_type;      /* TIDE_NORM_RMS or TIDE_NORM_LAYER                  */
+  int32_t path;           /* TIDE_PATH_AUTO / _SIMT / _TC                        */
+  int32_t reserved0;
+  int64_t n_rows;         /* rows of x (capacity when n_rows_dev != NULL)      */
+  int64_t hidden_dim;     /* H                                                   */
+  int64_t bottleneck_dim; /* B (router width)                                    */
+  int64_t n_total;        /* rows of out_buffer                                  */
+  const void *x;          /* [n_rows, H] hidden states of the active tokens     */
+  const int32_t *n_rows_dev; /* optional device count of valid rows (<= n_rows) */
+  /* final norm */
+  const float *norm_weight; /* [H] fp32                                          */
+  const float *norm_bias;   /* [H] fp32, LayerNorm only, may be NULL             */
+  float eps;
+  /* router (from tide_router_fold) */
+  float up_bias;          /* scalar added before the sigmoid (0 = reference)   */
+  const float *down_t;    /* [H, B] fp32: SIMT path                            */
+  const void *folded;     /* [B, H] dtype: tensor-core path                    */
+  const float *colsum;    /* [B]: LayerNorm on the tensor-core path            */
+  const float *bias_proj; /* [B]: LayerNorm with bias                          */
+  const float *up;        /* [B] fp32 up.weight                                */
+  float threshold;        /* exit iff score > threshold (strict)               */
+  int32_t reserved1;
+  /* token bookkeeping */
+  const int64_t *positions_in; /* [n_rows] original token position; NULL = row index */
+  const int32_t *slots_in;     /* [n_rows] KV slot id; may be NULL                  */
+  /* outputs (each may be NULL except counts_out) */
+  void *out_buffer;            /* [n_total, H]: exiting rows, final-normed       */
+  void *compact_out;           /* [n_rows, H]: surviving rows, stable order      */
+  int64_t *positions_out;      /* [n_rows]: surviving rows' positions            */
+  int32_t *slots_out;          /* [n_rows]: surviving rows' slots                */
+  int64_t *exit_positions_out; /* [n_rows]: exiting rows' positions, stable      */
+  float *scores_out;           /* [n_rows]: router scores                        */
+  int32_t *counts_out;         /* [2] device: {survivors, exits}                 */
+  int32_t *error_word;         /* device int32 bit mask, may be NULL             */
+  void *workspace;             /* from tide_checkpoint_workspace_size            */
+  size_t workspace_bytes;
+} tide_checkpoint_args;
+
+size_t tide_checkpoint_workspace_size(const tide_checkpoint_args *args);
+int tide_checkpoint(const tide_checkpoint_args *args, tide_stream_t stream);
+
+/* Which path tide_checkpoint would take for these arguments (TIDE_PATH_SIMT or
+ * TIDE_PATH_TC), or a negative TIDE_ERR_* code. */
+int tide_checkpoint_select_path(const tide_checkpoint_args *args);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TIDE_B200_H */

@@ -1,0 +1,96 @@
+"""The C ABI library loads without a GPU, exports every function that
+include/tide_b200.h declares, has a ctypes mirror with the header's struct
+layout, and rejects bad arguments before touching the device."""
+import ctypes
+import re
+import subprocess
+
+import pytest
+
+from tests.conftest import ROOT
+from tide_b200 import _native, capi
+
+HEADER = ROOT / "include" / "tide_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tide_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.lib()
+    names = declared_functions()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in tide_b200.h but not exported"
+    assert set(names) == set(capi.PROTOTYPES), "ctypes prototypes out of sync with the header"
+    assert lib.tide_abi_version() == 1
+
+
+def test_struct_layout_matches_header(tmp_path):
+    src = tmp_path / "probe.c"
+    fields = [f for f, _ in capi.CheckpointArgs._fields_]
+    body = "\n".join(f'  printf("{f} %zu\\n", offsetof(tide_checkpoint_args, {f}));' for f in fields)
+    src.write_text(f"""#include <stdio.h>
+#include <stddef.h>
+#include "tide_b200.h"
+int main(void) {{
+  printf("size %zu\\n", sizeof(tide_checkpoint_args));
+{body}
+  return 0;
+}}
+""")
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", str(src), "-o", str(exe)], check=True)
+    out = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                        check=True).stdout.splitlines())
+    assert int(out["size"]) == ctypes.sizeof(capi.CheckpointArgs)
+    for f in fields:
+        assert int(out[f]) == getattr(capi.CheckpointArgs, f).offset, f
+
+
+def test_argument_errors_need_no_gpu():
+    lib = _native.lib()
+    # bad dtype
+    rc = lib.tide_exit_scatter(7, None, None, None, 1, 8, 1, None, None)
+    assert rc == 1 and b"dtype" in lib.tide_last_error()
+    # bottleneck above 256
+    rc = lib.tide_fused_layernorm_route(2, 1, 1, 1, 1, 1e-6, 1, 4, 64, 512, None)
+    assert rc == 1
+    # checkpoint without counts / workspace
+    a = capi.CheckpointArgs(dtype=2, n_rows=4, hidden_dim=64, bottleneck_dim=16, n_total=4,
+                            x=16, norm_weight=16, up=16)
+    assert lib.tide_checkpoint(ctypes.byref(a), None) == 1
+    a.counts_out = 16
+    assert lib.tide_checkpoint(ctypes.byref(a), None) == 4  # workspace missing
+    assert lib.tide_checkpoint_select_path(ctypes.byref(a)) < 0
+    # zero-size requests are no-ops
+    assert lib.tide_exit_scatter(2, None, None, None, 0, 8, 0, None, None) == 0
+    assert lib.tide_norm_scatter(2, 0, None, None, None, None, None, 1e-5, 0, 8, 0, None, None) == 0
+
+
+def test_workspace_sizes_grow_with_rows():
+    lib = _native.lib()
+    small = capi.CheckpointArgs(n_rows=128)
+    big = capi.CheckpointArgs(n_rows=1 << 20)
+    assert lib.tide_checkpoint_workspace_size(ctypes.byref(big)) > \
+        lib.tide_checkpoint_workspace_size(ctypes.byref(small)) > 0
+    assert lib.tide_batch_compact_workspace_size(0) > 0
+
+
+def test_torch_extension_registers_operators():
+    ops = _native.ops()
+    for name in ("fused_layernorm_route", "batch_compact", "exit_scatter", "exit_projection",
+                 "norm_scatter", "router_fold", "checkpoint", "checkpoint_workspace_size"):
+        assert hasattr(ops, name), name
+    assert ops.checkpoint_workspace_size(1000) > 0
+
+
+def test_operators_have_no_cpu_kernel():
+    import torch
+    ops = _native.ops()
+    x = torch.zeros(4, 8)
+    with pytest.raises(NotImplementedError):
+        ops.exit_scatter(x, torch.zeros(4, dtype=torch.int32), x.clone())

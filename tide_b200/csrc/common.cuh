@@ -1,0 +1,139 @@
+// Shared device helpers for the sm_100a early-exit kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "tide_b200.h"
+
+namespace tide {
+
+// ---------------------------------------------------------------- elements
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+// A 16-byte vector holds kVec<T> elements.
+template <typename T> constexpr int kVec = 16 / (int)sizeof(T);
+
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4 &v, float *f) {
+  const T *e = reinterpret_cast<const T *>(&v);
+#pragma unroll
+  for (int i = 0; i < kVec<T>; ++i) f[i] = Elem<T>::to_f(e[i]);
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack16(const float *f) {
+  uint4 v;
+  T *e = reinterpret_cast<T *>(&v);
+#pragma unroll
+  for (int i = 0; i < kVec<T>; ++i) e[i] = Elem<T>::from_f(f[i]);
+  return v;
+}
+
+// Streaming 16-byte global accesses.
+__device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st_stream(uint4 *p, const uint4 &v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// ------------------------------------------------------------- reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Correctly rounded 1/sqrt(v): one IEEE sqrt and one IEEE division, the same
+// two roundings as torch.rsqrt's CPU path.
+__device__ __forceinline__ float rsqrt_rn(float v) { return __fdiv_rn(1.0f, __fsqrt_rn(v)); }
+
+// SiLU and sigmoid in fp32 (x * sigmoid(x), 1 / (1 + e^-x)).
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ void raise_error(int32_t *err, int bits) {
+  if (err) atomicOr(err, bits);
+}
+
+// -------------------------------------------------------------- look-back
+// Tile status word for the single-pass stable partition (decoupled
+// look-back, Merrill & Garland 2016): bits 62-63 flag, 31-61 exit count,
+// 0-30 survivor count.
+constexpr uint64_t kFlagAggregate = 1ull << 62;
+constexpr uint64_t kFlagPrefix = 2ull << 62;
+constexpr uint64_t kCountMask = (1ull << 31) - 1;
+// Spin bound for a look-back wait.  A predecessor tile is always held by a
+// running CTA (tiles are handed out in ticket order), so this only expires
+// if the device is wedged; the kernel then flags TIDE_DEVERR_TIMEOUT.
+constexpr int kSpinLimit = 1 << 24;
+
+__device__ __forceinline__ uint64_t pack_status(uint64_t flag, uint32_t keep, uint32_t exits) {
+  return flag | ((uint64_t)exits << 31) | (uint64_t)keep;
+}
+__device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t *p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u64(uint64_t *p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Decoupled look-back for tile `tile`: publishes this tile's aggregate,
+// accumulates predecessors until an inclusive prefix is found, publishes the
+// inclusive prefix and returns the exclusive one.  Called by one thread.
+// Returns false if a wait expired (prefix then undefined).
+__device__ __forceinline__ bool lookback(uint64_t *status, uint32_t tile, uint32_t keep,
+                                         uint32_t exits, uint32_t *keep_before,
+                                         uint32_t *exits_before) {
+  uint32_t kb = 0, eb = 0;
+  if (tile == 0) {
+    st_release_u64(&status[0], pack_status(kFlagPrefix, keep, exits));
+    *keep_before = 0;
+    *exits_before = 0;
+    return true;
+  }
+  st_release_u64(&status[tile], pack_status(kFlagAggregate, keep, exits));
+  int64_t j = (int64_t)tile - 1;
+  bool ok = true;
+  while (j >= 0) {
+    uint64_t s = 0;
+    int spins = 0;
+    while (((s = ld_acquire_u64(&status[j])) >> 62) == 0) {
+      if (++spins > kSpinLimit) { ok = false; break; }
+      __nanosleep(32);
+    }
+    if (!ok) break;
+    kb += (uint32_t)(s & kCountMask);
+    eb += (uint32_t)((s >> 31) & kCountMask);
+    if ((s >> 62) == 2) break;
+    --j;
+  }
+  st_release_u64(&status[tile], pack_status(kFlagPrefix, kb + keep, eb + exits));
+  *keep_before = kb;
+  *exits_before = eb;
+  return ok;
+}
+
+}  // namespace tide

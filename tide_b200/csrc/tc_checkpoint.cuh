@@ -1,0 +1,15 @@
+// Tensor-core (tcgen05) checkpoint kernel: declarations used by the C ABI.
+#pragma once
+
+#include <stddef.h>
+
+#include "common.cuh"
+
+namespace tide {
+
+bool tc_supported(const tide_checkpoint_args *a);
+const char *tc_unsupported_reason(const tide_checkpoint_args *a);
+size_t tc_workspace_bytes(int64_t n_rows);
+int tc_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t s, char *err, size_t err_len);
+
+}  // namespace tide

@@ -1,0 +1,342 @@
+// Thin PyTorch operator layer over the C ABI (include/tide_b200.h).
+//
+// Registers the reference's operator namespace `tide` with its four schemas
+// (csrc/extensions/torch_bindings.cpp:297-305 of the reference) plus the
+// router fold and the fused checkpoint.  Every operator validates its
+// tensors, launches on the caller's current CUDA stream (the reference used
+// the legacy default stream) and turns a non-zero C ABI status into a Python
+// RuntimeError.  Only CUDA implementations are registered: there is no CPU
+// fallback.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include "tide_b200.h"
+
+namespace {
+
+#define TIDE_CHECK_OK(call)                                                   \
+  do {                                                                        \
+    int _rc = (call);                                                         \
+    TORCH_CHECK(_rc == TIDE_OK, #call " failed (", _rc, "): ", tide_last_error()); \
+  } while (0)
+
+void check_cuda_contig(const at::Tensor &t, const char *name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+int to_dtype(at::ScalarType s, const char *op) {
+  switch (s) {
+    case at::kFloat: return TIDE_DTYPE_F32;
+    case at::kHalf: return TIDE_DTYPE_F16;
+    case at::kBFloat16: return TIDE_DTYPE_BF16;
+    default: TORCH_CHECK(false, op, ": unsupported dtype ", s);
+  }
+  return -1;
+}
+
+tide_stream_t cur_stream(const at::Tensor &t) {
+  return (tide_stream_t)at::cuda::getCurrentCUDAStream(t.device().index()).stream();
+}
+
+const void *opt_ptr(const std::optional<at::Tensor> &t) {
+  return t.has_value() && t->defined() ? t->data_ptr() : nullptr;
+}
+void *opt_mut(const std::optional<at::Tensor> &t) {
+  return t.has_value() && t->defined() ? t->data_ptr() : nullptr;
+}
+
+// ---- reference operators ------------------------------------------------
+
+at::Tensor fused_layernorm_route(const at::Tensor &input, const at::Tensor &norm_weight,
+                                 const at::Tensor &down_weight, const at::Tensor &up_weight,
+                                 double eps) {
+  check_cuda_contig(input, "input");
+  check_cuda_contig(norm_weight, "norm_weight");
+  check_cuda_contig(down_weight, "down_weight");
+  check_cuda_contig(up_weight, "up_weight");
+  TORCH_CHECK(input.dim() == 2, "input must be [N, D]");
+  TORCH_CHECK(down_weight.dim() == 2, "down_weight must be [D, B] (pre-transposed)");
+  const int64_t n = input.size(0), H = input.size(1), B = down_weight.size(1);
+  TORCH_CHECK(input.device() == norm_weight.device(), "Device mismatch");
+  TORCH_CHECK(norm_weight.numel() == H, "norm_weight dim mismatch");
+  TORCH_CHECK(down_weight.size(0) == H, "down_weight must be [D, B]");
+  TORCH_CHECK(up_weight.numel() == B, "up_weight must have B elements");
+  const c10::cuda::CUDAGuard guard(input.device());
+  auto nw = norm_weight.to(at::kFloat).contiguous();
+  auto dw = down_weight.to(at::kFloat).contiguous();
+  auto uw = up_weight.to(at::kFloat).contiguous();
+  auto scores = at::empty({n}, input.options().dtype(at::kFloat));
+  TIDE_CHECK_OK(tide_fused_layernorm_route(to_dtype(input.scalar_type(), "fused_layernorm_route"),
+                                           input.data_ptr(), nw.data_ptr<float>(),
+                                           dw.data_ptr<float>(), uw.data_ptr<float>(), (float)eps,
+                                           scores.data_ptr<float>(), n, H, B, cur_stream(input)));
+  return scores;
+}
+
+std::vector<at::Tensor> batch_compact(const at::Tensor &input, const at::Tensor &exit_mask) {
+  check_cuda_contig(input, "input");
+  check_cuda_contig(exit_mask, "exit_mask");
+  TORCH_CHECK(input.dim() == 2, "input must be [N, D]");
+  const int64_t n = input.size(0), H = input.size(1);
+  TORCH_CHECK(exit_mask.numel() == n, "exit_mask must have N elements");
+  const c10::cuda::CUDAGuard guard(input.device());
+  auto mask = exit_mask.to(at::kInt).contiguous();
+  auto opts_i = input.options().dtype(at::kInt);
+  auto compacted = at::empty({n, H}, input.options());
+  auto exited = at::empty({n, H}, input.options());
+  auto cont_idx = at::empty({n}, opts_i);
+  auto exit_idx = at::empty({n}, opts_i);
+  auto num_remaining = at::zeros({1}, opts_i);
+  auto ws = at::empty({(int64_t)tide_batch_compact_workspace_size(n)},
+                      input.options().dtype(at::kByte));
+  TIDE_CHECK_OK(tide_batch_compact(to_dtype(input.scalar_type(), "batch_compact"), input.data_ptr(),
+                                   mask.data_ptr<int32_t>(), compacted.data_ptr(), exited.data_ptr(),
+                                   cont_idx.data_ptr<int32_t>(), exit_idx.data_ptr<int32_t>(),
+                                   num_remaining.data_ptr<int32_t>(), n, H, ws.data_ptr(),
+                                   (size_t)ws.numel(), nullptr, cur_stream(input)));
+  // The op returns tensors sized by the survivor count, so the count is read
+  // back here (the reference does the same, torch_bindings.cpp:190).
+  const int64_t n_remain = num_remaining.item<int32_t>();
+  return {compacted.slice(0, 0, n_remain), exited.slice(0, 0, n - n_remain),
+          cont_idx.slice(0, 0, n_remain), exit_idx.slice(0, 0, n - n_remain), num_remaining};
+}
+
+void exit_scatter(const at::Tensor &exited_states, const at::Tensor &exit_positions,
+                  const at::Tensor &output_buffer) {
+  check_cuda_contig(exited_states, "exited_states");
+  check_cuda_contig(exit_positions, "exit_positions");
+  check_cuda_contig(output_buffer, "output_buffer");
+  TORCH_CHECK(exited_states.scalar_type() == output_buffer.scalar_type(),
+              "exited_states and output_buffer must have the same dtype");
+  TORCH_CHECK(exited_states.dim() == 2 && output_buffer.dim() == 2, "expected 2-D states");
+  const int64_t n = exited_states.size(0), H = exited_states.size(1);
+  TORCH_CHECK(output_buffer.size(1) == H, "hidden dims differ");
+  TORCH_CHECK(exit_positions.numel() == n, "exit_positions must have N_exit elements");
+  const c10::cuda::CUDAGuard guard(exited_states.device());
+  auto pos = exit_positions.to(at::kInt).contiguous();
+  TIDE_CHECK_OK(tide_exit_scatter(to_dtype(exited_states.scalar_type(), "exit_scatter"),
+                                  exited_states.data_ptr(), pos.data_ptr<int32_t>(),
+                                  output_buffer.data_ptr(), n, H, output_buffer.size(0), nullptr,
+                                  cur_stream(exited_states)));
+}
+
+void exit_projection(const at::Tensor &exited_states, const at::Tensor &norm_weight,
+                     const at::Tensor &exit_positions, const at::Tensor &output_buffer, double eps) {
+  check_cuda_contig(exited_states, "exited_states");
+  check_cuda_contig(norm_weight, "norm_weight");
+  check_cuda_contig(exit_positions, "exit_positions");
+  check_cuda_contig(output_buffer, "output_buffer");
+  TORCH_CHECK(exited_states.scalar_type() == output_buffer.scalar_type(),
+              "exited_states and output_buffer must have the same dtype");
+  TORCH_CHECK(exited_states.dim() == 2 && output_buffer.dim() == 2, "expected 2-D states");
+  const int64_t n = exited_states.size(0), H = exited_states.size(1);
+  TORCH_CHECK(output_buffer.size(1) == H && norm_weight.numel() == H, "hidden dims differ");
+  TORCH_CHECK(exit_positions.numel() == n, "exit_positions must have N_exit elements");
+  const c10::cuda::CUDAGuard guard(exited_states.device());
+  auto nw = norm_weight.to(at::kFloat).contiguous();
+  auto pos = exit_positions.to(at::kInt).contiguous();
+  TIDE_CHECK_OK(tide_exit_projection(to_dtype(exited_states.scalar_type(), "exit_projection"),
+                                     exited_states.data_ptr(), nw.data_ptr<float>(),
+                                     pos.data_ptr<int32_t>(), output_buffer.data_ptr(), (float)eps,
+                                     n, H, output_buffer.size(0), nullptr,
+                                     cur_stream(exited_states)));
+}
+
+void norm_scatter(const at::Tensor &rows, const at::Tensor &positions,
+                  const at::Tensor &output_buffer, const at::Tensor &norm_weight,
+                  const std::optional<at::Tensor> &norm_bias, int64_t norm_type, double eps) {
+  check_cuda_contig(rows, "rows");
+  check_cuda_contig(positions, "positions");
+  check_cuda_contig(output_buffer, "output_buffer");
+  check_cuda_contig(norm_weight, "norm_weight");
+  TORCH_CHECK(rows.dim() == 2 && output_buffer.dim() == 2, "expected 2-D rows/output_buffer");
+  TORCH_CHECK(rows.scalar_type() == output_buffer.scalar_type(), "rows/output_buffer dtype differ");
+  const int64_t n = rows.size(0), H = rows.size(1);
+  TORCH_CHECK(output_buffer.size(1) == H, "hidden dims differ");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && positions.numel() >= n,
+              "positions must be int64 with one entry per row");
+  TORCH_CHECK(norm_weight.scalar_type() == at::kFloat && norm_weight.numel() == H,
+              "norm_weight must be fp32 [H]");
+  const float *nb = nullptr;
+  if (norm_bias.has_value() && norm_bias->defined()) {
+    check_cuda_contig(*norm_bias, "norm_bias");
+    TORCH_CHECK(norm_bias->scalar_type() == at::kFloat && norm_bias->numel() == H,
+                "norm_bias must be fp32 [H]");
+    nb = norm_bias->data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard guard(rows.device());
+  TIDE_CHECK_OK(tide_norm_scatter(to_dtype(rows.scalar_type(), "norm_scatter"), (int)norm_type,
+                                  rows.data_ptr(), positions.data_ptr<int64_t>(),
+                                  output_buffer.data_ptr(), norm_weight.data_ptr<float>(), nb,
+                                  (float)eps, n, H, output_buffer.size(0), nullptr,
+                                  cur_stream(rows)));
+}
+
+// ---- router fold and fused checkpoint ----------------------------------
+
+std::vector<at::Tensor> router_fold(const at::Tensor &down, const at::Tensor &norm_weight,
+                                    const std::optional<at::Tensor> &norm_bias,
+                                    at::ScalarType fold_dtype) {
+  check_cuda_contig(down, "down");
+  TORCH_CHECK(down.dim() == 2, "down must be [B, H] (router.down.weight)");
+  const int64_t B = down.size(0), H = down.size(1);
+  const c10::cuda::CUDAGuard guard(down.device());
+  auto d = down.to(at::kFloat).contiguous();
+  auto w = norm_weight.to(at::kFloat).contiguous();
+  TORCH_CHECK(w.numel() == H, "norm_weight must have H elements");
+  at::Tensor bn;
+  if (norm_bias.has_value() && norm_bias->defined()) {
+    bn = norm_bias->to(at::kFloat).contiguous();
+    TORCH_CHECK(bn.numel() == H, "norm_bias must have H elements");
+  }
+  auto f32 = d.options();
+  auto down_t = at::empty({H, B}, f32);
+  auto folded = at::empty({B, H}, d.options().dtype(fold_dtype));
+  auto colsum = at::empty({B}, f32);
+  auto bias_proj = at::zeros({B}, f32);
+  TIDE_CHECK_OK(tide_router_fold(to_dtype(fold_dtype, "router_fold"), d.data_ptr<float>(),
+                                 w.data_ptr<float>(), bn.defined() ? bn.data_ptr<float>() : nullptr,
+                                 H, B, down_t.data_ptr<float>(), folded.data_ptr(),
+                                 colsum.data_ptr<float>(),
+                                 bn.defined() ? bias_proj.data_ptr<float>() : nullptr,
+                                 cur_stream(d)));
+  return {down_t, folded, colsum, bias_proj};
+}
+
+int64_t checkpoint_workspace_size(int64_t n_rows) {
+  tide_checkpoint_args a{};
+  a.n_rows = n_rows;
+  return (int64_t)tide_checkpoint_workspace_size(&a);
+}
+
+int64_t checkpoint(const at::Tensor &x, const std::optional<at::Tensor> &n_rows_dev,
+                   const at::Tensor &norm_weight, const std::optional<at::Tensor> &norm_bias,
+                   int64_t norm_type, double eps, const at::Tensor &down_t,
+                   const std::optional<at::Tensor> &folded, const std::optional<at::Tensor> &colsum,
+                   const std::optional<at::Tensor> &bias_proj, const at::Tensor &up,
+                   double up_bias, double threshold, const std::optional<at::Tensor> &positions,
+                   const std::optional<at::Tensor> &slots,
+                   const std::optional<at::Tensor> &out_buffer,
+                   const std::optional<at::Tensor> &compact_out,
+                   const std::optional<at::Tensor> &positions_out,
+                   const std::optional<at::Tensor> &slots_out,
+                   const std::optional<at::Tensor> &exit_positions_out,
+                   const std::optional<at::Tensor> &scores_out, const at::Tensor &counts,
+                   const at::Tensor &error_word, const at::Tensor &workspace, int64_t path) {
+  check_cuda_contig(x, "x");
+  TORCH_CHECK(x.dim() == 2, "x must be [N, H]");
+  const int64_t n = x.size(0), H = x.size(1);
+  const int64_t B = up.numel();
+  auto chk = [&](const std::optional<at::Tensor> &t, const char *name, at::ScalarType st,
+                 int64_t numel) {
+    if (!t.has_value() || !t->defined()) return;
+    check_cuda_contig(*t, name);
+    TORCH_CHECK(t->scalar_type() == st, name, " has dtype ", t->scalar_type(), ", expected ", st);
+    TORCH_CHECK(numel < 0 || t->numel() >= numel, name, " is too small");
+  };
+  chk(n_rows_dev, "n_rows_dev", at::kInt, 1);
+  chk(norm_bias, "norm_bias", at::kFloat, H);
+  chk(folded, "folded", x.scalar_type(), B * H);
+  chk(colsum, "colsum", at::kFloat, B);
+  chk(bias_proj, "bias_proj", at::kFloat, B);
+  chk(positions, "positions", at::kLong, n);
+  chk(slots, "slots", at::kInt, n);
+  chk(out_buffer, "out_buffer", x.scalar_type(), -1);
+  chk(compact_out, "compact_out", x.scalar_type(), n * H);
+  chk(positions_out, "positions_out", at::kLong, n);
+  chk(slots_out, "slots_out", at::kInt, n);
+  chk(exit_positions_out, "exit_positions_out", at::kLong, n);
+  chk(scores_out, "scores_out", at::kFloat, n);
+  check_cuda_contig(norm_weight, "norm_weight");
+  check_cuda_contig(down_t, "down_t");
+  check_cuda_contig(up, "up");
+  check_cuda_contig(counts, "counts");
+  check_cuda_contig(error_word, "error_word");
+  check_cuda_contig(workspace, "workspace");
+  TORCH_CHECK(norm_weight.scalar_type() == at::kFloat && norm_weight.numel() == H,
+              "norm_weight must be fp32 [H]");
+  TORCH_CHECK(down_t.scalar_type() == at::kFloat && down_t.numel() == H * B,
+              "down_t must be fp32 [H, B]");
+  TORCH_CHECK(up.scalar_type() == at::kFloat, "up must be fp32");
+  TORCH_CHECK(counts.scalar_type() == at::kInt && counts.numel() >= 2, "counts must be int32[2]");
+  TORCH_CHECK(error_word.scalar_type() == at::kInt && error_word.numel() >= 1,
+              "error_word must be int32[1]");
+  int64_t n_total = 0;
+  if (out_buffer.has_value() && out_buffer->defined()) {
+    TORCH_CHECK(out_buffer->dim() == 2 && out_buffer->size(1) == H, "out_buffer must be [N_total, H]");
+    n_total = out_buffer->size(0);
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  tide_checkpoint_args a{};
+  a.dtype = to_dtype(x.scalar_type(), "checkpoint");
+  a.norm_type = (int32_t)norm_type;
+  a.path = (int32_t)path;
+  a.n_rows = n;
+  a.hidden_dim = H;
+  a.bottleneck_dim = B;
+  a.n_total = n_total;
+  a.x = x.data_ptr();
+  a.n_rows_dev = static_cast<const int32_t *>(opt_ptr(n_rows_dev));
+  a.norm_weight = norm_weight.data_ptr<float>();
+  a.norm_bias = static_cast<const float *>(opt_ptr(norm_bias));
+  a.eps = (float)eps;
+  a.up_bias = (float)up_bias;
+  a.down_t = down_t.data_ptr<float>();
+  a.folded = opt_ptr(folded);
+  a.colsum = static_cast<const float *>(opt_ptr(colsum));
+  a.bias_proj = static_cast<const float *>(opt_ptr(bias_proj));
+  a.up = up.data_ptr<float>();
+  a.threshold = (float)threshold;
+  a.positions_in = static_cast<const int64_t *>(opt_ptr(positions));
+  a.slots_in = static_cast<const int32_t *>(opt_ptr(slots));
+  a.out_buffer = opt_mut(out_buffer);
+  a.compact_out = opt_mut(compact_out);
+  a.positions_out = static_cast<int64_t *>(opt_mut(positions_out));
+  a.slots_out = static_cast<int32_t *>(opt_mut(slots_out));
+  a.exit_positions_out = static_cast<int64_t *>(opt_mut(exit_positions_out));
+  a.scores_out = static_cast<float *>(opt_mut(scores_out));
+  a.counts_out = counts.data_ptr<int32_t>();
+  a.error_word = error_word.data_ptr<int32_t>();
+  a.workspace = workspace.data_ptr();
+  a.workspace_bytes = (size_t)workspace.numel() * workspace.element_size();
+  const int chosen = tide_checkpoint_select_path(&a);
+  TORCH_CHECK(chosen > 0, "checkpoint: ", tide_last_error());
+  TIDE_CHECK_OK(tide_checkpoint(&a, cur_stream(x)));
+  return chosen;
+}
+
+}  // namespace
+
+TORCH_LIBRARY(tide, m) {
+  m.def("fused_layernorm_route(Tensor input, Tensor norm_weight, Tensor down_weight, "
+        "Tensor up_weight, float eps) -> Tensor");
+  m.def("batch_compact(Tensor input, Tensor exit_mask) -> Tensor[]");
+  m.def("exit_scatter(Tensor exited_states, Tensor exit_positions, Tensor(a!) output_buffer) -> ()");
+  m.def("exit_projection(Tensor exited_states, Tensor norm_weight, Tensor exit_positions, "
+        "Tensor(a!) output_buffer, float eps) -> ()");
+  m.def("norm_scatter(Tensor rows, Tensor positions, Tensor(a!) output_buffer, "
+        "Tensor norm_weight, Tensor? norm_bias, int norm_type, float eps) -> ()");
+  m.def("router_fold(Tensor down, Tensor norm_weight, Tensor? norm_bias, ScalarType fold_dtype) "
+        "-> Tensor[]");
+  m.def("checkpoint_workspace_size(int n_rows) -> int", &checkpoint_workspace_size);
+  m.def("checkpoint(Tensor x, Tensor? n_rows_dev, Tensor norm_weight, Tensor? norm_bias, "
+        "int norm_type, float eps, Tensor down_t, Tensor? folded, Tensor? colsum, "
+        "Tensor? bias_proj, Tensor up, float up_bias, float threshold, Tensor? positions, "
+        "Tensor? slots, Tensor(a!)? out_buffer, Tensor(b!)? compact_out, "
+        "Tensor(c!)? positions_out, Tensor(d!)? slots_out, Tensor(e!)? exit_positions_out, "
+        "Tensor(f!)? scores_out, Tensor(g!) counts, Tensor(h!) error_word, "
+        "Tensor(i!) workspace, int path) -> int");
+}
+
+TORCH_LIBRARY_IMPL(tide, CUDA, m) {
+  m.impl("fused_layernorm_route", &fused_layernorm_route);
+  m.impl("batch_compact", &batch_compact);
+  m.impl("exit_scatter", &exit_scatter);
+  m.impl("exit_projection", &exit_projection);
+  m.impl("norm_scatter", &norm_scatter);
+  m.impl("router_fold", &router_fold);
+  m.impl("checkpoint", &checkpoint);
+}

@@ -1,0 +1,218 @@
+"""TIDERuntime: the early-exit runtime, drop-in for the reference's
+TIDE.TIDE (python/TIDE/runtime.py:56-389).
+
+The model still runs every layer (the reference's post-hoc design,
+runtime.py:151-156); what changes is each checkpoint.  The reference
+normalises and scores the whole [B*S, H] tensor with PyTorch ops and
+scatters exits with boolean indexing (runtime.py:168-188).  Here one native
+call per checkpoint scores only the still-active rows, decides, writes the
+exiting rows final-normed straight into the output buffer and compacts the
+positions of the survivors (torch.ops.tide.checkpoint, sm_100a kernels).
+The rows that never exit are final-normed and scattered by one more call
+(torch.ops.tide.norm_scatter).
+
+Semantics kept from the reference: router layer L scores hidden_states[L+1]
+(runtime.py:172); layers below config.min_layers are skipped (:169); exits
+are strict `score > exit_threshold` (:174) and sticky; the final norm is the
+model's own module type and eps (:129,177); last_stats is an ExitStats
+with exits recorded only for layers where some token exited (:176-180).
+The only supported device is CUDA: there is no CPU path.
+"""
+from __future__ import annotations
+
+import logging
+from pathlib import Path
+from typing import Dict, Optional
+
+import torch
+import torch.nn as nn
+
+from tide_b200 import _native
+from tide_b200.adapters.auto import get_adapter
+from tide_b200.config import TIDEConfig
+from tide_b200.ops import CheckpointRunner, PreparedRouter, norm_spec, prepare_router
+from tide_b200.router import RouterCheckpoint, TokenRouter
+from tide_b200.scheduler import ExitStats
+from tide_b200.utils import setup_logging
+
+logger = setup_logging()
+
+
+class TIDERuntime(nn.Module):
+    def __init__(self, model: nn.Module, router_path: str | Path,
+                 config: Optional[TIDEConfig] = None, use_cuda_kernels: bool = True):
+        super().__init__()
+        self.model = model
+        self.config = config or TIDEConfig()
+        self.adapter = get_adapter(model)
+        dev = self._device
+        if dev.type != "cuda":
+            raise RuntimeError("tide_b200.TIDE needs the model on a CUDA device: the early-exit "
+                               "path exists only as sm_100a kernels")
+        if not use_cuda_kernels:
+            logger.warning("use_cuda_kernels=False has no effect: tide_b200 always runs its "
+                           "CUDA kernels")
+        self.use_cuda = True
+        _native.ops()  # fail now, loudly, if the extension is missing
+        ckpt = RouterCheckpoint.load(router_path, device=str(dev))
+        self.routers: Dict[int, TokenRouter] = {}
+        for layer, r in ckpt.routers.items():
+            r.requires_grad_(False)
+            self.routers[int(layer)] = r
+        self._layers = self.adapter.get_layers(model)
+        self._final_norm = self.adapter.get_final_norm(model)
+        self._lm_head = self.adapter.get_lm_head(model)
+        self._norm = norm_spec(self._final_norm, dev)
+        self._prepared: Dict[tuple, PreparedRouter] = {}
+        self._runner = CheckpointRunner(dev)
+        self.last_stats: Optional[ExitStats] = None
+        logger.info(f"TIDERuntime initialized: {len(self._layers)} layers, "
+                    f"{len(self.routers)} routers, CUDA=on (sm_100a)")
+
+    @property
+    def _device(self) -> torch.device:
+        return next(self.model.parameters()).device
+
+    def _router(self, layer: int, dtype: torch.dtype) -> PreparedRouter:
+        key = (layer, dtype)
+        if key not in self._prepared:
+            r = self.routers[layer]
+            self._prepared[key] = prepare_router(r.down.weight, r.up.weight, r.up_bias_value,
+                                                 self._norm, dtype)
+        return self._prepared[key]
+
+    def _score_router(self, hidden: torch.Tensor, layer_idx: int) -> torch.Tensor:
+        """Router scores of hidden [..., H] in the leading shape
+        (runtime.py:108-132), computed by the native checkpoint kernels."""
+        flat = hidden.reshape(-1, hidden.shape[-1]).contiguous()
+        _native.require_cuda(flat, "hidden states")
+        scores = torch.empty(flat.shape[0], dtype=torch.float32, device=flat.device)
+        self._runner.run(flat, self._router(layer_idx, flat.dtype), self._norm,
+                         self.config.exit_threshold, scores_out=scores)
+        return scores.view(hidden.shape[:-1])
+
+    @torch.no_grad()
+    def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
+                **kwargs) -> torch.Tensor:
+        B, S = input_ids.shape
+        out = self.model(input_ids, attention_mask=attention_mask, output_hidden_states=True,
+                         return_dict=True)
+        hs = out.hidden_states
+        H = hs[-1].shape[-1]
+        dtype = hs[-1].dtype
+        dev = hs[-1].device
+        N = B * S
+        out_buf = torch.zeros(N, H, device=dev, dtype=dtype)
+        stats = ExitStats(total_tokens=N)
+        positions = torch.arange(N, device=dev, dtype=torch.int64)
+        spare = torch.empty_like(positions)
+        n_active = N
+        thr = self.config.exit_threshold
+        for layer in sorted(self.routers):
+            if layer < self.config.min_layers or n_active == 0:
+                continue
+            hidden = hs[layer + 1].reshape(N, H)
+            x = hidden if n_active == N else hidden.index_select(0, positions[:n_active])
+            counts = self._runner.run(x.contiguous(), self._router(layer, dtype), self._norm, thr,
+                                      positions=positions[:n_active], out_buffer=out_buf,
+                                      positions_out=spare)
+            n_surv, n_exit = (int(v) for v in counts.tolist())
+            if n_exit > 0:
+                stats.exits_per_layer[layer] = n_exit
+            positions, spare = spare, positions
+            n_active = n_surv
+        if n_active > 0:
+            final = hs[-1].reshape(N, H)
+            rows = final if n_active == N else final.index_select(0, positions[:n_active])
+            self._runner.norm_scatter(rows.contiguous(), positions[:n_active], out_buf, self._norm)
+        stats.remaining_tokens = n_active
+        self._runner.check_errors()
+        self.last_stats = stats
+        return self._lm_head(out_buf.view(B, S, H))
+
+    @torch.no_grad()
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 512,
+                 temperature: float = 1.0, top_k: int = 50, top_p: float = 0.9,
+                 **kwargs) -> torch.Tensor:
+        """Autoregressive decode with the reference's whole-batch exit rule
+        (runtime.py:223-313): every step runs all layers; the earliest
+        checkpoint at which every row's score passes the threshold supplies
+        the next-token logits via lm_head(final_norm(h)).  Generation stops
+        when every sampled token equals `eos_token_id` (default 2, the
+        reference's fixed id, runtime.py:257)."""
+        eos = kwargs.get("eos_token_id", 2)
+        B = input_ids.shape[0]
+        n_layers = len(self._layers)
+        generated = input_ids.clone()
+        gen_stats = ExitStats(total_tokens=0)
+        pre = self.model(generated, use_cache=True, return_dict=True)
+        past = pre.past_key_values
+        next_logits = pre.logits[:, -1, :]
+        positions = torch.arange(B, device=input_ids.device, dtype=torch.int64)
+        for _ in range(max_new_tokens):
+            nxt = sample_next_token(next_logits, temperature, top_k, top_p)
+            generated = torch.cat([generated, nxt], dim=-1)
+            if bool((nxt == eos).all()):
+                break
+            gen_stats.total_tokens += B
+            out = self.model(nxt, past_key_values=past, use_cache=True, return_dict=True,
+                             output_hidden_states=True)
+            past = out.past_key_values
+            hs = out.hidden_states
+            exit_layer = None
+            exit_hidden = None
+            for layer in sorted(self.routers):
+                if layer < self.config.min_layers:
+                    continue
+                h = hs[layer + 1][:, -1, :].contiguous()
+                counts = self._runner.run(h, self._router(layer, h.dtype), self._norm,
+                                          self.config.exit_threshold)
+                if int(counts[1].item()) == B:  # every row exits: (scores > thr).all()
+                    exit_layer, exit_hidden = layer, h
+                    break
+            if exit_layer is not None:
+                normed = torch.empty_like(exit_hidden)
+                self._runner.norm_scatter(exit_hidden, positions, normed, self._norm)
+                next_logits = self._lm_head(normed)
+                gen_stats.exits_per_layer[exit_layer] = gen_stats.exits_per_layer.get(exit_layer, 0) + B
+            else:
+                next_logits = out.logits[:, -1, :]
+                gen_stats.remaining_tokens += B
+        self._runner.check_errors()
+        self.last_stats = gen_stats
+        if gen_stats.total_tokens > 0:
+            runs = sum((l + 1) * c for l, c in gen_stats.exits_per_layer.items())
+            runs += gen_stats.remaining_tokens * n_layers
+            speedup = gen_stats.total_tokens * n_layers / runs if runs > 0 else 1.0
+            logger.info(f"Generation: {gen_stats.total_tokens} tokens, {gen_stats.total_exited} "
+                        f"exits ({gen_stats.exit_rate:.1%}), estimated {speedup:.2f}x "
+                        f"equivalent speedup")
+        return generated
+
+    @staticmethod
+    def calibrate(*args, **kwargs):
+        raise NotImplementedError(
+            "router calibration (offline training) is not part of tide_b200; router.pt files "
+            "written by the reference's calibrate() load here unchanged")
+
+
+def sample_next_token(logits: torch.Tensor, temperature: float, top_k: int,
+                      top_p: float) -> torch.Tensor:
+    """Temperature, top-k and nucleus (top-p) sampling of one token per row
+    (same rules as runtime.py:315-352); greedy when temperature <= 0."""
+    if temperature <= 0:
+        return logits.argmax(dim=-1, keepdim=True)
+    z = logits / temperature
+    if top_k > 0:
+        k = min(top_k, z.shape[-1])
+        kth = torch.topk(z, k, dim=-1).values[:, -1:]
+        z = z.masked_fill(z < kth, float("-inf"))
+    if top_p < 1.0:
+        sz, idx = torch.sort(z, descending=True, dim=-1)
+        cum = torch.softmax(sz, dim=-1).cumsum(dim=-1)
+        drop = cum > top_p
+        drop[:, 1:] = drop[:, :-1].clone()
+        drop[:, 0] = False
+        sz = sz.masked_fill(drop, float("-inf"))
+        z = torch.empty_like(z).scatter_(1, idx, sz)
+    return torch.multinomial(torch.softmax(z, dim=-1), num_samples=1)
