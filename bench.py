@@ -197,9 +197,9 @@ class Workload:
 
 
 def launches_per_checkpoint(path_used: int) -> int:
-    from tide_b200.capi import PATH_TC
-
-    return 1 if path_used == PATH_TC else 2
+    """Kernels of ours per checkpoint call: the router (SIMT or tensor-core)
+    and the stable-partition move kernel."""
+    return 2
 
 
 # ----------------------------------------------------------------- CPU leg

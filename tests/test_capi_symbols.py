@@ -94,3 +94,27 @@ def test_operators_have_no_cpu_kernel():
     x = torch.zeros(4, 8)
     with pytest.raises(NotImplementedError):
         ops.exit_scatter(x, torch.zeros(4, dtype=torch.int32), x.clone())
+
+
+def test_path_selection():
+    """bf16/fp16 with folded weights, H % 64 == 0 and B % 32 == 0 go to the
+    tensor-core path; fp32 and other shapes to the SIMT path."""
+    lib = _native.lib()
+
+    def sel(**kw):
+        base = dict(dtype=capi.DTYPE_BF16, n_rows=1000, hidden_dim=4096, bottleneck_dim=128,
+                    n_total=1000, x=1 << 20, norm_weight=16, up=16, counts_out=16,
+                    workspace=1 << 20, folded=1 << 21, colsum=16)
+        base.update(kw)
+        a = capi.CheckpointArgs(**base)
+        return lib.tide_checkpoint_select_path(ctypes.byref(a))
+
+    assert sel() == capi.PATH_TC
+    assert sel(dtype=capi.DTYPE_F16) == capi.PATH_TC
+    assert sel(dtype=capi.DTYPE_F32, folded=None) == capi.PATH_SIMT
+    assert sel(hidden_dim=4000) == capi.PATH_SIMT
+    assert sel(bottleneck_dim=48) == capi.PATH_SIMT
+    assert sel(folded=None) == capi.PATH_SIMT
+    assert sel(path=capi.PATH_SIMT) == capi.PATH_SIMT
+    assert sel(path=capi.PATH_TC, hidden_dim=4000) == -capi.DEVERR_TIMEOUT  # -TIDE_ERR_UNSUPPORTED
+    assert b"multiple of 64" in lib.tide_last_error()

@@ -58,7 +58,7 @@ def test_checkpoint_matches_reference(name):
         rows = g["normed_exit_rows_idx"]
         ours = res["out_buffer"][rows]
         ulp = O.ulp_distance(ours, g["normed_exit_rows"], dt)
-        assert ulp.max() <= (4 if dt == O.F32 else 1), ulp.max()
+        assert ulp.max() <= (8 if dt == O.F32 else 1), ulp.max()
 
 
 def test_compaction_kats():

@@ -314,17 +314,15 @@ int tide_checkpoint(const tide_checkpoint_args *a, tide_stream_t stream) {
                 tide_checkpoint_workspace_size(a), a->workspace_bytes);
   cudaStream_t s = (cudaStream_t)stream;
 
-  if (path == TIDE_PATH_TC) {
-    int rc = tide::tc_checkpoint_launch(a, s, g_err, sizeof(g_err));
-    return rc;
-  }
-
-  if (!a->down_t) return fail(TIDE_ERR_INVALID, "tide_checkpoint: SIMT path needs down_t");
   SimtWs w = simt_ws(a->workspace, n);
   if (cudaMemsetAsync(a->workspace, 0, w.partition_bytes, s) != cudaSuccess)
     return fail(TIDE_ERR_CUDA, "tide_checkpoint: memset failed");
   float *scores = a->scores_out ? a->scores_out : w.scores;
-  if (n > 0) {
+  if (path == TIDE_PATH_TC) {
+    int rc = tide::tc_route_launch(a, scores, w.stats, s, g_err, sizeof(g_err));
+    if (rc != TIDE_OK) return rc;
+  } else if (n > 0) {
+    if (!a->down_t) return fail(TIDE_ERR_INVALID, "tide_checkpoint: SIMT path needs down_t");
     tide::RouteParams rp{};
     rp.x = a->x; rp.n_cap = n; rp.n_dev = a->n_rows_dev;
     rp.H = (int)a->hidden_dim; rp.B = (int)a->bottleneck_dim; rp.norm_type = a->norm_type;

@@ -10,6 +10,8 @@ namespace tide {
 bool tc_supported(const tide_checkpoint_args *a);
 const char *tc_unsupported_reason(const tide_checkpoint_args *a);
 size_t tc_workspace_bytes(int64_t n_rows);
-int tc_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t s, char *err, size_t err_len);
+// Scores and per-row (mean, rstd) of the active rows on the tensor cores.
+int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_stats,
+                    cudaStream_t s, char *err, size_t err_len);
 
 }  // namespace tide
