@@ -381,13 +381,21 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   const int64_t tiles = (a->n_rows + kTcM - 1) / kTcM;
   const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
   cudaError_t e;
-  if (bf16) {
-    cudaFuncSetAttribute(tc_route_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    tc_route_kernel<true><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
-  } else {
-    cudaFuncSetAttribute(tc_route_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    tc_route_kernel<false><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
+  // the opt-in shared memory size is raised once per kernel to the budget
+  static bool attr_set[2] = {false, false};
+  if (!attr_set[bf16]) {
+    e = cudaFuncSetAttribute(bf16 ? (const void *)tc_route_kernel<true> : (const void *)tc_route_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBudget);
+    if (e != cudaSuccess) {
+      snprintf(err, err_len, "tensor-core route: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return TIDE_ERR_CUDA;
+    }
+    attr_set[bf16] = true;
   }
+  if (bf16)
+    tc_route_kernel<true><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
+  else
+    tc_route_kernel<false><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(err, err_len, "tensor-core route launch: %s", cudaGetErrorString(e));
