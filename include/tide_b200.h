@@ -92,6 +92,23 @@ int tide_batch_compact(int dtype, const void *input, const int32_t *exit_mask,
                        int64_t hidden_dim, void *workspace, size_t workspace_bytes,
                        int32_t *error_word, tide_stream_t stream);
 
+/* tide_batch_compact for callers that cannot allocate device memory: the
+ * same split, outputs and argument meaning, but no workspace argument.  For
+ * hosts that only lend the library the tensors they pass in (an FFI host
+ * whose GPU memory belongs to another runtime, code running where allocation
+ * is forbidden).  It has no counterpart in the reference.
+ * Its look-back scratch is a file-scope device array sized for at most
+ * TIDE_NOALLOC_MAX_ROWS rows (65,792 bytes, held by every GPU that loads the
+ * library until exit); larger n_tokens is rejected with TIDE_ERR_INVALID.  It
+ * calls no allocator.  The first call on a device looks the array's address
+ * up (make it before any stream capture).  All calls on a device share the
+ * array: calls whose kernels overlap on the GPU race, so serialise them. */
+#define TIDE_NOALLOC_MAX_ROWS 1048576
+int tide_batch_compact_noalloc(int dtype, const void *input, const int32_t *exit_mask,
+                               void *compacted, void *exited, int32_t *continue_indices,
+                               int32_t *exit_indices, int32_t *num_remaining, int64_t n_tokens,
+                               int64_t hidden_dim, int32_t *error_word, tide_stream_t stream);
+
 /* output_buffer[exit_positions[i]] = exited_states[i]  (bit copy) */
 int tide_exit_scatter(int dtype, const void *exited_states, const int32_t *exit_positions,
                       void *output_buffer, int64_t n_exited, int64_t hidden_dim,

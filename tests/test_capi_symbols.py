@@ -116,5 +116,5 @@ def test_path_selection():
     assert sel(bottleneck_dim=48) == capi.PATH_SIMT
     assert sel(folded=None) == capi.PATH_SIMT
     assert sel(path=capi.PATH_SIMT) == capi.PATH_SIMT
-    assert sel(path=capi.PATH_TC, hidden_dim=4000) == -capi.DEVERR_TIMEOUT  # -TIDE_ERR_UNSUPPORTED
+    assert sel(path=capi.PATH_TC, hidden_dim=4000) == -capi.ERR_UNSUPPORTED
     assert b"multiple of 64" in lib.tide_last_error()

@@ -10,6 +10,8 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 NORM_RMS, NORM_LAYER = 0, 1
 PATH_AUTO, PATH_SIMT, PATH_TC = 0, 1, 2
 OK = 0
+ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_ALIGNMENT = 1, 2, 3, 4, 5
+NOALLOC_MAX_ROWS = 1048576
 DEVERR_POSITION, DEVERR_TIMEOUT, DEVERR_COUNT = 1, 2, 4
 
 p = C.c_void_p
@@ -38,6 +40,7 @@ PROTOTYPES = {
     "tide_fused_layernorm_route": (C.c_int, [C.c_int, p, p, p, p, f32, p, i64, i64, i64, p]),
     "tide_batch_compact_workspace_size": (sz, [i64]),
     "tide_batch_compact": (C.c_int, [C.c_int, p, p, p, p, p, p, p, i64, i64, p, sz, p, p]),
+    "tide_batch_compact_noalloc": (C.c_int, [C.c_int, p, p, p, p, p, p, p, i64, i64, p, p]),
     "tide_exit_scatter": (C.c_int, [C.c_int, p, p, p, i64, i64, i64, p, p]),
     "tide_exit_projection": (C.c_int, [C.c_int, p, p, p, p, f32, i64, i64, i64, p, p]),
     "tide_norm_scatter": (C.c_int, [C.c_int, C.c_int, p, p, p, p, p, f32, i64, i64, i64, p, p]),

@@ -351,3 +351,8 @@ int tide_checkpoint(const tide_checkpoint_args *a, tide_stream_t stream) {
 }
 
 }  // extern "C"
+
+namespace tide {
+// Lets other translation units of the library report through tide_last_error().
+void set_last_error(const char *msg) { snprintf(g_err, sizeof(g_err), "%s", msg); }
+}  // namespace tide
