@@ -214,6 +214,10 @@ struct MoveParams {
   int32_t *err;
 };
 
+// Row moves: one warp per row, kRowUnroll 16-byte vectors per lane loaded
+// before any is stored, so a warp keeps up to 4 KB of the row in flight.
+constexpr int kRowUnroll = 8;
+
 template <typename T, bool VEC>
 __device__ __forceinline__ void copy_row(const T *__restrict__ src, T *__restrict__ dst, int64_t H,
                                          int lane) {
@@ -221,16 +225,19 @@ __device__ __forceinline__ void copy_row(const T *__restrict__ src, T *__restric
     const int64_t nv = H / kVec<T>;
     const uint4 *s = reinterpret_cast<const uint4 *>(src);
     uint4 *d = reinterpret_cast<uint4 *>(dst);
-    int64_t i = lane;
-    for (; i + 96 < nv; i += 128) {
-      uint4 a = ld_stream(s + i), b = ld_stream(s + i + 32), c = ld_stream(s + i + 64),
-            e = ld_stream(s + i + 96);
-      st_stream(d + i, a);
-      st_stream(d + i + 32, b);
-      st_stream(d + i + 64, c);
-      st_stream(d + i + 96, e);
+    for (int64_t base = lane; base < nv; base += 32 * kRowUnroll) {
+      uint4 v[kRowUnroll];
+#pragma unroll
+      for (int u = 0; u < kRowUnroll; ++u) {
+        const int64_t i = base + 32 * u;
+        if (i < nv) v[u] = ld_stream(s + i);
+      }
+#pragma unroll
+      for (int u = 0; u < kRowUnroll; ++u) {
+        const int64_t i = base + 32 * u;
+        if (i < nv) st_stream(d + i, v[u]);
+      }
     }
-    for (; i < nv; i += 32) st_stream(d + i, ld_stream(s + i));
   } else {
     for (int64_t i = lane; i < H; i += 32) dst[i] = src[i];
   }
@@ -238,40 +245,73 @@ __device__ __forceinline__ void copy_row(const T *__restrict__ src, T *__restric
 
 // y = final_norm(x) rounded to T.  RMSNorm: w * (x * rstd)
 // (LlamaRMSNorm / Qwen3RMSNorm).  LayerNorm: (x * rstd - mean * rstd) * w + b.
+template <typename T>
+__device__ __forceinline__ float norm_elem(float xv, float wv, float bv, float rstd, float shift,
+                                           int norm_type) {
+  if (norm_type == TIDE_NORM_RMS) return __fmul_rn(wv, __fmul_rn(xv, rstd));
+  const float t = __fadd_rn(__fmul_rn(xv, rstd), shift);
+  return __fadd_rn(__fmul_rn(t, wv), bv);
+}
+
 template <typename T, bool VEC>
 __device__ __forceinline__ void norm_row(const T *__restrict__ src, T *__restrict__ dst, int64_t H,
                                          int lane, float mean, float rstd, int norm_type,
                                          const float *__restrict__ w,
                                          const float *__restrict__ bias) {
   const float shift = -rstd * mean;
-  auto f = [&](float xv, float wv, float bv) -> float {
-    if (norm_type == TIDE_NORM_RMS) return __fmul_rn(wv, __fmul_rn(xv, rstd));
-    float t = __fadd_rn(__fmul_rn(xv, rstd), shift);
-    return __fadd_rn(__fmul_rn(t, wv), bv);
-  };
   if (VEC) {
     constexpr int V = kVec<T>;
     const int64_t nv = H / V;
     const uint4 *s = reinterpret_cast<const uint4 *>(src);
     uint4 *d = reinterpret_cast<uint4 *>(dst);
-    for (int64_t i = lane; i < nv; i += 32) {
-      float xv[V], y[V];
-      unpack16<T>(ld_stream(s + i), xv);
+    const bool wvec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(bias)) & 15u) == 0;
+    for (int64_t base = lane; base < nv; base += 32 * kRowUnroll) {
+      uint4 v[kRowUnroll];
 #pragma unroll
-      for (int j = 0; j < V; ++j) {
-        const int64_t col = i * V + j;
-        y[j] = f(xv[j], __ldg(w + col), bias ? __ldg(bias + col) : 0.f);
+      for (int u = 0; u < kRowUnroll; ++u) {
+        const int64_t i = base + 32 * u;
+        if (i < nv) v[u] = ld_stream(s + i);
       }
-      st_stream(d + i, pack16<T>(y));
+#pragma unroll
+      for (int u = 0; u < kRowUnroll; ++u) {
+        const int64_t i = base + 32 * u;
+        if (i >= nv) continue;
+        float xv[V], y[V], wv[V], bv[V];
+        unpack16<T>(v[u], xv);
+        const int64_t col = i * V;
+        if (wvec) {
+#pragma unroll
+          for (int j = 0; j < V; j += 4) {
+            const float4 w4 = __ldg(reinterpret_cast<const float4 *>(w + col + j));
+            wv[j] = w4.x; wv[j + 1] = w4.y; wv[j + 2] = w4.z; wv[j + 3] = w4.w;
+            if (bias) {
+              const float4 b4 = __ldg(reinterpret_cast<const float4 *>(bias + col + j));
+              bv[j] = b4.x; bv[j + 1] = b4.y; bv[j + 2] = b4.z; bv[j + 3] = b4.w;
+            } else {
+              bv[j] = bv[j + 1] = bv[j + 2] = bv[j + 3] = 0.f;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < V; ++j) {
+            wv[j] = __ldg(w + col + j);
+            bv[j] = bias ? __ldg(bias + col + j) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < V; ++j) y[j] = norm_elem<T>(xv[j], wv[j], bv[j], rstd, shift, norm_type);
+        st_stream(d + i, pack16<T>(y));
+      }
     }
   } else {
     for (int64_t i = lane; i < H; i += 32)
-      dst[i] = Elem<T>::from_f(f(Elem<T>::to_f(src[i]), w[i], bias ? bias[i] : 0.f));
+      dst[i] = Elem<T>::from_f(norm_elem<T>(Elem<T>::to_f(src[i]), w[i], bias ? bias[i] : 0.f,
+                                            rstd, shift, norm_type));
   }
 }
 
 template <typename T, bool VEC>
-__global__ void __launch_bounds__(kMoveThreads, 4) move_rows_kernel(MoveParams p) {
+__global__ void __launch_bounds__(kMoveThreads, 2) move_rows_kernel(MoveParams p) {
   __shared__ uint32_t s_tile;
   __shared__ uint32_t s_wkeep[kMoveTile / 32], s_wexit[kMoveTile / 32];
   __shared__ uint32_t s_keep_before, s_exits_before;

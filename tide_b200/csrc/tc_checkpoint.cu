@@ -64,7 +64,7 @@ __device__ __forceinline__ void unpack8_16(const uint4 &v, float *f, bool bf16) 
   }
 }
 
-template <bool BF16>
+template <bool BF16, bool LAYER>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_route_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_w, TcRouteParams p) {
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             ss = fmaf(f[e], f[e], ss);
-            sx += f[e];
+            if (LAYER) sx += f[e];
           }
         }
         __syncwarp();
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (!ok) break;
       float mean = 0.f, rstd;
-      if (p.norm_type == TIDE_NORM_RMS) {
+      if (!LAYER) {
         rstd = rsqrt_rn(ss / (float)p.H + p.eps);
       } else {
         mean = sx / (float)p.H;
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           float z;
-          if (p.norm_type == TIDE_NORM_RMS)
+          if (!LAYER)
             z = rstd * v[j];
           else
             z = fmaf(rstd, v[j] - mean * s_cs[c + j], s_bp[c + j]);
@@ -382,20 +382,26 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
   cudaError_t e;
   // the opt-in shared memory size is raised once per kernel to the budget
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[bf16]) {
-    e = cudaFuncSetAttribute(bf16 ? (const void *)tc_route_kernel<true> : (const void *)tc_route_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBudget);
+  const bool layer = a->norm_type == TIDE_NORM_LAYER;
+  const void *fn = bf16 ? (layer ? (const void *)tc_route_kernel<true, true> : (const void *)tc_route_kernel<true, false>)
+                        : (layer ? (const void *)tc_route_kernel<false, true> : (const void *)tc_route_kernel<false, false>);
+  static bool attr_set[4] = {false, false, false, false};
+  const int which = (bf16 ? 2 : 0) + (layer ? 1 : 0);
+  if (!attr_set[which]) {
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBudget);
     if (e != cudaSuccess) {
       snprintf(err, err_len, "tensor-core route: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return TIDE_ERR_CUDA;
     }
-    attr_set[bf16] = true;
+    attr_set[which] = true;
   }
-  if (bf16)
-    tc_route_kernel<true><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
-  else
-    tc_route_kernel<false><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
+  if (bf16) {
+    if (layer) tc_route_kernel<true, true><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
+    else tc_route_kernel<true, false><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
+  } else {
+    if (layer) tc_route_kernel<false, true><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
+    else tc_route_kernel<false, false><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(err, err_len, "tensor-core route launch: %s", cudaGetErrorString(e));
