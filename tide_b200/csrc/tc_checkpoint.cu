@@ -14,9 +14,10 @@
 //               [B x 64] per pipeline stage (128-byte swizzle);
 //   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K = 16) per
 //               stage into one of two fp32 accumulators of B columns;
-//   warps 4-7   row statistics from the x chunks (thread = row), then the
-//               epilogue: tcgen05.ld of the accumulator row, SiLU, up
-//               projection, sigmoid; writes the score and (mean, rstd).
+//   warps 4-11  row statistics from the x chunks (two threads per row, each
+//               half of the chunk's 128 bytes);
+//   warps 4-7   then the epilogue: tcgen05.ld of the accumulator row, SiLU,
+//               up projection, sigmoid; writes the score and (mean, rstd).
 // The survivors/exits are then moved by the stable-partition kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -30,10 +31,10 @@ namespace tide {
 
 constexpr int kTcM = 128;         // rows per tile (TMEM lanes)
 constexpr int kTcK = 64;          // columns per chunk: 128 bytes of 16-bit data
-constexpr int kTcThreads = 256;
+constexpr int kTcThreads = 384;  // warps 0-1 TMA/MMA, 4-11 statistics, 4-7 epilogue
 constexpr int kTcMaxStages = 8;
 constexpr int kTcSmemBudget = 227 * 1024;
-constexpr int kTcAux = 4096;      // barriers, flags, per-unit vectors
+constexpr int kTcAux = 8192;      // barriers, flags, per-unit vectors, half-row sums
 
 struct TcRouteParams {
   int64_t n_cap;
@@ -79,14 +80,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * stage_bytes);
   uint64_t *empty = full + S;
   uint64_t *acc_full = empty + S;
-  uint64_t *acc_empty = acc_full + 2;
-  uint64_t *drain = acc_empty + 2;
+  uint64_t *acc_empty = acc_full + 2;  // [0,1] accumulators, [2] half-sums slot
+  uint64_t *half_full = acc_empty + 3;
+  uint64_t *drain = half_full + 1;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   uint32_t *issued = reinterpret_cast<uint32_t *>(tmem_slot + 2);
   float *s_up = reinterpret_cast<float *>(tmem_slot + 4);
   float *s_cs = s_up + 256;
   float *s_bp = s_cs + 256;
+  float *s_half = s_bp + 256;  // [2][128] partial sums of the second half-rows
 
   int64_t n = p.n_cap;
   if (p.n_dev) {
@@ -99,12 +102,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 statistics warps
+      ptx::mbar_init(&empty[s], 1 + 8);  // MMA commit + 8 statistics warps
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&acc_full[a], 1);
       ptx::mbar_init(&acc_empty[a], 4);
     }
+    ptx::mbar_init(&acc_empty[2], 4);  // second-half sums consumed (per tile)
+    ptx::mbar_init(half_full, 128);  // one arrival per second-half thread
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
     *issued = 0;
@@ -192,39 +197,61 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------ statistics + epilogue
-    const int q = warp - 4;
-    const int r = q * 32 + lane;
+    // thread t of warps 4-11: row r = t % 128, half h = t / 128 of each
+    // chunk row (four of its eight 16-byte units, lane-rotated so a warp's
+    // reads of the swizzled tile hit distinct banks)
+    const int t = threadIdx.x - 128;
+    const int r = t & 127, h = t >> 7;
+    const int q = (warp - 4) & 3;
     uint32_t it = 0;
     int t_local = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++t_local) {
-      float ss = 0.f, sx = 0.f;
+      float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
       for (int kc = 0; kc < k_chunks; ++kc, ++it) {
         const uint32_t s = it % S, ph = (it / S) & 1u;
         if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
         const uint8_t *row = smem + (size_t)s * stage_bytes + (size_t)r * 128;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          // rotate the 16-byte unit per lane: conflict-free with the swizzle
-          const uint4 v = *reinterpret_cast<const uint4 *>(row + (((j + lane) & 7) << 4));
+        for (int j = 0; j < 4; ++j) {
+          const int unit = (h * 4 + j + lane) & 7;
+          const uint4 v = *reinterpret_cast<const uint4 *>(row + (unit << 4));
           float f[8];
           unpack8_16(v, f, BF16);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            ss = fmaf(f[e], f[e], ss);
-            if (LAYER) sx += f[e];
+          for (int e = 0; e < 8; e += 2) {
+            ss0 = fmaf(f[e], f[e], ss0);
+            ss1 = fmaf(f[e + 1], f[e + 1], ss1);
+            if (LAYER) { sx0 += f[e]; sx1 += f[e + 1]; }
           }
         }
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&empty[s]);
       }
       if (!ok) break;
+      const float ss = ss0 + ss1, sx = sx0 + sx1;
+      if (h == 1) {
+        // hand the second half to the epilogue thread of the same row
+        if (t_local > 0 && !ptx::mbar_wait(&acc_empty[2], (uint32_t)(t_local - 1) & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        s_half[r] = ss;
+        s_half[128 + r] = sx;
+        ptx::mbar_arrive(half_full);
+        continue;
+      }
+      if (!ptx::mbar_wait(half_full, (uint32_t)t_local & 1u, abort_flag)) { ok = false; break; }
+      const float ss_row = ss + s_half[r];
+      const float sx_row = sx + s_half[128 + r];
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&acc_empty[2]);
       float mean = 0.f, rstd;
       if (!LAYER) {
-        rstd = rsqrt_rn(ss / (float)p.H + p.eps);
+        rstd = rsqrt_rn(ss_row / (float)p.H + p.eps);
       } else {
-        mean = sx / (float)p.H;
-        const float var = fmaxf(ss / (float)p.H - mean * mean, 0.f);
+        mean = sx_row / (float)p.H;
+        const float var = fmaxf(ss_row / (float)p.H - mean * mean, 0.f);
         rstd = rsqrt_rn(var + p.eps);
       }
       const int acc = t_local & 1;
