@@ -212,9 +212,11 @@ class Workload:
 
 
 def launches_per_checkpoint(path_used: int) -> int:
-    """Kernels of ours per checkpoint call: the router (SIMT or tensor-core)
-    and the stable-partition move kernel."""
-    return 2
+    """Kernels of ours per checkpoint call: one for the fused single-pass
+    kernel, two (router + stable-partition move) otherwise."""
+    from tide_b200.capi import PATH_TC
+
+    return 1 if path_used == PATH_TC else 2
 
 
 # ----------------------------------------------------------------- CPU leg
@@ -279,7 +281,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--path", default="auto", choices=["auto", "simt", "tc"])
+    ap.add_argument("--path", default="auto", choices=["auto", "simt", "tc", "tc_split"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU (profiling runs)")
@@ -293,9 +295,9 @@ def main():
             dist.destroy_process_group()
         return
 
-    from tide_b200.capi import PATH_AUTO, PATH_SIMT, PATH_TC
+    from tide_b200.capi import PATH_AUTO, PATH_SIMT, PATH_TC, PATH_TC_SPLIT
 
-    path = {"auto": PATH_AUTO, "simt": PATH_SIMT, "tc": PATH_TC}[args.path]
+    path = {"auto": PATH_AUTO, "simt": PATH_SIMT, "tc": PATH_TC, "tc_split": PATH_TC_SPLIT}[args.path]
     wl = Workload(rank, path)
     for _ in range(max(args.warmup, 3)):
         wl.step()
@@ -350,7 +352,7 @@ def main():
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": None,
                 "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-                "kernel": "checkpoint 0 (32768 rows): router + partition/move",
+                "kernel": "checkpoint 0 (32768 rows), every kernel of the call",
                 "achieved_all_checkpoints": achieved_all,
                 "per_checkpoint_ms": per_ck, "algorithmic_bytes_per_step": sum(alg)}
 
@@ -400,7 +402,7 @@ def main():
                        "exit_fractions_of_batch": EXIT_FRACTIONS,
                        "rows_routed_per_step": rows_per_step, "active_rows": active,
                        "exits": exits_per_stage,
-                       "path": {0: "auto", 1: "simt", 2: "tc"}.get(path_used, path_used),
+                       "path": {1: "simt", 2: "tc_fused_single_pass", 3: "tc_split"}.get(path_used, path_used),
                        "parallelism": f"dp{world} (row shards, no collective)",
                        "l2": "inputs 1.1 GiB/step > 126 MB L2, no flush"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,

@@ -46,7 +46,11 @@ typedef void *tide_stream_t; /* a cudaStream_t */
 
 enum tide_dtype { TIDE_DTYPE_F32 = 0, TIDE_DTYPE_F16 = 1, TIDE_DTYPE_BF16 = 2 };
 enum tide_norm { TIDE_NORM_RMS = 0, TIDE_NORM_LAYER = 1 };
-enum tide_path { TIDE_PATH_AUTO = 0, TIDE_PATH_SIMT = 1, TIDE_PATH_TC = 2 };
+/* TIDE_PATH_TC: the single-pass fused cluster kernel (bf16/fp16, router width
+ * 128, hidden size with a resident weight slice); TIDE_PATH_TC_SPLIT: the
+ * tensor-core router followed by the stable-partition kernel; TIDE_PATH_SIMT:
+ * fp32 SIMT router + partition (any dtype and shape). */
+enum tide_path { TIDE_PATH_AUTO = 0, TIDE_PATH_SIMT = 1, TIDE_PATH_TC = 2, TIDE_PATH_TC_SPLIT = 3 };
 
 enum tide_status {
   TIDE_OK = 0,
@@ -190,8 +194,8 @@ typedef struct tide_checkpoint_args {
 size_t tide_checkpoint_workspace_size(const tide_checkpoint_args *args);
 int tide_checkpoint(const tide_checkpoint_args *args, tide_stream_t stream);
 
-/* Which path tide_checkpoint would take for these arguments (TIDE_PATH_SIMT or
- * TIDE_PATH_TC), or a negative TIDE_ERR_* code. */
+/* Which path tide_checkpoint would take for these arguments (TIDE_PATH_SIMT,
+ * TIDE_PATH_TC or TIDE_PATH_TC_SPLIT), or a negative TIDE_ERR_* code. */
 int tide_checkpoint_select_path(const tide_checkpoint_args *args);
 
 #ifdef __cplusplus

@@ -97,8 +97,10 @@ def test_operators_have_no_cpu_kernel():
 
 
 def test_path_selection():
-    """bf16/fp16 with folded weights, H % 64 == 0 and B % 32 == 0 go to the
-    tensor-core path; fp32 and other shapes to the SIMT path."""
+    """bf16/fp16 with folded weights go to the fused single-pass kernel when
+    the router is 128 wide and a weight slice of H stays resident, else to
+    the tensor-core split path (H % 64 == 0, B % 32 == 0); fp32 and other
+    shapes to the SIMT path."""
     lib = _native.lib()
 
     def sel(**kw):
@@ -114,6 +116,10 @@ def test_path_selection():
     assert sel(dtype=capi.DTYPE_F32, folded=None) == capi.PATH_SIMT
     assert sel(hidden_dim=4000) == capi.PATH_SIMT
     assert sel(bottleneck_dim=48) == capi.PATH_SIMT
+    assert sel(bottleneck_dim=64) == capi.PATH_TC_SPLIT       # fused kernel: 128 units only
+    assert sel(hidden_dim=8192) == capi.PATH_TC_SPLIT         # weight slice too large to stay resident
+    assert sel(hidden_dim=768) == capi.PATH_TC                # cluster of 2
+    assert sel(path=capi.PATH_TC_SPLIT) == capi.PATH_TC_SPLIT
     assert sel(folded=None) == capi.PATH_SIMT
     assert sel(path=capi.PATH_SIMT) == capi.PATH_SIMT
     assert sel(path=capi.PATH_TC, hidden_dim=4000) == -capi.ERR_UNSUPPORTED

@@ -8,7 +8,7 @@ import ctypes as C
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 NORM_RMS, NORM_LAYER = 0, 1
-PATH_AUTO, PATH_SIMT, PATH_TC = 0, 1, 2
+PATH_AUTO, PATH_SIMT, PATH_TC, PATH_TC_SPLIT = 0, 1, 2, 3
 OK = 0
 ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_ALIGNMENT = 1, 2, 3, 4, 5
 NOALLOC_MAX_ROWS = 1048576

@@ -285,24 +285,31 @@ int tide_checkpoint_select_path(const tide_checkpoint_args *a) {
   int rc = validate_checkpoint(a);
   if (rc != TIDE_OK) return -rc;
   if (a->path == TIDE_PATH_SIMT) return TIDE_PATH_SIMT;
-  const bool tc_ok = tide::tc_supported(a);
-  if (a->path == TIDE_PATH_TC) {
-    if (!tc_ok) {
-      fail(TIDE_ERR_UNSUPPORTED, "tide_checkpoint: tensor-core path does not take these arguments (%s)",
+  if (a->path == TIDE_PATH_TC_SPLIT) {
+    if (!tide::tc_supported(a)) {
+      fail(TIDE_ERR_UNSUPPORTED, "tide_checkpoint: tensor-core split path does not take these arguments (%s)",
            tide::tc_unsupported_reason(a));
       return -TIDE_ERR_UNSUPPORTED;
     }
-    return TIDE_PATH_TC;
+    return TIDE_PATH_TC_SPLIT;
   }
-  return tc_ok ? TIDE_PATH_TC : TIDE_PATH_SIMT;
+  if (a->path == TIDE_PATH_TC) {
+    if (tide::fused_supported(a)) return TIDE_PATH_TC;
+    if (tide::tc_supported(a)) return TIDE_PATH_TC_SPLIT;
+    fail(TIDE_ERR_UNSUPPORTED, "tide_checkpoint: tensor-core path does not take these arguments (%s)",
+         tide::tc_unsupported_reason(a));
+    return -TIDE_ERR_UNSUPPORTED;
+  }
+  if (tide::fused_supported(a)) return TIDE_PATH_TC;
+  return tide::tc_supported(a) ? TIDE_PATH_TC_SPLIT : TIDE_PATH_SIMT;
 }
 
 size_t tide_checkpoint_workspace_size(const tide_checkpoint_args *a) {
   if (!a) return 0;
   const int64_t n = a->n_rows > 0 ? a->n_rows : 0;
   size_t simt = simt_ws_bytes(n);
-  size_t tc = tide::tc_workspace_bytes(n);
-  return simt > tc ? simt : tc;
+  size_t fused = tide::fused_workspace_bytes(n);
+  return simt > fused ? simt : fused;
 }
 
 int tide_checkpoint(const tide_checkpoint_args *a, tide_stream_t stream) {
@@ -318,7 +325,7 @@ int tide_checkpoint(const tide_checkpoint_args *a, tide_stream_t stream) {
   if (cudaMemsetAsync(a->workspace, 0, w.partition_bytes, s) != cudaSuccess)
     return fail(TIDE_ERR_CUDA, "tide_checkpoint: memset failed");
   float *scores = a->scores_out ? a->scores_out : w.scores;
-  if (path == TIDE_PATH_TC) {
+  if (path == TIDE_PATH_TC_SPLIT) {
     int rc = tide::tc_route_launch(a, scores, w.stats, s, g_err, sizeof(g_err));
     if (rc != TIDE_OK) return rc;
   } else if (n > 0) {

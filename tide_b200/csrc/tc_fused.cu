@@ -1,0 +1,865 @@
+// Single-pass fused checkpoint (sm_100a): router -> exit decision -> stable
+// compaction -> final-norm exit scatter, every hidden row read from HBM once
+// and written once.
+//
+// A thread-block cluster of C CTAs works on 64-row tiles; CTA c owns the
+// hidden columns [c*H/C, (c+1)*H/C) (its K slice).  Each CTA keeps its slice of
+// the folded router weights W' = down * norm_weight ([128 x H/C], model dtype)
+// resident in shared memory for the whole launch, streams its slice of every
+// tile through a TMA ring and computes the transposed partial GEMM
+//     D_c[b, r] = sum_{k in slice c} W'[b, k] * x[r, k]
+// on the tensor cores (tcgen05.mma, M = 128 router units, N = 64 rows, fp32 in
+// TMEM).  Partial sums of x^2 (and x) come from the same shared-memory tiles.
+// The C partials are reduced in a fixed order by the CTA that owns each group
+// of 64/C rows, through distributed shared memory: sources store their
+// partials into the owner's slots, the owner sums, computes rstd, the router
+// logit, the score and the exit flag, and broadcasts {score, rstd, mean, flag}
+// of its rows to every CTA of the cluster.  Each CTA then writes its K slice
+// of every row of the tile -- survivors copied to the dense buffer at their
+// stable rank, exits final-normed to their original position -- reading the
+// row slice back from L2 (the cluster's tiles in flight are a few MiB).  Tile
+// offsets come from a decoupled look-back across tiles (Merrill & Garland
+// 2016) published by CTA rank 0 of each cluster.
+//
+// Reference semantics: python/TIDE/runtime.py:128-130 and :174-178 (score,
+// strict threshold, normed exit scatter), python/TIDE/scheduler.py:89-100
+// (stable compaction of rows and positions).
+//
+// Warp roles (512 threads):
+//   warp 0        TMA producer (resident W' slice once, then the x ring)
+//   warp 1        TMEM owner, MMA issuer
+//   warps 4-7     row statistics from the ring (two threads per row)
+//   warps 8-11    epilogue (tcgen05.ld of D_c), partial exchange, owner
+//                 reduction, decision and broadcast
+//   warps 12-15   write-out: look-back and the row moves
+// Every wait is bounded; on expiry the CTA raises TIDE_DEVERR_TIMEOUT,
+// stops, drains its in-flight copies and MMAs and meets its cluster at the
+// final barrier.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <stdio.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "tc_checkpoint.cuh"
+#include "tc_ptx.cuh"
+
+namespace tide {
+
+namespace fused {
+
+constexpr int kRows = 64;        // rows per tile (MMA N)
+constexpr int kUnits = 128;      // router units (MMA M)
+constexpr int kChunk = 64;       // columns per chunk (128 bytes of 16-bit data)
+constexpr int kThreads = 512;
+constexpr int kStages = 6;
+constexpr int kMaxSliceChunks = 8;  // W' slice <= 8 chunks = 128 KB
+constexpr uint32_t kTmemCols = 128;  // two 64-column fp32 accumulators
+constexpr int kSmemBudget = 227 * 1024;
+
+struct Params {
+  int64_t n_cap;
+  const int32_t *n_dev;
+  int H, C, slice, slice_chunks;
+  int norm_type;
+  float eps, up_bias, threshold;
+  const float *up, *colsum, *bias_proj, *w_norm, *b_norm;
+  const void *x;
+  const int64_t *pos_in;
+  const int32_t *slot_in;
+  void *out_buf;
+  int64_t n_total;
+  void *compact_out;
+  int64_t *pos_out;
+  int32_t *slot_out;
+  int64_t *exit_pos_out;
+  float *scores_out;
+  int32_t *counts;
+  uint64_t *status;
+  int32_t *err;
+};
+
+// shared-memory layout (offsets from the 1024-aligned base)
+struct Layout {
+  uint32_t w, ring, slots, slot_ss, info, stat, wn, bn, up, cs, bp, red, own, wg2, bars, end;
+};
+
+__host__ __device__ inline Layout layout(int slice_chunks, int C) {
+  Layout L;
+  uint32_t o = 0;
+  L.w = o;       o += (uint32_t)slice_chunks * kUnits * kChunk * 2;  // resident W' slice
+  L.ring = o;    o += (uint32_t)kStages * kRows * kChunk * 2;        // x chunks
+  L.slots = o;   o += (uint32_t)kUnits * kRows * 4;                  // [C][128][64/C] fp32
+  L.slot_ss = o; o += (uint32_t)kRows * 2 * 4;                        // [C][64/C][2]
+  L.info = o;    o += 2u * kRows * 16;                                // [2][64] {score, rstd, mean, flag}
+  L.stat = o;    o += 2u * 2 * kRows * 2 * 4;                         // [2 bufs][2 halves][64][ss, sx]
+  const uint32_t slice = (uint32_t)slice_chunks * kChunk;
+  L.wn = o;      o += slice * 4;
+  L.bn = o;      o += slice * 4;
+  L.up = o;      o += kUnits * 4;
+  L.cs = o;      o += kUnits * 4;
+  L.bp = o;      o += kUnits * 4;
+  L.red = o;     o += 4u * kRows * 4;                                 // [4 warps][64/C]
+  L.own = o;     o += 2u * kRows * 4;                                 // rstd, mean of owned rows
+  L.wg2 = o;     o += 256 + kRows * 4;                                // ranks, prefix, flags
+  o = (o + 15u) & ~15u;
+  L.bars = o;    o += 64 * 8;
+  L.end = o;
+  (void)C;
+  return L;
+}
+
+// barrier indices inside the bars array
+enum Bar {
+  kFull = 0,                 // [kStages]
+  kEmpty = kFull + kStages,  // [kStages]
+  kWFull = kEmpty + kStages,
+  kAccFull,                  // [2]
+  kAccEmpty = kAccFull + 2,  // [2]
+  kStatFull = kAccEmpty + 2, // [2]
+  kStatEmpty = kStatFull + 2,// [2]
+  kSlotsFull = kStatEmpty + 2,
+  kSlotFree,
+  kInfoFull,                 // [2]
+  kInfoFree = kInfoFull + 2, // [2]
+  kDrain = kInfoFree + 2,
+  kNumBars
+};
+static_assert(kNumBars <= 64, "barrier area");
+
+__device__ __forceinline__ void unpack8(const uint4 &v, float *f, bool bf16) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (bf16) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    } else {
+      const float2 t = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+}
+
+// Read-only look-back: exclusive prefix of `tile` from its predecessors.
+__device__ __forceinline__ bool lookback_read(const uint64_t *status, uint32_t tile,
+                                              uint32_t *keep_before, uint32_t *exits_before) {
+  uint32_t kb = 0, eb = 0;
+  int64_t j = (int64_t)tile - 1;
+  while (j >= 0) {
+    uint64_t s = 0;
+    int spins = 0;
+    while (((s = ld_acquire_u64(&status[j])) >> 62) == 0) {
+      if (++spins > kSpinLimit) {
+        *keep_before = kb;
+        *exits_before = eb;
+        return false;
+      }
+      __nanosleep(32);
+    }
+    kb += (uint32_t)(s & kCountMask);
+    eb += (uint32_t)((s >> 31) & kCountMask);
+    if ((s >> 62) == 2) break;
+    --j;
+  }
+  *keep_before = kb;
+  *exits_before = eb;
+  return true;
+}
+
+template <bool BF16, int C>
+__global__ void __launch_bounds__(kThreads, 1)
+    fused_checkpoint_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                            const __grid_constant__ CUtensorMap tmap_w, Params p) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr int R = kRows / C;  // rows owned by each CTA of the cluster
+  static_assert(R % 4 == 0, "owner rows come in float4 groups");
+  const bool LAYER = p.norm_type == TIDE_NORM_LAYER;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Layout L = layout(p.slice_chunks, C);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+  float *slots = reinterpret_cast<float *>(smem + L.slots);
+  float *slot_ss = reinterpret_cast<float *>(smem + L.slot_ss);
+  float4 *info = reinterpret_cast<float4 *>(smem + L.info);
+  float *stat = reinterpret_cast<float *>(smem + L.stat);
+  float *s_wn = reinterpret_cast<float *>(smem + L.wn);
+  float *s_bn = reinterpret_cast<float *>(smem + L.bn);
+  float *s_up = reinterpret_cast<float *>(smem + L.up);
+  float *s_cs = reinterpret_cast<float *>(smem + L.cs);
+  float *s_bp = reinterpret_cast<float *>(smem + L.bp);
+  float *s_red = reinterpret_cast<float *>(smem + L.red);
+  uint32_t *wg2 = reinterpret_cast<uint32_t *>(smem + L.wg2);
+  uint32_t *tmem_slot = wg2;              // [0]
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(wg2 + 1);
+  uint32_t *issued = wg2 + 2;
+  uint32_t *s_prefix = wg2 + 4;           // [4]: keep_before, exits_before, keep_t, exit_t
+  uint32_t *s_rank = wg2 + 64;            // [64] rank of each row among its kind
+  volatile int *s_stop1 = reinterpret_cast<volatile int *>(wg2 + 16);  // epilogue group
+  volatile int *s_stop2 = reinterpret_cast<volatile int *>(wg2 + 17);  // write-out group
+  float *s_rstd = reinterpret_cast<float *>(smem + L.own);            // [R] owned rows
+  float *s_mean = s_rstd + kRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_rank();
+  const int cluster_id = blockIdx.x / C;
+  const int n_clusters = gridDim.x / C;
+  const int slice = p.slice, nk = p.slice_chunks;
+  const uint32_t chunk_bytes = kRows * kChunk * 2;      // 8 KB
+  const uint32_t wchunk_bytes = kUnits * kChunk * 2;    // 16 KB
+
+  int64_t n = p.n_cap;
+  if (p.n_dev) {
+    int64_t nd = (int64_t)__ldg(p.n_dev);
+    if (nd < 0 || nd > p.n_cap) {
+      if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(p.err, TIDE_DEVERR_COUNT);
+      nd = nd < 0 ? 0 : p.n_cap;
+    }
+    n = nd;
+  }
+  const int n_tiles = (int)((n + kRows - 1) / kRows);
+
+  // ---------------------------------------------------------------- setup
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(&bars[kFull + s], 1);
+      ptx::mbar_init(&bars[kEmpty + s], 1 + 4);  // MMA commit + 4 statistics warps
+    }
+    ptx::mbar_init(&bars[kWFull], 1);
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&bars[kAccFull + a], 1);
+      ptx::mbar_init(&bars[kAccEmpty + a], 4);
+      ptx::mbar_init(&bars[kStatFull + a], 4);
+      ptx::mbar_init(&bars[kStatEmpty + a], 4);
+      ptx::mbar_init(&bars[kInfoFull + a], kRows);  // one arrival per row
+      ptx::mbar_init(&bars[kInfoFree + a], C);      // one arrival per CTA
+    }
+    ptx::mbar_init(&bars[kSlotsFull], 4 * C);       // 4 warps of every source
+    ptx::mbar_init(&bars[kSlotFree], C);            // every owner
+    ptx::mbar_init(&bars[kDrain], 1);
+    *abort_flag = 0;
+    *issued = 0;
+    *s_stop1 = 0;
+    *s_stop2 = 0;
+    ptx::fence_mbar_init();
+    ptx::fence_proxy_async();
+  }
+  const int col0 = (int)rank * slice;
+  for (int i = threadIdx.x; i < slice; i += kThreads) {
+    s_wn[i] = p.w_norm[col0 + i];
+    s_bn[i] = (LAYER && p.b_norm) ? p.b_norm[col0 + i] : 0.f;
+  }
+  for (int i = threadIdx.x; i < kUnits; i += kThreads) {
+    s_up[i] = p.up[i];
+    s_cs[i] = LAYER ? p.colsum[i] : 0.f;
+    s_bp[i] = (LAYER && p.bias_proj) ? p.bias_proj[i] : 0.f;
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  if (n_tiles == 0 && blockIdx.x == 0 && threadIdx.x == 0 && p.counts) {
+    p.counts[0] = 0;
+    p.counts[1] = 0;
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  ptx::cluster_sync();  // every CTA's barriers exist before any remote arrive
+  const uint32_t tmem_base = *tmem_slot;
+
+  const uint32_t bars_u32 = ptx::smem_u32(bars);
+  auto remote_bar = [&](int which, uint32_t cta) {
+    return ptx::map_to_rank(bars_u32 + (uint32_t)which * 8u, cta);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      ptx::prefetch_tmap(&tmap_x);
+      ptx::prefetch_tmap(&tmap_w);
+      ptx::mbar_expect_tx(&bars[kWFull], (uint32_t)nk * wchunk_bytes);
+      for (int kc = 0; kc < nk; ++kc)
+        ptx::tma_load_2d(smem + L.w + (size_t)kc * wchunk_bytes, &tmap_w, &bars[kWFull],
+                         col0 + kc * kChunk, 0);
+      uint32_t it = 0;
+      for (int tile = cluster_id; tile < n_tiles && !*abort_flag; tile += n_clusters) {
+        for (int kc = 0; kc < nk; ++kc, ++it) {
+          const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+          if (it >= (uint32_t)kStages && !ptx::mbar_wait(&bars[kEmpty + s], ph ^ 1u, abort_flag)) {
+            raise_error(p.err, TIDE_DEVERR_TIMEOUT);
+            *abort_flag = 1;
+            break;
+          }
+          ptx::mbar_expect_tx(&bars[kFull + s], chunk_bytes);
+          ptx::tma_load_2d(smem + L.ring + (size_t)s * chunk_bytes, &tmap_x, &bars[kFull + s],
+                           col0 + kc * kChunk, tile * kRows);
+          *issued = it + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = ptx::f16_idesc(BF16, kUnits, kRows);
+      bool ok = ptx::mbar_wait(&bars[kWFull], 0, abort_flag);
+      uint32_t it = 0;
+      int t_local = 0;
+      const uint32_t w_base = ptx::smem_u32(smem + L.w);
+      for (int tile = cluster_id; ok && tile < n_tiles && !*abort_flag;
+           tile += n_clusters, ++t_local) {
+        const int acc = t_local & 1;
+        if (t_local >= 2 &&
+            !ptx::mbar_wait(&bars[kAccEmpty + acc], ((uint32_t)(t_local >> 1) & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kRows);
+        for (int kc = 0; kc < nk; ++kc, ++it) {
+          const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+          if (!ptx::mbar_wait(&bars[kFull + s], ph, abort_flag)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const uint32_t a0 = w_base + (uint32_t)kc * wchunk_bytes;
+          const uint32_t b0 = ptx::smem_u32(smem + L.ring + (size_t)s * chunk_bytes);
+#pragma unroll
+          for (int k = 0; k < kChunk / 16; ++k)
+            ptx::mma_f16_ss(d_tmem, ptx::sw128_kmajor_desc(a0 + 32u * k),
+                            ptx::sw128_kmajor_desc(b0 + 32u * k), idesc,
+                            (kc > 0 || k > 0) ? 1u : 0u);
+          ptx::mma_commit(&bars[kEmpty + s]);
+        }
+        if (!ok) break;
+        ptx::mma_commit(&bars[kAccFull + acc]);
+      }
+      if (!ok) {
+        raise_error(p.err, TIDE_DEVERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      ptx::mma_commit(&bars[kDrain]);
+      volatile int never = 0;
+      if (!ptx::mbar_wait(&bars[kDrain], 0, &never)) raise_error(p.err, TIDE_DEVERR_TIMEOUT);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------- row statistics
+    const int t = threadIdx.x - 128;  // 0..127
+    const int r = t & (kRows - 1), h = t >> 6;
+    uint32_t it = 0;
+    int t_local = 0;
+    bool ok = true;
+    for (int tile = cluster_id; ok && tile < n_tiles; tile += n_clusters, ++t_local) {
+      float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
+      for (int kc = 0; kc < nk; ++kc, ++it) {
+        const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+        if (!ptx::mbar_wait(&bars[kFull + s], ph, abort_flag)) { ok = false; break; }
+        const uint8_t *row = smem + L.ring + (size_t)s * chunk_bytes + (size_t)r * 128;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int unit = (h * 4 + j + lane) & 7;
+          float f[8];
+          unpack8(*reinterpret_cast<const uint4 *>(row + (unit << 4)), f, BF16);
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            ss0 = fmaf(f[e], f[e], ss0);
+            ss1 = fmaf(f[e + 1], f[e + 1], ss1);
+            if (LAYER) { sx0 += f[e]; sx1 += f[e + 1]; }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&bars[kEmpty + s]);
+      }
+      if (!ok) break;
+      const int buf = t_local & 1;
+      if (t_local >= 2 &&
+          !ptx::mbar_wait(&bars[kStatEmpty + buf], ((uint32_t)(t_local >> 1) & 1u) ^ 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      float *st = stat + ((size_t)(buf * 2 + h) * kRows + r) * 2;
+      st[0] = ss0 + ss1;
+      st[1] = sx0 + sx1;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars[kStatFull + buf]);
+    }
+    if (!ok) {
+      raise_error(p.err, TIDE_DEVERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+  } else if (warp >= 8 && warp < 12) {
+    // ---------------------- epilogue, partial exchange, owner reduction
+    // All 128 threads pass every named barrier of an iteration; a failed
+    // wait only turns the rest of the iteration's work off (ok = false) and
+    // the group stops together at the iteration's end (s_stop1).
+    const int t = threadIdx.x - 256;   // 0..127 = router unit b = TMEM lane
+    const int q = warp & 3;            // TMEM lane quarter of this warp
+    const uint32_t slots_u32 = ptx::smem_u32(slots);
+    const uint32_t slot_ss_u32 = ptx::smem_u32(slot_ss);
+    const uint32_t info_u32 = ptx::smem_u32(info);
+    int t_local = 0;
+    for (int tile = cluster_id; tile < n_tiles; tile += n_clusters, ++t_local) {
+      bool ok = true;
+      const int buf = t_local & 1;
+      const uint32_t ph2 = (uint32_t)(t_local >> 1) & 1u;
+      // (1) this CTA's partial row statistics
+      float ss_part = 0.f, sx_part = 0.f;
+      ok = ptx::mbar_wait(&bars[kStatFull + buf], ph2, abort_flag);
+      if (ok && t < kRows) {
+        const float *st0 = stat + ((size_t)(buf * 2 + 0) * kRows + t) * 2;
+        const float *st1 = stat + ((size_t)(buf * 2 + 1) * kRows + t) * 2;
+        ss_part = st0[0] + st1[0];
+        sx_part = st0[1] + st1[1];
+      }
+      __syncwarp();
+      if (ok && lane == 0) ptx::mbar_arrive(&bars[kStatEmpty + buf]);
+      // (2) this CTA's partial D_c[b, 0..63] from TMEM
+      float d[kRows];
+      if (ok) ok = ptx::mbar_wait(&bars[kAccFull + buf], ph2, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        ptx::tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kRows);
+        ptx::tmem_ld32(taddr, d);
+        ptx::tmem_ld32(taddr + 32u, d + 32);
+        ptx::tc_fence_before();
+      }
+      __syncwarp();
+      if (ok && lane == 0) ptx::mbar_arrive(&bars[kAccEmpty + buf]);
+      // (3) send the partials to their owners (slot [src][b][R] at the owner)
+      if (ok && t_local >= 1)
+        ok = ptx::mbar_wait_cluster(&bars[kSlotFree], (uint32_t)(t_local - 1) & 1u, abort_flag);
+      if (ok) {
+#pragma unroll
+        for (int o = 0; o < C; ++o) {
+          const uint32_t base = ptx::map_to_rank(
+              slots_u32 + (uint32_t)(((int)rank * kUnits + t) * R) * 4u, (uint32_t)o);
+#pragma unroll
+          for (int j = 0; j < R; j += 4)
+            ptx::st_cluster_v4(base + (uint32_t)j * 4u, d[o * R + j], d[o * R + j + 1],
+                               d[o * R + j + 2], d[o * R + j + 3]);
+        }
+        if (t < kRows) {
+          const int o = t / R, rr = t % R;
+          const uint32_t a = ptx::map_to_rank(
+              slot_ss_u32 + (uint32_t)(((int)rank * R + rr) * 2) * 4u, (uint32_t)o);
+          ptx::st_cluster_v2(a, ss_part, sx_part);
+        }
+        ptx::fence_cluster();
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok && lane == 0)
+        for (int o = 0; o < C; ++o) ptx::mbar_arrive_cluster(remote_bar(kSlotsFull, (uint32_t)o));
+      // (4) owner: the statistics of the R owned rows, then their logits
+      if (ok) ok = ptx::mbar_wait_cluster(&bars[kSlotsFull], (uint32_t)t_local & 1u, abort_flag);
+      if (ok && t < R) {
+        float ss = 0.f, sx = 0.f;
+#pragma unroll
+        for (int src = 0; src < C; ++src) {
+          ss += slot_ss[(src * R + t) * 2];
+          sx += slot_ss[(src * R + t) * 2 + 1];
+        }
+        float mean = 0.f, rstd;
+        if (!LAYER) {
+          rstd = rsqrt_rn(ss / (float)p.H + p.eps);
+        } else {
+          mean = sx / (float)p.H;
+          rstd = rsqrt_rn(fmaxf(ss / (float)p.H - mean * mean, 0.f) + p.eps);
+        }
+        s_rstd[t] = rstd;
+        s_mean[t] = mean;
+      }
+      if (!ok) *s_stop1 = 1;
+      ptx::named_sync(1, 128);
+      ok = !*s_stop1;
+      if (ok) {
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+          float acc = 0.f;
+#pragma unroll
+          for (int src = 0; src < C; ++src) acc += slots[(src * kUnits + t) * R + rr];
+          const float rstd = s_rstd[rr];
+          const float z = LAYER ? fmaf(rstd, acc - s_mean[rr] * s_cs[t], s_bp[t]) : rstd * acc;
+          const float v = warp_sum(s_up[t] * silu_f(z));
+          if (lane == 0) s_red[q * R + rr] = v;
+        }
+      }
+      ptx::named_sync(1, 128);
+      // every slot of this tile has been read: sources may refill them
+      if (ok && t == 0)
+        for (int src = 0; src < C; ++src) ptx::mbar_arrive_cluster(remote_bar(kSlotFree, (uint32_t)src));
+      // (5) decide the owned rows and broadcast {score, rstd, mean, flag}
+      if (ok && t < R) {
+        const float logit = p.up_bias + s_red[0 * R + t] + s_red[1 * R + t] + s_red[2 * R + t] +
+                            s_red[3 * R + t];
+        const float score = sigmoid_f(logit);
+        const int row_in_tile = (int)rank * R + t;
+        const int64_t grow = (int64_t)tile * kRows + row_in_tile;
+        float flag = 0.f;  // 0 beyond the active rows, 1 survive, 2 exit
+        if (grow < n) {
+          flag = score > p.threshold ? 2.f : 1.f;
+          if (p.scores_out) p.scores_out[grow] = score;
+        }
+        if (t_local >= 2) ok = ptx::mbar_wait_cluster(&bars[kInfoFree + buf], ph2 ^ 1u, abort_flag);
+        if (ok) {
+#pragma unroll
+          for (int dcta = 0; dcta < C; ++dcta) {
+            const uint32_t a = ptx::map_to_rank(
+                info_u32 + (uint32_t)((buf * kRows + row_in_tile) * 16), (uint32_t)dcta);
+            ptx::st_cluster_v4(a, score, s_rstd[t], s_mean[t], flag);
+          }
+          ptx::fence_cluster();
+#pragma unroll
+          for (int dcta = 0; dcta < C; ++dcta)
+            ptx::mbar_arrive_cluster(remote_bar(kInfoFull + buf, (uint32_t)dcta));
+        }
+      }
+      if (!ok || *abort_flag) *s_stop1 = 1;
+      ptx::named_sync(1, 128);
+      if (*s_stop1) break;
+    }
+    if (*s_stop1) {
+      raise_error(p.err, TIDE_DEVERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+  } else if (warp >= 12) {
+    // -------------------------------------------- look-back, row moves
+    const int t = threadIdx.x - 384;  // 0..127
+    const int w4 = t >> 5;            // 0..3
+    int t_local = 0;
+    const T *x = static_cast<const T *>(p.x);
+    const int vec_per_row = slice / 8;  // 16-byte vectors of this CTA's slice (<= 64)
+    for (int tile = cluster_id; tile < n_tiles; tile += n_clusters, ++t_local) {
+      const int buf = t_local & 1;
+      const uint32_t ph2 = (uint32_t)(t_local >> 1) & 1u;
+      bool ok = ptx::mbar_wait_cluster(&bars[kInfoFull + buf], ph2, abort_flag);
+      if (!ok) *s_stop2 = 1;
+      ptx::named_sync(2, 128);
+      if (*s_stop2) break;
+      // ranks inside the tile (rows 0..63 by threads 0..63)
+      if (t < kRows) {
+        const int st = (int)info[buf * kRows + t].w;
+        const unsigned kb = __ballot_sync(0xffffffffu, st == 1);
+        const unsigned eb = __ballot_sync(0xffffffffu, st == 2);
+        const unsigned lt = (1u << lane) - 1u;
+        s_rank[t] = st == 1 ? __popc(kb & lt) : __popc(eb & lt);
+        if (lane == 0) {
+          s_prefix[8 + w4 * 2] = __popc(kb);
+          s_prefix[8 + w4 * 2 + 1] = __popc(eb);
+        }
+      }
+      ptx::named_sync(2, 128);
+      if (t < kRows && t >= 32) {
+        const int st = (int)info[buf * kRows + t].w;
+        s_rank[t] += st == 1 ? s_prefix[8] : s_prefix[9];
+      }
+      if (t == 0) {
+        const uint32_t keep_t = s_prefix[8] + s_prefix[10];
+        const uint32_t exit_t = s_prefix[9] + s_prefix[11];
+        uint32_t kb = 0, eb = 0;
+        bool lb_ok;
+        if (rank == 0)
+          lb_ok = lookback(p.status, (uint32_t)tile, keep_t, exit_t, &kb, &eb);
+        else
+          lb_ok = lookback_read(p.status, (uint32_t)tile, &kb, &eb);
+        if (!lb_ok) raise_error(p.err, TIDE_DEVERR_TIMEOUT);
+        s_prefix[0] = kb;
+        s_prefix[1] = eb;
+        if (rank == 0 && tile == n_tiles - 1 && p.counts) {
+          p.counts[0] = (int32_t)(kb + keep_t);
+          p.counts[1] = (int32_t)(eb + exit_t);
+        }
+      }
+      ptx::named_sync(2, 128);
+      const uint32_t keep_before = s_prefix[0], exits_before = s_prefix[1];
+      // token bookkeeping (rank 0 only)
+      if (rank == 0 && t < kRows) {
+        const int st = (int)info[buf * kRows + t].w;
+        const int64_t row = (int64_t)tile * kRows + t;
+        if (st == 1) {
+          const int64_t dst = (int64_t)keep_before + s_rank[t];
+          if (p.pos_out) p.pos_out[dst] = p.pos_in ? p.pos_in[row] : row;
+          if (p.slot_out) p.slot_out[dst] = p.slot_in ? p.slot_in[row] : (int32_t)row;
+        } else if (st == 2 && p.exit_pos_out) {
+          p.exit_pos_out[(int64_t)exits_before + s_rank[t]] = p.pos_in ? p.pos_in[row] : row;
+        }
+      }
+      // row moves: warp w4 handles rows w4*16 .. w4*16+15 in two batches of 8
+      for (int batch = 0; batch < 2; ++batch) {
+        const int r0 = w4 * 16 + batch * 8;
+        uint4 v[8][2];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = r0 + i;
+          const int st = (int)info[buf * kRows + r].w;
+          const int64_t row = (int64_t)tile * kRows + r;
+          const uint4 *src = reinterpret_cast<const uint4 *>(x + row * p.H + col0);
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int vi = lane + 32 * u;
+            if (st != 0 && vi < vec_per_row) v[i][u] = ld_stream(src + vi);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = r0 + i;
+          const float4 in = info[buf * kRows + r];
+          const int st = (int)in.w;
+          if (st == 0) continue;
+          const int64_t row = (int64_t)tile * kRows + r;
+          if (st == 1) {
+            if (!p.compact_out) continue;
+            const int64_t dst = (int64_t)keep_before + s_rank[r];
+            uint4 *d = reinterpret_cast<uint4 *>(static_cast<T *>(p.compact_out) + dst * p.H + col0);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int vi = lane + 32 * u;
+              if (vi < vec_per_row) st_stream(d + vi, v[i][u]);
+            }
+          } else {
+            if (!p.out_buf) continue;
+            const int64_t pos = p.pos_in ? p.pos_in[row] : row;
+            if (pos < 0 || pos >= p.n_total) {
+              if (lane == 0) raise_error(p.err, TIDE_DEVERR_POSITION);
+              continue;
+            }
+            const float rstd = in.y, mean = in.z, shift = -rstd * mean;
+            uint4 *d = reinterpret_cast<uint4 *>(static_cast<T *>(p.out_buf) + pos * p.H + col0);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int vi = lane + 32 * u;
+              if (vi >= vec_per_row) continue;
+              float xv[8], y[8];
+              unpack8(v[i][u], xv, BF16);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int c = vi * 8 + j;
+                if (!LAYER) {
+                  y[j] = __fmul_rn(s_wn[c], __fmul_rn(xv[j], rstd));
+                } else {
+                  const float tt = __fadd_rn(__fmul_rn(xv[j], rstd), shift);
+                  y[j] = __fadd_rn(__fmul_rn(tt, s_wn[c]), s_bn[c]);
+                }
+              }
+              st_stream(d + vi, pack16<T>(y));
+            }
+          }
+        }
+      }
+      // this CTA is done with info[buf]: tell every owner
+      ptx::named_sync(2, 128);
+      if (t == 0)
+        for (int o = 0; o < C; ++o) ptx::mbar_arrive_cluster(remote_bar(kInfoFree + buf, (uint32_t)o));
+      if (*abort_flag) *s_stop2 = 1;
+      ptx::named_sync(2, 128);
+      if (*s_stop2) break;
+    }
+    if (*s_stop2) {
+      raise_error(p.err, TIDE_DEVERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) {
+    // drain the TMA loads still in flight before the CTA can leave
+    const uint32_t n_issued = *issued;
+    volatile int never = 0;
+    for (int s = 0; s < kStages; ++s) {
+      if ((uint32_t)s >= n_issued) break;
+      const uint32_t count = (n_issued - (uint32_t)s + (uint32_t)kStages - 1) / (uint32_t)kStages;
+      ptx::mbar_wait(&bars[kFull + s], (count - 1) & 1u, &never);
+    }
+  }
+  __syncthreads();
+  ptx::cluster_sync();  // no CTA leaves while a peer may still write into it
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace fused
+
+// ------------------------------------------------------------------ host
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 fused_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+bool fused_tmap(CUtensorMap *m, const void *base, bool bf16, uint64_t rows, uint64_t cols,
+                uint32_t box_rows) {
+  auto enc = fused_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {(cuuint32_t)fused::kChunk, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+             const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Cluster size: the smallest C in {1, 2, 4, 8} whose K slice is a multiple
+// of 64 columns and whose W' slice fits the resident budget.
+int fused_cluster_size(int64_t H) {
+  for (int c = 1; c <= 8; c <<= 1) {
+    if (H % c) continue;
+    const int64_t slice = H / c;
+    if (slice % fused::kChunk) continue;
+    if (slice / fused::kChunk <= fused::kMaxSliceChunks) return c;
+  }
+  return 0;
+}
+
+size_t fused_smem_bytes(int64_t H) {
+  const int c = fused_cluster_size(H);
+  if (!c) return 0;
+  return 1024 + fused::layout((int)(H / c / fused::kChunk), c).end;
+}
+
+}  // namespace
+
+const char *fused_unsupported_reason(const tide_checkpoint_args *a) {
+  if (a->dtype != TIDE_DTYPE_BF16 && a->dtype != TIDE_DTYPE_F16) return "dtype is not bf16/fp16";
+  if (!a->folded) return "no folded router weights";
+  if (a->bottleneck_dim != fused::kUnits) return "bottleneck_dim is not 128";
+  if (!fused_cluster_size(a->hidden_dim)) return "hidden_dim has no cluster split with a resident weight slice";
+  if (fused_smem_bytes(a->hidden_dim) > (size_t)fused::kSmemBudget) return "shared memory budget";
+  if (a->norm_type == TIDE_NORM_LAYER && !a->colsum) return "LayerNorm needs colsum";
+  if (((uintptr_t)a->x | (uintptr_t)a->folded | (uintptr_t)a->out_buffer |
+       (uintptr_t)a->compact_out) & 15u)
+    return "x/folded/outputs not 16-byte aligned";
+  if (a->n_rows < 1) return "no rows";
+  if (a->n_rows > ((int64_t)1 << 30)) return "too many rows";
+  return nullptr;
+}
+
+bool fused_supported(const tide_checkpoint_args *a) { return fused_unsupported_reason(a) == nullptr; }
+
+size_t fused_workspace_bytes(int64_t n_rows) {
+  const int64_t tiles = n_rows > 0 ? (n_rows + fused::kRows - 1) / fused::kRows : 1;
+  return 256 + (((size_t)tiles * 8 + 255) / 256) * 256;
+}
+
+int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, char *err,
+                            size_t err_len) {
+  const bool bf16 = a->dtype == TIDE_DTYPE_BF16;
+  const int C = fused_cluster_size(a->hidden_dim);
+  const int slice = (int)(a->hidden_dim / C);
+  CUtensorMap tx, tw;
+  if (!fused_tmap(&tx, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, fused::kRows) ||
+      !fused_tmap(&tw, a->folded, bf16, (uint64_t)fused::kUnits, (uint64_t)a->hidden_dim,
+                  fused::kUnits)) {
+    snprintf(err, err_len, "fused checkpoint: cuTensorMapEncodeTiled failed");
+    return TIDE_ERR_CUDA;
+  }
+  uint64_t *status = reinterpret_cast<uint64_t *>(static_cast<char *>(a->workspace) + 256);
+  cudaError_t e = cudaMemsetAsync(a->workspace, 0, fused_workspace_bytes(a->n_rows), stream);
+  if (e != cudaSuccess) {
+    snprintf(err, err_len, "fused checkpoint: memset: %s", cudaGetErrorString(e));
+    return TIDE_ERR_CUDA;
+  }
+  fused::Params p{};
+  p.n_cap = a->n_rows;
+  p.n_dev = a->n_rows_dev;
+  p.H = (int)a->hidden_dim;
+  p.C = C;
+  p.slice = slice;
+  p.slice_chunks = slice / fused::kChunk;
+  p.norm_type = a->norm_type;
+  p.eps = a->eps;
+  p.up_bias = a->up_bias;
+  p.threshold = a->threshold;
+  p.up = a->up;
+  p.colsum = a->colsum;
+  p.bias_proj = a->bias_proj;
+  p.w_norm = a->norm_weight;
+  p.b_norm = a->norm_bias;
+  p.x = a->x;
+  p.pos_in = a->positions_in;
+  p.slot_in = a->slots_in;
+  p.out_buf = a->out_buffer;
+  p.n_total = a->n_total;
+  p.compact_out = a->compact_out;
+  p.pos_out = a->positions_out;
+  p.slot_out = a->slots_out;
+  p.exit_pos_out = a->exit_positions_out;
+  p.scores_out = a->scores_out;
+  p.counts = a->counts_out;
+  p.status = status;
+  p.err = a->error_word;
+
+  const void *fn = nullptr;
+  switch (C) {
+    case 1: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 1> : (const void *)fused::fused_checkpoint_kernel<false, 1>; break;
+    case 2: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 2> : (const void *)fused::fused_checkpoint_kernel<false, 2>; break;
+    case 4: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 4> : (const void *)fused::fused_checkpoint_kernel<false, 4>; break;
+    default: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 8> : (const void *)fused::fused_checkpoint_kernel<false, 8>; break;
+  }
+  static bool attr_set[2][9] = {};
+  if (!attr_set[bf16][C]) {
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, fused::kSmemBudget);
+    if (e != cudaSuccess) {
+      snprintf(err, err_len, "fused checkpoint: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return TIDE_ERR_CUDA;
+    }
+    attr_set[bf16][C] = true;
+  }
+  const size_t smem = fused_smem_bytes(a->hidden_dim);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(fused::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // one resident cluster per C SMs: every cluster runs for the whole launch
+  // so a look-back never waits on a tile whose cluster is not running
+  static int max_clusters[2][9] = {};
+  if (!max_clusters[bf16][C]) {
+    cfg.gridDim = dim3((unsigned)C, 1, 1);
+    int mc = 0;
+    e = cudaOccupancyMaxActiveClusters(&mc, fn, &cfg);
+    if (e != cudaSuccess || mc <= 0) {
+      snprintf(err, err_len, "fused checkpoint: no resident cluster of %d CTAs (%s)", C,
+               cudaGetErrorString(e));
+      return TIDE_ERR_CUDA;
+    }
+    max_clusters[bf16][C] = mc;
+  }
+  const int64_t tiles = (a->n_rows + fused::kRows - 1) / fused::kRows;
+  const int64_t g = tiles < max_clusters[bf16][C] ? tiles : max_clusters[bf16][C];
+  cfg.gridDim = dim3((unsigned)(g * C), 1, 1);
+  switch (C) {
+    case 1: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 1>, tx, tw, p)
+                     : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 1>, tx, tw, p); break;
+    case 2: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 2>, tx, tw, p)
+                     : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 2>, tx, tw, p); break;
+    case 4: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 4>, tx, tw, p)
+                     : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 4>, tx, tw, p); break;
+    default: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 8>, tx, tw, p)
+                      : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 8>, tx, tw, p); break;
+  }
+  if (e != cudaSuccess) {
+    snprintf(err, err_len, "fused checkpoint launch: %s", cudaGetErrorString(e));
+    return TIDE_ERR_CUDA;
+  }
+  return TIDE_OK;
+}
+
+}  // namespace tide
