@@ -76,7 +76,15 @@ def check_against_oracle(ck: Checkpoint, res: dict, dtype, kind, tol, out_ref=No
         normed = O.from_f32(O.final_norm(O.to_f32(x_np, dt), oracle_norm(kind, ck.norm_w, ck.norm_b, 0)
                                          | {"eps": res["eps"]}), dt)
         ulp = O.ulp_distance(out[pos_in[ex]], normed[ex], dt)
-        assert ulp.size == 0 or ulp.max() <= (8 if dtype == torch.float32 else 1)
+        bad = ulp > (8 if dtype == torch.float32 else 1)
+        if kind == "layer" and bad.any():
+            # LayerNorm's bias can cancel the normalised term: an output near
+            # zero then has ulps far below the fp32 rounding of its two terms.
+            # There the bar is the absolute fp32 error of those terms.
+            diff = np.abs(O.to_f32(out[pos_in[ex]], dt) - O.to_f32(normed[ex], dt))
+            scale = np.abs(O.to_f32(x_np[ex], dt)).max(axis=1, keepdims=True) * 4 + 1
+            bad &= diff > scale * 2.0 ** -20
+        assert not bad.any(), int(ulp.max())
         if out_ref is not None:  # rows nobody exited to stay untouched
             untouched = np.setdiff1d(np.arange(out.shape[0]), pos_in[ex])
             assert np.array_equal(out[untouched], out_ref[untouched])

@@ -320,6 +320,7 @@ int tide_checkpoint(const tide_checkpoint_args *a, tide_stream_t stream) {
     return fail(TIDE_ERR_WORKSPACE, "tide_checkpoint: workspace needs %zu bytes, got %zu",
                 tide_checkpoint_workspace_size(a), a->workspace_bytes);
   cudaStream_t s = (cudaStream_t)stream;
+  if (path == TIDE_PATH_TC) return tide::fused_checkpoint_launch(a, s, g_err, sizeof(g_err));
 
   SimtWs w = simt_ws(a->workspace, n);
   if (cudaMemsetAsync(a->workspace, 0, w.partition_bytes, s) != cudaSuccess)

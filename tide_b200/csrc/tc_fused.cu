@@ -665,6 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // drain the TMA loads still in flight before the CTA can leave
     const uint32_t n_issued = *issued;
     volatile int never = 0;
+    ptx::mbar_wait(&bars[kWFull], 0, &never);
     for (int s = 0; s < kStages; ++s) {
       if ((uint32_t)s >= n_issued) break;
       const uint32_t count = (n_issued - (uint32_t)s + (uint32_t)kStages - 1) / (uint32_t)kStages;
