@@ -82,7 +82,7 @@ struct Params {
 
 // shared-memory layout (offsets from the 1024-aligned base)
 struct Layout {
-  uint32_t w, ring, slots, slot_ss, info, stat, wn, bn, up, cs, bp, red, own, wg2, bars, end;
+  uint32_t w, ring, slots, slot_ss, info, stat, wn, bn, up, cs, bp, red, own, wg2, pos, bars, end;
 };
 
 __host__ __device__ inline Layout layout(int slice_chunks, int C) {
@@ -103,6 +103,7 @@ __host__ __device__ inline Layout layout(int slice_chunks, int C) {
   L.red = o;     o += 4u * kRows * 4;                                 // [4 warps][64/C]
   L.own = o;     o += 2u * kRows * 4;                                 // rstd, mean of owned rows
   L.wg2 = o;     o += 256 + kRows * 4;                                // ranks, prefix, flags
+  L.pos = o;     o += kRows * 8;                                      // positions of the tile's rows
   o = (o + 15u) & ~15u;
   L.bars = o;    o += 64 * 8;
   L.end = o;
@@ -200,6 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t *s_rank = wg2 + 64;            // [64] rank of each row among its kind
   volatile int *s_stop1 = reinterpret_cast<volatile int *>(wg2 + 16);  // epilogue group
   volatile int *s_stop2 = reinterpret_cast<volatile int *>(wg2 + 17);  // write-out group
+  int64_t *s_pos = reinterpret_cast<int64_t *>(smem + L.pos);         // [64] tile positions
   float *s_rstd = reinterpret_cast<float *>(smem + L.own);            // [R] owned rows
   float *s_mean = s_rstd + kRows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -445,8 +447,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               slot_ss_u32 + (uint32_t)(((int)rank * R + rr) * 2) * 4u, (uint32_t)o);
           ptx::st_cluster_v2(a, ss_part, sx_part);
         }
-        ptx::fence_cluster();
       }
+      // the warp barrier orders every lane's stores before lane 0's
+      // release-arrive at cluster scope
       ok = __all_sync(0xffffffffu, ok);
       if (ok && lane == 0)
         for (int o = 0; o < C; ++o) ptx::mbar_arrive_cluster(remote_bar(kSlotsFull, (uint32_t)o));
@@ -508,7 +511,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 info_u32 + (uint32_t)((buf * kRows + row_in_tile) * 16), (uint32_t)dcta);
             ptx::st_cluster_v4(a, score, s_rstd[t], s_mean[t], flag);
           }
-          ptx::fence_cluster();
 #pragma unroll
           for (int dcta = 0; dcta < C; ++dcta)
             ptx::mbar_arrive_cluster(remote_bar(kInfoFull + buf, (uint32_t)dcta));
@@ -536,9 +538,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) *s_stop2 = 1;
       ptx::named_sync(2, 128);
       if (*s_stop2) break;
-      // ranks inside the tile (rows 0..63 by threads 0..63)
+      // ranks inside the tile (rows 0..63 by threads 0..63); the tile's
+      // positions are fetched once here, in parallel
       if (t < kRows) {
         const int st = (int)info[buf * kRows + t].w;
+        const int64_t row = (int64_t)tile * kRows + t;
+        s_pos[t] = st == 0 ? -1 : (p.pos_in ? p.pos_in[row] : row);
         const unsigned kb = __ballot_sync(0xffffffffu, st == 1);
         const unsigned eb = __ballot_sync(0xffffffffu, st == 2);
         const unsigned lt = (1u << lane) - 1u;
@@ -578,10 +583,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t row = (int64_t)tile * kRows + t;
         if (st == 1) {
           const int64_t dst = (int64_t)keep_before + s_rank[t];
-          if (p.pos_out) p.pos_out[dst] = p.pos_in ? p.pos_in[row] : row;
+          if (p.pos_out) p.pos_out[dst] = s_pos[t];
           if (p.slot_out) p.slot_out[dst] = p.slot_in ? p.slot_in[row] : (int32_t)row;
         } else if (st == 2 && p.exit_pos_out) {
-          p.exit_pos_out[(int64_t)exits_before + s_rank[t]] = p.pos_in ? p.pos_in[row] : row;
+          p.exit_pos_out[(int64_t)exits_before + s_rank[t]] = s_pos[t];
         }
       }
       // row moves: warp w4 handles rows w4*16 .. w4*16+15 in two batches of 8
@@ -606,7 +611,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float4 in = info[buf * kRows + r];
           const int st = (int)in.w;
           if (st == 0) continue;
-          const int64_t row = (int64_t)tile * kRows + r;
           if (st == 1) {
             if (!p.compact_out) continue;
             const int64_t dst = (int64_t)keep_before + s_rank[r];
@@ -618,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
             if (!p.out_buf) continue;
-            const int64_t pos = p.pos_in ? p.pos_in[row] : row;
+            const int64_t pos = s_pos[r];
             if (pos < 0 || pos >= p.n_total) {
               if (lane == 0) raise_error(p.err, TIDE_DEVERR_POSITION);
               continue;
