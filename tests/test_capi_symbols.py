@@ -85,7 +85,7 @@ def test_torch_extension_registers_operators():
     for name in ("fused_layernorm_route", "batch_compact", "exit_scatter", "exit_projection",
                  "norm_scatter", "router_fold", "checkpoint", "checkpoint_workspace_size"):
         assert hasattr(ops, name), name
-    assert ops.checkpoint_workspace_size(1000) > 0
+    assert ops.checkpoint_workspace_size(1000, 4096) > ops.checkpoint_workspace_size(1000, 4000) > 0
 
 
 def test_operators_have_no_cpu_kernel():
@@ -111,14 +111,15 @@ def test_path_selection():
         a = capi.CheckpointArgs(**base)
         return lib.tide_checkpoint_select_path(ctypes.byref(a))
 
-    assert sel() == capi.PATH_TC
-    assert sel(dtype=capi.DTYPE_F16) == capi.PATH_TC
+    assert sel() == capi.PATH_TC_SPLIT
+    assert sel(dtype=capi.DTYPE_F16) == capi.PATH_TC_SPLIT
+    assert sel(path=capi.PATH_TC) == capi.PATH_TC
     assert sel(dtype=capi.DTYPE_F32, folded=None) == capi.PATH_SIMT
     assert sel(hidden_dim=4000) == capi.PATH_SIMT
     assert sel(bottleneck_dim=48) == capi.PATH_SIMT
     assert sel(bottleneck_dim=64) == capi.PATH_TC_SPLIT       # fused kernel: 128 units only
-    assert sel(hidden_dim=8192) == capi.PATH_TC_SPLIT         # weight slice too large to stay resident
-    assert sel(hidden_dim=768) == capi.PATH_TC                # cluster of 2
+    assert sel(hidden_dim=8192, path=capi.PATH_TC) == capi.PATH_TC_SPLIT  # slice too large to stay resident
+    assert sel(hidden_dim=768, path=capi.PATH_TC) == capi.PATH_TC   # cluster of 2
     assert sel(path=capi.PATH_TC_SPLIT) == capi.PATH_TC_SPLIT
     assert sel(folded=None) == capi.PATH_SIMT
     assert sel(path=capi.PATH_SIMT) == capi.PATH_SIMT

@@ -90,7 +90,7 @@ def check_against_oracle(ck: Checkpoint, res: dict, dtype, kind, tol, out_ref=No
             assert np.array_equal(out[untouched], out_ref[untouched])
 
 
-@pytest.mark.parametrize("path", [capi.PATH_SIMT, capi.PATH_AUTO, capi.PATH_TC_SPLIT])
+@pytest.mark.parametrize("path", [capi.PATH_SIMT, capi.PATH_TC, capi.PATH_TC_SPLIT])
 @pytest.mark.parametrize("name", list(GOLDEN_CASES))
 def test_checkpoint_golden(name, path):
     dtype = GOLDEN_DTYPE[name]
@@ -191,7 +191,7 @@ def test_checkpoint_device_row_count():
     assert np.array_equal(ck.positions_out.cpu().numpy()[: len(keep)], keep)
 
 
-@pytest.mark.parametrize("path", [capi.PATH_SIMT, capi.PATH_AUTO, capi.PATH_TC_SPLIT])
+@pytest.mark.parametrize("path", [capi.PATH_SIMT, capi.PATH_TC, capi.PATH_TC_SPLIT])
 def test_checkpoint_chain_on_device_counts(path):
     """Three checkpoints chained on device-side counts with no host sync in
     between; afterwards each stage is checked against the oracle on the rows

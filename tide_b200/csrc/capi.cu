@@ -300,15 +300,18 @@ int tide_checkpoint_select_path(const tide_checkpoint_args *a) {
          tide::tc_unsupported_reason(a));
     return -TIDE_ERR_UNSUPPORTED;
   }
+  // automatic choice: the tensor-core split path where it applies (measured
+  // faster today), else the fused single pass, else SIMT
+  if (tide::tc_supported(a)) return TIDE_PATH_TC_SPLIT;
   if (tide::fused_supported(a)) return TIDE_PATH_TC;
-  return tide::tc_supported(a) ? TIDE_PATH_TC_SPLIT : TIDE_PATH_SIMT;
+  return TIDE_PATH_SIMT;
 }
 
 size_t tide_checkpoint_workspace_size(const tide_checkpoint_args *a) {
   if (!a) return 0;
   const int64_t n = a->n_rows > 0 ? a->n_rows : 0;
   size_t simt = simt_ws_bytes(n);
-  size_t fused = tide::fused_workspace_bytes(n);
+  size_t fused = tide::fused_workspace_bytes(a);
   return simt > fused ? simt : fused;
 }
 

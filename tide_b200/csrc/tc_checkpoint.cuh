@@ -17,7 +17,7 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
 // Single-pass fused cluster kernel (tc_fused.cu).
 bool fused_supported(const tide_checkpoint_args *a);
 const char *fused_unsupported_reason(const tide_checkpoint_args *a);
-size_t fused_workspace_bytes(int64_t n_rows);
+size_t fused_workspace_bytes(const tide_checkpoint_args *a);
 int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t s, char *err, size_t err_len);
 
 }  // namespace tide

@@ -11,10 +11,12 @@
 // on the tensor cores (tcgen05.mma, M = 128 router units, N = 64 rows, fp32 in
 // TMEM).  Partial sums of x^2 (and x) come from the same shared-memory tiles.
 // The C partials are reduced in a fixed order by the CTA that owns each group
-// of 64/C rows, through distributed shared memory: sources store their
-// partials into the owner's slots, the owner sums, computes rstd, the router
-// logit, the score and the exit flag, and broadcasts {score, rstd, mean, flag}
-// of its rows to every CTA of the cluster.  Each CTA then writes its K slice
+// of 64/C rows.  They travel through an L2-resident exchange area of the
+// workspace (coalesced 128-byte stores and L2-only loads, double-buffered per
+// cluster); distributed shared memory carries only the mbarrier signals
+// between the CTAs.  The owner sums, computes rstd, the router logit, the
+// score and the exit flag, and publishes {score, rstd, mean, flag} of its rows
+// for every CTA of the cluster.  Each CTA then writes its K slice
 // of every row of the tile -- survivors copied to the dense buffer at their
 // stable rank, exits final-normed to their original position -- reading the
 // row slice back from L2 (the cluster's tiles in flight are a few MiB).  Tile
@@ -53,7 +55,7 @@ constexpr int kRows = 64;        // rows per tile (MMA N)
 constexpr int kUnits = 128;      // router units (MMA M)
 constexpr int kChunk = 64;       // columns per chunk (128 bytes of 16-bit data)
 constexpr int kThreads = 512;
-constexpr int kStages = 6;
+constexpr int kStages = 10;
 constexpr int kMaxSliceChunks = 8;  // W' slice <= 8 chunks = 128 KB
 constexpr uint32_t kTmemCols = 128;  // two 64-column fp32 accumulators
 constexpr int kSmemBudget = 227 * 1024;
@@ -77,8 +79,16 @@ struct Params {
   float *scores_out;
   int32_t *counts;
   uint64_t *status;
+  float *xchg;          // exchange area, xchg_stride floats per cluster
+  int64_t xchg_stride;
   int32_t *err;
 };
+
+// exchange area of one cluster (floats): partials [2][C][64][128], row
+// statistics [2][C][64][2], decisions [2][64] x float4
+__host__ __device__ inline int64_t xchg_floats(int C) {
+  return 2LL * C * kRows * kUnits + 2LL * C * kRows * 2 + 2LL * kRows * 4;
+}
 
 // shared-memory layout (offsets from the 1024-aligned base)
 struct Layout {
@@ -90,9 +100,9 @@ __host__ __device__ inline Layout layout(int slice_chunks, int C) {
   uint32_t o = 0;
   L.w = o;       o += (uint32_t)slice_chunks * kUnits * kChunk * 2;  // resident W' slice
   L.ring = o;    o += (uint32_t)kStages * kRows * kChunk * 2;        // x chunks
-  L.slots = o;   o += (uint32_t)kUnits * kRows * 4;                  // [C][128][64/C] fp32
-  L.slot_ss = o; o += (uint32_t)kRows * 2 * 4;                        // [C][64/C][2]
-  L.info = o;    o += 2u * kRows * 16;                                // [2][64] {score, rstd, mean, flag}
+  L.slots = o;   o += 0;                                             // (exchange is in L2)
+  L.slot_ss = o; o += 0;
+  L.info = o;    o += kRows * 16;                                     // this tile's decisions
   L.stat = o;    o += 2u * 2 * kRows * 2 * 4;                         // [2 bufs][2 halves][64][ss, sx]
   const uint32_t slice = (uint32_t)slice_chunks * kChunk;
   L.wn = o;      o += slice * 4;
@@ -120,9 +130,9 @@ enum Bar {
   kAccEmpty = kAccFull + 2,  // [2]
   kStatFull = kAccEmpty + 2, // [2]
   kStatEmpty = kStatFull + 2,// [2]
-  kSlotsFull = kStatEmpty + 2,
-  kSlotFree,
-  kInfoFull,                 // [2]
+  kSlotsFull = kStatEmpty + 2, // [2]
+  kSlotFree = kSlotsFull + 2,  // [2]
+  kInfoFull = kSlotFree + 2,   // [2]
   kInfoFree = kInfoFull + 2, // [2]
   kDrain = kInfoFree + 2,
   kNumBars
@@ -183,9 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Layout L = layout(p.slice_chunks, C);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
-  float *slots = reinterpret_cast<float *>(smem + L.slots);
-  float *slot_ss = reinterpret_cast<float *>(smem + L.slot_ss);
-  float4 *info = reinterpret_cast<float4 *>(smem + L.info);
+  float4 *info = reinterpret_cast<float4 *>(smem + L.info);  // [64] decisions of the tile
   float *stat = reinterpret_cast<float *>(smem + L.stat);
   float *s_wn = reinterpret_cast<float *>(smem + L.wn);
   float *s_bn = reinterpret_cast<float *>(smem + L.bn);
@@ -237,9 +245,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(&bars[kStatEmpty + a], 4);
       ptx::mbar_init(&bars[kInfoFull + a], kRows);  // one arrival per row
       ptx::mbar_init(&bars[kInfoFree + a], C);      // one arrival per CTA
+      ptx::mbar_init(&bars[kSlotsFull + a], 4 * C); // 4 warps of every source
+      ptx::mbar_init(&bars[kSlotFree + a], C);      // every owner
     }
-    ptx::mbar_init(&bars[kSlotsFull], 4 * C);       // 4 warps of every source
-    ptx::mbar_init(&bars[kSlotFree], C);            // every owner
     ptx::mbar_init(&bars[kDrain], 1);
     *abort_flag = 0;
     *issued = 0;
@@ -396,9 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the group stops together at the iteration's end (s_stop1).
     const int t = threadIdx.x - 256;   // 0..127 = router unit b = TMEM lane
     const int q = warp & 3;            // TMEM lane quarter of this warp
-    const uint32_t slots_u32 = ptx::smem_u32(slots);
-    const uint32_t slot_ss_u32 = ptx::smem_u32(slot_ss);
-    const uint32_t info_u32 = ptx::smem_u32(info);
+    float *xP = p.xchg + (size_t)cluster_id * (size_t)p.xchg_stride;
+    float *xS = xP + 2 * C * kRows * kUnits;
+    float4 *xI = reinterpret_cast<float4 *>(xS + 2 * C * kRows * 2);
     int t_local = 0;
     for (int tile = cluster_id; tile < n_tiles; tile += n_clusters, ++t_local) {
       bool ok = true;
@@ -428,39 +436,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (ok && lane == 0) ptx::mbar_arrive(&bars[kAccEmpty + buf]);
-      // (3) send the partials to their owners (slot [src][b][R] at the owner)
-      if (ok && t_local >= 1)
-        ok = ptx::mbar_wait_cluster(&bars[kSlotFree], (uint32_t)(t_local - 1) & 1u, abort_flag);
+      // (3) publish the partials: xP[buf][rank][r][b], coalesced over b
+      if (ok && t_local >= 2)
+        ok = ptx::mbar_wait_cluster(&bars[kSlotFree + buf], ph2 ^ 1u, abort_flag);
       if (ok) {
+        float *dst = xP + ((size_t)(buf * C + (int)rank) * kRows) * kUnits + t;
 #pragma unroll
-        for (int o = 0; o < C; ++o) {
-          const uint32_t base = ptx::map_to_rank(
-              slots_u32 + (uint32_t)(((int)rank * kUnits + t) * R) * 4u, (uint32_t)o);
-#pragma unroll
-          for (int j = 0; j < R; j += 4)
-            ptx::st_cluster_v4(base + (uint32_t)j * 4u, d[o * R + j], d[o * R + j + 1],
-                               d[o * R + j + 2], d[o * R + j + 3]);
-        }
+        for (int r = 0; r < kRows; ++r) __stcg(dst + (size_t)r * kUnits, d[r]);
         if (t < kRows) {
-          const int o = t / R, rr = t % R;
-          const uint32_t a = ptx::map_to_rank(
-              slot_ss_u32 + (uint32_t)(((int)rank * R + rr) * 2) * 4u, (uint32_t)o);
-          ptx::st_cluster_v2(a, ss_part, sx_part);
+          float *sd = xS + ((size_t)(buf * C + (int)rank) * kRows + t) * 2;
+          __stcg(sd, ss_part);
+          __stcg(sd + 1, sx_part);
         }
       }
       // the warp barrier orders every lane's stores before lane 0's
       // release-arrive at cluster scope
       ok = __all_sync(0xffffffffu, ok);
       if (ok && lane == 0)
-        for (int o = 0; o < C; ++o) ptx::mbar_arrive_cluster(remote_bar(kSlotsFull, (uint32_t)o));
+        for (int o = 0; o < C; ++o) ptx::mbar_arrive_cluster(remote_bar(kSlotsFull + buf, (uint32_t)o));
       // (4) owner: the statistics of the R owned rows, then their logits
-      if (ok) ok = ptx::mbar_wait_cluster(&bars[kSlotsFull], (uint32_t)t_local & 1u, abort_flag);
+      if (ok) ok = ptx::mbar_wait_cluster(&bars[kSlotsFull + buf], ph2, abort_flag);
+      const int row0 = (int)rank * R;  // first owned row of the tile
       if (ok && t < R) {
         float ss = 0.f, sx = 0.f;
 #pragma unroll
         for (int src = 0; src < C; ++src) {
-          ss += slot_ss[(src * R + t) * 2];
-          sx += slot_ss[(src * R + t) * 2 + 1];
+          const float *sd = xS + ((size_t)(buf * C + src) * kRows + row0 + t) * 2;
+          ss += __ldcg(sd);
+          sx += __ldcg(sd + 1);
         }
         float mean = 0.f, rstd;
         if (!LAYER) {
@@ -476,28 +479,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::named_sync(1, 128);
       ok = !*s_stop1;
       if (ok) {
+        float acc[R];
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) acc[rr] = 0.f;
+#pragma unroll
+        for (int src = 0; src < C; ++src) {
+          const float *sp = xP + ((size_t)(buf * C + src) * kRows + row0) * kUnits + t;
+#pragma unroll
+          for (int rr = 0; rr < R; ++rr) acc[rr] += __ldcg(sp + (size_t)rr * kUnits);
+        }
 #pragma unroll
         for (int rr = 0; rr < R; ++rr) {
-          float acc = 0.f;
-#pragma unroll
-          for (int src = 0; src < C; ++src) acc += slots[(src * kUnits + t) * R + rr];
           const float rstd = s_rstd[rr];
-          const float z = LAYER ? fmaf(rstd, acc - s_mean[rr] * s_cs[t], s_bp[t]) : rstd * acc;
+          const float z = LAYER ? fmaf(rstd, acc[rr] - s_mean[rr] * s_cs[t], s_bp[t]) : rstd * acc[rr];
           const float v = warp_sum(s_up[t] * silu_f(z));
           if (lane == 0) s_red[q * R + rr] = v;
         }
       }
       ptx::named_sync(1, 128);
-      // every slot of this tile has been read: sources may refill them
+      // every partial of this buffer has been read: sources may refill it
       if (ok && t == 0)
-        for (int src = 0; src < C; ++src) ptx::mbar_arrive_cluster(remote_bar(kSlotFree, (uint32_t)src));
-      // (5) decide the owned rows and broadcast {score, rstd, mean, flag}
+        for (int src = 0; src < C; ++src) ptx::mbar_arrive_cluster(remote_bar(kSlotFree + buf, (uint32_t)src));
+      // (5) decide the owned rows and publish {score, rstd, mean, flag}
       if (ok && t < R) {
         const float logit = p.up_bias + s_red[0 * R + t] + s_red[1 * R + t] + s_red[2 * R + t] +
                             s_red[3 * R + t];
         const float score = sigmoid_f(logit);
-        const int row_in_tile = (int)rank * R + t;
-        const int64_t grow = (int64_t)tile * kRows + row_in_tile;
+        const int64_t grow = (int64_t)tile * kRows + row0 + t;
         float flag = 0.f;  // 0 beyond the active rows, 1 survive, 2 exit
         if (grow < n) {
           flag = score > p.threshold ? 2.f : 1.f;
@@ -505,12 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (t_local >= 2) ok = ptx::mbar_wait_cluster(&bars[kInfoFree + buf], ph2 ^ 1u, abort_flag);
         if (ok) {
-#pragma unroll
-          for (int dcta = 0; dcta < C; ++dcta) {
-            const uint32_t a = ptx::map_to_rank(
-                info_u32 + (uint32_t)((buf * kRows + row_in_tile) * 16), (uint32_t)dcta);
-            ptx::st_cluster_v4(a, score, s_rstd[t], s_mean[t], flag);
-          }
+          __stcg(&xI[buf * kRows + row0 + t], make_float4(score, s_rstd[t], s_mean[t], flag));
 #pragma unroll
           for (int dcta = 0; dcta < C; ++dcta)
             ptx::mbar_arrive_cluster(remote_bar(kInfoFull + buf, (uint32_t)dcta));
@@ -531,17 +534,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     int t_local = 0;
     const T *x = static_cast<const T *>(p.x);
     const int vec_per_row = slice / 8;  // 16-byte vectors of this CTA's slice (<= 64)
+    const float4 *xI2 = reinterpret_cast<const float4 *>(
+        p.xchg + (size_t)cluster_id * (size_t)p.xchg_stride + 2 * C * kRows * kUnits + 2 * C * kRows * 2);
     for (int tile = cluster_id; tile < n_tiles; tile += n_clusters, ++t_local) {
       const int buf = t_local & 1;
       const uint32_t ph2 = (uint32_t)(t_local >> 1) & 1u;
       bool ok = ptx::mbar_wait_cluster(&bars[kInfoFull + buf], ph2, abort_flag);
+      if (ok && t < kRows) info[t] = __ldcg(&xI2[buf * kRows + t]);
       if (!ok) *s_stop2 = 1;
       ptx::named_sync(2, 128);
       if (*s_stop2) break;
+      // the decisions are copied: every owner may reuse this buffer
+      if (t == 0)
+        for (int o = 0; o < C; ++o) ptx::mbar_arrive_cluster(remote_bar(kInfoFree + buf, (uint32_t)o));
       // ranks inside the tile (rows 0..63 by threads 0..63); the tile's
       // positions are fetched once here, in parallel
       if (t < kRows) {
-        const int st = (int)info[buf * kRows + t].w;
+        const int st = (int)info[t].w;
         const int64_t row = (int64_t)tile * kRows + t;
         s_pos[t] = st == 0 ? -1 : (p.pos_in ? p.pos_in[row] : row);
         const unsigned kb = __ballot_sync(0xffffffffu, st == 1);
@@ -555,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ptx::named_sync(2, 128);
       if (t < kRows && t >= 32) {
-        const int st = (int)info[buf * kRows + t].w;
+        const int st = (int)info[t].w;
         s_rank[t] += st == 1 ? s_prefix[8] : s_prefix[9];
       }
       if (t == 0) {
@@ -579,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t keep_before = s_prefix[0], exits_before = s_prefix[1];
       // token bookkeeping (rank 0 only)
       if (rank == 0 && t < kRows) {
-        const int st = (int)info[buf * kRows + t].w;
+        const int st = (int)info[t].w;
         const int64_t row = (int64_t)tile * kRows + t;
         if (st == 1) {
           const int64_t dst = (int64_t)keep_before + s_rank[t];
@@ -596,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int r = r0 + i;
-          const int st = (int)info[buf * kRows + r].w;
+          const int st = (int)info[r].w;
           const int64_t row = (int64_t)tile * kRows + r;
           const uint4 *src = reinterpret_cast<const uint4 *>(x + row * p.H + col0);
 #pragma unroll
@@ -608,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int r = r0 + i;
-          const float4 in = info[buf * kRows + r];
+          const float4 in = info[r];
           const int st = (int)in.w;
           if (st == 0) continue;
           if (st == 1) {
@@ -650,10 +659,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // this CTA is done with info[buf]: tell every owner
       ptx::named_sync(2, 128);
-      if (t == 0)
-        for (int o = 0; o < C; ++o) ptx::mbar_arrive_cluster(remote_bar(kInfoFree + buf, (uint32_t)o));
       if (*abort_flag) *s_stop2 = 1;
       ptx::named_sync(2, 128);
       if (*s_stop2) break;
@@ -752,9 +758,19 @@ const char *fused_unsupported_reason(const tide_checkpoint_args *a) {
 
 bool fused_supported(const tide_checkpoint_args *a) { return fused_unsupported_reason(a) == nullptr; }
 
-size_t fused_workspace_bytes(int64_t n_rows) {
+// Workspace: 256 reserved bytes, the tile status words (zeroed per call),
+// then one exchange area per cluster that can be resident on any B200
+// (at most 160 SMs / C clusters).
+size_t fused_status_bytes(int64_t n_rows) {
   const int64_t tiles = n_rows > 0 ? (n_rows + fused::kRows - 1) / fused::kRows : 1;
-  return 256 + (((size_t)tiles * 8 + 255) / 256) * 256;
+  return (((size_t)tiles * 8 + 255) / 256) * 256;
+}
+
+size_t fused_workspace_bytes(const tide_checkpoint_args *a) {
+  const int C = fused_cluster_size(a->hidden_dim);
+  if (!C) return 0;
+  const size_t xchg = (size_t)(160 / C) * (size_t)fused::xchg_floats(C) * 4;
+  return 256 + fused_status_bytes(a->n_rows) + xchg;
 }
 
 int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, char *err,
@@ -769,8 +785,10 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
     snprintf(err, err_len, "fused checkpoint: cuTensorMapEncodeTiled failed");
     return TIDE_ERR_CUDA;
   }
-  uint64_t *status = reinterpret_cast<uint64_t *>(static_cast<char *>(a->workspace) + 256);
-  cudaError_t e = cudaMemsetAsync(a->workspace, 0, fused_workspace_bytes(a->n_rows), stream);
+  char *ws = static_cast<char *>(a->workspace);
+  uint64_t *status = reinterpret_cast<uint64_t *>(ws + 256);
+  float *xchg = reinterpret_cast<float *>(ws + 256 + fused_status_bytes(a->n_rows));
+  cudaError_t e = cudaMemsetAsync(a->workspace, 0, 256 + fused_status_bytes(a->n_rows), stream);
   if (e != cudaSuccess) {
     snprintf(err, err_len, "fused checkpoint: memset: %s", cudaGetErrorString(e));
     return TIDE_ERR_CUDA;
@@ -803,6 +821,8 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
   p.scores_out = a->scores_out;
   p.counts = a->counts_out;
   p.status = status;
+  p.xchg = xchg;
+  p.xchg_stride = fused::xchg_floats(C);
   p.err = a->error_word;
 
   const void *fn = nullptr;
@@ -848,7 +868,8 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
     max_clusters[bf16][C] = mc;
   }
   const int64_t tiles = (a->n_rows + fused::kRows - 1) / fused::kRows;
-  const int64_t g = tiles < max_clusters[bf16][C] ? tiles : max_clusters[bf16][C];
+  int64_t g = tiles < max_clusters[bf16][C] ? tiles : max_clusters[bf16][C];
+  if (g > 160 / C) g = 160 / C;  // the workspace holds 160 / C exchange areas
   cfg.gridDim = dim3((unsigned)(g * C), 1, 1);
   switch (C) {
     case 1: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 1>, tx, tw, p)

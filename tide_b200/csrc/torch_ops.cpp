@@ -206,9 +206,10 @@ std::vector<at::Tensor> router_fold(const at::Tensor &down, const at::Tensor &no
   return {down_t, folded, colsum, bias_proj};
 }
 
-int64_t checkpoint_workspace_size(int64_t n_rows) {
+int64_t checkpoint_workspace_size(int64_t n_rows, int64_t hidden_dim) {
   tide_checkpoint_args a{};
   a.n_rows = n_rows;
+  a.hidden_dim = hidden_dim;
   return (int64_t)tide_checkpoint_workspace_size(&a);
 }
 
@@ -321,7 +322,7 @@ TORCH_LIBRARY(tide, m) {
         "Tensor norm_weight, Tensor? norm_bias, int norm_type, float eps) -> ()");
   m.def("router_fold(Tensor down, Tensor norm_weight, Tensor? norm_bias, ScalarType fold_dtype) "
         "-> Tensor[]");
-  m.def("checkpoint_workspace_size(int n_rows) -> int", &checkpoint_workspace_size);
+  m.def("checkpoint_workspace_size(int n_rows, int hidden_dim) -> int", &checkpoint_workspace_size);
   m.def("checkpoint(Tensor x, Tensor? n_rows_dev, Tensor norm_weight, Tensor? norm_bias, "
         "int norm_type, float eps, Tensor down_t, Tensor? folded, Tensor? colsum, "
         "Tensor? bias_proj, Tensor up, float up_bias, float threshold, Tensor? positions, "

@@ -88,8 +88,8 @@ class CheckpointRunner:
         self.error_word = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.last_path = None
 
-    def _workspace(self, n_rows: int) -> torch.Tensor:
-        need = int(self.ops.checkpoint_workspace_size(n_rows))
+    def _workspace(self, n_rows: int, hidden_dim: int) -> torch.Tensor:
+        need = int(self.ops.checkpoint_workspace_size(n_rows, hidden_dim))
         if self.workspace.numel() < need:
             self.workspace = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self.workspace
@@ -100,7 +100,7 @@ class CheckpointRunner:
             counts: Optional[torch.Tensor] = None, path: int = PATH_AUTO) -> torch.Tensor:
         """One checkpoint; returns the device counts tensor {survivors, exits}."""
         counts = self.counts if counts is None else counts
-        ws = self._workspace(x.shape[0])
+        ws = self._workspace(x.shape[0], x.shape[1])
         self.last_path = self.ops.checkpoint(
             x, n_rows_dev, norm.weight, norm.bias, norm.kind, norm.eps, router.down_t,
             router.folded, router.colsum, router.bias_proj, router.up, router.up_bias,
