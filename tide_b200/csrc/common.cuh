@@ -91,13 +91,16 @@ constexpr int kSpinLimit = 1 << 24;
 __device__ __forceinline__ uint64_t pack_status(uint64_t flag, uint32_t keep, uint32_t exits) {
   return flag | ((uint64_t)exits << 31) | (uint64_t)keep;
 }
-__device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t *p) {
+// The status words carry their own counts, so publishing and polling them
+// needs no ordering with other memory: relaxed gpu-scope accesses suffice and
+// avoid waiting for this thread's earlier stores at every publication.
+__device__ __forceinline__ uint64_t ld_status(const uint64_t *p) {
   uint64_t v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_u64(uint64_t *p, uint64_t v) {
-  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_status(uint64_t *p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // Decoupled look-back for tile `tile`: publishes this tile's aggregate,
@@ -109,18 +112,18 @@ __device__ __forceinline__ bool lookback(uint64_t *status, uint32_t tile, uint32
                                          uint32_t *exits_before) {
   uint32_t kb = 0, eb = 0;
   if (tile == 0) {
-    st_release_u64(&status[0], pack_status(kFlagPrefix, keep, exits));
+    st_status(&status[0], pack_status(kFlagPrefix, keep, exits));
     *keep_before = 0;
     *exits_before = 0;
     return true;
   }
-  st_release_u64(&status[tile], pack_status(kFlagAggregate, keep, exits));
+  st_status(&status[tile], pack_status(kFlagAggregate, keep, exits));
   int64_t j = (int64_t)tile - 1;
   bool ok = true;
   while (j >= 0) {
     uint64_t s = 0;
     int spins = 0;
-    while (((s = ld_acquire_u64(&status[j])) >> 62) == 0) {
+    while (((s = ld_status(&status[j])) >> 62) == 0) {
       if (++spins > kSpinLimit) { ok = false; break; }
       __nanosleep(32);
     }
@@ -130,7 +133,7 @@ __device__ __forceinline__ bool lookback(uint64_t *status, uint32_t tile, uint32
     if ((s >> 62) == 2) break;
     --j;
   }
-  st_release_u64(&status[tile], pack_status(kFlagPrefix, kb + keep, eb + exits));
+  st_status(&status[tile], pack_status(kFlagPrefix, kb + keep, eb + exits));
   *keep_before = kb;
   *exits_before = eb;
   return ok;

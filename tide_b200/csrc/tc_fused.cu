@@ -162,7 +162,7 @@ __device__ __forceinline__ bool lookback_read(const uint64_t *status, uint32_t t
   while (j >= 0) {
     uint64_t s = 0;
     int spins = 0;
-    while (((s = ld_acquire_u64(&status[j])) >> 62) == 0) {
+    while (((s = ld_status(&status[j])) >> 62) == 0) {
       if (++spins > kSpinLimit) {
         *keep_before = kb;
         *exits_before = eb;
@@ -449,11 +449,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           __stcg(sd + 1, sx_part);
         }
       }
-      // the warp barrier orders every lane's stores before lane 0's
-      // release-arrive at cluster scope
+      // the warp barrier orders every lane's stores before lane 0's fence;
+      // one cluster-scope fence then covers all the arrivals
       ok = __all_sync(0xffffffffu, ok);
-      if (ok && lane == 0)
-        for (int o = 0; o < C; ++o) ptx::mbar_arrive_cluster(remote_bar(kSlotsFull + buf, (uint32_t)o));
+      if (ok && lane == 0) {
+        ptx::fence_cluster();
+        for (int o = 0; o < C; ++o)
+          ptx::mbar_arrive_cluster_relaxed(remote_bar(kSlotsFull + buf, (uint32_t)o));
+      }
       // (4) owner: the statistics of the R owned rows, then their logits
       if (ok) ok = ptx::mbar_wait_cluster(&bars[kSlotsFull + buf], ph2, abort_flag);
       const int row0 = (int)rank * R;  // first owned row of the tile
@@ -498,8 +501,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ptx::named_sync(1, 128);
       // every partial of this buffer has been read: sources may refill it
+      // (the loads have returned: a relaxed signal orders nothing else)
       if (ok && t == 0)
-        for (int src = 0; src < C; ++src) ptx::mbar_arrive_cluster(remote_bar(kSlotFree + buf, (uint32_t)src));
+        for (int src = 0; src < C; ++src)
+          ptx::mbar_arrive_cluster_relaxed(remote_bar(kSlotFree + buf, (uint32_t)src));
       // (5) decide the owned rows and publish {score, rstd, mean, flag}
       if (ok && t < R) {
         const float logit = p.up_bias + s_red[0 * R + t] + s_red[1 * R + t] + s_red[2 * R + t] +
@@ -514,9 +519,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (t_local >= 2) ok = ptx::mbar_wait_cluster(&bars[kInfoFree + buf], ph2 ^ 1u, abort_flag);
         if (ok) {
           __stcg(&xI[buf * kRows + row0 + t], make_float4(score, s_rstd[t], s_mean[t], flag));
+          ptx::fence_cluster();
 #pragma unroll
           for (int dcta = 0; dcta < C; ++dcta)
-            ptx::mbar_arrive_cluster(remote_bar(kInfoFull + buf, (uint32_t)dcta));
+            ptx::mbar_arrive_cluster_relaxed(remote_bar(kInfoFull + buf, (uint32_t)dcta));
         }
       }
       if (!ok || *abort_flag) *s_stop1 = 1;
@@ -546,7 +552,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*s_stop2) break;
       // the decisions are copied: every owner may reuse this buffer
       if (t == 0)
-        for (int o = 0; o < C; ++o) ptx::mbar_arrive_cluster(remote_bar(kInfoFree + buf, (uint32_t)o));
+        for (int o = 0; o < C; ++o)
+          ptx::mbar_arrive_cluster_relaxed(remote_bar(kInfoFree + buf, (uint32_t)o));
       // ranks inside the tile (rows 0..63 by threads 0..63); the tile's
       // positions are fetched once here, in parallel
       if (t < kRows) {
