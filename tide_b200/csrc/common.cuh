@@ -43,12 +43,20 @@ __device__ __forceinline__ uint4 pack16(const float *f) {
   return v;
 }
 
-// Streaming 16-byte global accesses.
+// Streaming 16-byte global accesses.  Rows are read once by the movers, so
+// their loads carry an L2 evict-first policy: lines they bring in from DRAM
+// are the first to go, and what the router left in L2 (the late column
+// chunks of every row) survives until the movers reach it.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
 __device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+               : "l"(p), "l"(l2_evict_first_policy()));
   return v;
 }
 __device__ __forceinline__ void st_stream(uint4 *p, const uint4 &v) {
@@ -71,6 +79,14 @@ __device__ __forceinline__ float rsqrt_rn(float v) { return __fdiv_rn(1.0f, __fs
 // SiLU and sigmoid in fp32 (x * sigmoid(x), 1 / (1 + e^-x)).
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+// Fast SiLU for the tensor-core paths (scores held to 1e-2): the hardware
+// exponential and the approximate division, ~1e-6 relative error and no
+// branches, so an unrolled loop of them keeps the MUFU pipe busy.  The
+// exponent is clamped at 80 (e^80 < 2^126, inside __fdividef's range); below
+// -80 SiLU is 0 to fp32 precision anyway.
+__device__ __forceinline__ float silu_fast(float x) {
+  return __fdividef(x, 1.0f + __expf(fminf(-x, 80.0f)));
+}
 
 __device__ __forceinline__ void raise_error(int32_t *err, int bits) {
   if (err) atomicOr(err, bits);

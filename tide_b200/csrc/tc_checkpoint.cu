@@ -9,15 +9,22 @@
 // memory tiles.  Reference semantics: python/TIDE/runtime.py:128-130 and
 // python/TIDE/router.py:18-19.
 //
-// Persistent CTAs, one per SM, take 128-row tiles round-robin.  Per CTA:
-//   warp 0      TMA producer: x chunk [128 rows x 64 cols] + W' chunk
-//               [B x 64] per pipeline stage (128-byte swizzle);
-//   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K = 16) per
-//               stage into one of two fp32 accumulators of B columns;
-//   warps 4-11  row statistics from the x chunks (two threads per row, each
-//               half of the chunk's 128 bytes);
-//   warps 4-7   then the epilogue: tcgen05.ld of the accumulator row, SiLU,
-//               up projection, sigmoid; writes the score and (mean, rstd).
+// Persistent CTAs, one per SM.  The rows are cut into 32-row units and each
+// CTA takes a contiguous, balanced range of units (so no SM does a whole
+// extra tile), walked in tiles of up to 256 rows.  Per CTA:
+//   warp 0      TMA producer: per pipeline stage, one [32 rows x 64 cols]
+//               box per unit of the tile plus the W' chunk [B x 64]
+//               (128-byte swizzle); the W' chunk is shared by both halves;
+//   warp 1      TMEM owner and MMA issuer: per stage and 128-row half,
+//               4 x tcgen05.mma (K = 16) into that half's fp32 accumulator
+//               of B columns (double-buffered across tiles when TMEM holds
+//               four);
+//   warps 4-11  row statistics from the x chunks (one thread per row),
+//               handed to the epilogue per tile through a double-buffered
+//               shared-memory slot;
+//   warps 12-15 the epilogue: tcgen05.ld of the accumulator rows, SiLU, up
+//               projection, sigmoid; writes the score and (mean, rstd).  It
+//               runs beside the statistics so the ring never waits for it.
 // The survivors/exits are then moved by the stable-partition kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -29,12 +36,15 @@
 
 namespace tide {
 
-constexpr int kTcM = 128;         // rows per tile (TMEM lanes)
+constexpr int kTcM = 128;         // rows per MMA half (TMEM lanes)
+constexpr int kTcUnit = 32;       // rows per TMA box / scheduling unit
+constexpr int kTcTileUnits = 8;   // units per tile: two 128-row halves
+constexpr int kTcTileRows = kTcUnit * kTcTileUnits;
 constexpr int kTcK = 64;          // columns per chunk: 128 bytes of 16-bit data
-constexpr int kTcThreads = 384;  // warps 0-1 TMA/MMA, 4-11 statistics, 4-7 epilogue
+constexpr int kTcThreads = 512;  // warps 0-1 TMA/MMA, 4-11 statistics, 12-15 epilogue
 constexpr int kTcMaxStages = 8;
 constexpr int kTcSmemBudget = 227 * 1024;
-constexpr int kTcAux = 8192;      // barriers, flags, per-unit vectors, half-row sums
+constexpr int kTcAux = 8192;      // barriers, flags, per-unit vectors, row statistics
 
 struct TcRouteParams {
   int64_t n_cap;
@@ -46,6 +56,7 @@ struct TcRouteParams {
   float2 *row_stats;
   int32_t *err;
   int stages;
+  int n_acc;  // accumulator sets in TMEM (2: double-buffered across tiles)
   uint32_t tmem_cols;
 };
 
@@ -73,30 +84,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = p.stages, B = p.B;
-  const uint32_t a_bytes = kTcM * kTcK * 2;
+  const int S = p.stages, B = p.B, NA = p.n_acc;
+  const uint32_t unit_bytes = kTcUnit * kTcK * 2;
+  const uint32_t a_bytes = kTcTileRows * kTcK * 2;
   const uint32_t b_bytes = (uint32_t)B * kTcK * 2;
   const uint32_t stage_bytes = a_bytes + b_bytes;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * stage_bytes);
   uint64_t *empty = full + S;
-  uint64_t *acc_full = empty + S;
-  uint64_t *acc_empty = acc_full + 2;  // [0,1] accumulators, [2] half-sums slot
-  uint64_t *half_full = acc_empty + 3;
-  uint64_t *drain = half_full + 1;
+  uint64_t *acc_full = empty + S;      // [2] accumulator set written
+  uint64_t *acc_empty = acc_full + 2;  // [2] accumulator set read
+  uint64_t *stat_full = acc_empty + 2; // [2] statistics slot written
+  uint64_t *stat_empty = stat_full + 2;// [2] statistics slot read
+  uint64_t *drain = stat_empty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   uint32_t *issued = reinterpret_cast<uint32_t *>(tmem_slot + 2);
   float *s_up = reinterpret_cast<float *>(tmem_slot + 4);
   float *s_cs = s_up + 256;
   float *s_bp = s_cs + 256;
-  float *s_half = s_bp + 256;  // [2][128] partial sums of the second half-rows
+  float *s_stat = s_bp + 256;  // [2 slots][256 rows][ss, sx]
 
   int64_t n = p.n_cap;
   if (p.n_dev) {
     int64_t nd = (int64_t)__ldg(p.n_dev);
     n = nd < 0 ? 0 : (nd > p.n_cap ? p.n_cap : nd);
   }
-  const int n_tiles = (int)((n + kTcM - 1) / kTcM);
+  // this CTA's balanced range of 32-row units
+  const int64_t units = (n + kTcUnit - 1) / kTcUnit;
+  const int64_t u_begin = (int64_t)blockIdx.x * units / gridDim.x;
+  const int64_t u_end = ((int64_t)blockIdx.x + 1) * units / gridDim.x;
   const int k_chunks = p.H / kTcK;
 
   if (threadIdx.x == 0) {
@@ -106,10 +122,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&acc_full[a], 1);
-      ptx::mbar_init(&acc_empty[a], 4);
+      ptx::mbar_init(&acc_empty[a], 4);   // 4 epilogue warps
+      ptx::mbar_init(&stat_full[a], 8);   // 8 statistics warps
+      ptx::mbar_init(&stat_empty[a], 4);  // 4 epilogue warps
     }
-    ptx::mbar_init(&acc_empty[2], 4);  // second-half sums consumed (per tile)
-    ptx::mbar_init(half_full, 128);  // one arrival per second-half thread
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
     *issued = 0;
@@ -136,7 +152,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       ptx::prefetch_tmap(&tmap_x);
       ptx::prefetch_tmap(&tmap_w);
       uint32_t it = 0;
-      for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
+      for (int64_t u0 = u_begin; u0 < u_end && !*abort_flag; u0 += kTcTileUnits) {
+        const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
         for (int kc = 0; kc < k_chunks; ++kc, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
           if (it >= (uint32_t)S && !ptx::mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
@@ -145,9 +162,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             break;
           }
           uint8_t *st = smem + (size_t)s * stage_bytes;
-          ptx::mbar_expect_tx(&full[s], stage_bytes);
-          ptx::tma_load_2d(st, &tmap_x, &full[s], kc * kTcK, tile * kTcM);
+          ptx::mbar_expect_tx(&full[s], (uint32_t)nu * unit_bytes + b_bytes);
           ptx::tma_load_2d(st + a_bytes, &tmap_w, &full[s], kc * kTcK, 0);
+          for (int j = 0; j < nu; ++j)
+            ptx::tma_load_2d(st + (size_t)j * unit_bytes, &tmap_x, &full[s], kc * kTcK,
+                             (int)((u0 + j) * kTcUnit));
           *issued = it + 1;
         }
       }
@@ -159,27 +178,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t it = 0;
       int t_local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < n_tiles && ok && !*abort_flag;
-           tile += gridDim.x, ++t_local) {
-        const int acc = t_local & 1;
-        const uint32_t acc_ph = (uint32_t)(t_local >> 1) & 1u;
-        if (t_local >= 2 && !ptx::mbar_wait(&acc_empty[acc], acc_ph ^ 1u, abort_flag)) {
+      for (int64_t u0 = u_begin; u0 < u_end && ok && !*abort_flag;
+           u0 += kTcTileUnits, ++t_local) {
+        const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
+        const int halves = nu > kTcTileUnits / 2 ? 2 : 1;
+        const int acc = t_local % NA;
+        const uint32_t acc_ph = (uint32_t)(t_local / NA) & 1u;
+        if (t_local >= NA && !ptx::mbar_wait(&acc_empty[acc], acc_ph ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * B);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 2 * B);
         for (int kc = 0; kc < k_chunks; ++kc, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
           if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
           const uint32_t a0 = ptx::smem_u32(smem + (size_t)s * stage_bytes);
           const uint32_t b0 = a0 + a_bytes;
+          for (int h = 0; h < halves; ++h) {
 #pragma unroll
-          for (int k = 0; k < kTcK / 16; ++k) {
-            ptx::mma_f16_ss(d_tmem, ptx::sw128_kmajor_desc(a0 + 32u * k),
-                            ptx::sw128_kmajor_desc(b0 + 32u * k), idesc,
-                            (kc > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < kTcK / 16; ++k) {
+              ptx::mma_f16_ss(d_tmem + (uint32_t)(h * B),
+                              ptx::sw128_kmajor_desc(a0 + (uint32_t)h * (kTcM * 128) + 32u * k),
+                              ptx::sw128_kmajor_desc(b0 + 32u * k), idesc,
+                              (kc > 0 || k > 0) ? 1u : 0u);
+            }
           }
           ptx::mma_commit(&empty[s]);
         }
@@ -195,92 +219,123 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       volatile int never = 0;
       if (!ptx::mbar_wait(drain, 0, &never)) raise_error(p.err, TIDE_DEVERR_TIMEOUT);
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------ statistics + epilogue
-    // thread t of warps 4-11: row r = t % 128, half h = t / 128 of each
-    // chunk row (four of its eight 16-byte units, lane-rotated so a warp's
-    // reads of the swizzled tile hit distinct banks)
+  } else if (warp >= 4 && warp < 12) {
+    // ------------------------------------------------- row statistics
+    // thread t of warps 4-11 owns row t of the tile and reads all eight
+    // 16-byte units of its chunk row, lane-rotated so a warp's reads of the
+    // swizzled tile hit distinct banks (the sum is order-free within a row).
     const int t = threadIdx.x - 128;
-    const int r = t & 127, h = t >> 7;
-    const int q = (warp - 4) & 3;
     uint32_t it = 0;
     int t_local = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++t_local) {
+    for (int64_t u0 = u_begin; u0 < u_end && ok; u0 += kTcTileUnits, ++t_local) {
+      const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
+      const bool live = (t >> 5) < nu;  // warp-uniform: a unit is one warp
       float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
       for (int kc = 0; kc < k_chunks; ++kc, ++it) {
         const uint32_t s = it % S, ph = (it / S) & 1u;
         if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
-        const uint8_t *row = smem + (size_t)s * stage_bytes + (size_t)r * 128;
+        if (live) {
+          const uint8_t *row = smem + (size_t)s * stage_bytes + (size_t)t * 128;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int unit = (h * 4 + j + lane) & 7;
-          const uint4 v = *reinterpret_cast<const uint4 *>(row + (unit << 4));
-          float f[8];
-          unpack8_16(v, f, BF16);
+          for (int j = 0; j < 8; ++j) {
+            const int unit = (j + lane) & 7;
+            const uint4 v = *reinterpret_cast<const uint4 *>(row + (unit << 4));
+            float f[8];
+            unpack8_16(v, f, BF16);
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            ss0 = fmaf(f[e], f[e], ss0);
-            ss1 = fmaf(f[e + 1], f[e + 1], ss1);
-            if (LAYER) { sx0 += f[e]; sx1 += f[e + 1]; }
+            for (int e = 0; e < 8; e += 2) {
+              ss0 = fmaf(f[e], f[e], ss0);
+              ss1 = fmaf(f[e + 1], f[e + 1], ss1);
+              if (LAYER) { sx0 += f[e]; sx1 += f[e + 1]; }
+            }
           }
         }
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&empty[s]);
       }
       if (!ok) break;
-      const float ss = ss0 + ss1, sx = sx0 + sx1;
-      if (h == 1) {
-        // hand the second half to the epilogue thread of the same row
-        if (t_local > 0 && !ptx::mbar_wait(&acc_empty[2], (uint32_t)(t_local - 1) & 1u, abort_flag)) {
-          ok = false;
-          break;
-        }
-        s_half[r] = ss;
-        s_half[128 + r] = sx;
-        ptx::mbar_arrive(half_full);
-        continue;
+      const int buf = t_local & 1;
+      if (t_local >= 2 &&
+          !ptx::mbar_wait(&stat_empty[buf], ((uint32_t)(t_local >> 1) & 1u) ^ 1u, abort_flag)) {
+        ok = false;
+        break;
       }
-      if (!ptx::mbar_wait(half_full, (uint32_t)t_local & 1u, abort_flag)) { ok = false; break; }
-      const float ss_row = ss + s_half[r];
-      const float sx_row = sx + s_half[128 + r];
+      float *st = s_stat + ((size_t)buf * kTcTileRows + t) * 2;
+      st[0] = ss0 + ss1;
+      st[1] = sx0 + sx1;
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&acc_empty[2]);
-      float mean = 0.f, rstd;
-      if (!LAYER) {
-        rstd = rsqrt_rn(ss_row / (float)p.H + p.eps);
-      } else {
-        mean = sx_row / (float)p.H;
-        const float var = fmaxf(ss_row / (float)p.H - mean * mean, 0.f);
-        rstd = rsqrt_rn(var + p.eps);
+      if (lane == 0) ptx::mbar_arrive(&stat_full[buf]);
+    }
+    if (!ok) {
+      raise_error(p.err, TIDE_DEVERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+  } else if (warp >= 12) {
+    // ----------------------------------------------------------- epilogue
+    // warp 12 + q reads TMEM lanes 32q..32q+31: rows 32q + lane of each half
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    int t_local = 0;
+    bool ok = true;
+    for (int64_t u0 = u_begin; u0 < u_end && ok; u0 += kTcTileUnits, ++t_local) {
+      const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
+      const int halves = nu > kTcTileUnits / 2 ? 2 : 1;
+      const int buf = t_local & 1;
+      if (!ptx::mbar_wait(&stat_full[buf], (uint32_t)(t_local >> 1) & 1u, abort_flag)) {
+        ok = false;
+        break;
       }
-      const int acc = t_local & 1;
-      const uint32_t acc_ph = (uint32_t)(t_local >> 1) & 1u;
-      if (!ptx::mbar_wait(&acc_full[acc], acc_ph, abort_flag)) { ok = false; break; }
-      ptx::tc_fence_after();
-      float logit = p.up_bias;
-      const uint32_t row_addr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * B);
-      for (int c = 0; c < B; c += 32) {
-        float v[32];
-        ptx::tmem_ld32(row_addr + (uint32_t)c, v);
+      float mean[2], rstd[2];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float z;
-          if (!LAYER)
-            z = rstd * v[j];
-          else
-            z = fmaf(rstd, v[j] - mean * s_cs[c + j], s_bp[c + j]);
-          logit = fmaf(s_up[c + j], silu_f(z), logit);
+      for (int h = 0; h < 2; ++h) {
+        const float *st = s_stat + ((size_t)buf * kTcTileRows + h * kTcM + r) * 2;
+        const float ss = st[0], sx = st[1];
+        if (!LAYER) {
+          mean[h] = 0.f;
+          rstd[h] = rsqrt_rn(ss / (float)p.H + p.eps);
+        } else {
+          mean[h] = sx / (float)p.H;
+          const float var = fmaxf(ss / (float)p.H - mean[h] * mean[h], 0.f);
+          rstd[h] = rsqrt_rn(var + p.eps);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&stat_empty[buf]);
+      const int acc = t_local % NA;
+      if (!ptx::mbar_wait(&acc_full[acc], (uint32_t)(t_local / NA) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      const int64_t row_lim_tile = (u0 + nu) * kTcUnit;
+      const int64_t row_lim = row_lim_tile < n ? row_lim_tile : n;
+      for (int h = 0; h < halves; ++h) {
+        float logit = p.up_bias;
+        const uint32_t row_addr =
+            tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 2 * B + h * B);
+        for (int c = 0; c < B; c += 32) {
+          float v[32];
+          ptx::tmem_ld32(row_addr + (uint32_t)c, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float z;
+            if (!LAYER)
+              z = rstd[h] * v[j];
+            else
+              z = fmaf(rstd[h], v[j] - mean[h] * s_cs[c + j], s_bp[c + j]);
+            logit = fmaf(s_up[c + j], silu_fast(z), logit);
+          }
+        }
+        const int64_t grow = u0 * kTcUnit + h * kTcM + r;
+        if (grow < row_lim) {
+          p.scores[grow] = sigmoid_f(logit);
+          if (p.row_stats) p.row_stats[grow] = make_float2(mean[h], rstd[h]);
         }
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&acc_empty[acc]);
-      const int64_t grow = (int64_t)tile * kTcM + r;
-      if (grow < n) {
-        p.scores[grow] = sigmoid_f(logit);
-        if (p.row_stats) p.row_stats[grow] = make_float2(mean, rstd);
-      }
     }
     if (!ok) {
       raise_error(p.err, TIDE_DEVERR_TIMEOUT);
@@ -337,14 +392,18 @@ bool make_tmap(CUtensorMap *m, const void *base, bool bf16, uint64_t rows, uint6
   return r == CUDA_SUCCESS;
 }
 
+// Two 128-row halves of B columns per accumulator set; two sets when TMEM's
+// 512 columns hold them (B <= 128).
+int n_acc_for(int B) { return 4 * B <= 512 ? 2 : 1; }
+
 uint32_t tmem_cols_for(int B) {
-  uint32_t need = 2u * (uint32_t)B, c = 32;
+  uint32_t need = (uint32_t)(n_acc_for(B) * 2 * B), c = 32;
   while (c < need) c <<= 1;
   return c;
 }
 
 int stages_for(int B) {
-  const int stage = kTcM * kTcK * 2 + B * kTcK * 2;
+  const int stage = kTcTileRows * kTcK * 2 + B * kTcK * 2;
   int s = (kTcSmemBudget - 1024 - kTcAux) / stage;
   return s > kTcMaxStages ? kTcMaxStages : s;
 }
@@ -383,7 +442,7 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   const bool bf16 = a->dtype == TIDE_DTYPE_BF16;
   const int B = (int)a->bottleneck_dim;
   CUtensorMap tx, tw;
-  if (!make_tmap(&tx, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcM) ||
+  if (!make_tmap(&tx, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcUnit) ||
       !make_tmap(&tw, a->folded, bf16, (uint64_t)B, (uint64_t)a->hidden_dim, (uint32_t)B)) {
     snprintf(err, err_len, "tensor-core route: cuTensorMapEncodeTiled failed");
     return TIDE_ERR_CUDA;
@@ -403,10 +462,11 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   p.row_stats = row_stats;
   p.err = a->error_word;
   p.stages = stages_for(B);
+  p.n_acc = n_acc_for(B);
   p.tmem_cols = tmem_cols_for(B);
-  const size_t smem = 1024 + (size_t)p.stages * (kTcM * kTcK * 2 + B * kTcK * 2) + kTcAux;
-  const int64_t tiles = (a->n_rows + kTcM - 1) / kTcM;
-  const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+  const size_t smem = 1024 + (size_t)p.stages * (kTcTileRows * kTcK * 2 + B * kTcK * 2) + kTcAux;
+  const int64_t units = (a->n_rows + kTcUnit - 1) / kTcUnit;
+  const int grid = (int)(units < sm_count() ? units : sm_count());
   cudaError_t e;
   // the opt-in shared memory size is raised once per kernel to the budget
   const bool layer = a->norm_type == TIDE_NORM_LAYER;
