@@ -99,7 +99,7 @@ def test_operators_have_no_cpu_kernel():
 def test_path_selection():
     """bf16/fp16 with folded weights go to the fused single-pass kernel when
     the router is 128 wide and a weight slice of H stays resident, else to
-    the tensor-core split path (H % 64 == 0, B % 32 == 0); fp32 and other
+    the tensor-core split path (H % 64 == 0, B <= 256); fp32 and other
     shapes to the SIMT path."""
     lib = _native.lib()
 
@@ -116,7 +116,7 @@ def test_path_selection():
     assert sel(path=capi.PATH_TC) == capi.PATH_TC
     assert sel(dtype=capi.DTYPE_F32, folded=None) == capi.PATH_SIMT
     assert sel(hidden_dim=4000) == capi.PATH_SIMT
-    assert sel(bottleneck_dim=48) == capi.PATH_SIMT
+    assert sel(bottleneck_dim=48) == capi.PATH_TC_SPLIT       # units padded to 128
     assert sel(bottleneck_dim=64) == capi.PATH_TC_SPLIT       # fused kernel: 128 units only
     assert sel(hidden_dim=8192, path=capi.PATH_TC) == capi.PATH_TC_SPLIT  # slice too large to stay resident
     assert sel(hidden_dim=768, path=capi.PATH_TC) == capi.PATH_TC   # cluster of 2

@@ -303,6 +303,31 @@ def test_fused_cluster_sizes(H):
         check_against_oracle(ck, res, dtype, kind, 1e-2, out_ref=out0)
 
 
+@pytest.mark.parametrize("B", [1, 48, 100, 128, 160, 256])
+def test_split_router_widths(B):
+    """The tensor-core split router at router widths that are not one full
+    128-unit block (padded units) and at two blocks (B > 128), RMSNorm and
+    LayerNorm, bf16 and fp16, ragged row counts."""
+    H, n = 1024, 2000 + B
+    for kind, dtype in (("rms", torch.bfloat16), ("layer", torch.float16)):
+        w = workloads.rows(n, H, dtype, b=B, seed=500 + B, norm_kind=kind, unit_norm_weight=False)
+        x = w["x"].to(DEV)
+        nw, nb = norm_tensors(w, dtype)
+        dt = TORCH2O[dtype]
+        norm = oracle_norm(kind, nw, nb, 1e-5)
+        z = O.router_logits(O.final_norm(O.to_f32(storage_np(x), dt), norm), w["down"].numpy(),
+                            w["up"].numpy())
+        bias = workloads.bias_for_exit_fraction(z, 0.25, THR)
+        out = torch.zeros_like(x)
+        ck = Checkpoint(x, kind, nw, nb, 1e-5, w["down"].to(DEV), w["up"].to(DEV), bias, THR,
+                        out_buffer=out, path=capi.PATH_TC_SPLIT)
+        assert ck.path() == capi.PATH_TC_SPLIT
+        ck()
+        res = O.checkpoint(storage_np(x), dt, norm, w["down"].numpy(), w["up"].numpy(), bias, THR)
+        res["eps"] = 1e-5
+        check_against_oracle(ck, res, dtype, kind, 1e-2, out_ref=np.zeros_like(storage_np(out)))
+
+
 @pytest.mark.parametrize("path", [capi.PATH_TC, capi.PATH_TC_SPLIT, capi.PATH_SIMT])
 def test_full_size_properties(path):
     """32768 x 4096 bf16 (one 8B-architecture prefill batch): properties that

@@ -7,6 +7,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "move_bulk.cuh"
 #include "simt_kernels.cuh"
 #include "tc_checkpoint.cuh"
 
@@ -86,9 +87,10 @@ template <typename T, bool VEC> struct ScatterLaunch {
   }
 };
 
-// Workspace of the stable partition: ticket (u32, padded) then tile status.
-size_t partition_ws_bytes(int64_t n) {
-  const int64_t tiles = n > 0 ? (n + tide::kMoveTile - 1) / tide::kMoveTile : 1;
+// Workspace of the stable partition: ticket (u32, padded) then one status
+// word per tile of `tile_rows` rows.
+size_t partition_ws_bytes(int64_t n, int64_t tile_rows = tide::kMoveTile) {
+  const int64_t tiles = n > 0 ? (n + tile_rows - 1) / tile_rows : 1;
   return 256 + align_up((size_t)tiles * 8, 256);
 }
 
@@ -100,15 +102,18 @@ struct SimtWs {
   float *scores;
   float2 *stats;
 };
+// The checkpoint's partition area is sized for the bulk mover's smaller
+// tiles, which covers the SIMT mover's too.
 size_t simt_ws_bytes(int64_t n) {
-  return partition_ws_bytes(n) + align_up((size_t)n * 4, 256) + align_up((size_t)n * 8, 256);
+  return partition_ws_bytes(n, tide::bulk_tile_rows()) + align_up((size_t)n * 4, 256) +
+         align_up((size_t)n * 8, 256);
 }
 SimtWs simt_ws(void *ws, int64_t n) {
   SimtWs w;
   char *b = static_cast<char *>(ws);
   w.ticket = reinterpret_cast<uint32_t *>(b);
   w.status = reinterpret_cast<uint64_t *>(b + 256);
-  w.partition_bytes = partition_ws_bytes(n);
+  w.partition_bytes = partition_ws_bytes(n, tide::bulk_tile_rows());
   w.scores = reinterpret_cast<float *>(b + w.partition_bytes);
   w.stats = reinterpret_cast<float2 *>(b + w.partition_bytes + align_up((size_t)n * 4, 256));
   return w;
@@ -326,13 +331,17 @@ int tide_checkpoint(const tide_checkpoint_args *a, tide_stream_t stream) {
   if (path == TIDE_PATH_TC) return tide::fused_checkpoint_launch(a, s, g_err, sizeof(g_err));
 
   SimtWs w = simt_ws(a->workspace, n);
-  if (cudaMemsetAsync(a->workspace, 0, w.partition_bytes, s) != cudaSuccess)
-    return fail(TIDE_ERR_CUDA, "tide_checkpoint: memset failed");
   float *scores = a->scores_out ? a->scores_out : w.scores;
   if (path == TIDE_PATH_TC_SPLIT) {
-    int rc = tide::tc_route_launch(a, scores, w.stats, s, g_err, sizeof(g_err));
+    // the router clears the partition workspace itself
+    int rc = tide::tc_route_launch(a, scores, w.stats, a->workspace, w.partition_bytes, s, g_err,
+                                   sizeof(g_err));
     if (rc != TIDE_OK) return rc;
-  } else if (n > 0) {
+  } else {
+    if (cudaMemsetAsync(a->workspace, 0, w.partition_bytes, s) != cudaSuccess)
+      return fail(TIDE_ERR_CUDA, "tide_checkpoint: memset failed");
+  }
+  if (path != TIDE_PATH_TC_SPLIT && n > 0) {
     if (!a->down_t) return fail(TIDE_ERR_INVALID, "tide_checkpoint: SIMT path needs down_t");
     tide::RouteParams rp{};
     rp.x = a->x; rp.n_cap = n; rp.n_dev = a->n_rows_dev;
@@ -356,6 +365,10 @@ int tide_checkpoint(const tide_checkpoint_args *a, tide_stream_t stream) {
   mp.counts = a->counts_out;
   mp.ticket = w.ticket; mp.status = w.status; mp.err = a->error_word;
   const bool vec = rows_vectorizable(a->dtype, a->hidden_dim, {a->x, a->out_buffer, a->compact_out});
+  if (tide::bulk_move_supported(a->dtype, a->hidden_dim, vec, mp)) {
+    if (tide::bulk_move_launch(a->dtype, mp, s) != TIDE_OK) return check_launch("tide_checkpoint(bulk move)");
+    return check_launch("tide_checkpoint(bulk move)");
+  }
   const int64_t grid = n > 0 ? (n + tide::kMoveTile - 1) / tide::kMoveTile : 1;
   dispatch_rows<MoveLaunch>(a->dtype, vec, mp, grid, s);
   return check_launch("tide_checkpoint(move)");

@@ -9,22 +9,33 @@
 // memory tiles.  Reference semantics: python/TIDE/runtime.py:128-130 and
 // python/TIDE/router.py:18-19.
 //
+// The product is taken transposed, D[unit][row] = W'[unit] . x[row], so one
+// tcgen05.mma covers M = 128 units x N = 256 rows: half the instructions of
+// row-major M = 128 tiles and fewer shared-memory operand bytes per FLOP.
+//
 // Persistent CTAs, one per SM.  The rows are cut into 32-row units and each
 // CTA takes a contiguous, balanced range of units (so no SM does a whole
 // extra tile), walked in tiles of up to 256 rows.  Per CTA:
-//   warp 0      TMA producer: per pipeline stage, one [32 rows x 64 cols]
-//               box per unit of the tile plus the W' chunk [B x 64]
-//               (128-byte swizzle); the W' chunk is shared by both halves;
-//   warp 1      TMEM owner and MMA issuer: per stage and 128-row half,
-//               4 x tcgen05.mma (K = 16) into that half's fp32 accumulator
-//               of B columns (double-buffered across tiles when TMEM holds
-//               four);
-//   warps 4-11  row statistics from the x chunks (one thread per row),
+//   warp 0      TMA producer: per pipeline stage the tile's x chunk
+//               [rows x 64 cols] (128-row boxes, 32-row boxes for a ragged
+//               tail) plus the W' chunk [128 units x 64] (128-byte swizzle);
+//   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K = 16) per
+//               stage and 128-unit block into an fp32 accumulator of 256
+//               columns (double-buffered across tiles when TMEM holds two);
+//   warps 4-7   row statistics from the x chunks (two rows per thread),
 //               handed to the epilogue per tile through a double-buffered
 //               shared-memory slot;
-//   warps 12-15 the epilogue: tcgen05.ld of the accumulator rows, SiLU, up
-//               projection, sigmoid; writes the score and (mean, rstd).  It
-//               runs beside the statistics so the ring never waits for it.
+//   warps 8-15  the epilogue, two groups of four warps, one per half of the
+//               tile's rows: warp 8+4g+q reads units 32q..32q+31 of its rows
+//               (tcgen05.ld), applies the norm scale and SiLU, weights by
+//               up[unit], sums the 32 units of each row with a butterfly of
+//               shuffles, then the four quarter warps' partial sums per row
+//               meet in shared memory; writes the score and (mean, rstd).
+// Launched as a programmatic dependent: barriers, TMEM and the tensor-map
+// prefetch are set up before griddepcontrol.wait, so they overlap the end of
+// the previous kernel; nothing global is read or written before it.  The
+// producer starts loading right after it; the other warps fetch the per-unit
+// vectors and clear the mover's workspace meanwhile (no separate memset).
 // The survivors/exits are then moved by the stable-partition kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -36,15 +47,16 @@
 
 namespace tide {
 
-constexpr int kTcM = 128;         // rows per MMA half (TMEM lanes)
-constexpr int kTcUnit = 32;       // rows per TMA box / scheduling unit
-constexpr int kTcTileUnits = 8;   // units per tile: two 128-row halves
-constexpr int kTcTileRows = kTcUnit * kTcTileUnits;
+constexpr int kTcM = 128;         // router units per MMA (TMEM lanes)
+constexpr int kTcUnit = 32;       // rows per scheduling unit / small TMA box
+constexpr int kTcBigBox = 128;    // rows per large TMA box
+constexpr int kTcTileUnits = 8;   // units per tile
+constexpr int kTcTileRows = kTcUnit * kTcTileUnits;  // MMA N
 constexpr int kTcK = 64;          // columns per chunk: 128 bytes of 16-bit data
-constexpr int kTcThreads = 512;  // warps 0-1 TMA/MMA, 4-11 statistics, 12-15 epilogue
+constexpr int kTcThreads = 512;  // warps 0-1 TMA/MMA, 4-7 statistics, 8-15 epilogue
 constexpr int kTcMaxStages = 8;
 constexpr int kTcSmemBudget = 227 * 1024;
-constexpr int kTcAux = 8192;      // barriers, flags, per-unit vectors, row statistics
+constexpr int kTcAux = 12288;     // barriers, flags, per-unit vectors, row statistics, partials
 
 struct TcRouteParams {
   int64_t n_cap;
@@ -56,8 +68,12 @@ struct TcRouteParams {
   float2 *row_stats;
   int32_t *err;
   int stages;
-  int n_acc;  // accumulator sets in TMEM (2: double-buffered across tiles)
+  int a_tiles;   // 128-unit blocks of W' (1 for B <= 128, else 2)
+  int w_rows;    // rows of one W' box: min(B, 128)
+  int n_acc;     // accumulator sets in TMEM (2: double-buffered across tiles)
   uint32_t tmem_cols;
+  uint4 *zero;        // stable-partition workspace the mover expects zeroed
+  int64_t zero_vec;   // its size in 16-byte words
 };
 
 __device__ __forceinline__ void unpack8_16(const uint4 &v, float *f, bool bf16) {
@@ -76,19 +92,38 @@ __device__ __forceinline__ void unpack8_16(const uint4 &v, float *f, bool bf16) 
   }
 }
 
+// Sum of v[0..31] over the 32 lanes of the warp, transposed: lane j returns
+// sum over lanes of v[j] (a butterfly that halves the vector at each step,
+// 31 shuffles in all).
+__device__ __forceinline__ float transpose_sum32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? v[i] : v[i + off];
+      const float keep = upper ? v[i + off] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
+}
+
 template <bool BF16, bool LAYER>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_route_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                    const __grid_constant__ CUtensorMap tmap_x_big,
                     const __grid_constant__ CUtensorMap tmap_w, TcRouteParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = p.stages, B = p.B, NA = p.n_acc;
+  const int S = p.stages, NA = p.n_acc, AT = p.a_tiles;
   const uint32_t unit_bytes = kTcUnit * kTcK * 2;
-  const uint32_t a_bytes = kTcTileRows * kTcK * 2;
-  const uint32_t b_bytes = (uint32_t)B * kTcK * 2;
-  const uint32_t stage_bytes = a_bytes + b_bytes;
+  const uint32_t x_bytes = kTcTileRows * kTcK * 2;  // B operand: 256 rows
+  const uint32_t w_tile_bytes = kTcM * kTcK * 2;    // A operand: 128 units
+  const uint32_t stage_bytes = x_bytes + (uint32_t)AT * w_tile_bytes;
+  const uint32_t w_load_bytes = (uint32_t)AT * (uint32_t)p.w_rows * kTcK * 2;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * stage_bytes);
   uint64_t *empty = full + S;
   uint64_t *acc_full = empty + S;      // [2] accumulator set written
@@ -99,10 +134,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   uint32_t *issued = reinterpret_cast<uint32_t *>(tmem_slot + 2);
-  float *s_up = reinterpret_cast<float *>(tmem_slot + 4);
+  float *s_up = reinterpret_cast<float *>(tmem_slot + 4);  // [256], 0 beyond B
   float *s_cs = s_up + 256;
   float *s_bp = s_cs + 256;
   float *s_stat = s_bp + 256;  // [2 slots][256 rows][ss, sx]
+  float *s_part = s_stat + 2 * kTcTileRows * 2;  // [4 warps][256 rows]
+  volatile int *s_vote = reinterpret_cast<volatile int *>(s_part + 4 * kTcTileRows);  // [8]
+
+  const int k_chunks = p.H / kTcK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 statistics warps
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&acc_full[a], 1);
+      ptx::mbar_init(&acc_empty[a], 8);   // 8 epilogue warps
+      ptx::mbar_init(&stat_full[a], 4);   // 4 statistics warps
+      ptx::mbar_init(&stat_empty[a], 8);  // 8 epilogue warps
+    }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    *issued = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmap_x);
+    ptx::prefetch_tmap(&tmap_x_big);
+    ptx::prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, p.tmem_cols);
+    ptx::tmem_relinquish();
+  }
+  __syncthreads();
+  ptx::grid_dependency_wait();
+  if (threadIdx.x == 0) ptx::grid_dependents_launch();
 
   int64_t n = p.n_cap;
   if (p.n_dev) {
@@ -113,47 +181,48 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int64_t units = (n + kTcUnit - 1) / kTcUnit;
   const int64_t u_begin = (int64_t)blockIdx.x * units / gridDim.x;
   const int64_t u_end = ((int64_t)blockIdx.x + 1) * units / gridDim.x;
-  const int k_chunks = p.H / kTcK;
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], 1 + 8);  // MMA commit + 8 statistics warps
+  uint32_t tmem_base = 0;
+  if (warp != 0) {
+    // warps 1-15, while the producer already streams: per-unit vectors,
+    // this CTA's slice of the mover's workspace, zero padding of W' past B
+    const int t1 = threadIdx.x - 32;
+    if (p.zero) {
+      const int64_t per = (p.zero_vec + gridDim.x - 1) / gridDim.x;
+      const int64_t z0 = (int64_t)blockIdx.x * per;
+      const int64_t z1 = z0 + per < p.zero_vec ? z0 + per : p.zero_vec;
+      for (int64_t i = z0 + t1; i < z1; i += kTcThreads - 32) p.zero[i] = make_uint4(0, 0, 0, 0);
     }
-    for (int a = 0; a < 2; ++a) {
-      ptx::mbar_init(&acc_full[a], 1);
-      ptx::mbar_init(&acc_empty[a], 4);   // 4 epilogue warps
-      ptx::mbar_init(&stat_full[a], 8);   // 8 statistics warps
-      ptx::mbar_init(&stat_empty[a], 4);  // 4 epilogue warps
+    for (int i = t1; i < 256; i += kTcThreads - 32) {
+      const bool in = i < p.B;
+      s_up[i] = in ? p.up[i] : 0.f;
+      s_cs[i] = in && p.colsum ? p.colsum[i] : 0.f;
+      s_bp[i] = in && p.bias_proj ? p.bias_proj[i] : 0.f;
     }
-    ptx::mbar_init(drain, 1);
-    *abort_flag = 0;
-    *issued = 0;
-    ptx::fence_mbar_init();
-    ptx::fence_proxy_async();
+    if (p.w_rows < kTcM) {
+      // W' rows past B are never loaded: zero them once in every stage so
+      // the padded units contribute exactly 0 (the loads write other rows)
+      for (int s = 0; s < S; ++s) {
+        uint4 *w = reinterpret_cast<uint4 *>(smem + (size_t)s * stage_bytes + x_bytes +
+                                             (size_t)p.w_rows * 128);
+        const int n16 = (kTcM - p.w_rows) * 128 / 16;
+        for (int i = t1; i < n16; i += kTcThreads - 32) w[i] = make_uint4(0, 0, 0, 0);
+      }
+      ptx::fence_proxy_async();
+    }
+    ptx::tc_fence_before();
+    ptx::named_sync(2, kTcThreads - 32);
+    ptx::tc_fence_after();
+    tmem_base = *tmem_slot;
   }
-  for (int i = threadIdx.x; i < B; i += kTcThreads) {
-    s_up[i] = p.up[i];
-    s_cs[i] = p.colsum ? p.colsum[i] : 0.f;
-    s_bp[i] = p.bias_proj ? p.bias_proj[i] : 0.f;
-  }
-  if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, p.tmem_cols);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
-      ptx::prefetch_tmap(&tmap_x);
-      ptx::prefetch_tmap(&tmap_w);
       uint32_t it = 0;
       for (int64_t u0 = u_begin; u0 < u_end && !*abort_flag; u0 += kTcTileUnits) {
         const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
+        const int n_big = nu / (kTcBigBox / kTcUnit);
         for (int kc = 0; kc < k_chunks; ++kc, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
           if (it >= (uint32_t)S && !ptx::mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
@@ -162,9 +231,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             break;
           }
           uint8_t *st = smem + (size_t)s * stage_bytes;
-          ptx::mbar_expect_tx(&full[s], (uint32_t)nu * unit_bytes + b_bytes);
-          ptx::tma_load_2d(st + a_bytes, &tmap_w, &full[s], kc * kTcK, 0);
-          for (int j = 0; j < nu; ++j)
+          ptx::mbar_expect_tx(&full[s], (uint32_t)nu * unit_bytes + w_load_bytes);
+          for (int a = 0; a < AT; ++a)
+            ptx::tma_load_2d(st + x_bytes + (size_t)a * w_tile_bytes, &tmap_w, &full[s], kc * kTcK,
+                             a * kTcM);
+          for (int j = 0; j < n_big; ++j)
+            ptx::tma_load_2d(st + (size_t)j * (kTcBigBox / kTcUnit) * unit_bytes, &tmap_x_big,
+                             &full[s], kc * kTcK, (int)((u0 + j * (kTcBigBox / kTcUnit)) * kTcUnit));
+          for (int j = n_big * (kTcBigBox / kTcUnit); j < nu; ++j)
             ptx::tma_load_2d(st + (size_t)j * unit_bytes, &tmap_x, &full[s], kc * kTcK,
                              (int)((u0 + j) * kTcUnit));
           *issued = it + 1;
@@ -174,14 +248,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = ptx::f16_idesc(BF16, kTcM, B);
+      const uint32_t idesc = ptx::f16_idesc(BF16, kTcM, kTcTileRows);
       uint32_t it = 0;
       int t_local = 0;
       bool ok = true;
       for (int64_t u0 = u_begin; u0 < u_end && ok && !*abort_flag;
            u0 += kTcTileUnits, ++t_local) {
-        const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
-        const int halves = nu > kTcTileUnits / 2 ? 2 : 1;
         const int acc = t_local % NA;
         const uint32_t acc_ph = (uint32_t)(t_local / NA) & 1u;
         if (t_local >= NA && !ptx::mbar_wait(&acc_empty[acc], acc_ph ^ 1u, abort_flag)) {
@@ -189,19 +261,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 2 * B);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * AT * kTcTileRows);
         for (int kc = 0; kc < k_chunks; ++kc, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
           if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
-          const uint32_t a0 = ptx::smem_u32(smem + (size_t)s * stage_bytes);
-          const uint32_t b0 = a0 + a_bytes;
-          for (int h = 0; h < halves; ++h) {
+          const uint32_t xs = ptx::smem_u32(smem + (size_t)s * stage_bytes);
+          const uint32_t ws = xs + x_bytes;
+          for (int a = 0; a < AT; ++a) {
 #pragma unroll
             for (int k = 0; k < kTcK / 16; ++k) {
-              ptx::mma_f16_ss(d_tmem + (uint32_t)(h * B),
-                              ptx::sw128_kmajor_desc(a0 + (uint32_t)h * (kTcM * 128) + 32u * k),
-                              ptx::sw128_kmajor_desc(b0 + 32u * k), idesc,
+              ptx::mma_f16_ss(d_tmem + (uint32_t)(a * kTcTileRows),
+                              ptx::sw128_kmajor_desc(ws + (uint32_t)a * w_tile_bytes + 32u * k),
+                              ptx::sw128_kmajor_desc(xs + 32u * k), idesc,
                               (kc > 0 || k > 0) ? 1u : 0u);
             }
           }
@@ -219,24 +291,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       volatile int never = 0;
       if (!ptx::mbar_wait(drain, 0, &never)) raise_error(p.err, TIDE_DEVERR_TIMEOUT);
     }
-  } else if (warp >= 4 && warp < 12) {
+  } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------- row statistics
-    // thread t of warps 4-11 owns row t of the tile and reads all eight
-    // 16-byte units of its chunk row, lane-rotated so a warp's reads of the
-    // swizzled tile hit distinct banks (the sum is order-free within a row).
+    // thread t of warps 4-7 owns rows t and t + 128 of the tile and reads all
+    // eight 16-byte units of each chunk row, lane-rotated so a warp's reads
+    // of the swizzled tile hit distinct banks (the sum is order-free within
+    // a row).
     const int t = threadIdx.x - 128;
     uint32_t it = 0;
     int t_local = 0;
     bool ok = true;
     for (int64_t u0 = u_begin; u0 < u_end && ok; u0 += kTcTileUnits, ++t_local) {
       const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
-      const bool live = (t >> 5) < nu;  // warp-uniform: a unit is one warp
-      float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
+      float ss[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, sx[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
       for (int kc = 0; kc < k_chunks; ++kc, ++it) {
         const uint32_t s = it % S, ph = (it / S) & 1u;
         if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
-        if (live) {
-          const uint8_t *row = smem + (size_t)s * stage_bytes + (size_t)t * 128;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = t + h * 128;
+          if ((r >> 5) >= nu) continue;  // warp-uniform: a unit is one warp
+          const uint8_t *row = smem + (size_t)s * stage_bytes + (size_t)r * 128;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int unit = (j + lane) & 7;
@@ -245,9 +320,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             unpack8_16(v, f, BF16);
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
-              ss0 = fmaf(f[e], f[e], ss0);
-              ss1 = fmaf(f[e + 1], f[e + 1], ss1);
-              if (LAYER) { sx0 += f[e]; sx1 += f[e + 1]; }
+              ss[h][0] = fmaf(f[e], f[e], ss[h][0]);
+              ss[h][1] = fmaf(f[e + 1], f[e + 1], ss[h][1]);
+              if (LAYER) { sx[h][0] += f[e]; sx[h][1] += f[e + 1]; }
             }
           }
         }
@@ -261,9 +336,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ok = false;
         break;
       }
-      float *st = s_stat + ((size_t)buf * kTcTileRows + t) * 2;
-      st[0] = ss0 + ss1;
-      st[1] = sx0 + sx1;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float *st = s_stat + ((size_t)buf * kTcTileRows + t + h * 128) * 2;
+        const float ssum = ss[h][0] + ss[h][1], xsum = sx[h][0] + sx[h][1];
+        if (!LAYER) {
+          st[0] = rsqrt_rn(ssum / (float)p.H + p.eps);
+          st[1] = 0.f;
+        } else {
+          const float mean = xsum / (float)p.H;
+          const float var = fmaxf(ssum / (float)p.H - mean * mean, 0.f);
+          st[0] = rsqrt_rn(var + p.eps);
+          st[1] = mean;
+        }
+      }
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&stat_full[buf]);
     }
@@ -271,71 +357,77 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       raise_error(p.err, TIDE_DEVERR_TIMEOUT);
       *abort_flag = 1;
     }
-  } else if (warp >= 12) {
+  } else if (warp >= 8) {
     // ----------------------------------------------------------- epilogue
-    // warp 12 + q reads TMEM lanes 32q..32q+31: rows 32q + lane of each half
+    // warp 8 + 4g + q reads TMEM lanes 32q..32q+31 (units a*128 + 32q + lane)
+    // of the rows in chunks 4g..4g+3 (rows 128g..128g+127) of the tile
     const int q = warp & 3;
-    const int r = q * 32 + lane;
+    const int g = (warp - 8) >> 2;
+    const int et = threadIdx.x - 256;  // 0..255
     int t_local = 0;
     bool ok = true;
     for (int64_t u0 = u_begin; u0 < u_end && ok; u0 += kTcTileUnits, ++t_local) {
       const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
-      const int halves = nu > kTcTileUnits / 2 ? 2 : 1;
       const int buf = t_local & 1;
-      if (!ptx::mbar_wait(&stat_full[buf], (uint32_t)(t_local >> 1) & 1u, abort_flag)) {
-        ok = false;
-        break;
-      }
-      float mean[2], rstd[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const float *st = s_stat + ((size_t)buf * kTcTileRows + h * kTcM + r) * 2;
-        const float ss = st[0], sx = st[1];
-        if (!LAYER) {
-          mean[h] = 0.f;
-          rstd[h] = rsqrt_rn(ss / (float)p.H + p.eps);
-        } else {
-          mean[h] = sx / (float)p.H;
-          const float var = fmaxf(ss / (float)p.H - mean[h] * mean[h], 0.f);
-          rstd[h] = rsqrt_rn(var + p.eps);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&stat_empty[buf]);
       const int acc = t_local % NA;
-      if (!ptx::mbar_wait(&acc_full[acc], (uint32_t)(t_local / NA) & 1u, abort_flag)) {
-        ok = false;
-        break;
-      }
+      bool got = ptx::mbar_wait(&stat_full[buf], (uint32_t)(t_local >> 1) & 1u, abort_flag) &&
+                 ptx::mbar_wait(&acc_full[acc], (uint32_t)(t_local / NA) & 1u, abort_flag);
+      // the four epilogue warps vote and leave together, so each named
+      // barrier below is reached by all of them or by none
+      got = __all_sync(0xffffffffu, got);
+      if (lane == 0) s_vote[warp - 8] = got ? 1 : 0;
+      ptx::named_sync(1, 256);
+      bool all = true;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) all = all && s_vote[w] != 0;
+      if (!all) { ok = false; break; }
       ptx::tc_fence_after();
-      const int64_t row_lim_tile = (u0 + nu) * kTcUnit;
-      const int64_t row_lim = row_lim_tile < n ? row_lim_tile : n;
-      for (int h = 0; h < halves; ++h) {
-        float logit = p.up_bias;
-        const uint32_t row_addr =
-            tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 2 * B + h * B);
-        for (int c = 0; c < B; c += 32) {
+      const float *st = s_stat + (size_t)buf * kTcTileRows * 2;
+      float part[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int a = 0; a < AT; ++a) {
+        const int u = a * kTcM + q * 32 + lane;
+        const float up = s_up[u], cs = s_cs[u], bp = s_bp[u];
+        const uint32_t base = tmem_base + ((uint32_t)(q * 32) << 16) +
+                              (uint32_t)((acc * AT + a) * kTcTileRows);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = g * 4 + cc;
+          if (c >= nu) break;  // warp-uniform
           float v[32];
-          ptx::tmem_ld32(row_addr + (uint32_t)c, v);
+          ptx::tmem_ld32(base + (uint32_t)(c * 32), v);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
+            const float rstd = st[(c * 32 + j) * 2];
             float z;
             if (!LAYER)
-              z = rstd[h] * v[j];
+              z = rstd * v[j];
             else
-              z = fmaf(rstd[h], v[j] - mean[h] * s_cs[c + j], s_bp[c + j]);
-            logit = fmaf(s_up[c + j], silu_fast(z), logit);
+              z = fmaf(rstd, v[j] - st[(c * 32 + j) * 2 + 1] * cs, bp);
+            v[j] = up * silu_fast(z);
           }
-        }
-        const int64_t grow = u0 * kTcUnit + h * kTcM + r;
-        if (grow < row_lim) {
-          p.scores[grow] = sigmoid_f(logit);
-          if (p.row_stats) p.row_stats[grow] = make_float2(mean[h], rstd[h]);
+          part[cc] += transpose_sum32(v, lane);
         }
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&acc_empty[acc]);
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        if (g * 4 + cc < nu) s_part[q * kTcTileRows + (g * 4 + cc) * 32 + lane] = part[cc];
+      ptx::named_sync(1, 256);
+      const int64_t row_lim_tile = (u0 + nu) * kTcUnit;
+      const int64_t row_lim = row_lim_tile < n ? row_lim_tile : n;
+      for (int r = et; r < nu * kTcUnit; r += 256) {
+        const float logit = p.up_bias + ((s_part[r] + s_part[kTcTileRows + r]) +
+                                         (s_part[2 * kTcTileRows + r] + s_part[3 * kTcTileRows + r]));
+        const int64_t grow = u0 * kTcUnit + r;
+        if (grow < row_lim) {
+          p.scores[grow] = sigmoid_f(logit);
+          if (p.row_stats) p.row_stats[grow] = make_float2(st[r * 2 + 1], st[r * 2]);
+        }
+      }
+      ptx::named_sync(1, 256);  // s_part and the statistics slot are free again
+      if (lane == 0) ptx::mbar_arrive(&stat_empty[buf]);
     }
     if (!ok) {
       raise_error(p.err, TIDE_DEVERR_TIMEOUT);
@@ -392,18 +484,13 @@ bool make_tmap(CUtensorMap *m, const void *base, bool bf16, uint64_t rows, uint6
   return r == CUDA_SUCCESS;
 }
 
-// Two 128-row halves of B columns per accumulator set; two sets when TMEM's
-// 512 columns hold them (B <= 128).
-int n_acc_for(int B) { return 4 * B <= 512 ? 2 : 1; }
-
-uint32_t tmem_cols_for(int B) {
-  uint32_t need = (uint32_t)(n_acc_for(B) * 2 * B), c = 32;
-  while (c < need) c <<= 1;
-  return c;
-}
+// 128-unit blocks of W' (the MMA's M), each with a 256-column accumulator;
+// two accumulator sets in TMEM's 512 columns when one block covers B.
+int a_tiles_for(int B) { return B <= kTcM ? 1 : 2; }
+int n_acc_for(int B) { return a_tiles_for(B) == 1 ? 2 : 1; }
 
 int stages_for(int B) {
-  const int stage = kTcTileRows * kTcK * 2 + B * kTcK * 2;
+  const int stage = kTcTileRows * kTcK * 2 + a_tiles_for(B) * kTcM * kTcK * 2;
   int s = (kTcSmemBudget - 1024 - kTcAux) / stage;
   return s > kTcMaxStages ? kTcMaxStages : s;
 }
@@ -425,7 +512,7 @@ const char *tc_unsupported_reason(const tide_checkpoint_args *a) {
   if (a->dtype != TIDE_DTYPE_BF16 && a->dtype != TIDE_DTYPE_F16) return "dtype is not bf16/fp16";
   if (!a->folded) return "no folded router weights";
   if (a->hidden_dim % kTcK != 0) return "hidden_dim is not a multiple of 64";
-  if (a->bottleneck_dim % 32 != 0 || a->bottleneck_dim > 256) return "bottleneck_dim not in {32,...,256}";
+  if (a->bottleneck_dim < 1 || a->bottleneck_dim > 256) return "bottleneck_dim not in [1, 256]";
   if (a->norm_type == TIDE_NORM_LAYER && !a->colsum) return "LayerNorm needs colsum";
   if (a->n_rows < 1) return "no rows";
   if (((uintptr_t)a->x & 15u) || ((uintptr_t)a->folded & 15u)) return "x/folded not 16-byte aligned";
@@ -438,12 +525,15 @@ bool tc_supported(const tide_checkpoint_args *a) { return tc_unsupported_reason(
 size_t tc_workspace_bytes(int64_t) { return 0; }
 
 int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_stats,
-                    cudaStream_t stream, char *err, size_t err_len) {
+                    void *zero, size_t zero_bytes, cudaStream_t stream, char *err,
+                    size_t err_len) {
   const bool bf16 = a->dtype == TIDE_DTYPE_BF16;
   const int B = (int)a->bottleneck_dim;
-  CUtensorMap tx, tw;
+  const int w_rows = B < kTcM ? B : kTcM;
+  CUtensorMap tx, txb, tw;
   if (!make_tmap(&tx, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcUnit) ||
-      !make_tmap(&tw, a->folded, bf16, (uint64_t)B, (uint64_t)a->hidden_dim, (uint32_t)B)) {
+      !make_tmap(&txb, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcBigBox) ||
+      !make_tmap(&tw, a->folded, bf16, (uint64_t)B, (uint64_t)a->hidden_dim, (uint32_t)w_rows)) {
     snprintf(err, err_len, "tensor-core route: cuTensorMapEncodeTiled failed");
     return TIDE_ERR_CUDA;
   }
@@ -462,9 +552,14 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   p.row_stats = row_stats;
   p.err = a->error_word;
   p.stages = stages_for(B);
+  p.a_tiles = a_tiles_for(B);
+  p.w_rows = w_rows;
   p.n_acc = n_acc_for(B);
-  p.tmem_cols = tmem_cols_for(B);
-  const size_t smem = 1024 + (size_t)p.stages * (kTcTileRows * kTcK * 2 + B * kTcK * 2) + kTcAux;
+  p.tmem_cols = 512;
+  p.zero = static_cast<uint4 *>(zero);
+  p.zero_vec = (int64_t)(zero_bytes / 16);
+  const size_t smem =
+      1024 + (size_t)p.stages * (kTcTileRows * kTcK * 2 + p.a_tiles * kTcM * kTcK * 2) + kTcAux;
   const int64_t units = (a->n_rows + kTcUnit - 1) / kTcUnit;
   const int grid = (int)(units < sm_count() ? units : sm_count());
   cudaError_t e;
@@ -472,22 +567,38 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   const bool layer = a->norm_type == TIDE_NORM_LAYER;
   const void *fn = bf16 ? (layer ? (const void *)tc_route_kernel<true, true> : (const void *)tc_route_kernel<true, false>)
                         : (layer ? (const void *)tc_route_kernel<false, true> : (const void *)tc_route_kernel<false, false>);
-  static bool attr_set[4] = {false, false, false, false};
+  static bool attr_set[64][4] = {};
   const int which = (bf16 ? 2 : 0) + (layer ? 1 : 0);
-  if (!attr_set[which]) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev][which]) {
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBudget);
     if (e != cudaSuccess) {
       snprintf(err, err_len, "tensor-core route: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return TIDE_ERR_CUDA;
     }
-    attr_set[which] = true;
+    if (dev >= 0 && dev < 64) attr_set[dev][which] = true;
   }
-  if (bf16) {
-    if (layer) tc_route_kernel<true, true><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
-    else tc_route_kernel<true, false><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
-  } else {
-    if (layer) tc_route_kernel<false, true><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
-    else tc_route_kernel<false, false><<<grid, kTcThreads, smem, stream>>>(tx, tw, p);
+  // programmatic dependent launch: the prologue overlaps the previous kernel
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (bf16)
+    e = layer ? cudaLaunchKernelEx(&cfg, tc_route_kernel<true, true>, tx, txb, tw, p)
+              : cudaLaunchKernelEx(&cfg, tc_route_kernel<true, false>, tx, txb, tw, p);
+  else
+    e = layer ? cudaLaunchKernelEx(&cfg, tc_route_kernel<false, true>, tx, txb, tw, p)
+              : cudaLaunchKernelEx(&cfg, tc_route_kernel<false, false>, tx, txb, tw, p);
+  if (e != cudaSuccess) {
+    snprintf(err, err_len, "tensor-core route launch: %s", cudaGetErrorString(e));
+    return TIDE_ERR_CUDA;
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) {

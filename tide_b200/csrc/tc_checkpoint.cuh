@@ -10,9 +10,11 @@ namespace tide {
 bool tc_supported(const tide_checkpoint_args *a);
 const char *tc_unsupported_reason(const tide_checkpoint_args *a);
 size_t tc_workspace_bytes(int64_t n_rows);
-// Scores and per-row (mean, rstd) of the active rows on the tensor cores.
-int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_stats,
-                    cudaStream_t s, char *err, size_t err_len);
+// Scores and per-row (mean, rstd) of the active rows on the tensor cores;
+// also clears `zero` (zero_bytes, a multiple of 16), the stable-partition
+// workspace of the mover launched after it.
+int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_stats, void *zero,
+                    size_t zero_bytes, cudaStream_t s, char *err, size_t err_len);
 
 // Single-pass fused cluster kernel (tc_fused.cu).
 bool fused_supported(const tide_checkpoint_args *a);
