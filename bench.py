@@ -194,21 +194,25 @@ class Workload:
         for k in range(len(LAYERS)):
             self.checkpoint(k, xs)
 
-    def capture(self, xs=None):
-        """One CUDA graph per checkpoint (its memset and kernels), so a step is
-        six graph launches and the host never throttles the device."""
-        graphs = []
+    def capture(self, xs=None, per_checkpoint: bool = False):
+        """CUDA graphs of the sweep: one graph for the whole step (its kernels
+        overlap their neighbours' prologues through programmatic dependent
+        launch, kernel to kernel), or one graph per checkpoint.  The graphs
+        hold kernels only; timing events and host copies stay outside."""
+        out = []
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
-            for k in range(len(LAYERS)):
+            groups = [[k] for k in range(len(LAYERS))] if per_checkpoint else [list(range(len(LAYERS)))]
+            for ks in groups:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=s):
-                    self.checkpoint(k, xs)
-                graphs.append(g)
+                    for k in ks:
+                        self.checkpoint(k, xs)
+                out.append(g)
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
-        return graphs
+        return out
 
 
 def launches_per_checkpoint(path_used: int) -> int:
@@ -309,27 +313,38 @@ def main():
     active = (counts[:, 0] + counts[:, 1]).tolist()
     wl.runner.check_errors()
 
-    graphs = wl.capture()
+    step_graph = wl.capture()[0]
+    ck_graphs = wl.capture(per_checkpoint=True)
     for _ in range(2):
-        for g in graphs:
+        step_graph.replay()
+        for g in ck_graphs:
             g.replay()
     torch.cuda.synchronize()
 
-    # timed region: device-resident inputs; each checkpoint is one graph
-    # launch bracketed by CUDA events on the launching (current) stream
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in LAYERS] for _ in range(args.steps)]
+    # timed region: device-resident inputs, one graph launch per step on the
+    # current stream, CUDA events before the first and after the last
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
-        for i in range(args.steps):
-            for k, g in enumerate(graphs):
+        t_start.record()
+        for _ in range(args.steps):
+            step_graph.replay()
+        t_end.record()
+        torch.cuda.synchronize()
+        # per-launch device time of each checkpoint's kernels (the roofline's
+        # denominator): its own graph, CUDA events around every replay
+        reps = max(3, min(args.steps, 50))
+        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in LAYERS] for _ in range(reps)]
+        for i in range(reps):
+            for k, g in enumerate(ck_graphs):
                 ev[i][k][0].record()
                 g.replay()
                 ev[i][k][1].record()
         torch.cuda.synchronize()
-    elapsed = ev[0][0][0].elapsed_time(ev[-1][-1][1]) / 1000.0
-    per_ck = [sum(ev[i][k][0].elapsed_time(ev[i][k][1]) for i in range(args.steps)) / args.steps
+    elapsed = t_start.elapsed_time(t_end) / 1000.0
+    per_ck = [sum(ev[i][k][0].elapsed_time(ev[i][k][1]) for i in range(reps)) / reps
               for k in range(len(LAYERS))]
     del ev
     barrier(world)
@@ -342,7 +357,7 @@ def main():
     e = 2
     alg = [algorithmic_bytes(active[k], exits_per_stage[k], HIDDEN, e) for k in range(len(LAYERS))]
     achieved = alg[0] / (per_ck[0] / 1000.0) / 1e9  # the first (largest) checkpoint
-    achieved_all = sum(alg) / (sum(per_ck) / 1000.0) / 1e9
+    achieved_all = sum(alg) / (elapsed / args.steps) / 1e9
     peaks = {}
     try:
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -353,15 +368,16 @@ def main():
                 "frac": achieved / peak, "traffic": None,
                 "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
                 "kernel": "checkpoint 0 (32768 rows), every kernel of the call",
-                "achieved_all_checkpoints": achieved_all,
-                "per_checkpoint_ms": per_ck, "algorithmic_bytes_per_step": sum(alg)}
+                "per_checkpoint_ms": per_ck, "per_checkpoint_reps": reps,
+                "achieved_all_checkpoints": achieved_all, "algorithmic_bytes_per_step": sum(alg)}
 
     # e2e through the public operator with host buffers: H2D of the step's
     # hidden states from pinned memory, the checkpoint graphs, D2H of counts
     host_x = [x.cpu().pin_memory() for x in wl.x]
     dev_x = [torch.empty_like(x) for x in wl.x]
-    e_graphs = wl.capture(dev_x)
     host_counts = torch.empty_like(wl.counts, device="cpu").pin_memory()
+
+    e_graph = wl.capture(dev_x)[0]
     barrier(world)
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -369,8 +385,7 @@ def main():
     for _ in range(args.e2e_steps):
         for k in range(len(LAYERS)):
             dev_x[k].copy_(host_x[k], non_blocking=True)
-        for g in e_graphs:
-            g.replay()
+        e_graph.replay()
         host_counts.copy_(wl.counts, non_blocking=True)
     e_end.record()
     torch.cuda.synchronize()
@@ -378,7 +393,7 @@ def main():
     e2e = {"value": world * rows_per_step * args.e2e_steps / e_el, "unit": "tokens/s",
            "h2d_bytes_per_step": int(sum(x.numel() * x.element_size() for x in host_x)),
            "d2h_bytes_per_step": int(host_counts.numel() * 4), "steps": args.e2e_steps}
-    del e_graphs, graphs
+    del e_graph, step_graph, ck_graphs
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
