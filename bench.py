@@ -42,6 +42,12 @@ ROWS, HIDDEN, BOTTLENECK = 16 * 2048, 4096, 128
 WORKLOAD = "llama8b_prefill_checkpoints"
 
 
+# DRAM bytes (read + write) of checkpoint 0's two kernels (router + mover),
+# 32768 rows x 4096 bf16, from the warm-cache ncu launch list of this
+# benchmark (profiles/launches__llama8b_prefill_checkpoints.md).
+NCU_TRAFFIC_CKPT0 = {"rows": 32768, "path": "tc_split", "bytes": (269.5 + 61.7 + 218.7 + 208.8) * 1e6}
+
+
 def algorithmic_bytes(n: int, exits: int, h: int, e: int) -> int:
     """Bytes a single pass must move for one checkpoint of n rows: read every
     row and write it once (survivor to the dense buffer, exit to its
@@ -108,37 +114,21 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- setup
 def dist_setup(n_gpus: int):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
+    from tide_b200 import dist as tdist
 
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
-    return world, rank, local
+    return tdist.init("nccl" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else None)
 
 
 def barrier(world):
-    if world > 1:
-        import torch.distributed as dist
+    from tide_b200 import dist as tdist
 
-        dist.barrier()
+    tdist.barrier(world)
 
 
 def max_over_ranks(world, v: float) -> float:
-    if world == 1:
-        return v
-    import torch.distributed as dist
+    from tide_b200 import dist as tdist
 
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return tdist.max_over_ranks(world, v)
 
 
 class Workload:
@@ -353,6 +343,11 @@ def main():
     counts_after = wl.counts.cpu()
     assert torch.equal(counts_after, counts), "graph replay changed the exit counts"
     wl.runner.check_errors()
+    from tide_b200 import dist as tdist
+
+    # every rank: global {survivors, exits} per checkpoint (host bookkeeping,
+    # outside the timed region)
+    global_counts = tdist.sum_counts(world, wl.counts).cpu()
 
     e = 2
     alg = [algorithmic_bytes(active[k], exits_per_stage[k], HIDDEN, e) for k in range(len(LAYERS))]
@@ -364,10 +359,14 @@ def main():
     except Exception:
         pass
     peak = peaks.get("hbm_gbs", 6650.0)
+    path_name = {1: "simt", 2: "tc_fused_single_pass", 3: "tc_split"}.get(path_used, path_used)
+    traffic = (NCU_TRAFFIC_CKPT0["bytes"] if ROWS == NCU_TRAFFIC_CKPT0["rows"]
+               and path_name == NCU_TRAFFIC_CKPT0["path"] else None)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "traffic": None,
+                "frac": achieved / peak, "traffic": traffic,
+                "traffic_source": "ncu launch list (warm caches), profiles/" if traffic else None,
                 "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-                "kernel": "checkpoint 0 (32768 rows), every kernel of the call",
+                "kernel": f"checkpoint 0 ({ROWS} rows x {HIDDEN}), both kernels of the call",
                 "per_checkpoint_ms": per_ck, "per_checkpoint_reps": reps,
                 "achieved_all_checkpoints": achieved_all, "algorithmic_bytes_per_step": sum(alg)}
 
@@ -417,7 +416,8 @@ def main():
                        "exit_fractions_of_batch": EXIT_FRACTIONS,
                        "rows_routed_per_step": rows_per_step, "active_rows": active,
                        "exits": exits_per_stage,
-                       "path": {1: "simt", 2: "tc_fused_single_pass", 3: "tc_split"}.get(path_used, path_used),
+                       "global_exits_all_ranks": global_counts[:, 1].tolist(),
+                       "path": path_name,
                        "parallelism": f"dp{world} (row shards, no collective)",
                        "l2": "inputs 1.1 GiB/step > 126 MB L2, no flush"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
