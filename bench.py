@@ -214,6 +214,16 @@ def launches_per_checkpoint(path_used: int) -> int:
 
 
 # ----------------------------------------------------------------- CPU leg
+def host_threads() -> int:
+    """Every host core for the CPU legs: torchrun sets OMP_NUM_THREADS=1 per
+    rank, so the BLAS pool is raised explicitly."""
+    from threadpoolctl import threadpool_limits
+
+    n = os.cpu_count() or 1
+    threadpool_limits(limits=n)
+    return n
+
+
 def cpu_checkpoint_sample(x_bf16: np.ndarray, down: np.ndarray, up: np.ndarray, bias: float):
     """The oracle on one checkpoint's rows (the reference's CPU path,
     restated): returns seconds."""
@@ -248,13 +258,13 @@ def run_reference(args, world, rank):
     torch.cuda.set_device(0)
     wl = Workload(rank, 0)
     rows = 4096
+    cores = host_threads()
     x, down, up, bias = cpu_sample_inputs(wl, rows)
     for _ in range(args.warmup):
         cpu_checkpoint_sample(x, down, up, bias)
     ts = [cpu_checkpoint_sample(x, down, up, bias) for _ in range(args.steps)]
     t = sum(ts)
     v = rows * args.steps / t
-    cores = os.cpu_count()
     line = {
         "impl": "reference", "metric": "router_compact_scatter_tokens_per_s", "value": v,
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -397,10 +407,11 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rows = 4096
+        cores = host_threads()
         x, down, up, bias = cpu_sample_inputs(wl, rows)
         cpu_checkpoint_sample(x, down, up, bias)
         t = min(cpu_checkpoint_sample(x, down, up, bias) for _ in range(3))
-        cpu = {"value": rows / t, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+        cpu = {"value": rows / t, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"oracle, one checkpoint of {rows} rows x {HIDDEN} bf16 (layer-8 router), "
                          f"best of 3"}
 
