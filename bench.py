@@ -213,6 +213,35 @@ def launches_per_checkpoint(path_used: int) -> int:
     return 1 if path_used == PATH_TC else 2
 
 
+def gather_timings(world: int, wl: "Workload", reps: int = 5) -> dict:
+    """The step's two collectives, timed on their own (not part of `value`):
+    the all-gather of every rank's exit counts and of every rank's output
+    rows (ncclAllGather over NVLink).  CUDA events, max over ranks."""
+    from tide_b200 import dist as tdist
+
+    rows_out = torch.empty((world * ROWS, HIDDEN), dtype=wl.out.dtype, device=wl.out.device)
+    res = {}
+    for name, fn, nbytes in (
+            ("exit_counts", lambda: tdist.all_gather_counts(world, wl.counts),
+             wl.counts.numel() * 4),
+            ("output_rows", lambda: tdist.all_gather_rows(world, wl.out, rows_out),
+             wl.out.numel() * wl.out.element_size())):
+        fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(world, a.elapsed_time(b) / reps)
+        res[name] = {"ms": ms, "bytes_per_rank": nbytes,
+                     "busbw_GBps": (world - 1) * nbytes / (ms / 1000.0) / 1e9}
+    del rows_out
+    return res
+
+
 # ----------------------------------------------------------------- CPU leg
 def host_threads() -> int:
     """Every host core for the CPU legs: torchrun sets OMP_NUM_THREADS=1 per
@@ -358,6 +387,7 @@ def main():
     # every rank: global {survivors, exits} per checkpoint (host bookkeeping,
     # outside the timed region)
     global_counts = tdist.sum_counts(world, wl.counts).cpu()
+    collectives = gather_timings(world, wl) if world > 1 else None
 
     e = 2
     alg = [algorithmic_bytes(active[k], exits_per_stage[k], HIDDEN, e) for k in range(len(LAYERS))]
@@ -433,6 +463,7 @@ def main():
                        "l2": "inputs 1.1 GiB/step > 126 MB L2, no flush"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": n_launch, "clocks": clocks.summary(),
+            "collectives_timed_separately": collectives,
             "prefill_tokens_per_s": world * ROWS * args.steps / elapsed,
         }
         print(json.dumps(line), flush=True)

@@ -42,6 +42,9 @@ def _collectives(rank: int, world: int, port: int, q) -> None:
                    remaining_tokens=100 * (r + 1) - (r + 3))
     g = td.global_stats(w, st)
     out["stats"] = (g.total_tokens, dict(g.exits_per_layer), g.remaining_tokens, g.summary())
+    rows = torch.full((3, 4), float(r), dtype=torch.bfloat16)
+    out["rows"] = td.all_gather_rows(w, rows).float().tolist()
+    out["gcounts"] = td.all_gather_counts(w, torch.tensor([[r, 2 * r]], dtype=torch.int32)).tolist()
     td.barrier(w)
     dist.destroy_process_group()
     q.put(out)
@@ -99,6 +102,8 @@ def test_two_rank_collectives():
         total, exits, remaining, text = d["stats"]
         assert total == 300 and exits == {4: 3, 8: 4} and remaining == 300 - 7
         assert text.startswith("Total tokens: 300, Exited: 7")
+        assert d["rows"] == [[0.0] * 4] * 3 + [[1.0] * 4] * 3
+        assert d["gcounts"] == [[[0, 0]], [[1, 2]]]
 
 
 def test_rank_that_never_joins_is_detected():

@@ -96,3 +96,24 @@ def shard_range(n: int, world: int, rank: int) -> Tuple[int, int]:
     if world < 1 or not (0 <= rank < world) or n < 0:
         raise ValueError(f"bad shard request n={n} world={world} rank={rank}")
     return n * rank // world, n * (rank + 1) // world
+
+
+def all_gather_rows(world: int, rows: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Every rank's rows stacked in rank order ([world * n, ...]): the end-of-
+    step gather of the output rows (or of rank-local lm_head results).  With
+    NCCL on NVLink/NVSwitch it runs as one ncclAllGather."""
+    if world == 1:
+        return rows if out is None else out.copy_(rows)
+    import torch.distributed as dist
+
+    if out is None:
+        out = torch.empty((world * rows.shape[0],) + tuple(rows.shape[1:]), dtype=rows.dtype,
+                          device=rows.device)
+    dist.all_gather_into_tensor(out, rows.contiguous())
+    return out
+
+
+def all_gather_counts(world: int, counts: torch.Tensor) -> torch.Tensor:
+    """Per-rank exit counts of every rank, [world, ...] in rank order."""
+    return all_gather_rows(world, counts.reshape(1, *counts.shape)).reshape(world, *counts.shape)
+
