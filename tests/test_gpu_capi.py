@@ -370,6 +370,54 @@ def test_full_size_properties(path):
     assert int(out[untouched].abs().sum()) == 0
 
 
+# the bandwidth sweep's shapes: N up to 1M rows, H 2048..8192, exit fractions
+# 0..0.9 (the largest case holds 3 x 16 GiB of rows on the device)
+SWEEP = [(65536, 2048, 0.0), (65536, 5120, 0.1), (16384, 8192, 0.5), (262144, 4096, 0.9),
+         (1048576, 2048, 0.1), (1048576, 8192, 0.5)]
+
+
+@pytest.mark.parametrize("n,H,f", SWEEP)
+def test_bandwidth_sweep_properties(n, H, f):
+    """Size-independent properties at the sweep's shapes, default path:
+    decisions follow the scores, scores within 1e-2 of a torch fp32 router,
+    counts add up, positions are the stable partition, survivors are
+    bit-exact copies, exits are their row's final norm (<= 1 ulp), rows
+    nobody exited to stay zero."""
+    w = workloads.rows(n, H, torch.bfloat16, seed=n % 1000 + H, device=DEV)
+    x, nw = w["x"], w["norm_weight"]
+    z = workloads.prebias_logits_torch(x, "rms", nw, None, 1e-5, w["down"], w["up"])
+    bias = workloads.bias_for_exit_fraction(z, f, THR)
+    out = torch.zeros_like(x)
+    ck = Checkpoint(x, "rms", nw, None, 1e-5, w["down"], w["up"], bias, THR, out_buffer=out)
+    ck()
+    torch.cuda.synchronize()
+    assert int(ck.error_word.item()) == 0
+    s = ck.scores_out
+    assert float((s - torch.sigmoid(z + bias)).abs().max()) <= 1e-2
+    ex = s > THR
+    c = ck.counts.cpu().tolist()
+    assert c == [int((~ex).sum()), int(ex.sum())]
+    assert abs(c[1] - f * n) <= max(2, 0.001 * n)
+    keep_idx = torch.nonzero(~ex).flatten()
+    ex_idx = torch.nonzero(ex).flatten()
+    assert torch.equal(ck.positions_out[: c[0]], keep_idx)
+    assert torch.equal(ck.exit_positions_out[: c[1]], ex_idx)
+    step = 65536
+    for a in range(0, c[0], step):
+        assert torch.equal(ck.compact_out[a:a + step][: c[0] - a], x[keep_idx[a:a + step]])
+    for a in range(0, c[1], step):
+        idx = ex_idx[a:a + step]
+        xf = x[idx].float()
+        normed = (nw * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5))).to(torch.bfloat16)
+        diff = (out[idx].view(torch.int16).int() - normed.view(torch.int16).int()).abs()
+        assert int(diff.max()) <= 1
+    untouched = torch.ones(n, dtype=torch.bool, device=DEV)
+    untouched[ex_idx] = False
+    for a in range(0, n, step):
+        sel = untouched[a:a + step]
+        assert int(out[a:a + step][sel].abs().sum()) == 0
+
+
 # ---------------------------------------------------------- reference ops
 
 
