@@ -411,8 +411,9 @@ def main():
                 "achieved_all_checkpoints": achieved_all, "algorithmic_bytes_per_step": sum(alg)}
 
     # e2e through the public operator with host buffers: H2D of the step's
-    # hidden states from pinned memory, the checkpoint graphs, D2H of counts
-    host_x = [x.cpu().pin_memory() for x in wl.x]
+    # hidden states from pinned memory (the rows each checkpoint routes), the
+    # step graph, D2H of the counts
+    host_x = [x[: active[k]].cpu().pin_memory() for k, x in enumerate(wl.x)]
     dev_x = [torch.empty_like(x) for x in wl.x]
     host_counts = torch.empty_like(wl.counts, device="cpu").pin_memory()
 
@@ -423,7 +424,7 @@ def main():
     e_start.record()
     for _ in range(args.e2e_steps):
         for k in range(len(LAYERS)):
-            dev_x[k].copy_(host_x[k], non_blocking=True)
+            dev_x[k][: active[k]].copy_(host_x[k], non_blocking=True)
         e_graph.replay()
         host_counts.copy_(wl.counts, non_blocking=True)
     e_end.record()

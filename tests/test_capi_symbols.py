@@ -97,10 +97,11 @@ def test_operators_have_no_cpu_kernel():
 
 
 def test_path_selection():
-    """bf16/fp16 with folded weights go to the fused single-pass kernel when
-    the router is 128 wide and a weight slice of H stays resident, else to
-    the tensor-core split path (H % 64 == 0, B <= 256); fp32 and other
-    shapes to the SIMT path."""
+    """bf16/fp16 with folded weights: up to 6144 rows the fused single-pass
+    kernel when the router is 128 wide and a weight slice of H stays
+    resident; above that, or when the fused kernel does not apply, the
+    tensor-core split path (H % 64 == 0, B <= 256); fp32 and other shapes to
+    the SIMT path."""
     lib = _native.lib()
 
     def sel(**kw):
@@ -111,12 +112,15 @@ def test_path_selection():
         a = capi.CheckpointArgs(**base)
         return lib.tide_checkpoint_select_path(ctypes.byref(a))
 
-    assert sel() == capi.PATH_TC_SPLIT
-    assert sel(dtype=capi.DTYPE_F16) == capi.PATH_TC_SPLIT
+    assert sel() == capi.PATH_TC                               # up to 6144 rows: fused single pass
+    assert sel(n_rows=6145, n_total=6145) == capi.PATH_TC_SPLIT
+    assert sel(n_rows=32768, n_total=32768) == capi.PATH_TC_SPLIT
+    assert sel(dtype=capi.DTYPE_F16) == capi.PATH_TC
+    assert sel(n_rows=32768, n_total=32768, dtype=capi.DTYPE_F16) == capi.PATH_TC_SPLIT
     assert sel(path=capi.PATH_TC) == capi.PATH_TC
     assert sel(dtype=capi.DTYPE_F32, folded=None) == capi.PATH_SIMT
     assert sel(hidden_dim=4000) == capi.PATH_SIMT
-    assert sel(bottleneck_dim=48) == capi.PATH_TC_SPLIT       # units padded to 128
+    assert sel(bottleneck_dim=48) == capi.PATH_TC_SPLIT       # units padded to 128 (fused: 128 only)
     assert sel(bottleneck_dim=64) == capi.PATH_TC_SPLIT       # fused kernel: 128 units only
     assert sel(hidden_dim=8192, path=capi.PATH_TC) == capi.PATH_TC_SPLIT  # slice too large to stay resident
     assert sel(hidden_dim=768, path=capi.PATH_TC) == capi.PATH_TC   # cluster of 2

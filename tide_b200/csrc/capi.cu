@@ -305,8 +305,12 @@ int tide_checkpoint_select_path(const tide_checkpoint_args *a) {
          tide::tc_unsupported_reason(a));
     return -TIDE_ERR_UNSUPPORTED;
   }
-  // automatic choice: the tensor-core split path where it applies (measured
-  // faster today), else the fused single pass, else SIMT
+  // automatic choice, from measured latencies at H = 4096 bf16: up to ~6K
+  // rows the fused single pass (one launch, ~20 us at 256 rows) beats the
+  // split path, whose router streams all of W' through each of its few CTAs
+  // (~50 us floor); above that the split path wins.  SIMT otherwise.
+  constexpr int64_t kFusedAutoMaxRows = 6144;
+  if (a->n_rows <= kFusedAutoMaxRows && tide::fused_supported(a)) return TIDE_PATH_TC;
   if (tide::tc_supported(a)) return TIDE_PATH_TC_SPLIT;
   if (tide::fused_supported(a)) return TIDE_PATH_TC;
   return TIDE_PATH_SIMT;
