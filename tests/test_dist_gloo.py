@@ -50,6 +50,15 @@ def _collectives(rank: int, world: int, port: int, q) -> None:
     q.put(out)
 
 
+def _put_and_exit(q, item) -> None:
+    """Deliver `item` before the process ends without any cleanup (the queue's
+    feeder thread is flushed first)."""
+    q.put(item)
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
 def _dead_peer(rank: int, world: int, port: int, q) -> None:
     _env(rank, world, port)
     import torch.distributed as dist
@@ -58,15 +67,15 @@ def _dead_peer(rank: int, world: int, port: int, q) -> None:
 
     w, r, _ = td.init("gloo", timeout_s=3)
     if r == 1:
-        q.put({"rank": 1, "left": True})
-        os._exit(0)  # leaves between steps, never joins the next collective
+        # leaves between steps, never joins the next collective
+        _put_and_exit(q, {"rank": 1, "left": True})
     t0 = time.time()
     try:
         td.max_over_ranks(w, 1.0)
-        q.put({"rank": 0, "raised": False})
+        item = {"rank": 0, "raised": False}
     except Exception as e:  # the timeout or the closed peer connection
-        q.put({"rank": 0, "raised": True, "after_s": time.time() - t0, "err": type(e).__name__})
-    os._exit(0)
+        item = {"rank": 0, "raised": True, "after_s": time.time() - t0, "err": type(e).__name__}
+    _put_and_exit(q, item)
 
 
 def _run(target, world=2, timeout=120):

@@ -125,10 +125,14 @@ def test_checkpoint_golden(name, path):
     check_against_oracle(ck, res, dtype, w["norm_kind"], tol, out_ref=np.zeros_like(storage_np(out)))
 
 
-@pytest.mark.parametrize("n", [0, 1, 31, 33, 63, 64, 65, 127, 128, 129, 1025, 5000])
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-def test_checkpoint_sizes_positions_slots(n, dtype):
-    H = 256
+@pytest.mark.parametrize("n", [0, 1, 31, 32, 33, 63, 64, 65, 127, 128, 129, 1023, 1024, 1025, 5000])
+@pytest.mark.parametrize("dtype,H", [(torch.bfloat16, 256), (torch.float16, 256),
+                                     (torch.float32, 256), (torch.bfloat16, 1024)])
+@pytest.mark.parametrize("path", [capi.PATH_AUTO, capi.PATH_TC_SPLIT])
+def test_checkpoint_sizes_positions_slots(n, dtype, H, path):
+    """Sizes around the warp, tile and 1024 boundaries on the automatic path
+    (fused single pass / SIMT at these sizes) and on the split path (its
+    mover: 16-byte SIMT rows at H = 256, bulk copies at H = 1024)."""
     w = workloads.rows(max(n, 1), H, dtype, b=128, seed=100 + n, unit_norm_weight=False)
     x = w["x"][:n].to(DEV).contiguous()
     nw, nb = norm_tensors(w, dtype)
@@ -144,12 +148,13 @@ def test_checkpoint_sizes_positions_slots(n, dtype):
                         w["up"].numpy()) if n else np.zeros(0)
     bias = workloads.bias_for_exit_fraction(z, 0.4, THR)
     ck = Checkpoint(x, "rms", nw, None, 1e-5, w["down"].to(DEV), w["up"].to(DEV), bias, THR,
-                    positions=positions, slots=slots, out_buffer=out)
+                    positions=positions, slots=slots, out_buffer=out, path=path)
+    used = skip_unless_path(ck, path)
     ck()
     res = O.checkpoint(storage_np(x), dt, norm, w["down"].numpy(), w["up"].numpy(), bias, THR,
                        positions=positions.cpu().numpy(), slots=slots.cpu().numpy())
     res["eps"] = 1e-5
-    check_against_oracle(ck, res, dtype, "rms", score_tol(dtype, ck.path()), out_ref=out0)
+    check_against_oracle(ck, res, dtype, "rms", score_tol(dtype, used), out_ref=out0)
 
 
 @pytest.mark.parametrize("fraction", [0.0, 1.0])

@@ -114,6 +114,29 @@ def test_threshold_pins(tmp_path):
     assert rt.last_stats.exits_per_layer == {3: 32}
 
 
+def test_profile_timings(tmp_path):
+    """TIDEConfig.profile: NVTX ranges and the device time of every checkpoint
+    (and of the final scatter of the rows that never exit) after a forward;
+    the outputs are those of an unprofiled forward."""
+    model = llama()
+    write_routers(tmp_path / "router.pt", 256, [1, 2], bias=0.8)
+    ids = torch.randint(0, 512, (2, 24), generator=torch.Generator().manual_seed(3)).to(DEV)
+    plain = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.7,
+                                                                          min_layers=0))
+    prof = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.7,
+                                                                         min_layers=0, profile=True))
+    with torch.no_grad():
+        a = plain(ids)
+        b = prof(ids)
+    assert torch.equal(a, b)
+    assert plain.last_timings == {}
+    t = prof.last_timings
+    assert set(t) >= {"checkpoint.layer1", "checkpoint.layer2"}
+    if prof.last_stats.remaining_tokens > 0:
+        assert "finalize" in t
+    assert all(v > 0 for v in t.values())
+
+
 def test_reference_router_file_loads(tmp_path):
     """A router.pt written by the reference (no bias key) drives the runtime."""
     from tests.conftest import GOLDEN

@@ -66,6 +66,10 @@ class TIDERuntime(nn.Module):
         self._prepared: Dict[tuple, PreparedRouter] = {}
         self._runner = CheckpointRunner(dev)
         self.last_stats: Optional[ExitStats] = None
+        # TIDEConfig.profile (declared by the reference, config.py:21, never
+        # read there): NVTX ranges around every checkpoint and the device time
+        # of each, in milliseconds, after a forward
+        self.last_timings: Dict[str, float] = {}
         logger.info(f"TIDERuntime initialized: {len(self._layers)} layers, "
                     f"{len(self.routers)} routers, CUDA=on (sm_100a)")
 
@@ -108,26 +112,47 @@ class TIDERuntime(nn.Module):
         spare = torch.empty_like(positions)
         n_active = N
         thr = self.config.exit_threshold
+        prof = bool(self.config.profile)
+        events = []
         for layer in sorted(self.routers):
             if layer < self.config.min_layers or n_active == 0:
                 continue
+            if prof:
+                torch.cuda.nvtx.range_push(f"tide.checkpoint.layer{layer}")
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record()
             hidden = hs[layer + 1].reshape(N, H)
             x = hidden if n_active == N else hidden.index_select(0, positions[:n_active])
             counts = self._runner.run(x.contiguous(), self._router(layer, dtype), self._norm, thr,
                                       positions=positions[:n_active], out_buffer=out_buf,
                                       positions_out=spare)
+            if prof:
+                ev[1].record()
+                torch.cuda.nvtx.range_pop()
+                events.append((f"checkpoint.layer{layer}", ev))
             n_surv, n_exit = (int(v) for v in counts.tolist())
             if n_exit > 0:
                 stats.exits_per_layer[layer] = n_exit
             positions, spare = spare, positions
             n_active = n_surv
         if n_active > 0:
+            if prof:
+                torch.cuda.nvtx.range_push("tide.finalize")
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record()
             final = hs[-1].reshape(N, H)
             rows = final if n_active == N else final.index_select(0, positions[:n_active])
             self._runner.norm_scatter(rows.contiguous(), positions[:n_active], out_buf, self._norm)
+            if prof:
+                ev[1].record()
+                torch.cuda.nvtx.range_pop()
+                events.append(("finalize", ev))
         stats.remaining_tokens = n_active
         self._runner.check_errors()
         self.last_stats = stats
+        if prof:
+            torch.cuda.synchronize()
+            self.last_timings = {name: a.elapsed_time(b) for name, (a, b) in events}
         return self._lm_head(out_buf.view(B, S, H))
 
     @torch.no_grad()
