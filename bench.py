@@ -13,10 +13,17 @@ counts chain on the device between checkpoints (no host sync).  One step =
 the six checkpoints.  Inputs (1.1 GiB per step) exceed the 126 MB L2, so no
 explicit flush is needed between steps.
 
+Second workload ("qwen3_8b_decode_checkpoints", --workload): one decode step
+of a Qwen3-8B-architecture batch of 256 sequences, routers at layers
+3/7/.../31 (eight checkpoints, H = 4096), each exiting ~10 % of the rows
+still active; the small-batch regime where launch and latency, not HBM,
+set the time.
+
 Multi-GPU: one process per GPU under torchrun; every rank processes its own
 batch (weak scaling, no data-path collective); timing is the max over ranks.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload llama8b_prefill_checkpoints|qwen3_8b_decode_checkpoints]
 """
 from __future__ import annotations
 
@@ -36,10 +43,20 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 THRESHOLD = 0.85
-LAYERS = [8, 12, 16, 20, 24, 28]
-EXIT_FRACTIONS = [0.05, 0.10, 0.15, 0.20, 0.20, 0.30]  # of the whole batch
-ROWS, HIDDEN, BOTTLENECK = 16 * 2048, 4096, 128
+WORKLOADS = {
+    # exits: fraction of the whole batch per checkpoint (the last takes the rest)
+    "llama8b_prefill_checkpoints": {"rows": 16 * 2048, "layers": [8, 12, 16, 20, 24, 28],
+                                    "exit_fractions": [0.05, 0.10, 0.15, 0.20, 0.20, 0.30],
+                                    "of": "batch"},
+    # exits: fraction of the rows still active at each checkpoint
+    "qwen3_8b_decode_checkpoints": {"rows": 256, "layers": [3, 7, 11, 15, 19, 23, 27, 31],
+                                    "exit_fractions": [0.10] * 8, "of": "active"},
+}
 WORKLOAD = "llama8b_prefill_checkpoints"
+LAYERS = WORKLOADS[WORKLOAD]["layers"]
+EXIT_FRACTIONS = WORKLOADS[WORKLOAD]["exit_fractions"]
+EXITS_OF = WORKLOADS[WORKLOAD]["of"]
+ROWS, HIDDEN, BOTTLENECK = WORKLOADS[WORKLOAD]["rows"], 4096, 128
 
 
 # DRAM bytes (read + write) of checkpoint 0's two kernels (router + mover),
@@ -152,7 +169,10 @@ class Workload:
             up = 0.02 * torch.randn(1, BOTTLENECK, generator=g, device=dev)
             z = workloads.prebias_logits_torch(x[:active], "rms", self.norm.weight, None, 1e-5,
                                                down, up)
-            exits = int(round(EXIT_FRACTIONS[k] * ROWS)) if k < len(LAYERS) - 1 else active
+            if EXITS_OF == "batch":
+                exits = int(round(EXIT_FRACTIONS[k] * ROWS)) if k < len(LAYERS) - 1 else active
+            else:
+                exits = int(round(EXIT_FRACTIONS[k] * active))
             bias = workloads.bias_for_exit_fraction(z, exits / active, THRESHOLD)
             self.routers.append(prepare_router(down, up, bias, self.norm, torch.bfloat16))
             self.x.append(x)
@@ -166,6 +186,7 @@ class Workload:
         self.pos = [torch.empty(ROWS, dtype=torch.int64, device=dev) for _ in range(2)]
         self.slots = [torch.empty(ROWS, dtype=torch.int32, device=dev) for _ in range(2)]
         self.counts = torch.zeros(len(LAYERS), 2, dtype=torch.int32, device=dev)
+        self.paths = {}  # path the library chose for each checkpoint
 
     def checkpoint(self, k: int, xs=None):
         """Checkpoint k of the sweep: positions, slots and the live row count
@@ -179,6 +200,7 @@ class Workload:
                         slots=slot_in, out_buffer=self.out, compact_out=self.compact,
                         positions_out=self.pos[k % 2], slots_out=self.slots[k % 2],
                         n_rows_dev=cnt, counts=self.counts[k], path=self.path)
+        self.paths[k] = self.runner.last_path
 
     def step(self, xs=None):
         for k in range(len(LAYERS)):
@@ -211,6 +233,9 @@ def launches_per_checkpoint(path_used: int) -> int:
     from tide_b200.capi import PATH_TC
 
     return 1 if path_used == PATH_TC else 2
+
+
+PATH_NAMES = {1: "simt", 2: "tc_fused_single_pass", 3: "tc_split"}
 
 
 def gather_timings(world: int, wl: "Workload", reps: int = 5) -> dict:
@@ -286,7 +311,7 @@ def run_reference(args, world, rank):
         return
     torch.cuda.set_device(0)
     wl = Workload(rank, 0)
-    rows = 4096
+    rows = min(4096, ROWS)
     cores = host_threads()
     x, down, up, bias = cpu_sample_inputs(wl, rows)
     for _ in range(args.warmup):
@@ -300,7 +325,8 @@ def run_reference(args, world, rank):
         "ms_per_step": 1000 * t / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD, "sample_rows_per_step": rows, "hidden": HIDDEN,
-                   "bottleneck": BOTTLENECK, "checkpoint": "layer 8 router, 5% exit"},
+                   "bottleneck": BOTTLENECK,
+                   "checkpoint": f"first router (layer {LAYERS[0]}), {EXIT_FRACTIONS[0]:.0%} exit"},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"one checkpoint ({rows} rows x {HIDDEN} bf16) per step"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -317,9 +343,12 @@ def main():
     ap.add_argument("--path", default="auto", choices=["auto", "simt", "tc", "tc_split"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU (profiling runs)")
+    ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--rows", type=int, default=None, help="rows per GPU (profiling runs)")
     args = ap.parse_args()
-    globals()["ROWS"] = args.rows
+    wk = WORKLOADS[args.workload]
+    globals().update(WORKLOAD=args.workload, LAYERS=wk["layers"], EXIT_FRACTIONS=wk["exit_fractions"],
+                     EXITS_OF=wk["of"], ROWS=args.rows if args.rows else wk["rows"])
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
         run_reference(args, world, rank)
@@ -399,7 +428,7 @@ def main():
     except Exception:
         pass
     peak = peaks.get("hbm_gbs", 6650.0)
-    path_name = {1: "simt", 2: "tc_fused_single_pass", 3: "tc_split"}.get(path_used, path_used)
+    path_name = PATH_NAMES.get(wl.paths[0], wl.paths[0])
     traffic = (NCU_TRAFFIC_CKPT0["bytes"] if ROWS == NCU_TRAFFIC_CKPT0["rows"]
                and path_name == NCU_TRAFFIC_CKPT0["path"] else None)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -437,16 +466,16 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rows = 4096
+        rows = min(4096, ROWS)
         cores = host_threads()
         x, down, up, bias = cpu_sample_inputs(wl, rows)
         cpu_checkpoint_sample(x, down, up, bias)
         t = min(cpu_checkpoint_sample(x, down, up, bias) for _ in range(3))
         cpu = {"value": rows / t, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"oracle, one checkpoint of {rows} rows x {HIDDEN} bf16 (layer-8 router), "
-                         f"best of 3"}
+               "sample": f"oracle, one checkpoint of {rows} rows x {HIDDEN} bf16 "
+                         f"(layer-{LAYERS[0]} router), best of 3"}
 
-    n_launch = launches_per_checkpoint(path_used) * len(LAYERS) * args.steps
+    n_launch = sum(launches_per_checkpoint(p) for p in wl.paths.values()) * args.steps
     if rank == 0:
         line = {
             "metric": "router_compact_scatter_tokens_per_s", "value": value, "unit": "tokens/s",
@@ -455,11 +484,13 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "hidden": HIDDEN,
                        "bottleneck": BOTTLENECK, "checkpoint_layers": LAYERS,
-                       "exit_fractions_of_batch": EXIT_FRACTIONS,
+                       f"exit_fractions_of_{EXITS_OF}": EXIT_FRACTIONS,
                        "rows_routed_per_step": rows_per_step, "active_rows": active,
                        "exits": exits_per_stage,
                        "global_exits_all_ranks": global_counts[:, 1].tolist(),
                        "path": path_name,
+                       "path_per_checkpoint": [PATH_NAMES.get(wl.paths[k], wl.paths[k])
+                                               for k in range(len(LAYERS))],
                        "parallelism": f"dp{world} (row shards, no collective)",
                        "l2": "inputs 1.1 GiB/step > 126 MB L2, no flush"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,

@@ -47,6 +47,7 @@ constexpr int kMaxSlots = 64;
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kAux = 4096;      // barriers, descriptors, flags
 constexpr uint32_t kMinRowBytes = 2048;
+constexpr int kExitUnroll = 4;  // vectors per lane in flight when norming an exit row
 constexpr int kMaxPending = 0;  // bulk stores a mover leaves reading their slots (more measured slower)
 
 struct TileDesc {
@@ -312,21 +313,38 @@ __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams 
           const float rstd = ms.y, shift = -ms.y * ms.x;
           const uint4 *sv = reinterpret_cast<const uint4 *>(src);
           uint4 *dv = reinterpret_cast<uint4 *>(dst);
-          for (int64_t i = lane; i < nv; i += 32) {
-            float xv[V], y[V];
-            unpack16<T>(sv[i], xv);
-            const int64_t col = i * V;
+          // kExitUnroll independent 16-byte vectors per lane per trip: their
+          // shared-memory and weight loads are all in flight before the math
+          for (int64_t i0 = lane; i0 < nv; i0 += 32 * kExitUnroll) {
+            uint4 xr[kExitUnroll];
+            float4 w4[kExitUnroll][V / 4], b4[kExitUnroll][V / 4];
 #pragma unroll
-            for (int j = 0; j < V; j += 4) {
-              const float4 w4 = __ldg(reinterpret_cast<const float4 *>(p.w_norm + col + j));
-              float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (p.b_norm) b4 = __ldg(reinterpret_cast<const float4 *>(p.b_norm + col + j));
-              y[j] = norm_elem<T>(xv[j], w4.x, b4.x, rstd, shift, p.norm_type);
-              y[j + 1] = norm_elem<T>(xv[j + 1], w4.y, b4.y, rstd, shift, p.norm_type);
-              y[j + 2] = norm_elem<T>(xv[j + 2], w4.z, b4.z, rstd, shift, p.norm_type);
-              y[j + 3] = norm_elem<T>(xv[j + 3], w4.w, b4.w, rstd, shift, p.norm_type);
+            for (int u = 0; u < kExitUnroll; ++u) {
+              const int64_t i = i0 + 32 * u;
+              if (i >= nv) continue;
+              xr[u] = sv[i];
+#pragma unroll
+              for (int j = 0; j < V / 4; ++j) {
+                w4[u][j] = __ldg(reinterpret_cast<const float4 *>(p.w_norm + i * V) + j);
+                b4[u][j] = p.b_norm ? __ldg(reinterpret_cast<const float4 *>(p.b_norm + i * V) + j)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
             }
-            st_stream(dv + i, pack16<T>(y));
+#pragma unroll
+            for (int u = 0; u < kExitUnroll; ++u) {
+              const int64_t i = i0 + 32 * u;
+              if (i >= nv) continue;
+              float xv[V], y[V];
+              unpack16<T>(xr[u], xv);
+#pragma unroll
+              for (int j = 0; j < V / 4; ++j) {
+                y[4 * j] = norm_elem<T>(xv[4 * j], w4[u][j].x, b4[u][j].x, rstd, shift, p.norm_type);
+                y[4 * j + 1] = norm_elem<T>(xv[4 * j + 1], w4[u][j].y, b4[u][j].y, rstd, shift, p.norm_type);
+                y[4 * j + 2] = norm_elem<T>(xv[4 * j + 2], w4[u][j].z, b4[u][j].z, rstd, shift, p.norm_type);
+                y[4 * j + 3] = norm_elem<T>(xv[4 * j + 3], w4[u][j].w, b4[u][j].w, rstd, shift, p.norm_type);
+              }
+              st_stream(dv + i, pack16<T>(y));
+            }
           }
           __syncwarp();
         } else {

@@ -22,10 +22,11 @@
 //   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K = 16) per
 //               stage and 128-unit block into an fp32 accumulator of 256
 //               columns (double-buffered across tiles when TMEM holds two);
-//   warps 4-7   row statistics from the x chunks (two rows per thread),
+//   warps 4-11  row statistics from the x chunks (one row per thread),
 //               handed to the epilogue per tile through a double-buffered
 //               shared-memory slot;
-//   warps 8-15  the epilogue, two groups of four warps, one per half of the
+//   warps 8-15  the epilogue (warps 8-11 after their statistics of the
+//               tile), two groups of four warps, one per half of the
 //               tile's rows: warp 8+4g+q reads units 32q..32q+31 of its rows
 //               (tcgen05.ld), applies the norm scale and SiLU, weights by
 //               up[unit], sums the 32 units of each row with a butterfly of
@@ -53,7 +54,7 @@ constexpr int kTcBigBox = 128;    // rows per large TMA box
 constexpr int kTcTileUnits = 8;   // units per tile
 constexpr int kTcTileRows = kTcUnit * kTcTileUnits;  // MMA N
 constexpr int kTcK = 64;          // columns per chunk: 128 bytes of 16-bit data
-constexpr int kTcThreads = 512;  // warps 0-1 TMA/MMA, 4-7 statistics, 8-15 epilogue
+constexpr int kTcThreads = 512;  // warps 0-1 TMA/MMA, 4-11 statistics, 8-15 epilogue
 constexpr int kTcMaxStages = 8;
 constexpr int kTcSmemBudget = 227 * 1024;
 constexpr int kTcAux = 12288;     // barriers, flags, per-unit vectors, row statistics, partials
@@ -146,12 +147,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 statistics warps
+      ptx::mbar_init(&empty[s], 1 + 8);  // MMA commit + 8 statistics warps
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&acc_full[a], 1);
       ptx::mbar_init(&acc_empty[a], 8);   // 8 epilogue warps
-      ptx::mbar_init(&stat_full[a], 4);   // 4 statistics warps
+      ptx::mbar_init(&stat_full[a], 8);   // 8 statistics warps
       ptx::mbar_init(&stat_empty[a], 8);  // 8 epilogue warps
     }
     ptx::mbar_init(drain, 1);
@@ -291,88 +292,82 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       volatile int never = 0;
       if (!ptx::mbar_wait(drain, 0, &never)) raise_error(p.err, TIDE_DEVERR_TIMEOUT);
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ------------------------------------------------- row statistics
-    // thread t of warps 4-7 owns rows t and t + 128 of the tile and reads all
-    // eight 16-byte units of each chunk row, lane-rotated so a warp's reads
-    // of the swizzled tile hit distinct banks (the sum is order-free within
-    // a row).
-    const int t = threadIdx.x - 128;
+  } else if (warp >= 4) {
+    // ------------------------------------- row statistics and epilogue
+    // Statistics: thread t of warps 4-11 owns row t of the tile and reads
+    // all eight 16-byte units of its chunk row, lane-rotated so a warp's
+    // reads of the swizzled tile hit distinct banks (the sum is order-free
+    // within a row).  Epilogue: warp 8 + 4g + q reads TMEM lanes 32q..32q+31
+    // (units a*128 + 32q + lane) of the rows in chunks 4g..4g+3.  Warps 8-11
+    // do both, in that order per tile: while the rows stream they have no
+    // epilogue to run (a CTA's range is one tile up to 37888 rows), and eight
+    // statistics warps keep each stage's release short.
+    const bool do_stats = warp < 12;
+    const bool do_epi = warp >= 8;
+    const int t = threadIdx.x - 128;   // statistics row 0..255
+    const int q = warp & 3;
+    const int g = (warp - 8) >> 2;
+    const int et = threadIdx.x - 256;  // 0..255 in the epilogue
     uint32_t it = 0;
     int t_local = 0;
     bool ok = true;
-    for (int64_t u0 = u_begin; u0 < u_end && ok; u0 += kTcTileUnits, ++t_local) {
+    for (int64_t u0 = u_begin; u0 < u_end; u0 += kTcTileUnits, ++t_local) {
       const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
-      float ss[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, sx[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-      for (int kc = 0; kc < k_chunks; ++kc, ++it) {
-        const uint32_t s = it % S, ph = (it / S) & 1u;
-        if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+      const int buf = t_local & 1;
+      if (do_stats && ok) {
+        const bool live = (t >> 5) < nu;  // warp-uniform: a unit is one warp
+        float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
+        for (int kc = 0; kc < k_chunks; ++kc, ++it) {
+          const uint32_t s = it % S, ph = (it / S) & 1u;
+          if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+          if (live) {
+            const uint8_t *row = smem + (size_t)s * stage_bytes + (size_t)t * 128;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int r = t + h * 128;
-          if ((r >> 5) >= nu) continue;  // warp-uniform: a unit is one warp
-          const uint8_t *row = smem + (size_t)s * stage_bytes + (size_t)r * 128;
+            for (int j = 0; j < 8; ++j) {
+              const int unit = (j + lane) & 7;
+              const uint4 v = *reinterpret_cast<const uint4 *>(row + (unit << 4));
+              float f[8];
+              unpack8_16(v, f, BF16);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int unit = (j + lane) & 7;
-            const uint4 v = *reinterpret_cast<const uint4 *>(row + (unit << 4));
-            float f[8];
-            unpack8_16(v, f, BF16);
-#pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              ss[h][0] = fmaf(f[e], f[e], ss[h][0]);
-              ss[h][1] = fmaf(f[e + 1], f[e + 1], ss[h][1]);
-              if (LAYER) { sx[h][0] += f[e]; sx[h][1] += f[e + 1]; }
+              for (int e = 0; e < 8; e += 2) {
+                ss0 = fmaf(f[e], f[e], ss0);
+                ss1 = fmaf(f[e + 1], f[e + 1], ss1);
+                if (LAYER) { sx0 += f[e]; sx1 += f[e + 1]; }
+              }
             }
           }
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&empty[s]);
         }
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&empty[s]);
-      }
-      if (!ok) break;
-      const int buf = t_local & 1;
-      if (t_local >= 2 &&
-          !ptx::mbar_wait(&stat_empty[buf], ((uint32_t)(t_local >> 1) & 1u) ^ 1u, abort_flag)) {
-        ok = false;
-        break;
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float *st = s_stat + ((size_t)buf * kTcTileRows + t + h * 128) * 2;
-        const float ssum = ss[h][0] + ss[h][1], xsum = sx[h][0] + sx[h][1];
-        if (!LAYER) {
-          st[0] = rsqrt_rn(ssum / (float)p.H + p.eps);
-          st[1] = 0.f;
-        } else {
-          const float mean = xsum / (float)p.H;
-          const float var = fmaxf(ssum / (float)p.H - mean * mean, 0.f);
-          st[0] = rsqrt_rn(var + p.eps);
-          st[1] = mean;
+        if (ok && t_local >= 2 &&
+            !ptx::mbar_wait(&stat_empty[buf], ((uint32_t)(t_local >> 1) & 1u) ^ 1u, abort_flag))
+          ok = false;
+        if (ok) {
+          float *st = s_stat + ((size_t)buf * kTcTileRows + t) * 2;
+          const float ssum = ss0 + ss1, xsum = sx0 + sx1;
+          if (!LAYER) {
+            st[0] = rsqrt_rn(ssum / (float)p.H + p.eps);
+            st[1] = 0.f;
+          } else {
+            const float mean = xsum / (float)p.H;
+            const float var = fmaxf(ssum / (float)p.H - mean * mean, 0.f);
+            st[0] = rsqrt_rn(var + p.eps);
+            st[1] = mean;
+          }
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&stat_full[buf]);
         }
       }
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&stat_full[buf]);
-    }
-    if (!ok) {
-      raise_error(p.err, TIDE_DEVERR_TIMEOUT);
-      *abort_flag = 1;
-    }
-  } else if (warp >= 8) {
-    // ----------------------------------------------------------- epilogue
-    // warp 8 + 4g + q reads TMEM lanes 32q..32q+31 (units a*128 + 32q + lane)
-    // of the rows in chunks 4g..4g+3 (rows 128g..128g+127) of the tile
-    const int q = warp & 3;
-    const int g = (warp - 8) >> 2;
-    const int et = threadIdx.x - 256;  // 0..255
-    int t_local = 0;
-    bool ok = true;
-    for (int64_t u0 = u_begin; u0 < u_end && ok; u0 += kTcTileUnits, ++t_local) {
-      const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
-      const int buf = t_local & 1;
+      if (!do_epi) {
+        if (!ok) break;
+        continue;
+      }
+      // ---- epilogue of this tile (warps 8-15)
       const int acc = t_local % NA;
-      bool got = ptx::mbar_wait(&stat_full[buf], (uint32_t)(t_local >> 1) & 1u, abort_flag) &&
+      bool got = ok &&
+                 ptx::mbar_wait(&stat_full[buf], (uint32_t)(t_local >> 1) & 1u, abort_flag) &&
                  ptx::mbar_wait(&acc_full[acc], (uint32_t)(t_local / NA) & 1u, abort_flag);
-      // the four epilogue warps vote and leave together, so each named
+      // the eight epilogue warps vote and leave together, so each named
       // barrier below is reached by all of them or by none
       got = __all_sync(0xffffffffu, got);
       if (lane == 0) s_vote[warp - 8] = got ? 1 : 0;
