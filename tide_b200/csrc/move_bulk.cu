@@ -47,7 +47,10 @@ constexpr int kMaxSlots = 64;
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kAux = 4096;      // barriers, descriptors, flags
 constexpr uint32_t kMinRowBytes = 2048;
-constexpr int kExitUnroll = 4;  // vectors per lane in flight when norming an exit row
+// 16-byte vectors per lane in flight when norming an exit row: eight for
+// RMSNorm (weights only), four for LayerNorm (weights and bias), which keeps
+// both within the registers of one CTA per SM without spills
+template <bool LN> constexpr int kExitUnroll = LN ? 4 : 8;
 constexpr int kMaxPending = 0;  // bulk stores a mover leaves reading their slots (more measured slower)
 
 struct TileDesc {
@@ -95,7 +98,7 @@ __device__ __forceinline__ void fail(const MoveParams &p, const BulkSmem &m) {
   *m.abort_flag = 1;
 }
 
-template <typename T>
+template <typename T, bool LN>
 __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams p, int NS) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const uint32_t row_bytes = (uint32_t)(p.H * (int64_t)sizeof(T));
@@ -313,35 +316,43 @@ __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams 
           const float rstd = ms.y, shift = -ms.y * ms.x;
           const uint4 *sv = reinterpret_cast<const uint4 *>(src);
           uint4 *dv = reinterpret_cast<uint4 *>(dst);
-          // kExitUnroll independent 16-byte vectors per lane per trip: their
+          // UN independent 16-byte vectors per lane per trip: their
           // shared-memory and weight loads are all in flight before the math
-          for (int64_t i0 = lane; i0 < nv; i0 += 32 * kExitUnroll) {
-            uint4 xr[kExitUnroll];
-            float4 w4[kExitUnroll][V / 4], b4[kExitUnroll][V / 4];
+          constexpr int UN = kExitUnroll<LN>;
+          constexpr int NT = LN ? TIDE_NORM_LAYER : TIDE_NORM_RMS;
+          for (int64_t i0 = lane; i0 < nv; i0 += 32 * UN) {
+            uint4 xr[UN];
+            float4 w4[UN][V / 4], b4[LN ? UN : 1][V / 4];
 #pragma unroll
-            for (int u = 0; u < kExitUnroll; ++u) {
+            for (int u = 0; u < UN; ++u) {
               const int64_t i = i0 + 32 * u;
               if (i >= nv) continue;
               xr[u] = sv[i];
 #pragma unroll
               for (int j = 0; j < V / 4; ++j) {
                 w4[u][j] = __ldg(reinterpret_cast<const float4 *>(p.w_norm + i * V) + j);
-                b4[u][j] = p.b_norm ? __ldg(reinterpret_cast<const float4 *>(p.b_norm + i * V) + j)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (LN)
+                  b4[LN ? u : 0][j] = p.b_norm ? __ldg(reinterpret_cast<const float4 *>(p.b_norm + i * V) + j)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
               }
             }
+            if (!LN) {
 #pragma unroll
-            for (int u = 0; u < kExitUnroll; ++u) {
+              for (int j = 0; j < V / 4; ++j) b4[0][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
               const int64_t i = i0 + 32 * u;
               if (i >= nv) continue;
               float xv[V], y[V];
               unpack16<T>(xr[u], xv);
 #pragma unroll
               for (int j = 0; j < V / 4; ++j) {
-                y[4 * j] = norm_elem<T>(xv[4 * j], w4[u][j].x, b4[u][j].x, rstd, shift, p.norm_type);
-                y[4 * j + 1] = norm_elem<T>(xv[4 * j + 1], w4[u][j].y, b4[u][j].y, rstd, shift, p.norm_type);
-                y[4 * j + 2] = norm_elem<T>(xv[4 * j + 2], w4[u][j].z, b4[u][j].z, rstd, shift, p.norm_type);
-                y[4 * j + 3] = norm_elem<T>(xv[4 * j + 3], w4[u][j].w, b4[u][j].w, rstd, shift, p.norm_type);
+                const float4 bb = b4[LN ? u : 0][j];
+                y[4 * j] = norm_elem<T>(xv[4 * j], w4[u][j].x, bb.x, rstd, shift, NT);
+                y[4 * j + 1] = norm_elem<T>(xv[4 * j + 1], w4[u][j].y, bb.y, rstd, shift, NT);
+                y[4 * j + 2] = norm_elem<T>(xv[4 * j + 2], w4[u][j].z, bb.z, rstd, shift, NT);
+                y[4 * j + 3] = norm_elem<T>(xv[4 * j + 3], w4[u][j].w, bb.w, rstd, shift, NT);
               }
               st_stream(dv + i, pack16<T>(y));
             }
@@ -398,7 +409,7 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-template <typename T>
+template <typename T, bool LN>
 int launch_t(const MoveParams &p, cudaStream_t s) {
   const uint32_t row_bytes = (uint32_t)(p.H * (int64_t)sizeof(T));
   const int NS = slots_for(row_bytes);
@@ -407,7 +418,7 @@ int launch_t(const MoveParams &p, cudaStream_t s) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    if (cudaFuncSetAttribute(move_rows_bulk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(move_rows_bulk_kernel<T, LN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBudget) != cudaSuccess)
       return TIDE_ERR_CUDA;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
@@ -425,7 +436,7 @@ int launch_t(const MoveParams &p, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, move_rows_bulk_kernel<T>, p, NS) != cudaSuccess) return TIDE_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, move_rows_bulk_kernel<T, LN>, p, NS) != cudaSuccess) return TIDE_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? TIDE_OK : TIDE_ERR_CUDA;
 }
 
@@ -447,10 +458,14 @@ bool bulk_move_supported(int dtype, int64_t H, bool vec, const MoveParams &p) {
 }
 
 int bulk_move_launch(int dtype, const MoveParams &p, cudaStream_t s) {
+  const bool ln = p.norm_type == TIDE_NORM_LAYER;
   switch (dtype) {
-    case TIDE_DTYPE_F32: return launch_t<float>(p, s);
-    case TIDE_DTYPE_F16: return launch_t<__half>(p, s);
-    default: return launch_t<__nv_bfloat16>(p, s);
+    case TIDE_DTYPE_F32:
+      return ln ? launch_t<float, true>(p, s) : launch_t<float, false>(p, s);
+    case TIDE_DTYPE_F16:
+      return ln ? launch_t<__half, true>(p, s) : launch_t<__half, false>(p, s);
+    default:
+      return ln ? launch_t<__nv_bfloat16, true>(p, s) : launch_t<__nv_bfloat16, false>(p, s);
   }
 }
 
