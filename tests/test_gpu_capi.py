@@ -423,6 +423,48 @@ def test_bandwidth_sweep_properties(n, H, f):
         assert int(out[a:a + step][sel].abs().sum()) == 0
 
 
+def test_layernorm_fp16_large_split():
+    """LayerNorm on fp16 rows at 65536 x 2048 on the split path (bulk mover,
+    LayerNorm exits): decisions follow the scores, scores within 1e-2 of a
+    torch fp32 router, stable compaction, exits equal to the oracle's final
+    norm of their row (the same bar as the small cases)."""
+    n, H, dtype = 65536, 2048, torch.float16
+    w = workloads.rows(n, H, dtype, seed=2049, norm_kind="layer", unit_norm_weight=False,
+                       device=DEV)
+    x = w["x"]
+    nw, nb = norm_tensors(w, dtype)
+    z = workloads.prebias_logits_torch(x, "layer", nw, nb, 1e-5, w["down"], w["up"])
+    bias = workloads.bias_for_exit_fraction(z, 0.3, THR)
+    out = torch.zeros_like(x)
+    ck = Checkpoint(x, "layer", nw, nb, 1e-5, w["down"], w["up"], bias, THR, out_buffer=out,
+                    path=capi.PATH_TC_SPLIT)
+    assert ck.path() == capi.PATH_TC_SPLIT
+    ck()
+    torch.cuda.synchronize()
+    assert int(ck.error_word.item()) == 0
+    s = ck.scores_out
+    assert float((s - torch.sigmoid(z + bias)).abs().max()) <= 1e-2
+    ex = s > THR
+    c = ck.counts.cpu().tolist()
+    assert c == [int((~ex).sum()), int(ex.sum())]
+    keep_idx = torch.nonzero(~ex).flatten()
+    ex_idx = torch.nonzero(ex).flatten()
+    assert torch.equal(ck.positions_out[: c[0]], keep_idx)
+    assert torch.equal(ck.compact_out[: c[0]], x[keep_idx])
+    dt = TORCH2O[dtype]
+    norm = oracle_norm("layer", nw, nb, 1e-5)
+    x_ex = storage_np(x[ex_idx])
+    normed = O.from_f32(O.final_norm(O.to_f32(x_ex, dt), norm), dt)
+    got = storage_np(out[ex_idx])
+    ulp = O.ulp_distance(got, normed, dt)
+    bad = ulp > 1
+    if bad.any():  # cancellation in x - mean: fp32-level absolute error is the bar
+        diff = np.abs(O.to_f32(got, dt) - O.to_f32(normed, dt))
+        scale = np.abs(O.to_f32(x_ex, dt)).max(axis=1, keepdims=True) * 4 + 1
+        bad &= diff > scale * 2.0 ** -20
+    assert not bad.any(), int(ulp.max())
+
+
 # ---------------------------------------------------------- reference ops
 
 
