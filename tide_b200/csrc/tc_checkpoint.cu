@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               z = rstd * v[j];
             else
               z = fmaf(rstd, v[j] - st[(c * 32 + j) * 2 + 1] * cs, bp);
-            v[j] = up * silu_fast(z);
+            v[j] = up * silu_tanh(z);
           }
           part[cc] += transpose_sum32(v, lane);
         }

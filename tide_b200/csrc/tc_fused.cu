@@ -495,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int rr = 0; rr < R; ++rr) {
           const float rstd = s_rstd[rr];
           const float z = LAYER ? fmaf(rstd, acc[rr] - s_mean[rr] * s_cs[t], s_bp[t]) : rstd * acc[rr];
-          const float v = warp_sum(s_up[t] * silu_fast(z));
+          const float v = warp_sum(s_up[t] * silu_tanh(z));
           if (lane == 0) s_red[q * R + rr] = v;
         }
       }
