@@ -839,14 +839,18 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
     case 4: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 4> : (const void *)fused::fused_checkpoint_kernel<false, 4>; break;
     default: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 8> : (const void *)fused::fused_checkpoint_kernel<false, 8>; break;
   }
-  static bool attr_set[2][9] = {};
-  if (!attr_set[bf16][C]) {
+  // per device: the attribute and the occupancy belong to a device's context
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  static bool attr_set[64][2][9] = {};
+  if (!attr_set[dev][bf16][C]) {
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, fused::kSmemBudget);
     if (e != cudaSuccess) {
       snprintf(err, err_len, "fused checkpoint: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return TIDE_ERR_CUDA;
     }
-    attr_set[bf16][C] = true;
+    attr_set[dev][bf16][C] = true;
   }
   const size_t smem = fused_smem_bytes(a->hidden_dim);
   cudaLaunchConfig_t cfg = {};
@@ -862,8 +866,8 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
   cfg.numAttrs = 1;
   // one resident cluster per C SMs: every cluster runs for the whole launch
   // so a look-back never waits on a tile whose cluster is not running
-  static int max_clusters[2][9] = {};
-  if (!max_clusters[bf16][C]) {
+  static int max_clusters[64][2][9] = {};
+  if (!max_clusters[dev][bf16][C]) {
     cfg.gridDim = dim3((unsigned)C, 1, 1);
     int mc = 0;
     e = cudaOccupancyMaxActiveClusters(&mc, fn, &cfg);
@@ -872,10 +876,10 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
                cudaGetErrorString(e));
       return TIDE_ERR_CUDA;
     }
-    max_clusters[bf16][C] = mc;
+    max_clusters[dev][bf16][C] = mc;
   }
   const int64_t tiles = (a->n_rows + fused::kRows - 1) / fused::kRows;
-  int64_t g = tiles < max_clusters[bf16][C] ? tiles : max_clusters[bf16][C];
+  int64_t g = tiles < max_clusters[dev][bf16][C] ? tiles : max_clusters[dev][bf16][C];
   if (g > 160 / C) g = 160 / C;  // the workspace holds 160 / C exchange areas
   cfg.gridDim = dim3((unsigned)(g * C), 1, 1);
   switch (C) {
