@@ -96,6 +96,25 @@ def test_forward_matches_oracle(tmp_path, family):
         torch.testing.assert_close(logits.float(), ref_logits.float(), atol=2e-2, rtol=2e-2)
 
 
+def test_logits_to_keep(tmp_path):
+    """logits_to_keep = k gives the last k positions of the full logits (the
+    same exit decisions and buffer; lm_head only on the kept rows)."""
+    model = llama()
+    write_routers(tmp_path / "router.pt", 256, [1, 2], bias=0.8)
+    rt = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.7,
+                                                                       min_layers=0))
+    ids = torch.randint(0, 512, (2, 24), generator=torch.Generator().manual_seed(4)).to(DEV)
+    with torch.no_grad():
+        full = rt(ids)
+        stats = rt.last_stats
+        last = rt(ids, logits_to_keep=1)
+        last3 = rt(ids, logits_to_keep=3)
+    assert last.shape == (2, 1, 512) and last3.shape == (2, 3, 512)
+    torch.testing.assert_close(last, full[:, -1:, :], atol=0, rtol=0)
+    torch.testing.assert_close(last3, full[:, -3:, :], atol=0, rtol=0)
+    assert rt.last_stats == stats
+
+
 def test_threshold_pins(tmp_path):
     model = llama()
     write_routers(tmp_path / "router.pt", 256, [1, 3], bias=0.0)

@@ -96,11 +96,24 @@ class TIDERuntime(nn.Module):
         return scores.view(hidden.shape[:-1])
 
     @torch.no_grad()
+    def _hidden_states(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor]):
+        """The model's per-layer hidden states.  Its own logits are not used
+        (the exit buffer goes through lm_head below), so the model is asked
+        for one position's logits where it takes `logits_to_keep`."""
+        kw = dict(attention_mask=attention_mask, output_hidden_states=True, return_dict=True)
+        try:
+            return self.model(input_ids, logits_to_keep=1, **kw)
+        except TypeError:
+            return self.model(input_ids, **kw)
+
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
-                **kwargs) -> torch.Tensor:
+                logits_to_keep: int = 0, **kwargs) -> torch.Tensor:
+        """Post-hoc early exit over the model's hidden states (reference
+        runtime.py:134-192): logits [B, S, V].  `logits_to_keep` > 0 keeps
+        only the last that many positions ([B, logits_to_keep, V]), so lm_head
+        runs on the rows whose logits are used, e.g. 1 before sampling."""
         B, S = input_ids.shape
-        out = self.model(input_ids, attention_mask=attention_mask, output_hidden_states=True,
-                         return_dict=True)
+        out = self._hidden_states(input_ids, attention_mask)
         hs = out.hidden_states
         H = hs[-1].shape[-1]
         dtype = hs[-1].dtype
@@ -153,7 +166,10 @@ class TIDERuntime(nn.Module):
         if prof:
             torch.cuda.synchronize()
             self.last_timings = {name: a.elapsed_time(b) for name, (a, b) in events}
-        return self._lm_head(out_buf.view(B, S, H))
+        rows = out_buf.view(B, S, H)
+        if logits_to_keep > 0:
+            rows = rows[:, -logits_to_keep:, :]
+        return self._lm_head(rows)
 
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 512,
