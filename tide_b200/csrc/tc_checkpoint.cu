@@ -55,9 +55,24 @@ constexpr int kTcTileUnits = 8;   // units per tile
 constexpr int kTcTileRows = kTcUnit * kTcTileUnits;  // MMA N
 constexpr int kTcK = 64;          // columns per chunk: 128 bytes of 16-bit data
 constexpr int kTcThreads = 512;  // warps 0-1 TMA/MMA, 4-11 statistics, 8-15 epilogue
-constexpr int kTcMaxStages = 8;
+constexpr int kTcMaxStages = 12;
+// K chunks per pipeline stage: the largest of 4, 2, 1 dividing the chunk
+// count that still leaves kTcMinStages stages in the ring.  Every stage (one
+// mbarrier phase) costs a fixed ~0.28 us on top of its bytes, so thin tiles
+// move several K chunks per stage.
+#ifndef TIDE_ROUTER_MAX_KC
+#define TIDE_ROUTER_MAX_KC 4
+#endif
+#ifndef TIDE_ROUTER_MIN_STAGES
+#define TIDE_ROUTER_MIN_STAGES 3
+#endif
+constexpr int kTcMaxKc = TIDE_ROUTER_MAX_KC;
+constexpr int kTcMinStages = TIDE_ROUTER_MIN_STAGES;
 constexpr int kTcSmemBudget = 227 * 1024;
 constexpr int kTcAux = 12288;     // barriers, flags, per-unit vectors, row statistics, partials
+static_assert((2 * kTcMaxStages + 9) * 8 + 16 + 3 * 256 * 4 + 2 * 256 * 2 * 4 + 4 * 256 * 4 +
+                      8 * 4 <= kTcAux,
+              "auxiliary shared-memory area");
 
 struct TcRouteParams {
   int64_t n_cap;
@@ -68,7 +83,7 @@ struct TcRouteParams {
   float *scores;
   float2 *row_stats;
   int32_t *err;
-  int stages;
+  uint32_t ring_bytes;  // shared memory for the pipeline stages
   int a_tiles;   // 128-unit blocks of W' (1 for B <= 128, else 2)
   int w_rows;    // rows of one W' box: min(B, 128)
   int n_acc;     // accumulator sets in TMEM (2: double-buffered across tiles)
@@ -119,15 +134,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = p.stages, NA = p.n_acc, AT = p.a_tiles;
+  const int NA = p.n_acc, AT = p.a_tiles;
   const uint32_t unit_bytes = kTcUnit * kTcK * 2;
-  const uint32_t x_bytes = kTcTileRows * kTcK * 2;  // B operand: 256 rows
   const uint32_t w_tile_bytes = kTcM * kTcK * 2;    // A operand: 128 units
-  const uint32_t stage_bytes = x_bytes + (uint32_t)AT * w_tile_bytes;
   const uint32_t w_load_bytes = (uint32_t)AT * (uint32_t)p.w_rows * kTcK * 2;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * stage_bytes);
-  uint64_t *empty = full + S;
-  uint64_t *acc_full = empty + S;      // [2] accumulator set written
+  // barriers and the small vectors first, the pipeline stages after them
+  // (their size depends on the live row count, known only after the wait)
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+  uint64_t *empty = full + kTcMaxStages;
+  uint64_t *acc_full = empty + kTcMaxStages;  // [2] accumulator set written
   uint64_t *acc_empty = acc_full + 2;  // [2] accumulator set read
   uint64_t *stat_full = acc_empty + 2; // [2] statistics slot written
   uint64_t *stat_empty = stat_full + 2;// [2] statistics slot read
@@ -143,9 +158,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   volatile int *s_vote = reinterpret_cast<volatile int *>(s_part + 4 * kTcTileRows);  // [8]
 
   const int k_chunks = p.H / kTcK;
+  uint8_t *ring = smem + kTcAux;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
+    for (int s = 0; s < kTcMaxStages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1 + 8);  // MMA commit + 8 statistics warps
     }
@@ -182,6 +198,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int64_t units = (n + kTcUnit - 1) / kTcUnit;
   const int64_t u_begin = (int64_t)blockIdx.x * units / gridDim.x;
   const int64_t u_end = ((int64_t)blockIdx.x + 1) * units / gridDim.x;
+  // Stage geometry from the largest range of any CTA: one K chunk of the
+  // tile is tile_units units of 32 rows (the MMA's N) plus the W' chunk; a
+  // stage holds KC chunks [x_0 .. x_KC-1][W'_0 .. W'_KC-1], so a CTA with few
+  // rows moves more bytes per stage and keeps the ring full.
+  const int64_t max_units = (units + gridDim.x - 1) / gridDim.x;
+  const int tile_units = max_units >= kTcTileUnits ? kTcTileUnits : (max_units < 1 ? 1 : (int)max_units);
+  const uint32_t x_bytes = (uint32_t)tile_units * unit_bytes;  // one chunk of the B operand
+  const uint32_t wc_bytes = (uint32_t)AT * w_tile_bytes;       // one chunk of the A operand
+  int KC = 1;
+  for (int c = kTcMaxKc; c > 1; c >>= 1)
+    if (k_chunks % c == 0 && p.ring_bytes / ((uint32_t)c * (x_bytes + wc_bytes)) >= (uint32_t)kTcMinStages) {
+      KC = c;
+      break;
+    }
+  const uint32_t w_off = (uint32_t)KC * x_bytes;  // W' chunks follow the x chunks
+  const uint32_t stage_bytes = (uint32_t)KC * (x_bytes + wc_bytes);
+  const int S_fit = (int)(p.ring_bytes / stage_bytes);
+  const int S = S_fit > kTcMaxStages ? kTcMaxStages : S_fit;
+  const int k_stages = k_chunks / KC;
 
   uint32_t tmem_base = 0;
   if (warp != 0) {
@@ -203,12 +238,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (p.w_rows < kTcM) {
       // W' rows past B are never loaded: zero them once in every stage so
       // the padded units contribute exactly 0 (the loads write other rows)
-      for (int s = 0; s < S; ++s) {
-        uint4 *w = reinterpret_cast<uint4 *>(smem + (size_t)s * stage_bytes + x_bytes +
-                                             (size_t)p.w_rows * 128);
-        const int n16 = (kTcM - p.w_rows) * 128 / 16;
-        for (int i = t1; i < n16; i += kTcThreads - 32) w[i] = make_uint4(0, 0, 0, 0);
-      }
+      for (int s = 0; s < S; ++s)
+        for (int c = 0; c < KC; ++c) {
+          uint4 *w = reinterpret_cast<uint4 *>(ring + (size_t)s * stage_bytes + w_off +
+                                               (size_t)c * wc_bytes + (size_t)p.w_rows * 128);
+          const int n16 = (kTcM - p.w_rows) * 128 / 16;
+          for (int i = t1; i < n16; i += kTcThreads - 32) w[i] = make_uint4(0, 0, 0, 0);
+        }
       ptx::fence_proxy_async();
     }
     ptx::tc_fence_before();
@@ -224,24 +260,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int64_t u0 = u_begin; u0 < u_end && !*abort_flag; u0 += kTcTileUnits) {
         const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
         const int n_big = nu / (kTcBigBox / kTcUnit);
-        for (int kc = 0; kc < k_chunks; ++kc, ++it) {
+        for (int ks = 0; ks < k_stages; ++ks, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
           if (it >= (uint32_t)S && !ptx::mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
             raise_error(p.err, TIDE_DEVERR_TIMEOUT);
             *abort_flag = 1;
             break;
           }
-          uint8_t *st = smem + (size_t)s * stage_bytes;
-          ptx::mbar_expect_tx(&full[s], (uint32_t)nu * unit_bytes + w_load_bytes);
-          for (int a = 0; a < AT; ++a)
-            ptx::tma_load_2d(st + x_bytes + (size_t)a * w_tile_bytes, &tmap_w, &full[s], kc * kTcK,
-                             a * kTcM);
-          for (int j = 0; j < n_big; ++j)
-            ptx::tma_load_2d(st + (size_t)j * (kTcBigBox / kTcUnit) * unit_bytes, &tmap_x_big,
-                             &full[s], kc * kTcK, (int)((u0 + j * (kTcBigBox / kTcUnit)) * kTcUnit));
-          for (int j = n_big * (kTcBigBox / kTcUnit); j < nu; ++j)
-            ptx::tma_load_2d(st + (size_t)j * unit_bytes, &tmap_x, &full[s], kc * kTcK,
-                             (int)((u0 + j) * kTcUnit));
+          uint8_t *st = ring + (size_t)s * stage_bytes;
+          ptx::mbar_expect_tx(&full[s], (uint32_t)KC * ((uint32_t)nu * unit_bytes + w_load_bytes));
+          for (int c = 0; c < KC; ++c) {
+            const int col = (ks * KC + c) * kTcK;
+            uint8_t *xc = st + (size_t)c * x_bytes;
+            for (int a = 0; a < AT; ++a)
+              ptx::tma_load_2d(st + w_off + (size_t)c * wc_bytes + (size_t)a * w_tile_bytes, &tmap_w,
+                               &full[s], col, a * kTcM);
+            for (int j = 0; j < n_big; ++j)
+              ptx::tma_load_2d(xc + (size_t)j * (kTcBigBox / kTcUnit) * unit_bytes, &tmap_x_big,
+                               &full[s], col, (int)((u0 + j * (kTcBigBox / kTcUnit)) * kTcUnit));
+            for (int j = n_big * (kTcBigBox / kTcUnit); j < nu; ++j)
+              ptx::tma_load_2d(xc + (size_t)j * unit_bytes, &tmap_x, &full[s], col,
+                               (int)((u0 + j) * kTcUnit));
+          }
           *issued = it + 1;
         }
       }
@@ -249,7 +289,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = ptx::f16_idesc(BF16, kTcM, kTcTileRows);
+      const uint32_t idesc = ptx::f16_idesc(BF16, kTcM, tile_units * kTcUnit);
       uint32_t it = 0;
       int t_local = 0;
       bool ok = true;
@@ -263,19 +303,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * AT * kTcTileRows);
-        for (int kc = 0; kc < k_chunks; ++kc, ++it) {
+        for (int ks = 0; ks < k_stages; ++ks, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
           if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
-          const uint32_t xs = ptx::smem_u32(smem + (size_t)s * stage_bytes);
-          const uint32_t ws = xs + x_bytes;
-          for (int a = 0; a < AT; ++a) {
+          const uint32_t st = ptx::smem_u32(ring + (size_t)s * stage_bytes);
+          for (int c = 0; c < KC; ++c) {
+            const uint32_t xs = st + (uint32_t)c * x_bytes;
+            const uint32_t ws = st + w_off + (uint32_t)c * wc_bytes;
+            for (int a = 0; a < AT; ++a) {
 #pragma unroll
-            for (int k = 0; k < kTcK / 16; ++k) {
-              ptx::mma_f16_ss(d_tmem + (uint32_t)(a * kTcTileRows),
-                              ptx::sw128_kmajor_desc(ws + (uint32_t)a * w_tile_bytes + 32u * k),
-                              ptx::sw128_kmajor_desc(xs + 32u * k), idesc,
-                              (kc > 0 || k > 0) ? 1u : 0u);
+              for (int k = 0; k < kTcK / 16; ++k) {
+                ptx::mma_f16_ss(d_tmem + (uint32_t)(a * kTcTileRows),
+                                ptx::sw128_kmajor_desc(ws + (uint32_t)a * w_tile_bytes + 32u * k),
+                                ptx::sw128_kmajor_desc(xs + 32u * k), idesc,
+                                (ks > 0 || c > 0 || k > 0) ? 1u : 0u);
+              }
             }
           }
           ptx::mma_commit(&empty[s]);
@@ -317,22 +360,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (do_stats && ok) {
         const bool live = (t >> 5) < nu;  // warp-uniform: a unit is one warp
         float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
-        for (int kc = 0; kc < k_chunks; ++kc, ++it) {
+        for (int ks = 0; ks < k_stages; ++ks, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
           if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
           if (live) {
-            const uint8_t *row = smem + (size_t)s * stage_bytes + (size_t)t * 128;
+            for (int c = 0; c < KC; ++c) {
+              const uint8_t *row =
+                  ring + (size_t)s * stage_bytes + (size_t)c * x_bytes + (size_t)t * 128;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int unit = (j + lane) & 7;
-              const uint4 v = *reinterpret_cast<const uint4 *>(row + (unit << 4));
-              float f[8];
-              unpack8_16(v, f, BF16);
+              for (int j = 0; j < 8; ++j) {
+                const int unit = (j + lane) & 7;
+                const uint4 v = *reinterpret_cast<const uint4 *>(row + (unit << 4));
+                float f[8];
+                unpack8_16(v, f, BF16);
 #pragma unroll
-              for (int e = 0; e < 8; e += 2) {
-                ss0 = fmaf(f[e], f[e], ss0);
-                ss1 = fmaf(f[e + 1], f[e + 1], ss1);
-                if (LAYER) { sx0 += f[e]; sx1 += f[e + 1]; }
+                for (int e = 0; e < 8; e += 2) {
+                  ss0 = fmaf(f[e], f[e], ss0);
+                  ss1 = fmaf(f[e + 1], f[e + 1], ss1);
+                  if (LAYER) { sx0 += f[e]; sx1 += f[e + 1]; }
+                }
               }
             }
           }
@@ -484,11 +530,6 @@ bool make_tmap(CUtensorMap *m, const void *base, bool bf16, uint64_t rows, uint6
 int a_tiles_for(int B) { return B <= kTcM ? 1 : 2; }
 int n_acc_for(int B) { return a_tiles_for(B) == 1 ? 2 : 1; }
 
-int stages_for(int B) {
-  const int stage = kTcTileRows * kTcK * 2 + a_tiles_for(B) * kTcM * kTcK * 2;
-  int s = (kTcSmemBudget - 1024 - kTcAux) / stage;
-  return s > kTcMaxStages ? kTcMaxStages : s;
-}
 
 int sm_count() {
   static int n[64] = {};
@@ -548,15 +589,14 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   p.scores = scores;
   p.row_stats = row_stats;
   p.err = a->error_word;
-  p.stages = stages_for(B);
+  p.ring_bytes = (uint32_t)(kTcSmemBudget - 1024 - kTcAux);
   p.a_tiles = a_tiles_for(B);
   p.w_rows = w_rows;
   p.n_acc = n_acc_for(B);
   p.tmem_cols = 512;
   p.zero = static_cast<uint4 *>(zero);
   p.zero_vec = (int64_t)(zero_bytes / 16);
-  const size_t smem =
-      1024 + (size_t)p.stages * (kTcTileRows * kTcK * 2 + p.a_tiles * kTcM * kTcK * 2) + kTcAux;
+  const size_t smem = kTcSmemBudget;
   const int64_t units = (a->n_rows + kTcUnit - 1) / kTcUnit;
   const int grid = (int)(units < sm_count() ? units : sm_count());
   cudaError_t e;
