@@ -16,9 +16,10 @@
 // Persistent CTAs, one per SM.  The rows are cut into 32-row units and each
 // CTA takes a contiguous, balanced range of units (so no SM does a whole
 // extra tile), walked in tiles of up to 256 rows.  Per CTA:
-//   warp 0      TMA producer: per pipeline stage the tile's x chunk
-//               [rows x 64 cols] (128-row boxes, 32-row boxes for a ragged
-//               tail) plus the W' chunk [128 units x 64] (128-byte swizzle);
+//   warps 0, 2  TMA producers: per pipeline stage KC K-chunks of the tile,
+//               x [rows x 64 cols] (boxes of 128, 64 and 32 rows; warp 2)
+//               and W' [128 units x 64] (warp 0, which also arms the
+//               stage), all with the 128-byte swizzle;
 //   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K = 16) per
 //               stage and 128-unit block into an fp32 accumulator of 256
 //               columns (double-buffered across tiles when TMEM holds two);
@@ -51,6 +52,7 @@ namespace tide {
 constexpr int kTcM = 128;         // router units per MMA (TMEM lanes)
 constexpr int kTcUnit = 32;       // rows per scheduling unit / small TMA box
 constexpr int kTcBigBox = 128;    // rows per large TMA box
+constexpr int kTcMidBox = 64;     // rows per middle TMA box
 constexpr int kTcTileUnits = 8;   // units per tile
 constexpr int kTcTileRows = kTcUnit * kTcTileUnits;  // MMA N
 constexpr int kTcK = 64;          // columns per chunk: 128 bytes of 16-bit data
@@ -129,6 +131,7 @@ template <bool BF16, bool LAYER>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_route_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_x_big,
+                    const __grid_constant__ CUtensorMap tmap_x_mid,
                     const __grid_constant__ CUtensorMap tmap_w, TcRouteParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -149,7 +152,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t *drain = stat_empty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  uint32_t *issued = reinterpret_cast<uint32_t *>(tmem_slot + 2);
+  uint32_t *issued = reinterpret_cast<uint32_t *>(tmem_slot + 2);    // stages armed (warp 0)
+  uint32_t *issued_x = reinterpret_cast<uint32_t *>(tmem_slot + 3);  // stages with x issued (warp 2)
   float *s_up = reinterpret_cast<float *>(tmem_slot + 4);  // [256], 0 beyond B
   float *s_cs = s_up + 256;
   float *s_bp = s_cs + 256;
@@ -174,11 +178,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
     *issued = 0;
+    *issued_x = 0;
     ptx::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&tmap_x);
     ptx::prefetch_tmap(&tmap_x_big);
+    ptx::prefetch_tmap(&tmap_x_mid);
     ptx::prefetch_tmap(&tmap_w);
   }
   if (warp == 1) {
@@ -219,17 +225,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int k_stages = k_chunks / KC;
 
   uint32_t tmem_base = 0;
-  if (warp != 0) {
-    // warps 1-15, while the producer already streams: per-unit vectors,
-    // this CTA's slice of the mover's workspace, zero padding of W' past B
-    const int t1 = threadIdx.x - 32;
+  // the setup group: warps 1 and 3-15 (warps 0 and 2 are the producers)
+  constexpr int kSetupThreads = kTcThreads - 64;
+  if (warp != 0 && warp != 2) {
+    // while the producers already stream: per-unit vectors, this CTA's
+    // slice of the mover's workspace, zero padding of W' past B
+    const int t1 = warp == 1 ? lane : threadIdx.x - 64;
     if (p.zero) {
       const int64_t per = (p.zero_vec + gridDim.x - 1) / gridDim.x;
       const int64_t z0 = (int64_t)blockIdx.x * per;
       const int64_t z1 = z0 + per < p.zero_vec ? z0 + per : p.zero_vec;
-      for (int64_t i = z0 + t1; i < z1; i += kTcThreads - 32) p.zero[i] = make_uint4(0, 0, 0, 0);
+      for (int64_t i = z0 + t1; i < z1; i += kSetupThreads) p.zero[i] = make_uint4(0, 0, 0, 0);
     }
-    for (int i = t1; i < 256; i += kTcThreads - 32) {
+    for (int i = t1; i < 256; i += kSetupThreads) {
       const bool in = i < p.B;
       s_up[i] = in ? p.up[i] : 0.f;
       s_cs[i] = in && p.colsum ? p.colsum[i] : 0.f;
@@ -243,23 +251,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           uint4 *w = reinterpret_cast<uint4 *>(ring + (size_t)s * stage_bytes + w_off +
                                                (size_t)c * wc_bytes + (size_t)p.w_rows * 128);
           const int n16 = (kTcM - p.w_rows) * 128 / 16;
-          for (int i = t1; i < n16; i += kTcThreads - 32) w[i] = make_uint4(0, 0, 0, 0);
+          for (int i = t1; i < n16; i += kSetupThreads) w[i] = make_uint4(0, 0, 0, 0);
         }
       ptx::fence_proxy_async();
     }
     ptx::tc_fence_before();
-    ptx::named_sync(2, kTcThreads - 32);
+    ptx::named_sync(2, kSetupThreads);
     ptx::tc_fence_after();
     tmem_base = *tmem_slot;
   }
 
-  if (warp == 0) {
-    // ------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------ TMA producers
+    // Issuing a copy holds the issuing thread for a fixed time, so two
+    // threads share each stage: warp 0 arms the stage for all its bytes and
+    // loads the W' chunks, warp 2 loads the x chunks (boxes of 128, 64 and
+    // 32 rows, at most three per chunk).  A copy may land before the stage
+    // is armed; the barrier's transaction count absorbs that.
     if (lane == 0) {
+      const bool arm = warp == 0;
       uint32_t it = 0;
       for (int64_t u0 = u_begin; u0 < u_end && !*abort_flag; u0 += kTcTileUnits) {
         const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
         const int n_big = nu / (kTcBigBox / kTcUnit);
+        const bool mid = (nu % (kTcBigBox / kTcUnit)) >= kTcMidBox / kTcUnit;
+        const int u_mid = n_big * (kTcBigBox / kTcUnit);                  // first unit of the 64-row box
+        const int u_small = u_mid + (mid ? kTcMidBox / kTcUnit : 0);      // first unit of the 32-row box
         for (int ks = 0; ks < k_stages; ++ks, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
           if (it >= (uint32_t)S && !ptx::mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
@@ -268,21 +285,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             break;
           }
           uint8_t *st = ring + (size_t)s * stage_bytes;
-          ptx::mbar_expect_tx(&full[s], (uint32_t)KC * ((uint32_t)nu * unit_bytes + w_load_bytes));
-          for (int c = 0; c < KC; ++c) {
-            const int col = (ks * KC + c) * kTcK;
-            uint8_t *xc = st + (size_t)c * x_bytes;
-            for (int a = 0; a < AT; ++a)
-              ptx::tma_load_2d(st + w_off + (size_t)c * wc_bytes + (size_t)a * w_tile_bytes, &tmap_w,
-                               &full[s], col, a * kTcM);
-            for (int j = 0; j < n_big; ++j)
-              ptx::tma_load_2d(xc + (size_t)j * (kTcBigBox / kTcUnit) * unit_bytes, &tmap_x_big,
-                               &full[s], col, (int)((u0 + j * (kTcBigBox / kTcUnit)) * kTcUnit));
-            for (int j = n_big * (kTcBigBox / kTcUnit); j < nu; ++j)
-              ptx::tma_load_2d(xc + (size_t)j * unit_bytes, &tmap_x, &full[s], col,
-                               (int)((u0 + j) * kTcUnit));
+          if (arm) {
+            ptx::mbar_expect_tx(&full[s], (uint32_t)KC * ((uint32_t)nu * unit_bytes + w_load_bytes));
+            for (int c = 0; c < KC; ++c)
+              for (int a = 0; a < AT; ++a)
+                ptx::tma_load_2d(st + w_off + (size_t)c * wc_bytes + (size_t)a * w_tile_bytes, &tmap_w,
+                                 &full[s], (ks * KC + c) * kTcK, a * kTcM);
+            *issued = it + 1;
+          } else {
+            for (int c = 0; c < KC; ++c) {
+              const int col = (ks * KC + c) * kTcK;
+              uint8_t *xc = st + (size_t)c * x_bytes;
+              for (int j = 0; j < n_big; ++j)
+                ptx::tma_load_2d(xc + (size_t)j * (kTcBigBox / kTcUnit) * unit_bytes, &tmap_x_big,
+                                 &full[s], col, (int)((u0 + j * (kTcBigBox / kTcUnit)) * kTcUnit));
+              if (mid)
+                ptx::tma_load_2d(xc + (size_t)u_mid * unit_bytes, &tmap_x_mid, &full[s], col,
+                                 (int)((u0 + u_mid) * kTcUnit));
+              if (u_small < nu)
+                ptx::tma_load_2d(xc + (size_t)u_small * unit_bytes, &tmap_x, &full[s], col,
+                                 (int)((u0 + u_small) * kTcUnit));
+            }
+            *issued_x = it + 1;
           }
-          *issued = it + 1;
         }
       }
     }
@@ -479,7 +504,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) {
     // drain the TMA loads still in flight before the CTA exits
-    const uint32_t n_issued = *issued;
+    // a stage either producer touched (the other may have stopped first:
+    // then its phase never completes and the bounded wait gives up)
+    const uint32_t n_issued = *issued > *issued_x ? *issued : *issued_x;
     volatile int never = 0;
     for (int s = 0; s < S; ++s) {
       if ((uint32_t)s >= n_issued) break;
@@ -568,9 +595,10 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   const bool bf16 = a->dtype == TIDE_DTYPE_BF16;
   const int B = (int)a->bottleneck_dim;
   const int w_rows = B < kTcM ? B : kTcM;
-  CUtensorMap tx, txb, tw;
+  CUtensorMap tx, txb, txm, tw;
   if (!make_tmap(&tx, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcUnit) ||
       !make_tmap(&txb, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcBigBox) ||
+      !make_tmap(&txm, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcMidBox) ||
       !make_tmap(&tw, a->folded, bf16, (uint64_t)B, (uint64_t)a->hidden_dim, (uint32_t)w_rows)) {
     snprintf(err, err_len, "tensor-core route: cuTensorMapEncodeTiled failed");
     return TIDE_ERR_CUDA;
@@ -628,11 +656,11 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (bf16)
-    e = layer ? cudaLaunchKernelEx(&cfg, tc_route_kernel<true, true>, tx, txb, tw, p)
-              : cudaLaunchKernelEx(&cfg, tc_route_kernel<true, false>, tx, txb, tw, p);
+    e = layer ? cudaLaunchKernelEx(&cfg, tc_route_kernel<true, true>, tx, txb, txm, tw, p)
+              : cudaLaunchKernelEx(&cfg, tc_route_kernel<true, false>, tx, txb, txm, tw, p);
   else
-    e = layer ? cudaLaunchKernelEx(&cfg, tc_route_kernel<false, true>, tx, txb, tw, p)
-              : cudaLaunchKernelEx(&cfg, tc_route_kernel<false, false>, tx, txb, tw, p);
+    e = layer ? cudaLaunchKernelEx(&cfg, tc_route_kernel<false, true>, tx, txb, txm, tw, p)
+              : cudaLaunchKernelEx(&cfg, tc_route_kernel<false, false>, tx, txb, txm, tw, p);
   if (e != cudaSuccess) {
     snprintf(err, err_len, "tensor-core route launch: %s", cudaGetErrorString(e));
     return TIDE_ERR_CUDA;
