@@ -99,13 +99,23 @@ __device__ __forceinline__ void fail(const MoveParams &p, const BulkSmem &m) {
 }
 
 template <typename T, bool LN>
-__global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams p, int NS) {
+__global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams p, int NS, int staged) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const uint32_t row_bytes = (uint32_t)(p.H * (int64_t)sizeof(T));
   uint8_t *slots = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   BulkSmem m = carve(slots + (size_t)NS * row_bytes, NS);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the final norm's weight (bit 0) and bias (bit 1) vectors, staged in
+  // shared memory when they fit beside the slots: an exit row reads the
+  // whole weight vector, which otherwise partly misses L1 under the slots
+  float *s_w = reinterpret_cast<float *>(slots + (size_t)NS * row_bytes + kAux);
+  float *s_b = s_w + ((staged & 1) ? p.H : 0);
+  // model weights, never written by the kernel this one overlaps with
+  for (int64_t i = threadIdx.x; i < p.H; i += kThreads) {
+    if (staged & 1) s_w[i] = p.w_norm[i];
+    if (staged & 2) s_b[i] = p.b_norm[i];
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -330,10 +340,13 @@ __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams 
               xr[u] = sv[i];
 #pragma unroll
               for (int j = 0; j < V / 4; ++j) {
-                w4[u][j] = __ldg(reinterpret_cast<const float4 *>(p.w_norm + i * V) + j);
+                w4[u][j] = (staged & 1) ? reinterpret_cast<const float4 *>(s_w + i * V)[j]
+                                        : __ldg(reinterpret_cast<const float4 *>(p.w_norm + i * V) + j);
                 if (LN)
-                  b4[LN ? u : 0][j] = p.b_norm ? __ldg(reinterpret_cast<const float4 *>(p.b_norm + i * V) + j)
-                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                  b4[LN ? u : 0][j] =
+                      (staged & 2) ? reinterpret_cast<const float4 *>(s_b + i * V)[j]
+                      : p.b_norm   ? __ldg(reinterpret_cast<const float4 *>(p.b_norm + i * V) + j)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
               }
             }
             if (!LN) {
@@ -413,7 +426,18 @@ template <typename T, bool LN>
 int launch_t(const MoveParams &p, cudaStream_t s) {
   const uint32_t row_bytes = (uint32_t)(p.H * (int64_t)sizeof(T));
   const int NS = slots_for(row_bytes);
-  const size_t smem = 128 + (size_t)NS * row_bytes + kAux;
+  size_t smem = 128 + (size_t)NS * row_bytes + kAux;
+  // stage the norm vectors in what the slots leave of the budget
+  int staged = 0;
+  const size_t vec_bytes = (size_t)p.H * sizeof(float);
+  if (p.row_stats && p.w_norm && smem + vec_bytes <= (size_t)kSmemBudget) {
+    staged |= 1;
+    smem += vec_bytes;
+    if (LN && p.b_norm && smem + vec_bytes <= (size_t)kSmemBudget) {
+      staged |= 2;
+      smem += vec_bytes;
+    }
+  }
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -436,7 +460,8 @@ int launch_t(const MoveParams &p, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, move_rows_bulk_kernel<T, LN>, p, NS) != cudaSuccess) return TIDE_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, move_rows_bulk_kernel<T, LN>, p, NS, staged) != cudaSuccess)
+    return TIDE_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? TIDE_OK : TIDE_ERR_CUDA;
 }
 
