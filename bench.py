@@ -206,7 +206,7 @@ class Workload:
         for k in range(len(LAYERS)):
             self.checkpoint(k, xs)
 
-    def capture(self, xs=None, per_checkpoint: bool = False):
+    def capture(self, xs=None, per_checkpoint: bool = False, calls: int = 1):
         """CUDA graphs of the sweep: one graph for the whole step (its kernels
         overlap their neighbours' prologues through programmatic dependent
         launch, kernel to kernel), or one graph per checkpoint.  The graphs
@@ -215,7 +215,8 @@ class Workload:
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
-            groups = [[k] for k in range(len(LAYERS))] if per_checkpoint else [list(range(len(LAYERS)))]
+            groups = ([[k] * calls for k in range(len(LAYERS))] if per_checkpoint
+                      else [list(range(len(LAYERS)))])
             for ks in groups:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=s):
@@ -225,6 +226,10 @@ class Workload:
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         return out
+
+
+# calls of one checkpoint per timing graph (the per-checkpoint roofline times)
+CK_CALLS = 8
 
 
 def launches_per_checkpoint(path_used: int) -> int:
@@ -372,7 +377,7 @@ def main():
     wl.runner.check_errors()
 
     step_graph = wl.capture()[0]
-    ck_graphs = wl.capture(per_checkpoint=True)
+    ck_graphs = wl.capture(per_checkpoint=True, calls=CK_CALLS)
     for _ in range(2):
         step_graph.replay()
         for g in ck_graphs:
@@ -391,7 +396,9 @@ def main():
         t_end.record()
         torch.cuda.synchronize()
         # per-launch device time of each checkpoint's kernels (the roofline's
-        # denominator): its own graph, CUDA events around every replay
+        # denominator): a graph of CK_CALLS back-to-back calls of that
+        # checkpoint (each launch overlaps the previous one's tail, as in the
+        # step), CUDA events around every replay
         reps = max(3, min(args.steps, 50))
         ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in LAYERS] for _ in range(reps)]
@@ -402,7 +409,7 @@ def main():
                 ev[i][k][1].record()
         torch.cuda.synchronize()
     elapsed = t_start.elapsed_time(t_end) / 1000.0
-    per_ck = [sum(ev[i][k][0].elapsed_time(ev[i][k][1]) for i in range(reps)) / reps
+    per_ck = [sum(ev[i][k][0].elapsed_time(ev[i][k][1]) for i in range(reps)) / (reps * CK_CALLS)
               for k in range(len(LAYERS))]
     del ev
     barrier(world)
@@ -437,6 +444,7 @@ def main():
                 "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
                 "kernel": f"checkpoint 0 ({ROWS} rows x {HIDDEN}), both kernels of the call",
                 "per_checkpoint_ms": per_ck, "per_checkpoint_reps": reps,
+                "per_checkpoint_calls_per_graph": CK_CALLS,
                 "achieved_all_checkpoints": achieved_all, "algorithmic_bytes_per_step": sum(alg)}
 
     # e2e through the public operator with host buffers: H2D of the step's

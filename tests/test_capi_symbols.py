@@ -97,7 +97,7 @@ def test_operators_have_no_cpu_kernel():
 
 
 def test_path_selection():
-    """bf16/fp16 with folded weights: up to 6144 rows the fused single-pass
+    """bf16/fp16 with folded weights: up to 3584 rows the fused single-pass
     kernel when the router is 128 wide and a weight slice of H stays
     resident; above that, or when the fused kernel does not apply, the
     tensor-core split path (H % 64 == 0, B <= 256); fp32 and other shapes to
@@ -112,8 +112,9 @@ def test_path_selection():
         a = capi.CheckpointArgs(**base)
         return lib.tide_checkpoint_select_path(ctypes.byref(a))
 
-    assert sel() == capi.PATH_TC                               # up to 6144 rows: fused single pass
-    assert sel(n_rows=6145, n_total=6145) == capi.PATH_TC_SPLIT
+    assert sel() == capi.PATH_TC                               # up to 3584 rows: fused single pass
+    assert sel(n_rows=3584, n_total=3584) == capi.PATH_TC
+    assert sel(n_rows=3585, n_total=3585) == capi.PATH_TC_SPLIT
     assert sel(n_rows=32768, n_total=32768) == capi.PATH_TC_SPLIT
     assert sel(dtype=capi.DTYPE_F16) == capi.PATH_TC
     assert sel(n_rows=32768, n_total=32768, dtype=capi.DTYPE_F16) == capi.PATH_TC_SPLIT

@@ -305,11 +305,12 @@ int tide_checkpoint_select_path(const tide_checkpoint_args *a) {
          tide::tc_unsupported_reason(a));
     return -TIDE_ERR_UNSUPPORTED;
   }
-  // automatic choice, from measured latencies at H = 4096 bf16: up to ~6K
-  // rows the fused single pass (one launch, ~20 us at 256 rows) beats the
-  // split path, whose router streams all of W' through each of its few CTAs
-  // (~50 us floor); above that the split path wins.  SIMT otherwise.
-  constexpr int64_t kFusedAutoMaxRows = 6144;
+  // automatic choice, from measured latencies at H = 4096 bf16 (10 % and
+  // 50 % exits): up to 3072 rows the fused single pass (one launch, ~21 us
+  // at 256 rows, 40 us at 3072) beats the split path (38-46 us there, its
+  // router streams all of W' through each CTA); from 4096 rows on the split
+  // path wins.  SIMT otherwise.
+  constexpr int64_t kFusedAutoMaxRows = 3584;
   if (a->n_rows <= kFusedAutoMaxRows && tide::fused_supported(a)) return TIDE_PATH_TC;
   if (tide::tc_supported(a)) return TIDE_PATH_TC_SPLIT;
   if (tide::fused_supported(a)) return TIDE_PATH_TC;

@@ -5,14 +5,11 @@
 // A thread-block cluster of C CTAs works on 64-row tiles; CTA c owns the
 // hidden columns [c*H/C, (c+1)*H/C) (its K slice).  Each CTA keeps its slice of
 // the folded router weights W' = down * norm_weight ([128 x H/C], model dtype)
-// resident in tensor memory for the whole launch (the MMA's A operand: lane =
-// router unit, each 32-bit column two consecutive K elements, written once
-// with tcgen05.st), streams its slice of every tile through a TMA ring and
-// computes the transposed partial GEMM
+// resident in shared memory for the whole launch, streams its slice of every
+// tile through a TMA ring and computes the transposed partial GEMM
 //     D_c[b, r] = sum_{k in slice c} W'[b, k] * x[r, k]
-// on the tensor cores (tcgen05.mma with A in TMEM, M = 128 router units, N =
-// 64 rows, fp32 in TMEM).  Partial sums of x^2 (and x) come from the same
-// shared-memory tiles.
+// on the tensor cores (tcgen05.mma, M = 128 router units, N = 64 rows, fp32 in
+// TMEM).  Partial sums of x^2 (and x) come from the same shared-memory tiles.
 // The C partials are reduced in a fixed order by the CTA that owns each group
 // of 64/C rows.  They travel through an L2-resident exchange area of the
 // workspace (coalesced 128-byte stores and L2-only loads, double-buffered per
@@ -60,8 +57,7 @@ constexpr int kChunk = 64;       // columns per chunk (128 bytes of 16-bit data)
 constexpr int kThreads = 512;
 constexpr int kStages = 10;
 constexpr int kMaxSliceChunks = 8;  // W' slice <= 8 chunks = 128 KB
-constexpr uint32_t kTmemCols = 512;  // two 64-column fp32 accumulators + W' slice
-constexpr uint32_t kTmemW = 256;     // first TMEM column of the resident W' slice
+constexpr uint32_t kTmemCols = 128;  // two 64-column fp32 accumulators
 constexpr int kSmemBudget = 227 * 1024;
 
 struct Params {
@@ -74,7 +70,6 @@ struct Params {
   const void *x;
   const int64_t *pos_in;
   const int32_t *slot_in;
-  const void *w_folded;  // W' [128 x H], model dtype
   void *out_buf;
   int64_t n_total;
   void *compact_out;
@@ -103,7 +98,7 @@ struct Layout {
 __host__ __device__ inline Layout layout(int slice_chunks, int C) {
   Layout L;
   uint32_t o = 0;
-  L.w = o;                                                           // (W' lives in TMEM)
+  L.w = o;       o += (uint32_t)slice_chunks * kUnits * kChunk * 2;  // resident W' slice
   L.ring = o;    o += (uint32_t)kStages * kRows * kChunk * 2;        // x chunks
   L.slots = o;   o += 0;                                             // (exchange is in L2)
   L.slot_ss = o; o += 0;
@@ -223,6 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_clusters = gridDim.x / C;
   const int slice = p.slice, nk = p.slice_chunks;
   const uint32_t chunk_bytes = kRows * kChunk * 2;      // 8 KB
+  const uint32_t wchunk_bytes = kUnits * kChunk * 2;    // 16 KB
 
   int64_t n = p.n_cap;
   if (p.n_dev) {
@@ -241,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(&bars[kFull + s], 1);
       ptx::mbar_init(&bars[kEmpty + s], 1 + 4);  // MMA commit + 4 statistics warps
     }
-    ptx::mbar_init(&bars[kWFull], 4);  // the four warps that write W' into TMEM
+    ptx::mbar_init(&bars[kWFull], 1);
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&bars[kAccFull + a], 1);
       ptx::mbar_init(&bars[kAccEmpty + a], 4);
@@ -293,6 +289,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       ptx::prefetch_tmap(&tmap_x);
+      ptx::prefetch_tmap(&tmap_w);
+      ptx::mbar_expect_tx(&bars[kWFull], (uint32_t)nk * wchunk_bytes);
+      for (int kc = 0; kc < nk; ++kc)
+        ptx::tma_load_2d(smem + L.w + (size_t)kc * wchunk_bytes, &tmap_w, &bars[kWFull],
+                         col0 + kc * kChunk, 0);
       uint32_t it = 0;
       for (int tile = cluster_id; tile < n_tiles && !*abort_flag; tile += n_clusters) {
         for (int kc = 0; kc < nk; ++kc, ++it) {
@@ -316,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = ptx::mbar_wait(&bars[kWFull], 0, abort_flag);
       uint32_t it = 0;
       int t_local = 0;
-      const uint32_t w_tmem = tmem_base + kTmemW;
+      const uint32_t w_base = ptx::smem_u32(smem + L.w);
       for (int tile = cluster_id; ok && tile < n_tiles && !*abort_flag;
            tile += n_clusters, ++t_local) {
         const int acc = t_local & 1;
@@ -331,10 +332,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
           if (!ptx::mbar_wait(&bars[kFull + s], ph, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
+          const uint32_t a0 = w_base + (uint32_t)kc * wchunk_bytes;
           const uint32_t b0 = ptx::smem_u32(smem + L.ring + (size_t)s * chunk_bytes);
 #pragma unroll
           for (int k = 0; k < kChunk / 16; ++k)
-            ptx::mma_f16_ts(d_tmem, w_tmem + (uint32_t)(kc * (kChunk / 2) + k * 8),
+            ptx::mma_f16_ss(d_tmem, ptx::sw128_kmajor_desc(a0 + 32u * k),
                             ptx::sw128_kmajor_desc(b0 + 32u * k), idesc,
                             (kc > 0 || k > 0) ? 1u : 0u);
           ptx::mma_commit(&bars[kEmpty + s]);
@@ -402,32 +404,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the group stops together at the iteration's end (s_stop1).
     const int t = threadIdx.x - 256;   // 0..127 = router unit b = TMEM lane
     const int q = warp & 3;            // TMEM lane quarter of this warp
-    {
-      // this CTA's W' slice into TMEM (the MMA's A operand): lane = unit,
-      // 32-bit column j = elements 2j, 2j+1 of the slice, as in memory
-      const uint4 *wsrc = reinterpret_cast<const uint4 *>(
-          static_cast<const T *>(p.w_folded) + (size_t)t * p.H + col0);
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + kTmemW;
-      // 16 loads (256 bytes of the unit's slice) in flight before each batch
-      // of stores
-      for (int j0 = 0; j0 < slice / 16; j0 += 8) {
-        uint4 ld[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (j0 * 2 + i < slice / 8) ld[i] = __ldg(wsrc + j0 * 2 + i);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if (j0 + i >= slice / 16) break;
-          const uint32_t v[8] = {ld[2 * i].x, ld[2 * i].y, ld[2 * i].z, ld[2 * i].w,
-                                 ld[2 * i + 1].x, ld[2 * i + 1].y, ld[2 * i + 1].z, ld[2 * i + 1].w};
-          ptx::tmem_st8(taddr + (uint32_t)((j0 + i) * 8), v);
-        }
-      }
-      ptx::tmem_st_wait();
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&bars[kWFull]);
-    }
     float *xP = p.xchg + (size_t)cluster_id * (size_t)p.xchg_stride;
     float *xS = xP + 2 * C * kRows * kUnits;
     float4 *xI = reinterpret_cast<float4 *>(xS + 2 * C * kRows * 2);
@@ -706,6 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // drain the TMA loads still in flight before the CTA can leave
     const uint32_t n_issued = *issued;
     volatile int never = 0;
+    ptx::mbar_wait(&bars[kWFull], 0, &never);
     for (int s = 0; s < kStages; ++s) {
       if ((uint32_t)s >= n_issued) break;
       const uint32_t count = (n_issued - (uint32_t)s + (uint32_t)kStages - 1) / (uint32_t)kStages;
@@ -842,7 +819,6 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
   p.x = a->x;
   p.pos_in = a->positions_in;
   p.slot_in = a->slots_in;
-  p.w_folded = a->folded;
   p.out_buf = a->out_buffer;
   p.n_total = a->n_total;
   p.compact_out = a->compact_out;
