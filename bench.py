@@ -62,7 +62,7 @@ ROWS, HIDDEN, BOTTLENECK = WORKLOADS[WORKLOAD]["rows"], 4096, 128
 # DRAM bytes (read + write) of checkpoint 0's two kernels (router + mover),
 # 32768 rows x 4096 bf16, from the warm-cache ncu launch list of this
 # benchmark (profiles/launches__llama8b_prefill_checkpoints.md).
-NCU_TRAFFIC_CKPT0 = {"rows": 32768, "path": "tc_split", "bytes": (269.5 + 63.0 + 221.3 + 208.8) * 1e6}
+NCU_TRAFFIC_CKPT0 = {"rows": 32768, "path": "tc_split", "bytes": (269.5 + 63.3 + 221.3 + 209.0) * 1e6}
 
 
 def algorithmic_bytes(n: int, exits: int, h: int, e: int) -> int:
