@@ -6,6 +6,8 @@ decisions identical except for rows whose oracle score lies within that
 tolerance of the threshold; final-normed exit rows within 1 ulp of the
 storage dtype (bf16/fp16) or 8 ulp (fp32, ~1e-6 relative: the row
 statistics are sums whose order differs from the reference's)."""
+import types
+
 import numpy as np
 import pytest
 import torch
@@ -331,6 +333,45 @@ def test_split_router_widths(B):
         res = O.checkpoint(storage_np(x), dt, norm, w["down"].numpy(), w["up"].numpy(), bias, THR)
         res["eps"] = 1e-5
         check_against_oracle(ck, res, dtype, kind, 1e-2, out_ref=np.zeros_like(storage_np(out)))
+
+
+@pytest.mark.parametrize("units", [1, 2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("device_count", [False, True])
+def test_split_router_tile_geometry(units, device_count):
+    """The split router sizes its pipeline from the live row count: the
+    largest CTA tile (1-8 units of 32 rows, also the MMA's N), the K chunks
+    per stage and the 128/64/32-row boxes follow from it.  Row counts that
+    give every tile size on this GPU, ragged last units, and a live count on
+    the device below the launch capacity; parity with the oracle."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    H = 1024
+    n_cap = sms * 32 * units
+    n = n_cap - 17 if device_count else n_cap - 5
+    w = workloads.rows(n_cap, H, torch.bfloat16, seed=900 + units, unit_norm_weight=False)
+    x = w["x"].to(DEV)
+    nw, nb = norm_tensors(w, torch.bfloat16)
+    norm = oracle_norm("rms", nw, nb, 1e-5)
+    x_live = storage_np(x)[:n]
+    z = O.router_logits(O.final_norm(O.to_f32(x_live, O.BF16), norm), w["down"].numpy(), w["up"].numpy())
+    bias = workloads.bias_for_exit_fraction(z, 0.2, THR)
+    out = torch.zeros_like(x)
+    if device_count:
+        cnt = torch.tensor([n], dtype=torch.int32, device=DEV)
+        ck = Checkpoint(x, "rms", nw, nb, 1e-5, w["down"].to(DEV), w["up"].to(DEV), bias, THR,
+                        out_buffer=out, n_rows_dev=cnt, path=capi.PATH_TC_SPLIT)
+    else:
+        ck = Checkpoint(x[:n], "rms", nw, nb, 1e-5, w["down"].to(DEV), w["up"].to(DEV), bias, THR,
+                        out_buffer=out, n_total=n_cap, path=capi.PATH_TC_SPLIT)
+    assert ck.path() == capi.PATH_TC_SPLIT
+    ck()
+    res = O.checkpoint(x_live, O.BF16, norm, w["down"].numpy(), w["up"].numpy(), bias, THR)
+    res["eps"] = 1e-5
+    live = types.SimpleNamespace(
+        x=ck.x[:n], scores_out=ck.scores_out[:n], counts=ck.counts, error_word=ck.error_word,
+        positions=None, slots=None, positions_out=ck.positions_out,
+        exit_positions_out=ck.exit_positions_out, compact_out=ck.compact_out, out_buffer=out,
+        norm_w=ck.norm_w, norm_b=ck.norm_b)
+    check_against_oracle(live, res, torch.bfloat16, "rms", 1e-2)
 
 
 @pytest.mark.parametrize("path", [capi.PATH_TC, capi.PATH_TC_SPLIT, capi.PATH_SIMT])
