@@ -16,9 +16,12 @@
 //               runs the decoupled look-back (Merrill & Garland 2016) for the
 //               tile's exclusive prefix, then writes the positions / slots /
 //               exit positions of the tile's rows itself;
-//   warp 1      loader: one bulk load per row that has data to move, into
+//   warps 1, 10 loaders: one bulk load per row that has data to move, into
 //               the ring of row slots, as soon as the tile's rows are known
-//               (before its prefix is);
+//               (before its prefix is); warp 1 issues the even slot
+//               sequence numbers, warp 10 the odd ones (issuing a copy holds
+//               the issuing thread for ~0.3 us, which at 4 KB rows would cap
+//               one loader near 2 TB/s);
 //   warps 2-9   movers: slot q belongs to mover q % 8; a survivor is stored
 //               with one bulk store to compact_out[prefix + rank]; an exit is
 //               normed from shared memory by the warp and written with
@@ -26,8 +29,9 @@
 //               stores reading their slots while it goes on and frees them
 //               oldest first, at the latest before it waits for sequence q:
 //               then every slot of sequence <= q - slots is free, which is
-//               the one the loader needs for q, so the loader never waits on
-//               a slot whose mover is waiting on the loader.
+//               the one a loader needs for q, so a loader never waits on a
+//               slot whose mover is waiting on it (each mover's sequence
+//               numbers share one parity: it is fed by one loader).
 // Every wait is bounded; on expiry the kernel sets TIDE_DEVERR_TIMEOUT, stops
 // all roles, waits for its own loads in flight and returns.  Launched as a
 // programmatic dependent of the router: the barriers are set up before
@@ -40,8 +44,9 @@ namespace tide {
 namespace {
 
 constexpr int kTileRows = 32;
-constexpr int kMovers = 8;
-constexpr int kThreads = 32 * (2 + kMovers);
+constexpr int kMovers = 8;   // even: the slot sequence q of mover q % 8 has one parity
+constexpr int kLoaders = 2;  // loader of slot sequence q: q % 2
+constexpr int kThreads = 32 * (2 + kMovers + 1);
 constexpr int kTiles = 4;       // tile descriptors in flight
 constexpr int kMaxSlots = 64;
 constexpr int kSmemBudget = 227 * 1024;
@@ -75,7 +80,7 @@ struct BulkSmem {
   SlotDesc *sdesc;                          // [slots]
   TileDesc *td;                             // [kTiles]
   volatile int *abort_flag;
-  uint32_t *issued;                         // bulk loads + end markers issued
+  uint32_t *issued;                         // [2] next slot sequence of each loader
 };
 
 __device__ __forceinline__ BulkSmem carve(uint8_t *aux, int NS) {
@@ -89,7 +94,7 @@ __device__ __forceinline__ BulkSmem carve(uint8_t *aux, int NS) {
   m.sdesc = reinterpret_cast<SlotDesc *>(m.td_free + kTiles);
   m.td = reinterpret_cast<TileDesc *>(m.sdesc + kMaxSlots);
   m.abort_flag = reinterpret_cast<volatile int *>(m.td + kTiles);
-  m.issued = reinterpret_cast<uint32_t *>(m.td + kTiles) + 1;
+  m.issued = reinterpret_cast<uint32_t *>(m.td + kTiles) + 1;  // two words
   return m;
 }
 
@@ -125,10 +130,11 @@ __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams 
     for (int e = 0; e < kTiles; ++e) {
       ptx::mbar_init(&m.td_rows[e], 1);
       ptx::mbar_init(&m.td_prefix[e], 1);
-      ptx::mbar_init(&m.td_free[e], 2);  // loader done with it + last row moved
+      ptx::mbar_init(&m.td_free[e], kLoaders + 1);  // both loaders done with it + last row moved
     }
     *m.abort_flag = 0;
-    *m.issued = 0;
+    m.issued[0] = 0;
+    m.issued[1] = 0;
     ptx::fence_mbar_init();
     ptx::fence_proxy_async();
   }
@@ -229,9 +235,12 @@ __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams 
         if (p.num_remaining) p.num_remaining[0] = (int32_t)kt;
       }
     }
-  } else if (warp == 1) {
-    // --------------------------------------------------------------- loader
+  } else if (warp == 1 || warp == 2 + kMovers) {
+    // -------------------------------------------------------------- loaders
+    // Both walk every tile's rows in order, numbering them q; loader `par`
+    // issues the rows with q % 2 == par.
     if (lane == 0) {
+      const uint32_t par = warp == 1 ? 0u : 1u;
       uint32_t q = 0;
       bool ok = true;
       for (uint32_t k = 0; ok; ++k) {
@@ -243,9 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams 
         uint32_t mm = d.move_mask;
         const int64_t row0 = d.row0;
         const uint32_t n_move = d.n_move;
-        while (mm) {
+        for (; mm; ++q) {
           const int r = __ffs(mm) - 1;
           mm &= mm - 1u;
+          if ((q & 1u) != par) continue;
           const int s = (int)(q % (uint32_t)NS);
           if (q >= (uint32_t)NS && !ptx::mbar_wait(&m.empty[s], ((q / NS) & 1u) ^ 1u, m.abort_flag)) {
             ok = false;
@@ -255,14 +265,15 @@ __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams 
           ptx::mbar_expect_tx(&m.full[s], row_bytes);
           ptx::bulk_load(slots + (size_t)s * row_bytes, x + (row0 + r) * p.H, row_bytes, &m.full[s],
                          pol);
-          *m.issued = ++q;
+          m.issued[par] = q + 1;
         }
         if (!ok) break;
         ptx::mbar_arrive(&m.td_free[e]);
-        if (n_move == 0) ptx::mbar_arrive(&m.td_free[e]);
+        if (n_move == 0 && par == 0) ptx::mbar_arrive(&m.td_free[e]);  // no row to move: stands in for the last one
       }
       // one end marker per mover
-      for (int i = 0; ok && i < kMovers; ++i) {
+      for (int i = 0; ok && i < kMovers; ++i, ++q) {
+        if ((q & 1u) != par) continue;
         const int s = (int)(q % (uint32_t)NS);
         if (q >= (uint32_t)NS && !ptx::mbar_wait(&m.empty[s], ((q / NS) & 1u) ^ 1u, m.abort_flag)) {
           ok = false;
@@ -270,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams 
         }
         m.sdesc[s] = SlotDesc{0, 0, 0, 1};
         ptx::mbar_arrive(&m.full[s]);
-        *m.issued = ++q;
+        m.issued[par] = q + 1;
       }
       if (!ok) fail(p, m);
     }
@@ -399,12 +410,21 @@ __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams 
 
   __syncthreads();
   if (threadIdx.x == 32 && *m.abort_flag) {
-    // wait for every bulk load this CTA issued before its shared memory goes
-    const uint32_t total = *m.issued;
+    // wait for every bulk load this CTA issued before its shared memory goes:
+    // per slot, the latest use q that its loader issued (loader q % 2 has
+    // issued every q of its parity below issued[q % 2]; the loaders are
+    // never more than a ring apart)
+    const uint32_t next[2] = {m.issued[0], m.issued[1]};
+    const uint32_t total = next[0] > next[1] ? next[0] : next[1];
     volatile int never = 0;
     for (int s = 0; s < NS && (uint32_t)s < total; ++s) {
-      const uint32_t uses = (total - (uint32_t)s + (uint32_t)NS - 1) / (uint32_t)NS;
-      ptx::mbar_wait(&m.full[s], (uses - 1) & 1u, &never);
+      int64_t q = (int64_t)s + (int64_t)((total - 1u - (uint32_t)s) / (uint32_t)NS) * NS;
+      for (; q >= 0; q -= NS) {
+        if ((uint64_t)q < next[q & 1]) {
+          ptx::mbar_wait(&m.full[s], (uint32_t)(q / NS) & 1u, &never);
+          break;
+        }
+      }
     }
   }
 }
