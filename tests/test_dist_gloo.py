@@ -59,12 +59,15 @@ def _put_and_exit(q, item) -> None:
     os._exit(0)
 
 
-def _dead_peer(rank: int, world: int, port: int, q) -> None:
+def _dead_peer(rank: int, world: int, port: int, q, ready) -> None:
     _env(rank, world, port)
     import torch.distributed as dist
 
     from tide_b200 import dist as td
 
+    # both ranks have imported torch before the short-timeout rendezvous (a
+    # cold first import can take far longer than the 3 s timeout)
+    ready.wait(timeout=300)
     w, r, _ = td.init("gloo", timeout_s=3)
     if r == 1:
         # leaves between steps, never joins the next collective
@@ -78,11 +81,12 @@ def _dead_peer(rank: int, world: int, port: int, q) -> None:
     _put_and_exit(q, item)
 
 
-def _run(target, world=2, timeout=120):
+def _run(target, world=2, timeout=120, sync=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    extra = (ctx.Barrier(world),) if sync else ()
+    ps = [ctx.Process(target=target, args=(r, world, port, q) + extra) for r in range(world)]
     for p in ps:
         p.start()
     res = []
@@ -116,7 +120,7 @@ def test_two_rank_collectives():
 
 
 def test_rank_that_never_joins_is_detected():
-    res, _ = _run(_dead_peer, timeout=90)
+    res, _ = _run(_dead_peer, timeout=400, sync=True)
     r0 = [d for d in res if d["rank"] == 0]
     assert r0 and r0[0]["raised"], res
     assert r0[0]["after_s"] < 60
