@@ -429,6 +429,11 @@ __global__ void __launch_bounds__(kThreads, 1) move_rows_bulk_kernel(MoveParams 
   }
 }
 
+// The slot count is a multiple of kMovers, so every use of a slot belongs to
+// the same mover (q % kMovers is fixed by q % slots) and comes after its
+// previous use.  The waits on a slot are by phase parity, which cannot tell
+// the phase before the last from the next one: a second mover could wait on
+// a slot's next use while its current load is in flight and read it early.
 int slots_for(uint32_t row_bytes) {
   int s = (int)((kSmemBudget - 128 - kAux) / row_bytes);
   if (s > kMaxSlots) s = kMaxSlots;
