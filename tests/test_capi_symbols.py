@@ -97,7 +97,8 @@ def test_operators_have_no_cpu_kernel():
 
 
 def test_path_selection():
-    """bf16/fp16 with folded weights: up to 3584 rows the fused single-pass
+    """bf16/fp16 with folded weights: up to 3584 rows (H <= 4096; 2560 at
+    H = 5120, 5120 at H = 8192) the fused single-pass
     kernel when the router is 128 wide and a weight slice of H stays
     resident; above that, or when the fused kernel does not apply, the
     tensor-core split path (H % 64 == 0, B <= 256); fp32 and other shapes to
@@ -123,7 +124,13 @@ def test_path_selection():
     assert sel(hidden_dim=4000) == capi.PATH_SIMT
     assert sel(bottleneck_dim=48) == capi.PATH_TC_SPLIT       # units padded to 128 (fused: 128 only)
     assert sel(bottleneck_dim=64) == capi.PATH_TC_SPLIT       # fused kernel: 128 units only
-    assert sel(hidden_dim=8192, path=capi.PATH_TC) == capi.PATH_TC_SPLIT  # slice too large to stay resident
+    assert sel(hidden_dim=8192, path=capi.PATH_TC) == capi.PATH_TC        # 16-CTA clusters, 8-chunk slices
+    assert sel(hidden_dim=5120) == capi.PATH_TC                              # 16-CTA clusters, 5-chunk slices
+    assert sel(hidden_dim=5120, n_rows=2560, n_total=2560) == capi.PATH_TC
+    assert sel(hidden_dim=5120, n_rows=2561, n_total=2561) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=8192, n_rows=5120, n_total=5120) == capi.PATH_TC
+    assert sel(hidden_dim=8192, n_rows=5121, n_total=5121) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=16384, path=capi.PATH_TC) == capi.PATH_TC_SPLIT  # slice too large to stay resident
     assert sel(hidden_dim=768, path=capi.PATH_TC) == capi.PATH_TC   # cluster of 2
     assert sel(path=capi.PATH_TC_SPLIT) == capi.PATH_TC_SPLIT
     assert sel(folded=None) == capi.PATH_SIMT

@@ -279,10 +279,11 @@ def test_bad_exit_position_is_flagged_not_written():
     assert ck.counts.cpu().tolist() == [0, n]
 
 
-@pytest.mark.parametrize("H", [256, 512, 768, 1024, 2048, 4096])
+@pytest.mark.parametrize("H", [256, 512, 768, 1024, 2048, 4096, 5120, 8192])
 def test_fused_cluster_sizes(H):
     """The fused kernel at every cluster size it uses (H 256/512 -> 1 CTA,
-    768/1024 -> 2, 2048 -> 4, 4096 -> 8), RMSNorm and LayerNorm."""
+    768/1024 -> 2, 2048 -> 4, 4096 -> 8, 5120/8192 -> 16, a non-portable
+    cluster size), RMSNorm and LayerNorm."""
     dtype = torch.bfloat16
     n = 3000
     for kind in ("rms", "layer"):

@@ -305,13 +305,13 @@ int tide_checkpoint_select_path(const tide_checkpoint_args *a) {
          tide::tc_unsupported_reason(a));
     return -TIDE_ERR_UNSUPPORTED;
   }
-  // automatic choice, from measured latencies at H = 4096 bf16 (10 % and
-  // 50 % exits): up to 3072 rows the fused single pass (one launch, ~21 us
-  // at 256 rows, 40 us at 3072) beats the split path (38-46 us there, its
-  // router streams all of W' through each CTA); from 4096 rows on the split
-  // path wins.  SIMT otherwise.
-  constexpr int64_t kFusedAutoMaxRows = 3584;
-  if (a->n_rows <= kFusedAutoMaxRows && tide::fused_supported(a)) return TIDE_PATH_TC;
+  // automatic choice, from measured latencies: the fused single pass (one
+  // launch, ~21 us at 256 rows) up to a row count that depends on the hidden
+  // size (3584 rows at H <= 4096), the split path above it (its router
+  // streams all of W' through each CTA, a floor of ~38 us at H = 4096).
+  // SIMT otherwise.
+  if (a->n_rows <= tide::fused_auto_max_rows(a->hidden_dim) && tide::fused_supported(a))
+    return TIDE_PATH_TC;
   if (tide::tc_supported(a)) return TIDE_PATH_TC_SPLIT;
   if (tide::fused_supported(a)) return TIDE_PATH_TC;
   return TIDE_PATH_SIMT;
@@ -333,7 +333,13 @@ int tide_checkpoint(const tide_checkpoint_args *a, tide_stream_t stream) {
     return fail(TIDE_ERR_WORKSPACE, "tide_checkpoint: workspace needs %zu bytes, got %zu",
                 tide_checkpoint_workspace_size(a), a->workspace_bytes);
   cudaStream_t s = (cudaStream_t)stream;
-  if (path == TIDE_PATH_TC) return tide::fused_checkpoint_launch(a, s, g_err, sizeof(g_err));
+  if (path == TIDE_PATH_TC) {
+    const int rc = tide::fused_checkpoint_launch(a, s, g_err, sizeof(g_err));
+    // a device that cannot hold one cluster of the size this hidden_dim
+    // needs: the automatic choice falls back to the split path
+    if (!(rc == TIDE_ERR_UNSUPPORTED && a->path == TIDE_PATH_AUTO && tide::tc_supported(a))) return rc;
+    path = TIDE_PATH_TC_SPLIT;
+  }
 
   SimtWs w = simt_ws(a->workspace, n);
   float *scores = a->scores_out ? a->scores_out : w.scores;

@@ -18,6 +18,9 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
 
 // Single-pass fused cluster kernel (tc_fused.cu).
 bool fused_supported(const tide_checkpoint_args *a);
+// Largest row count for which the automatic path choice takes the fused
+// single pass at this hidden size (0: the fused kernel does not apply).
+int64_t fused_auto_max_rows(int64_t H);
 const char *fused_unsupported_reason(const tide_checkpoint_args *a);
 size_t fused_workspace_bytes(const tide_checkpoint_args *a);
 int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t s, char *err, size_t err_len);

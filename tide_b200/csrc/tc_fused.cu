@@ -728,10 +728,13 @@ bool fused_tmap(CUtensorMap *m, const void *base, bool bf16, uint64_t rows, uint
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Cluster size: the smallest C in {1, 2, 4, 8} whose K slice is a multiple
-// of 64 columns and whose W' slice fits the resident budget.
+// Cluster size: the smallest C in {1, 2, 4, 8, 16} whose K slice is a
+// multiple of 64 columns and whose W' slice fits the resident budget.  16 is
+// a non-portable cluster size (opted into per kernel); it lets H = 5120 and
+// 8192 keep a resident slice.
+constexpr int kMaxCluster = 16;
 int fused_cluster_size(int64_t H) {
-  for (int c = 1; c <= 8; c <<= 1) {
+  for (int c = 1; c <= kMaxCluster; c <<= 1) {
     if (H % c) continue;
     const int64_t slice = H / c;
     if (slice % fused::kChunk) continue;
@@ -764,6 +767,19 @@ const char *fused_unsupported_reason(const tide_checkpoint_args *a) {
 }
 
 bool fused_supported(const tide_checkpoint_args *a) { return fused_unsupported_reason(a) == nullptr; }
+
+// Measured crossovers against the split path (bf16, 10 % and 50 % exits):
+// with clusters of at most 8 CTAs (H <= 4096) the fused pass wins up to
+// 3072 rows and loses from 4096 on.  16-CTA clusters are fewer on the GPU:
+// at H = 5120 the fused pass wins up to 2048 rows and loses from 3072; at
+// H = 8192, where the split router streams 2 MiB of W' through each CTA, it
+// wins up to 4096 rows and loses from 6144.
+int64_t fused_auto_max_rows(int64_t H) {
+  const int C = fused_cluster_size(H);
+  if (C == 0) return 0;
+  if (C <= 8) return 3584;
+  return H >= 8192 ? 5120 : 2560;
+}
 
 // Workspace: 256 reserved bytes, the tile status words (zeroed per call),
 // then one exchange area per cluster that can be resident on any B200
@@ -837,15 +853,17 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
     case 1: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 1> : (const void *)fused::fused_checkpoint_kernel<false, 1>; break;
     case 2: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 2> : (const void *)fused::fused_checkpoint_kernel<false, 2>; break;
     case 4: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 4> : (const void *)fused::fused_checkpoint_kernel<false, 4>; break;
-    default: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 8> : (const void *)fused::fused_checkpoint_kernel<false, 8>; break;
+    case 8: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 8> : (const void *)fused::fused_checkpoint_kernel<false, 8>; break;
+    default: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 16> : (const void *)fused::fused_checkpoint_kernel<false, 16>; break;
   }
-  // per device: the attribute and the occupancy belong to a device's context
+  // per device: the attributes and the occupancy belong to a device's context
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  static bool attr_set[64][2][9] = {};
+  static bool attr_set[64][2][kMaxCluster + 1] = {};
   if (!attr_set[dev][bf16][C]) {
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, fused::kSmemBudget);
+    if (e == cudaSuccess && C > 8) e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) {
       snprintf(err, err_len, "fused checkpoint: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return TIDE_ERR_CUDA;
@@ -865,16 +883,19 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // one resident cluster per C SMs: every cluster runs for the whole launch
-  // so a look-back never waits on a tile whose cluster is not running
-  static int max_clusters[64][2][9] = {};
+  // so a look-back never waits on a tile whose cluster is not running.  A
+  // device that cannot hold one cluster of this size reports
+  // TIDE_ERR_UNSUPPORTED before anything is launched.
+  static int max_clusters[64][2][kMaxCluster + 1] = {};
   if (!max_clusters[dev][bf16][C]) {
     cfg.gridDim = dim3((unsigned)C, 1, 1);
     int mc = 0;
     e = cudaOccupancyMaxActiveClusters(&mc, fn, &cfg);
     if (e != cudaSuccess || mc <= 0) {
+      (void)cudaGetLastError();
       snprintf(err, err_len, "fused checkpoint: no resident cluster of %d CTAs (%s)", C,
                cudaGetErrorString(e));
-      return TIDE_ERR_CUDA;
+      return TIDE_ERR_UNSUPPORTED;
     }
     max_clusters[dev][bf16][C] = mc;
   }
@@ -889,8 +910,10 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
                      : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 2>, tx, tw, p); break;
     case 4: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 4>, tx, tw, p)
                      : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 4>, tx, tw, p); break;
-    default: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 8>, tx, tw, p)
-                      : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 8>, tx, tw, p); break;
+    case 8: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 8>, tx, tw, p)
+                     : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 8>, tx, tw, p); break;
+    default: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 16>, tx, tw, p)
+                      : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 16>, tx, tw, p); break;
   }
   if (e != cudaSuccess) {
     snprintf(err, err_len, "fused checkpoint launch: %s", cudaGetErrorString(e));
