@@ -338,6 +338,7 @@ int tide_checkpoint(const tide_checkpoint_args *a, tide_stream_t stream) {
     // a device that cannot hold one cluster of the size this hidden_dim
     // needs: the automatic choice falls back to the split path
     if (!(rc == TIDE_ERR_UNSUPPORTED && a->path == TIDE_PATH_AUTO && tide::tc_supported(a))) return rc;
+    g_err[0] = '\0';  // not an error of this call: it goes on with the split path
     path = TIDE_PATH_TC_SPLIT;
   }
 
