@@ -199,6 +199,49 @@ def test_checkpoint_device_row_count():
 
 
 @pytest.mark.parametrize("path", [capi.PATH_SIMT, capi.PATH_TC, capi.PATH_TC_SPLIT])
+@pytest.mark.parametrize("live", [0, 1, 63, 64, 65])
+def test_device_row_count_edges(path, live):
+    """A live count on the device of 0 (an earlier checkpoint exited every
+    row), 1, and around a 64-row tile, below a launch capacity of 1000 rows:
+    nothing past the live rows is read or written; with no live rows the
+    counts are {0, 0} and every output stays untouched."""
+    n_cap, H = 1000, 512
+    dtype = torch.bfloat16
+    w = workloads.rows(n_cap, H, dtype, seed=70 + live, unit_norm_weight=False)
+    x = w["x"].to(DEV)
+    nw = w["norm_weight"].to(DEV)
+    norm = oracle_norm("rms", nw, None, 1e-5)
+    x_live = storage_np(x)[:live]
+    z = O.router_logits(O.final_norm(O.to_f32(storage_np(x), O.BF16), norm), w["down"].numpy(),
+                        w["up"].numpy())
+    bias = workloads.bias_for_exit_fraction(z, 0.4, THR)
+    out = torch.zeros_like(x)
+    out0 = storage_np(out).copy()
+    cnt = torch.tensor([live], dtype=torch.int32, device=DEV)
+    ck = Checkpoint(x, "rms", nw, None, 1e-5, w["down"].to(DEV), w["up"].to(DEV), bias, THR,
+                    out_buffer=out, n_rows_dev=cnt, path=path)
+    assert ck.path() == path
+    ck()
+    torch.cuda.synchronize()
+    assert int(ck.error_word.item()) == 0
+    assert np.all(ck.scores_out.cpu().numpy()[live:] == -1.0)
+    if live == 0:
+        assert ck.counts.cpu().tolist() == [0, 0]
+        assert np.all(ck.positions_out.cpu().numpy() == -7)
+        assert np.all(ck.exit_positions_out.cpu().numpy() == -7)
+        assert np.array_equal(storage_np(out), out0)
+        return
+    res = O.checkpoint(x_live, O.BF16, norm, w["down"].numpy(), w["up"].numpy(), bias, THR)
+    res["eps"] = 1e-5
+    view = types.SimpleNamespace(
+        x=ck.x[:live], scores_out=ck.scores_out[:live], counts=ck.counts, error_word=ck.error_word,
+        positions=None, slots=None, positions_out=ck.positions_out,
+        exit_positions_out=ck.exit_positions_out, compact_out=ck.compact_out, out_buffer=out,
+        norm_w=ck.norm_w, norm_b=ck.norm_b)
+    check_against_oracle(view, res, dtype, "rms", score_tol(dtype, path), out_ref=out0)
+
+
+@pytest.mark.parametrize("path", [capi.PATH_SIMT, capi.PATH_TC, capi.PATH_TC_SPLIT])
 def test_checkpoint_chain_on_device_counts(path):
     """Three checkpoints chained on device-side counts with no host sync in
     between; afterwards each stage is checked against the oracle on the rows
