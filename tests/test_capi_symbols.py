@@ -97,8 +97,8 @@ def test_operators_have_no_cpu_kernel():
 
 
 def test_path_selection():
-    """bf16/fp16 with folded weights: up to 3584 rows (H <= 4096; 2560 at
-    H = 5120, 5120 at H = 8192) the fused single-pass
+    """bf16/fp16 with folded weights: up to a row count set per hidden size
+    from measured crossovers (3584 rows at H = 4096) the fused single-pass
     kernel when the router is 128 wide and a weight slice of H stays
     resident; above that, or when the fused kernel does not apply, the
     tensor-core split path (H % 64 == 0, B <= 256); fp32 and other shapes to
@@ -130,6 +130,13 @@ def test_path_selection():
     assert sel(hidden_dim=5120, n_rows=2561, n_total=2561) == capi.PATH_TC_SPLIT
     assert sel(hidden_dim=8192, n_rows=5120, n_total=5120) == capi.PATH_TC
     assert sel(hidden_dim=8192, n_rows=5121, n_total=5121) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=768, n_rows=4608, n_total=4608) == capi.PATH_TC     # GPT-2 width: SIMT mover on the split path
+    assert sel(hidden_dim=768, n_rows=4609, n_total=4609) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=1024, n_rows=1024, n_total=1024) == capi.PATH_TC
+    assert sel(hidden_dim=1024, n_rows=1025, n_total=1025) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=2048, n_rows=2560, n_total=2560) == capi.PATH_TC
+    assert sel(hidden_dim=2048, n_rows=2561, n_total=2561) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=512, n_rows=1025, n_total=1025) == capi.PATH_TC_SPLIT
     assert sel(hidden_dim=16384, path=capi.PATH_TC) == capi.PATH_TC_SPLIT  # slice too large to stay resident
     assert sel(hidden_dim=768, path=capi.PATH_TC) == capi.PATH_TC   # cluster of 2
     assert sel(path=capi.PATH_TC_SPLIT) == capi.PATH_TC_SPLIT

@@ -167,4 +167,56 @@ __device__ __forceinline__ bool lookback(uint64_t *status, uint32_t tile, uint32
   return ok;
 }
 
+// Warp-wide decoupled look-back: the 32 lanes read 32 predecessors per
+// round trip (lane l reads tile base - l) and stop at the nearest inclusive
+// prefix, waiting only for the predecessors in front of it.  Where many
+// tiles are in flight at once (small clusters, many of them), one thread
+// reading one predecessor per round trip would walk the whole wave.  With
+// `publish`, lane 0 publishes the tile's aggregate first and its inclusive
+// prefix at the end.  Every lane gets the exclusive prefix.  Called by a
+// whole warp; returns false (warp-uniformly) if a wait expired, the prefix
+// then being a lower bound.
+__device__ __forceinline__ bool warp_lookback(uint64_t *status, uint32_t tile, uint32_t keep,
+                                              uint32_t exits, bool publish, uint32_t *keep_before,
+                                              uint32_t *exits_before) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  if (publish && lane == 0)
+    st_status(&status[tile], pack_status(tile == 0 ? kFlagPrefix : kFlagAggregate, keep, exits));
+  uint32_t kb = 0, eb = 0;
+  bool ok = true;
+  for (int64_t base = (int64_t)tile - 1; base >= 0; base -= 32) {
+    const int64_t j = base - lane;
+    // before tile 0: an empty inclusive prefix
+    uint64_t s = j >= 0 ? ld_status(&status[j]) : kFlagPrefix;
+    uint32_t incl = 0;
+    int stop = 31;
+    for (int spins = 0;; ++spins) {
+      incl = __ballot_sync(full, (s >> 62) == 2);
+      stop = incl ? __ffs(incl) - 1 : 31;
+      const bool wait_me = (s >> 62) == 0 && lane <= stop;
+      if (!__any_sync(full, wait_me)) break;
+      if (spins > kSpinLimit) { ok = false; break; }
+      __nanosleep(32);
+      if (wait_me) s = ld_status(&status[j]);
+    }
+    if (!ok) break;
+    uint32_t k = lane <= stop ? (uint32_t)(s & kCountMask) : 0u;
+    uint32_t e = lane <= stop ? (uint32_t)((s >> 31) & kCountMask) : 0u;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      k += __shfl_xor_sync(full, k, o);
+      e += __shfl_xor_sync(full, e, o);
+    }
+    kb += k;
+    eb += e;
+    if (incl) break;
+  }
+  if (publish && lane == 0 && tile != 0)
+    st_status(&status[tile], pack_status(kFlagPrefix, kb + keep, eb + exits));
+  *keep_before = kb;
+  *exits_before = eb;
+  return ok;
+}
+
 }  // namespace tide

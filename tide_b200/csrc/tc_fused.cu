@@ -574,21 +574,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = (int)info[t].w;
         s_rank[t] += st == 1 ? s_prefix[8] : s_prefix[9];
       }
-      if (t == 0) {
+      if (w4 == 0) {
+        // The tile's prefix (rank 0 publishes the tile's counts, the other
+        // CTAs only read).  Small clusters are many: up to 148 / C tiles are
+        // in flight at once, and warp 12 reads their predecessors 32 per
+        // round trip.  With 8 or 16 CTAs per cluster a tile has few live
+        // predecessors and one thread walking them measured faster.
         const uint32_t keep_t = s_prefix[8] + s_prefix[10];
         const uint32_t exit_t = s_prefix[9] + s_prefix[11];
         uint32_t kb = 0, eb = 0;
-        bool lb_ok;
-        if (rank == 0)
-          lb_ok = lookback(p.status, (uint32_t)tile, keep_t, exit_t, &kb, &eb);
-        else
-          lb_ok = lookback_read(p.status, (uint32_t)tile, &kb, &eb);
-        if (!lb_ok) raise_error(p.err, TIDE_DEVERR_TIMEOUT);
-        s_prefix[0] = kb;
-        s_prefix[1] = eb;
-        if (rank == 0 && tile == n_tiles - 1 && p.counts) {
-          p.counts[0] = (int32_t)(kb + keep_t);
-          p.counts[1] = (int32_t)(eb + exit_t);
+        bool lb_ok = true;
+        if constexpr (C <= 4) {
+          lb_ok = warp_lookback(p.status, (uint32_t)tile, keep_t, exit_t, rank == 0, &kb, &eb);
+        } else if (lane == 0) {
+          lb_ok = rank == 0 ? lookback(p.status, (uint32_t)tile, keep_t, exit_t, &kb, &eb)
+                            : lookback_read(p.status, (uint32_t)tile, &kb, &eb);
+        }
+        if (lane == 0) {
+          if (!lb_ok) raise_error(p.err, TIDE_DEVERR_TIMEOUT);
+          s_prefix[0] = kb;
+          s_prefix[1] = eb;
+          if (rank == 0 && tile == n_tiles - 1 && p.counts) {
+            p.counts[0] = (int32_t)(kb + keep_t);
+            p.counts[1] = (int32_t)(eb + exit_t);
+          }
         }
       }
       ptx::named_sync(2, 128);
@@ -768,17 +777,27 @@ const char *fused_unsupported_reason(const tide_checkpoint_args *a) {
 
 bool fused_supported(const tide_checkpoint_args *a) { return fused_unsupported_reason(a) == nullptr; }
 
-// Measured crossovers against the split path (bf16, 10 % and 50 % exits):
-// with clusters of at most 8 CTAs (H <= 4096) the fused pass wins up to
-// 3072 rows and loses from 4096 on.  16-CTA clusters are fewer on the GPU:
-// at H = 5120 the fused pass wins up to 2048 rows and loses from 3072; at
-// H = 8192, where the split router streams 2 MiB of W' through each CTA, it
-// wins up to 4096 rows and loses from 6144.
+// Measured crossovers against the split path (bf16, 10-50 % exits), by
+// cluster size:
+//   1 CTA  (H <= 512):  the split path wins from 1536 rows.
+//   2 CTAs (H 768-1024): rows under 2 KB (H = 768) leave the split path the
+//          SIMT mover, and the fused pass wins up to 4096 rows (loses from
+//          5120); with 2 KB rows (H = 1024) the split path wins from 1536.
+//   4 CTAs (H = 2048):  fused up to 2048 rows, split from 3072.
+//   8 CTAs (H = 4096):  fused up to 3072 rows, split from 4096.
+//   16 CTAs: H = 5120 fused up to 2048 rows, split from 3072; H = 8192, whose
+//          split router streams 2 MiB of W' through each CTA, fused up to
+//          4096, split from 6144.
 int64_t fused_auto_max_rows(int64_t H) {
   const int C = fused_cluster_size(H);
-  if (C == 0) return 0;
-  if (C <= 8) return 3584;
-  return H >= 8192 ? 5120 : 2560;
+  switch (C) {
+    case 0: return 0;
+    case 1: return 1024;
+    case 2: return H * 2 < 2048 ? 4608 : 1024;
+    case 4: return 2560;
+    case 8: return 3584;
+    default: return H >= 8192 ? 5120 : 2560;
+  }
 }
 
 // Workspace: 256 reserved bytes, the tile status words (zeroed per call),
