@@ -101,8 +101,9 @@ def test_path_selection():
     from measured crossovers (3584 rows at H = 4096) the fused single-pass
     kernel when the router is 128 wide and a weight slice of H stays
     resident; above that, or when the fused kernel does not apply, the
-    tensor-core split path (H % 64 == 0, B <= 256); fp32 and other shapes to
-    the SIMT path."""
+    tensor-core split path (H % 64 == 0, B <= 256).  fp32 rows with folded
+    fp32 weights and H % 32 == 0 take the split path too (error-compensated
+    tf32 products); other shapes the SIMT path."""
     lib = _native.lib()
 
     def sel(**kw):
@@ -121,6 +122,12 @@ def test_path_selection():
     assert sel(n_rows=32768, n_total=32768, dtype=capi.DTYPE_F16) == capi.PATH_TC_SPLIT
     assert sel(path=capi.PATH_TC) == capi.PATH_TC
     assert sel(dtype=capi.DTYPE_F32, folded=None) == capi.PATH_SIMT
+    assert sel(dtype=capi.DTYPE_F32) == capi.PATH_TC_SPLIT     # fp32: 3 x tf32 split router
+    assert sel(dtype=capi.DTYPE_F32, n_rows=8, n_total=8) == capi.PATH_TC_SPLIT
+    assert sel(dtype=capi.DTYPE_F32, path=capi.PATH_TC) == capi.PATH_TC_SPLIT
+    assert sel(dtype=capi.DTYPE_F32, hidden_dim=800) == capi.PATH_TC_SPLIT   # 800 = 25 x 32
+    assert sel(dtype=capi.DTYPE_F32, hidden_dim=784) == capi.PATH_SIMT
+    assert sel(dtype=capi.DTYPE_F32, path=capi.PATH_SIMT) == capi.PATH_SIMT
     assert sel(hidden_dim=4000) == capi.PATH_SIMT
     assert sel(bottleneck_dim=48) == capi.PATH_TC_SPLIT       # units padded to 128 (fused: 128 only)
     assert sel(bottleneck_dim=64) == capi.PATH_TC_SPLIT       # fused kernel: 128 units only

@@ -418,6 +418,35 @@ def test_split_router_tile_geometry(units, device_count):
     check_against_oracle(live, res, torch.bfloat16, "rms", 1e-2)
 
 
+@pytest.mark.parametrize("kind", ["rms", "layer"])
+@pytest.mark.parametrize("n,H,B", [(1, 768, 128), (100, 768, 128), (4096, 768, 128),
+                                   (5000, 1024, 200), (12000, 4096, 128), (777, 800, 48)])
+def test_fp32_tensor_core_router(n, H, B, kind):
+    """fp32 rows on the split path: kind::tf32 MMAs on hi/lo operand splits,
+    three products per K step.  Scores within 1e-5 of the oracle (the fp32
+    bar), exits final-normed within 8 ulp, stable compaction.  Tiles of 1-4
+    units, a router wider than 128 (two 128-unit blocks) and narrower (padded
+    units), H = 800 (25 chunks of 32 columns).  LayerNorm rows carry a mean
+    of 3: the statistics are taken about each row's first value, so the
+    variance does not cancel away."""
+    w = workloads.rows(n, H, torch.float32, b=B, seed=1300 + n, norm_kind=kind,
+                       unit_norm_weight=False)
+    x = (w["x"] + 3.0 if kind == "layer" else w["x"]).to(DEV).contiguous()
+    nw, nb = norm_tensors(w, torch.float32)
+    norm = oracle_norm(kind, nw, nb, 1e-5)
+    z = O.router_logits(O.final_norm(O.to_f32(storage_np(x), O.F32), norm), w["down"].numpy(),
+                        w["up"].numpy())
+    bias = workloads.bias_for_exit_fraction(z, 0.3, THR)
+    out = torch.zeros(n + 3, H, device=DEV)
+    ck = Checkpoint(x, kind, nw, nb, 1e-5, w["down"].to(DEV), w["up"].to(DEV), bias, THR,
+                    out_buffer=out, n_total=n + 3, path=capi.PATH_TC_SPLIT)
+    assert ck.path() == capi.PATH_TC_SPLIT
+    ck()
+    res = O.checkpoint(storage_np(x), O.F32, norm, w["down"].numpy(), w["up"].numpy(), bias, THR)
+    res["eps"] = 1e-5
+    check_against_oracle(ck, res, torch.float32, kind, 1e-5, out_ref=np.zeros((n + 3, H), np.float32))
+
+
 @pytest.mark.parametrize("path", [capi.PATH_TC, capi.PATH_TC_SPLIT, capi.PATH_SIMT])
 def test_full_size_properties(path):
     """32768 x 4096 bf16 (one 8B-architecture prefill batch): properties that

@@ -39,6 +39,18 @@
 // producer starts loading right after it; the other warps fetch the per-unit
 // vectors and clear the mover's workspace meanwhile (no separate memset).
 // The survivors/exits are then moved by the stable-partition kernel.
+//
+// fp32 rows take the same pipeline with kind::tf32 MMAs and error-compensated
+// products ("3xTF32"): each operand v is split as hi = v rounded to tf32 and
+// lo = v - hi (exact), and D accumulates W'hi.xhi + W'lo.xhi + W'hi.xlo,
+// which leaves out only W'lo.xlo and the tf32 rounding of the lo parts
+// (about 2^-21 of each product) -- the fp32 score bar of 1e-5 holds, where a
+// single tf32 product (2^-11) would not.  A K chunk is still 128 bytes of a
+// row (32 fp32 columns), so the shared-memory layout and descriptors are the
+// ones of the 16-bit case.  Warps 4-7 split each landed stage in place (hi
+// over the loaded values, lo into the stage's second half, x and W' alike)
+// while they take the row statistics; the MMA waits for that instead of the
+// TMA.  Tiles are at most 128 rows so that three stages fit.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdio.h>
@@ -72,9 +84,10 @@ constexpr int kTcMaxKc = TIDE_ROUTER_MAX_KC;
 constexpr int kTcMinStages = TIDE_ROUTER_MIN_STAGES;
 constexpr int kTcSmemBudget = 227 * 1024;
 constexpr int kTcAux = 12288;     // barriers, flags, per-unit vectors, row statistics, partials
-static_assert((2 * kTcMaxStages + 9) * 8 + 16 + 3 * 256 * 4 + 2 * 256 * 2 * 4 + 4 * 256 * 4 +
+static_assert((3 * kTcMaxStages + 9) * 8 + 16 + 3 * 256 * 4 + 2 * 256 * 2 * 4 + 4 * 256 * 4 +
                       8 * 4 <= kTcAux,
               "auxiliary shared-memory area");
+constexpr int kTcTileUnitsF32 = 4;  // fp32: stages hold hi and lo, so tiles of 128 rows
 
 struct TcRouteParams {
   int64_t n_cap;
@@ -127,7 +140,27 @@ __device__ __forceinline__ float transpose_sum32(float (&v)[32], int lane) {
   return v[0];
 }
 
-template <bool BF16, bool LAYER>
+// v = hi + lo with hi = v rounded to tf32 (to nearest, ties away from zero:
+// add half of the 13 dropped bits, then clear them) and lo = v - hi, exact
+// because hi is within a factor of two of v.  Magnitudes that would round
+// past the largest finite float (and Inf/NaN) are truncated instead.
+__device__ __forceinline__ void split_tf32(float v, float &hi, float &lo) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t r = (b & 0x7fffffffu) < 0x7f7ff000u ? b + 0x1000u : b;
+  hi = __uint_as_float(r & 0xffffe000u);
+  lo = v - hi;
+}
+__device__ __forceinline__ void split_tf32_16(uint8_t *hi_at, uint8_t *lo_at) {
+  float4 v = *reinterpret_cast<const float4 *>(hi_at), h, l;
+  split_tf32(v.x, h.x, l.x);
+  split_tf32(v.y, h.y, l.y);
+  split_tf32(v.z, h.z, l.z);
+  split_tf32(v.w, h.w, l.w);
+  *reinterpret_cast<float4 *>(hi_at) = h;
+  *reinterpret_cast<float4 *>(lo_at) = l;
+}
+
+template <bool BF16, bool LAYER, bool F32>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_route_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_x_big,
@@ -138,9 +171,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NA = p.n_acc, AT = p.a_tiles;
-  const uint32_t unit_bytes = kTcUnit * kTcK * 2;
-  const uint32_t w_tile_bytes = kTcM * kTcK * 2;    // A operand: 128 units
-  const uint32_t w_load_bytes = (uint32_t)AT * (uint32_t)p.w_rows * kTcK * 2;
+  // a K chunk is 128 bytes of a row: 64 16-bit or 32 fp32 columns
+  constexpr int kCols = F32 ? 32 : kTcK;
+  constexpr int kTileMax = F32 ? kTcTileUnitsF32 : kTcTileUnits;  // units per tile
+  constexpr int kStatWarps = F32 ? 4 : 8;
+  const uint32_t unit_bytes = kTcUnit * 128;
+  const uint32_t w_tile_bytes = kTcM * 128;    // A operand: 128 units
+  const uint32_t w_load_bytes = (uint32_t)AT * (uint32_t)p.w_rows * 128;
   // barriers and the small vectors first, the pipeline stages after them
   // (their size depends on the live row count, known only after the wait)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
@@ -150,7 +187,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t *stat_full = acc_empty + 2; // [2] statistics slot written
   uint64_t *stat_empty = stat_full + 2;// [2] statistics slot read
   uint64_t *drain = stat_empty + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *conv = drain + 1;  // [kTcMaxStages] fp32: stage split into hi/lo
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(conv + kTcMaxStages);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   uint32_t *issued = reinterpret_cast<uint32_t *>(tmem_slot + 2);    // stages armed (warp 0)
   uint32_t *issued_x = reinterpret_cast<uint32_t *>(tmem_slot + 3);  // stages with x issued (warp 2)
@@ -161,18 +199,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   float *s_part = s_stat + 2 * kTcTileRows * 2;  // [4 warps][256 rows]
   volatile int *s_vote = reinterpret_cast<volatile int *>(s_part + 4 * kTcTileRows);  // [8]
 
-  const int k_chunks = p.H / kTcK;
+  const int k_chunks = p.H / kCols;
   uint8_t *ring = smem + kTcAux;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcMaxStages; ++s) {
       ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], 1 + 8);  // MMA commit + 8 statistics warps
+      // MMA commit + 8 statistics warps; fp32: the MMA commit alone (the
+      // MMAs wait for the split, the statistics warps' last use of a stage)
+      ptx::mbar_init(&empty[s], F32 ? 1 : 1 + 8);
+      ptx::mbar_init(&conv[s], kStatWarps);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&acc_full[a], 1);
       ptx::mbar_init(&acc_empty[a], 8);   // 8 epilogue warps
-      ptx::mbar_init(&stat_full[a], 8);   // 8 statistics warps
+      ptx::mbar_init(&stat_full[a], kStatWarps);
       ptx::mbar_init(&stat_empty[a], 8);  // 8 epilogue warps
     }
     ptx::mbar_init(drain, 1);
@@ -209,17 +250,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // stage holds KC chunks [x_0 .. x_KC-1][W'_0 .. W'_KC-1], so a CTA with few
   // rows moves more bytes per stage and keeps the ring full.
   const int64_t max_units = (units + gridDim.x - 1) / gridDim.x;
-  const int tile_units = max_units >= kTcTileUnits ? kTcTileUnits : (max_units < 1 ? 1 : (int)max_units);
+  const int tile_units = max_units >= kTileMax ? kTileMax : (max_units < 1 ? 1 : (int)max_units);
   const uint32_t x_bytes = (uint32_t)tile_units * unit_bytes;  // one chunk of the B operand
   const uint32_t wc_bytes = (uint32_t)AT * w_tile_bytes;       // one chunk of the A operand
+  // fp32 stages hold the lo parts in a second half of the same layout
+  const uint32_t chunk_bytes = (F32 ? 2u : 1u) * (x_bytes + wc_bytes);
   int KC = 1;
   for (int c = kTcMaxKc; c > 1; c >>= 1)
-    if (k_chunks % c == 0 && p.ring_bytes / ((uint32_t)c * (x_bytes + wc_bytes)) >= (uint32_t)kTcMinStages) {
+    if (k_chunks % c == 0 && p.ring_bytes / ((uint32_t)c * chunk_bytes) >= (uint32_t)kTcMinStages) {
       KC = c;
       break;
     }
   const uint32_t w_off = (uint32_t)KC * x_bytes;  // W' chunks follow the x chunks
-  const uint32_t stage_bytes = (uint32_t)KC * (x_bytes + wc_bytes);
+  const uint32_t lo_off = (uint32_t)KC * (x_bytes + wc_bytes);  // fp32: the lo half
+  const uint32_t stage_bytes = (uint32_t)KC * chunk_bytes;
   const int S_fit = (int)(p.ring_bytes / stage_bytes);
   const int S = S_fit > kTcMaxStages ? kTcMaxStages : S_fit;
   const int k_stages = k_chunks / KC;
@@ -271,8 +315,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       const bool arm = warp == 0;
       uint32_t it = 0;
-      for (int64_t u0 = u_begin; u0 < u_end && !*abort_flag; u0 += kTcTileUnits) {
-        const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
+      for (int64_t u0 = u_begin; u0 < u_end && !*abort_flag; u0 += kTileMax) {
+        const int nu = (int)(u_end - u0 < kTileMax ? u_end - u0 : kTileMax);
         const int n_big = nu / (kTcBigBox / kTcUnit);
         const bool mid = (nu % (kTcBigBox / kTcUnit)) >= kTcMidBox / kTcUnit;
         const int u_mid = n_big * (kTcBigBox / kTcUnit);                  // first unit of the 64-row box
@@ -290,11 +334,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int c = 0; c < KC; ++c)
               for (int a = 0; a < AT; ++a)
                 ptx::tma_load_2d(st + w_off + (size_t)c * wc_bytes + (size_t)a * w_tile_bytes, &tmap_w,
-                                 &full[s], (ks * KC + c) * kTcK, a * kTcM);
+                                 &full[s], (ks * KC + c) * kCols, a * kTcM);
             *issued = it + 1;
           } else {
             for (int c = 0; c < KC; ++c) {
-              const int col = (ks * KC + c) * kTcK;
+              const int col = (ks * KC + c) * kCols;
               uint8_t *xc = st + (size_t)c * x_bytes;
               for (int j = 0; j < n_big; ++j)
                 ptx::tma_load_2d(xc + (size_t)j * (kTcBigBox / kTcUnit) * unit_bytes, &tmap_x_big,
@@ -314,12 +358,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = ptx::f16_idesc(BF16, kTcM, tile_units * kTcUnit);
+      const uint32_t idesc = F32 ? ptx::tf32_idesc(kTcM, tile_units * kTcUnit)
+                                 : ptx::f16_idesc(BF16, kTcM, tile_units * kTcUnit);
       uint32_t it = 0;
       int t_local = 0;
       bool ok = true;
       for (int64_t u0 = u_begin; u0 < u_end && ok && !*abort_flag;
-           u0 += kTcTileUnits, ++t_local) {
+           u0 += kTileMax, ++t_local) {
         const int acc = t_local % NA;
         const uint32_t acc_ph = (uint32_t)(t_local / NA) & 1u;
         if (t_local >= NA && !ptx::mbar_wait(&acc_empty[acc], acc_ph ^ 1u, abort_flag)) {
@@ -330,19 +375,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * AT * kTcTileRows);
         for (int ks = 0; ks < k_stages; ++ks, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
-          if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+          if (!ptx::mbar_wait(F32 ? &conv[s] : &full[s], ph, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
           const uint32_t st = ptx::smem_u32(ring + (size_t)s * stage_bytes);
           for (int c = 0; c < KC; ++c) {
             const uint32_t xs = st + (uint32_t)c * x_bytes;
             const uint32_t ws = st + w_off + (uint32_t)c * wc_bytes;
             for (int a = 0; a < AT; ++a) {
+              // four K steps of 32 bytes: 16 columns of kind::f16, 8 of tf32
 #pragma unroll
-              for (int k = 0; k < kTcK / 16; ++k) {
-                ptx::mma_f16_ss(d_tmem + (uint32_t)(a * kTcTileRows),
-                                ptx::sw128_kmajor_desc(ws + (uint32_t)a * w_tile_bytes + 32u * k),
-                                ptx::sw128_kmajor_desc(xs + 32u * k), idesc,
-                                (ks > 0 || c > 0 || k > 0) ? 1u : 0u);
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t wa = ws + (uint32_t)a * w_tile_bytes + 32u * k, xb = xs + 32u * k;
+                const uint32_t d = d_tmem + (uint32_t)(a * kTcTileRows);
+                const uint32_t acc_in = (ks > 0 || c > 0 || k > 0) ? 1u : 0u;
+                if constexpr (F32) {
+                  ptx::mma_tf32_ss(d, ptx::sw128_kmajor_desc(wa), ptx::sw128_kmajor_desc(xb), idesc, acc_in);
+                  ptx::mma_tf32_ss(d, ptx::sw128_kmajor_desc(wa + lo_off), ptx::sw128_kmajor_desc(xb),
+                                   idesc, 1u);
+                  ptx::mma_tf32_ss(d, ptx::sw128_kmajor_desc(wa), ptx::sw128_kmajor_desc(xb + lo_off),
+                                   idesc, 1u);
+                } else {
+                  ptx::mma_f16_ss(d, ptx::sw128_kmajor_desc(wa), ptx::sw128_kmajor_desc(xb), idesc, acc_in);
+                }
               }
             }
           }
@@ -370,7 +424,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // do both, in that order per tile: while the rows stream they have no
     // epilogue to run (a CTA's range is one tile up to 37888 rows), and eight
     // statistics warps keep each stage's release short.
-    const bool do_stats = warp < 12;
+    // fp32: warps 4-7 alone take the statistics (and split the stages), so
+    // the epilogue of one tile never holds up the MMAs of the next.
+    const bool do_stats = warp < 4 + kStatWarps;
     const bool do_epi = warp >= 8;
     const int t = threadIdx.x - 128;   // statistics row 0..255
     const int q = warp & 3;
@@ -379,10 +435,77 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t it = 0;
     int t_local = 0;
     bool ok = true;
-    for (int64_t u0 = u_begin; u0 < u_end; u0 += kTcTileUnits, ++t_local) {
-      const int nu = (int)(u_end - u0 < kTcTileUnits ? u_end - u0 : kTcTileUnits);
+    for (int64_t u0 = u_begin; u0 < u_end; u0 += kTileMax, ++t_local) {
+      const int nu = (int)(u_end - u0 < kTileMax ? u_end - u0 : kTileMax);
       const int buf = t_local & 1;
-      if (do_stats && ok) {
+      if constexpr (F32) {
+        if (do_stats && ok) {
+          // thread t owns row t of the tile: its statistics, and the split of
+          // its 128 bytes of each chunk; the 128 threads split W' together.
+          // Per-chunk sums in fp32, across chunks in fp64.  LayerNorm sums
+          // x - x[0], so a large mean does not cancel the variance away.
+          const bool live = (t >> 5) < nu;
+          double ssd = 0.0, sxd = 0.0;
+          float shift = 0.f;
+          for (int ks = 0; ks < k_stages; ++ks, ++it) {
+            const uint32_t s = it % S, ph = (it / S) & 1u;
+            if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+            uint8_t *stg = ring + (size_t)s * stage_bytes;
+            for (int c = 0; c < KC; ++c) {
+              if (live) {
+                uint8_t *row = stg + (size_t)c * x_bytes + (size_t)t * 128;
+                // the row's first column: 16-byte unit 0, at (0 ^ row) of the swizzle
+                if (LAYER && ks == 0 && c == 0) shift = *reinterpret_cast<const float *>(row + ((t & 7) << 4));
+                float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int unit = (j + lane) & 7;
+                  uint8_t *at = row + (unit << 4);
+                  const float4 v = *reinterpret_cast<const float4 *>(at);
+                  if (LAYER) {
+                    const float d0 = v.x - shift, d1 = v.y - shift, d2 = v.z - shift, d3 = v.w - shift;
+                    ss0 = fmaf(d0, d0, fmaf(d2, d2, ss0));
+                    ss1 = fmaf(d1, d1, fmaf(d3, d3, ss1));
+                    sx0 += d0 + d2;
+                    sx1 += d1 + d3;
+                  } else {
+                    ss0 = fmaf(v.x, v.x, fmaf(v.z, v.z, ss0));
+                    ss1 = fmaf(v.y, v.y, fmaf(v.w, v.w, ss1));
+                  }
+                  split_tf32_16(at, at + lo_off);
+                }
+                ssd += (double)(ss0 + ss1);
+                sxd += (double)(sx0 + sx1);
+              }
+              uint8_t *w = stg + w_off + (size_t)c * wc_bytes;
+              for (int i = t; i < AT * (kTcM * 128 / 16); i += kStatWarps * 32)
+                split_tf32_16(w + (size_t)i * 16, w + lo_off + (size_t)i * 16);
+            }
+            // the MMAs read the split through the async proxy
+            ptx::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&conv[s]);
+          }
+          if (ok && t_local >= 2 &&
+              !ptx::mbar_wait(&stat_empty[buf], ((uint32_t)(t_local >> 1) & 1u) ^ 1u, abort_flag))
+            ok = false;
+          if (ok) {
+            float *st = s_stat + ((size_t)buf * kTcTileRows + t) * 2;
+            const double inv_h = 1.0 / (double)p.H;
+            if (!LAYER) {
+              st[0] = rsqrt_rn((float)(ssd * inv_h) + p.eps);
+              st[1] = 0.f;
+            } else {
+              const double md = sxd * inv_h;
+              const double var = ssd * inv_h - md * md;
+              st[0] = rsqrt_rn((float)(var > 0.0 ? var : 0.0) + p.eps);
+              st[1] = (float)((double)shift + md);
+            }
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&stat_full[buf]);
+          }
+        }
+      } else if (do_stats && ok) {
         const bool live = (t >> 5) < nu;  // warp-uniform: a unit is one warp
         float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
         for (int ks = 0; ks < k_stages; ++ks, ++it) {
@@ -537,16 +660,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-bool make_tmap(CUtensorMap *m, const void *base, bool bf16, uint64_t rows, uint64_t cols,
+// A [rows, cols] row-major matrix of `dtype` (TIDE_DTYPE_*), read in boxes
+// of 128 bytes of a row (64 16-bit or 32 fp32 columns) by box_rows rows.
+bool make_tmap(CUtensorMap *m, const void *base, int dtype, uint64_t rows, uint64_t cols,
                uint32_t box_rows) {
   auto enc = encode_fn();
   if (!enc) return false;
+  const uint64_t esize = dtype == TIDE_DTYPE_F32 ? 4 : 2;
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * 2};
-  cuuint32_t box[2] = {(cuuint32_t)kTcK, box_rows};
+  cuuint64_t strides[1] = {cols * esize};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esize), box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                   const_cast<void *>(base), dims, strides, box, estr,
+  const CUtensorMapDataType t = dtype == TIDE_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                : dtype == TIDE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(m, t, 2, const_cast<void *>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -574,9 +702,12 @@ int sm_count() {
 }  // namespace
 
 const char *tc_unsupported_reason(const tide_checkpoint_args *a) {
-  if (a->dtype != TIDE_DTYPE_BF16 && a->dtype != TIDE_DTYPE_F16) return "dtype is not bf16/fp16";
+  if (a->dtype != TIDE_DTYPE_BF16 && a->dtype != TIDE_DTYPE_F16 && a->dtype != TIDE_DTYPE_F32)
+    return "bad dtype";
   if (!a->folded) return "no folded router weights";
-  if (a->hidden_dim % kTcK != 0) return "hidden_dim is not a multiple of 64";
+  // a K chunk is 128 bytes of a row
+  if (a->dtype == TIDE_DTYPE_F32 && a->hidden_dim % 32 != 0) return "hidden_dim is not a multiple of 32";
+  if (a->dtype != TIDE_DTYPE_F32 && a->hidden_dim % kTcK != 0) return "hidden_dim is not a multiple of 64";
   if (a->bottleneck_dim < 1 || a->bottleneck_dim > 256) return "bottleneck_dim not in [1, 256]";
   if (a->norm_type == TIDE_NORM_LAYER && !a->colsum) return "LayerNorm needs colsum";
   if (a->n_rows < 1) return "no rows";
@@ -592,14 +723,14 @@ size_t tc_workspace_bytes(int64_t) { return 0; }
 int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_stats,
                     void *zero, size_t zero_bytes, cudaStream_t stream, char *err,
                     size_t err_len) {
-  const bool bf16 = a->dtype == TIDE_DTYPE_BF16;
+  const int dt = a->dtype;
   const int B = (int)a->bottleneck_dim;
   const int w_rows = B < kTcM ? B : kTcM;
   CUtensorMap tx, txb, txm, tw;
-  if (!make_tmap(&tx, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcUnit) ||
-      !make_tmap(&txb, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcBigBox) ||
-      !make_tmap(&txm, a->x, bf16, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcMidBox) ||
-      !make_tmap(&tw, a->folded, bf16, (uint64_t)B, (uint64_t)a->hidden_dim, (uint32_t)w_rows)) {
+  if (!make_tmap(&tx, a->x, dt, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcUnit) ||
+      !make_tmap(&txb, a->x, dt, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcBigBox) ||
+      !make_tmap(&txm, a->x, dt, (uint64_t)a->n_rows, (uint64_t)a->hidden_dim, kTcMidBox) ||
+      !make_tmap(&tw, a->folded, dt, (uint64_t)B, (uint64_t)a->hidden_dim, (uint32_t)w_rows)) {
     snprintf(err, err_len, "tensor-core route: cuTensorMapEncodeTiled failed");
     return TIDE_ERR_CUDA;
   }
@@ -630,14 +761,19 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   cudaError_t e;
   // the opt-in shared memory size is raised once per kernel to the budget
   const bool layer = a->norm_type == TIDE_NORM_LAYER;
-  const void *fn = bf16 ? (layer ? (const void *)tc_route_kernel<true, true> : (const void *)tc_route_kernel<true, false>)
-                        : (layer ? (const void *)tc_route_kernel<false, true> : (const void *)tc_route_kernel<false, false>);
-  static bool attr_set[64][4] = {};
-  const int which = (bf16 ? 2 : 0) + (layer ? 1 : 0);
+  using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, TcRouteParams);
+  // [dtype][layer]: fp32, fp16, bf16 (TIDE_DTYPE_* order)
+  static const Kern kernels[3][2] = {
+      {tc_route_kernel<false, false, true>, tc_route_kernel<false, true, true>},
+      {tc_route_kernel<false, false, false>, tc_route_kernel<false, true, false>},
+      {tc_route_kernel<true, false, false>, tc_route_kernel<true, true, false>}};
+  const Kern fn = kernels[dt][layer ? 1 : 0];
+  static bool attr_set[64][6] = {};
+  const int which = dt * 2 + (layer ? 1 : 0);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev][which]) {
-    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBudget);
+    e = cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBudget);
     if (e != cudaSuccess) {
       snprintf(err, err_len, "tensor-core route: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return TIDE_ERR_CUDA;
@@ -655,12 +791,7 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (bf16)
-    e = layer ? cudaLaunchKernelEx(&cfg, tc_route_kernel<true, true>, tx, txb, txm, tw, p)
-              : cudaLaunchKernelEx(&cfg, tc_route_kernel<true, false>, tx, txb, txm, tw, p);
-  else
-    e = layer ? cudaLaunchKernelEx(&cfg, tc_route_kernel<false, true>, tx, txb, txm, tw, p)
-              : cudaLaunchKernelEx(&cfg, tc_route_kernel<false, false>, tx, txb, txm, tw, p);
+  e = cudaLaunchKernelEx(&cfg, fn, tx, txb, txm, tw, p);
   if (e != cudaSuccess) {
     snprintf(err, err_len, "tensor-core route launch: %s", cudaGetErrorString(e));
     return TIDE_ERR_CUDA;

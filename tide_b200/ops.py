@@ -70,7 +70,7 @@ def prepare_router(down: torch.Tensor, up: torch.Tensor, up_bias: float, norm: N
     bias = norm.bias if norm.kind == NORM_LAYER else None
     down_t, folded, colsum, bias_proj = ops.router_fold(down.detach().float().contiguous(),
                                                         norm.weight, bias, fold_dtype)
-    return PreparedRouter(down_t=down_t, folded=folded if fold_dtype != torch.float32 else None,
+    return PreparedRouter(down_t=down_t, folded=folded,
                           colsum=colsum, bias_proj=bias_proj if bias is not None else None,
                           up=up.detach().float().reshape(-1).contiguous(), up_bias=float(up_bias),
                           bottleneck=int(down.shape[0]))
