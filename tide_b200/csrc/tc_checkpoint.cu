@@ -175,6 +175,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   constexpr int kCols = F32 ? 32 : kTcK;
   constexpr int kTileMax = F32 ? kTcTileUnitsF32 : kTcTileUnits;  // units per tile
   constexpr int kStatWarps = F32 ? 4 : 8;
+  // fp32 stages are twice as large; two of them with two K chunks each
+  // measured faster on thin tiles than three single-chunk stages
+  constexpr int kMinStages = F32 ? 2 : kTcMinStages;
   const uint32_t unit_bytes = kTcUnit * 128;
   const uint32_t w_tile_bytes = kTcM * 128;    // A operand: 128 units
   const uint32_t w_load_bytes = (uint32_t)AT * (uint32_t)p.w_rows * 128;
@@ -208,7 +211,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // MMA commit + 8 statistics warps; fp32: the MMA commit alone (the
       // MMAs wait for the split, the statistics warps' last use of a stage)
       ptx::mbar_init(&empty[s], F32 ? 1 : 1 + 8);
-      ptx::mbar_init(&conv[s], kStatWarps);
+      ptx::mbar_init(&conv[s], 4 + 8);  // fp32: warps 4-15 split the stage
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&acc_full[a], 1);
@@ -257,7 +260,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t chunk_bytes = (F32 ? 2u : 1u) * (x_bytes + wc_bytes);
   int KC = 1;
   for (int c = kTcMaxKc; c > 1; c >>= 1)
-    if (k_chunks % c == 0 && p.ring_bytes / ((uint32_t)c * chunk_bytes) >= (uint32_t)kTcMinStages) {
+    if (k_chunks % c == 0 && p.ring_bytes / ((uint32_t)c * chunk_bytes) >= (uint32_t)kMinStages) {
       KC = c;
       break;
     }
@@ -424,8 +427,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // do both, in that order per tile: while the rows stream they have no
     // epilogue to run (a CTA's range is one tile up to 37888 rows), and eight
     // statistics warps keep each stage's release short.
-    // fp32: warps 4-7 alone take the statistics (and split the stages), so
-    // the epilogue of one tile never holds up the MMAs of the next.
+    // fp32: warps 4-7 take the statistics and split the x chunks, warps
+    // 8-15 split the W' chunks before their epilogue of each tile.
     const bool do_stats = warp < 4 + kStatWarps;
     const bool do_epi = warp >= 8;
     const int t = threadIdx.x - 128;   // statistics row 0..255
@@ -439,28 +442,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int nu = (int)(u_end - u0 < kTileMax ? u_end - u0 : kTileMax);
       const int buf = t_local & 1;
       if constexpr (F32) {
-        if (do_stats && ok) {
-          // thread t owns row t of the tile: its statistics, and the split of
-          // its 128 bytes of each chunk; the 128 threads split W' together.
-          // Per-chunk sums in fp32, across chunks in fp64.  LayerNorm sums
+        if (ok && warp < 8) {
+          // warps 4-7: the x rows.  A tile of 32/64/(96, 128) rows gets
+          // 4/2/1 threads per row, each on 2/4/8 of the row's eight 16-byte
+          // units (lane-rotated by row: distinct banks in each quarter warp),
+          // so one warp never splits a whole thin tile alone.  Statistics:
+          // per-chunk sums in fp32, across chunks in fp64, over the row's
+          // threads with shuffles at the end of the tile.  LayerNorm sums
           // x - x[0], so a large mean does not cancel the variance away.
-          const bool live = (t >> 5) < nu;
+          const int tpr = tile_units == 1 ? 4 : (tile_units == 2 ? 2 : 1);
+          const int upt = 8 / tpr;
+          const int k = threadIdx.x - 128;  // 0..127
+          const int r = k / tpr, part = k % tpr;
+          const bool live = r < nu * kTcUnit;
           double ssd = 0.0, sxd = 0.0;
           float shift = 0.f;
           for (int ks = 0; ks < k_stages; ++ks, ++it) {
             const uint32_t s = it % S, ph = (it / S) & 1u;
             if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
             uint8_t *stg = ring + (size_t)s * stage_bytes;
-            for (int c = 0; c < KC; ++c) {
-              if (live) {
-                uint8_t *row = stg + (size_t)c * x_bytes + (size_t)t * 128;
+            if (live) {
+              for (int c = 0; c < KC; ++c) {
+                uint8_t *row = stg + (size_t)c * x_bytes + (size_t)r * 128;
                 // the row's first column: 16-byte unit 0, at (0 ^ row) of the swizzle
-                if (LAYER && ks == 0 && c == 0) shift = *reinterpret_cast<const float *>(row + ((t & 7) << 4));
+                if (LAYER && ks == 0 && c == 0) shift = *reinterpret_cast<const float *>(row + ((r & 7) << 4));
                 float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const int unit = (j + lane) & 7;
-                  uint8_t *at = row + (unit << 4);
+                for (int j = 0; j < upt; ++j) {
+                  uint8_t *at = row + (((part * upt + j + r) & 7) << 4);
                   const float4 v = *reinterpret_cast<const float4 *>(at);
                   if (LAYER) {
                     const float d0 = v.x - shift, d1 = v.y - shift, d2 = v.z - shift, d3 = v.w - shift;
@@ -477,32 +485,52 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ssd += (double)(ss0 + ss1);
                 sxd += (double)(sx0 + sx1);
               }
-              uint8_t *w = stg + w_off + (size_t)c * wc_bytes;
-              for (int i = t; i < AT * (kTcM * 128 / 16); i += kStatWarps * 32)
-                split_tf32_16(w + (size_t)i * 16, w + lo_off + (size_t)i * 16);
             }
             // the MMAs read the split through the async proxy
             ptx::fence_proxy_async();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&conv[s]);
           }
+          // a row's threads are adjacent lanes (tpr divides 32)
+          for (int off = 1; off < tpr; off <<= 1) {
+            ssd += __shfl_xor_sync(0xffffffffu, ssd, off);
+            sxd += __shfl_xor_sync(0xffffffffu, sxd, off);
+          }
           if (ok && t_local >= 2 &&
               !ptx::mbar_wait(&stat_empty[buf], ((uint32_t)(t_local >> 1) & 1u) ^ 1u, abort_flag))
             ok = false;
           if (ok) {
-            float *st = s_stat + ((size_t)buf * kTcTileRows + t) * 2;
-            const double inv_h = 1.0 / (double)p.H;
-            if (!LAYER) {
-              st[0] = rsqrt_rn((float)(ssd * inv_h) + p.eps);
-              st[1] = 0.f;
-            } else {
-              const double md = sxd * inv_h;
-              const double var = ssd * inv_h - md * md;
-              st[0] = rsqrt_rn((float)(var > 0.0 ? var : 0.0) + p.eps);
-              st[1] = (float)((double)shift + md);
+            if (part == 0) {
+              float *st = s_stat + ((size_t)buf * kTcTileRows + r) * 2;
+              const double inv_h = 1.0 / (double)p.H;
+              if (!LAYER) {
+                st[0] = rsqrt_rn((float)(ssd * inv_h) + p.eps);
+                st[1] = 0.f;
+              } else {
+                const double md = sxd * inv_h;
+                const double var = ssd * inv_h - md * md;
+                st[0] = rsqrt_rn((float)(var > 0.0 ? var : 0.0) + p.eps);
+                st[1] = (float)((double)shift + md);
+              }
             }
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&stat_full[buf]);
+          }
+        } else if (ok) {
+          // warps 8-15: the W' chunks of this tile's stages (their epilogue of
+          // the tile follows), 16-byte words spread over the 256 threads
+          for (int ks = 0; ks < k_stages; ++ks, ++it) {
+            const uint32_t s = it % S, ph = (it / S) & 1u;
+            if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+            uint8_t *stg = ring + (size_t)s * stage_bytes;
+            for (int c = 0; c < KC; ++c) {
+              uint8_t *w = stg + w_off + (size_t)c * wc_bytes;
+              for (int i = et; i < AT * (kTcM * 128 / 16); i += 256)
+                split_tf32_16(w + (size_t)i * 16, w + lo_off + (size_t)i * 16);
+            }
+            ptx::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&conv[s]);
           }
         }
       } else if (do_stats && ok) {
