@@ -420,13 +420,15 @@ def test_split_router_tile_geometry(units, device_count):
 
 @pytest.mark.parametrize("kind", ["rms", "layer"])
 @pytest.mark.parametrize("n,H,B", [(1, 768, 128), (100, 768, 128), (4096, 768, 128),
-                                   (5000, 1024, 200), (12000, 4096, 128), (777, 800, 48)])
+                                   (5000, 1024, 200), (12000, 4096, 128), (777, 800, 48),
+                                   (25000, 512, 128), (40000, 256, 128)])
 def test_fp32_tensor_core_router(n, H, B, kind):
     """fp32 rows on the split path: kind::tf32 MMAs on hi/lo operand splits,
     three products per K step.  Scores within 1e-5 of the oracle (the fp32
-    bar), exits final-normed within 8 ulp, stable compaction.  Tiles of 1-4
-    units, a router wider than 128 (two 128-unit blocks) and narrower (padded
-    units), H = 800 (25 chunks of 32 columns).  LayerNorm rows carry a mean
+    bar), exits final-normed within 8 ulp, stable compaction.  Tiles of 1-8
+    units (6 at 25000 rows; two tiles per CTA, 8 units and 1, at 40000), a
+    router wider than 128 (two 128-unit blocks) and narrower (padded units),
+    H = 800 (25 chunks of 32 columns).  LayerNorm rows carry a mean
     of 3: the statistics are taken about each row's first value, so the
     variance does not cancel away."""
     w = workloads.rows(n, H, torch.float32, b=B, seed=1300 + n, norm_kind=kind,

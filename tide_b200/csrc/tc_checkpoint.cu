@@ -47,10 +47,10 @@
 // (about 2^-21 of each product) -- the fp32 score bar of 1e-5 holds, where a
 // single tf32 product (2^-11) would not.  A K chunk is still 128 bytes of a
 // row (32 fp32 columns), so the shared-memory layout and descriptors are the
-// ones of the 16-bit case.  Warps 4-7 split each landed stage in place (hi
+// ones of the 16-bit case.  Warps 4-15 split each landed stage in place (hi
 // over the loaded values, lo into the stage's second half, x and W' alike)
 // while they take the row statistics; the MMA waits for that instead of the
-// TMA.  Tiles are at most 128 rows so that three stages fit.
+// TMA.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdio.h>
@@ -87,7 +87,6 @@ constexpr int kTcAux = 12288;     // barriers, flags, per-unit vectors, row stat
 static_assert((3 * kTcMaxStages + 9) * 8 + 16 + 3 * 256 * 4 + 2 * 256 * 2 * 4 + 4 * 256 * 4 +
                       8 * 4 <= kTcAux,
               "auxiliary shared-memory area");
-constexpr int kTcTileUnitsF32 = 4;  // fp32: stages hold hi and lo, so tiles of 128 rows
 
 struct TcRouteParams {
   int64_t n_cap;
@@ -173,10 +172,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int NA = p.n_acc, AT = p.a_tiles;
   // a K chunk is 128 bytes of a row: 64 16-bit or 32 fp32 columns
   constexpr int kCols = F32 ? 32 : kTcK;
-  constexpr int kTileMax = F32 ? kTcTileUnitsF32 : kTcTileUnits;  // units per tile
-  constexpr int kStatWarps = F32 ? 4 : 8;
-  // fp32 stages are twice as large; two of them with two K chunks each
-  // measured faster on thin tiles than three single-chunk stages
+  constexpr int kTileMax = kTcTileUnits;  // units per tile
+  // fp32 stages are twice as large: two of them (two K chunks each on thin
+  // tiles; 256-row tiles) measured faster than more, smaller stages
   constexpr int kMinStages = F32 ? 2 : kTcMinStages;
   const uint32_t unit_bytes = kTcUnit * 128;
   const uint32_t w_tile_bytes = kTcM * 128;    // A operand: 128 units
@@ -216,7 +214,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&acc_full[a], 1);
       ptx::mbar_init(&acc_empty[a], 8);   // 8 epilogue warps
-      ptx::mbar_init(&stat_full[a], kStatWarps);
+      ptx::mbar_init(&stat_full[a], 8);   // 8 statistics warps
       ptx::mbar_init(&stat_empty[a], 8);  // 8 epilogue warps
     }
     ptx::mbar_init(drain, 1);
@@ -427,9 +425,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // do both, in that order per tile: while the rows stream they have no
     // epilogue to run (a CTA's range is one tile up to 37888 rows), and eight
     // statistics warps keep each stage's release short.
-    // fp32: warps 4-7 take the statistics and split the x chunks, warps
-    // 8-15 split the W' chunks before their epilogue of each tile.
-    const bool do_stats = warp < 4 + kStatWarps;
+    // fp32: warps 4-11 take the statistics and split the x chunks, warps
+    // 4-15 the W' chunks, warps 8-15 before their epilogue of each tile.
+    const bool do_stats = warp < 12;
     const bool do_epi = warp >= 8;
     const int t = threadIdx.x - 128;   // statistics row 0..255
     const int q = warp & 3;
@@ -442,27 +440,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int nu = (int)(u_end - u0 < kTileMax ? u_end - u0 : kTileMax);
       const int buf = t_local & 1;
       if constexpr (F32) {
-        if (ok && warp < 8) {
-          // warps 4-7: the x rows.  A tile of 32/64/(96, 128) rows gets
-          // 4/2/1 threads per row, each on 2/4/8 of the row's eight 16-byte
-          // units (lane-rotated by row: distinct banks in each quarter warp),
-          // so one warp never splits a whole thin tile alone.  Statistics:
-          // per-chunk sums in fp32, across chunks in fp64, over the row's
-          // threads with shuffles at the end of the tile.  LayerNorm sums
-          // x - x[0], so a large mean does not cancel the variance away.
-          const int tpr = tile_units == 1 ? 4 : (tile_units == 2 ? 2 : 1);
+        if (ok) {
+          // warps 4-11: the x rows.  A tile of 32/64/(96, 128)/(160-256) rows
+          // gets 8/4/2/1 threads per row, each on 1/2/4/8 of the row's eight
+          // 16-byte units (lane-rotated by row: distinct banks in each
+          // quarter warp).  Statistics: per-chunk sums in fp32, across chunks
+          // in fp64, over the row's threads with shuffles at the end of the
+          // tile.  LayerNorm sums x - x[0], so a large mean does not cancel
+          // the variance away.  Then warps 4-15 split the W' chunks together.
+          const bool xg = warp < 12;
+          const int k = threadIdx.x - 128;  // 0..383
+          const int tpr = tile_units == 1 ? 8 : (tile_units == 2 ? 4 : (tile_units <= 4 ? 2 : 1));
           const int upt = 8 / tpr;
-          const int k = threadIdx.x - 128;  // 0..127
           const int r = k / tpr, part = k % tpr;
-          const bool live = r < nu * kTcUnit;
+          const bool live = xg && r < nu * kTcUnit;
           double ssd = 0.0, sxd = 0.0;
           float shift = 0.f;
           for (int ks = 0; ks < k_stages; ++ks, ++it) {
             const uint32_t s = it % S, ph = (it / S) & 1u;
             if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
             uint8_t *stg = ring + (size_t)s * stage_bytes;
-            if (live) {
-              for (int c = 0; c < KC; ++c) {
+            for (int c = 0; c < KC; ++c) {
+              if (live) {
                 uint8_t *row = stg + (size_t)c * x_bytes + (size_t)r * 128;
                 // the row's first column: 16-byte unit 0, at (0 ^ row) of the swizzle
                 if (LAYER && ks == 0 && c == 0) shift = *reinterpret_cast<const float *>(row + ((r & 7) << 4));
@@ -485,52 +484,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ssd += (double)(ss0 + ss1);
                 sxd += (double)(sx0 + sx1);
               }
+              uint8_t *w = stg + w_off + (size_t)c * wc_bytes;
+              for (int i = k; i < AT * (kTcM * 128 / 16); i += 384)
+                split_tf32_16(w + (size_t)i * 16, w + lo_off + (size_t)i * 16);
             }
             // the MMAs read the split through the async proxy
             ptx::fence_proxy_async();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&conv[s]);
           }
-          // a row's threads are adjacent lanes (tpr divides 32)
-          for (int off = 1; off < tpr; off <<= 1) {
-            ssd += __shfl_xor_sync(0xffffffffu, ssd, off);
-            sxd += __shfl_xor_sync(0xffffffffu, sxd, off);
-          }
-          if (ok && t_local >= 2 &&
-              !ptx::mbar_wait(&stat_empty[buf], ((uint32_t)(t_local >> 1) & 1u) ^ 1u, abort_flag))
-            ok = false;
-          if (ok) {
-            if (part == 0) {
-              float *st = s_stat + ((size_t)buf * kTcTileRows + r) * 2;
-              const double inv_h = 1.0 / (double)p.H;
-              if (!LAYER) {
-                st[0] = rsqrt_rn((float)(ssd * inv_h) + p.eps);
-                st[1] = 0.f;
-              } else {
-                const double md = sxd * inv_h;
-                const double var = ssd * inv_h - md * md;
-                st[0] = rsqrt_rn((float)(var > 0.0 ? var : 0.0) + p.eps);
-                st[1] = (float)((double)shift + md);
+          if (xg) {
+            // a row's threads are adjacent lanes (tpr divides 32)
+            for (int off = 1; off < tpr; off <<= 1) {
+              ssd += __shfl_xor_sync(0xffffffffu, ssd, off);
+              sxd += __shfl_xor_sync(0xffffffffu, sxd, off);
+            }
+            if (ok && t_local >= 2 &&
+                !ptx::mbar_wait(&stat_empty[buf], ((uint32_t)(t_local >> 1) & 1u) ^ 1u, abort_flag))
+              ok = false;
+            if (ok) {
+              if (part == 0) {
+                float *st = s_stat + ((size_t)buf * kTcTileRows + r) * 2;
+                const double inv_h = 1.0 / (double)p.H;
+                if (!LAYER) {
+                  st[0] = rsqrt_rn((float)(ssd * inv_h) + p.eps);
+                  st[1] = 0.f;
+                } else {
+                  const double md = sxd * inv_h;
+                  const double var = ssd * inv_h - md * md;
+                  st[0] = rsqrt_rn((float)(var > 0.0 ? var : 0.0) + p.eps);
+                  st[1] = (float)((double)shift + md);
+                }
               }
+              __syncwarp();
+              if (lane == 0) ptx::mbar_arrive(&stat_full[buf]);
             }
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&stat_full[buf]);
-          }
-        } else if (ok) {
-          // warps 8-15: the W' chunks of this tile's stages (their epilogue of
-          // the tile follows), 16-byte words spread over the 256 threads
-          for (int ks = 0; ks < k_stages; ++ks, ++it) {
-            const uint32_t s = it % S, ph = (it / S) & 1u;
-            if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
-            uint8_t *stg = ring + (size_t)s * stage_bytes;
-            for (int c = 0; c < KC; ++c) {
-              uint8_t *w = stg + w_off + (size_t)c * wc_bytes;
-              for (int i = et; i < AT * (kTcM * 128 / 16); i += 256)
-                split_tf32_16(w + (size_t)i * 16, w + lo_off + (size_t)i * 16);
-            }
-            ptx::fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&conv[s]);
           }
         }
       } else if (do_stats && ok) {
