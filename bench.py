@@ -13,6 +13,10 @@ counts chain on the device between checkpoints (no host sync).  One step =
 the six checkpoints.  Inputs (1.1 GiB per step) exceed the 126 MB L2, so no
 explicit flush is needed between steps.
 
+Third workload ("kernel_fp32_4096x768", --workload): the reference's own
+kernel-level case, one checkpoint of 4096 fp32 rows of H = 768 (N(0,1) times
+a per-row scale U(0.5, 2)), RMSNorm weight N(1, 0.02), 30 % exits.
+
 Second workload ("qwen3_8b_decode_checkpoints", --workload): one decode step
 of a Qwen3-8B-architecture batch of 256 sequences, routers at layers
 3/7/.../31 (eight checkpoints, H = 4096), each exiting ~10 % of the rows
@@ -23,7 +27,8 @@ Multi-GPU: one process per GPU under torchrun; every rank processes its own
 batch (weak scaling, no data-path collective); timing is the max over ranks.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload llama8b_prefill_checkpoints|qwen3_8b_decode_checkpoints]
+                  [--workload llama8b_prefill_checkpoints|qwen3_8b_decode_checkpoints|
+                              kernel_fp32_4096x768]
 """
 from __future__ import annotations
 
@@ -51,12 +56,17 @@ WORKLOADS = {
     # exits: fraction of the rows still active at each checkpoint
     "qwen3_8b_decode_checkpoints": {"rows": 256, "layers": [3, 7, 11, 15, 19, 23, 27, 31],
                                     "exit_fractions": [0.10] * 8, "of": "active"},
+    # one router over fp32 rows scaled per row, RMSNorm weight N(1, 0.02)
+    "kernel_fp32_4096x768": {"rows": 4096, "layers": [0], "exit_fractions": [0.30],
+                             "of": "active", "hidden": 768, "dtype": "f32", "inputs": "scaled"},
 }
+DTYPE_NAMES = {"bf16": torch.bfloat16, "f32": torch.float32}
 WORKLOAD = "llama8b_prefill_checkpoints"
 LAYERS = WORKLOADS[WORKLOAD]["layers"]
 EXIT_FRACTIONS = WORKLOADS[WORKLOAD]["exit_fractions"]
 EXITS_OF = WORKLOADS[WORKLOAD]["of"]
 ROWS, HIDDEN, BOTTLENECK = WORKLOADS[WORKLOAD]["rows"], 4096, 128
+DTYPE = "bf16"
 
 
 # DRAM bytes (read + write) of checkpoint 0's two kernels (router + mover),
@@ -159,12 +169,19 @@ class Workload:
         dev = torch.device("cuda")
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
         self.path = path
-        self.norm = NormSpec(NORM_RMS, torch.ones(HIDDEN, device=dev), None, 1e-5)
+        dt = DTYPE_NAMES[DTYPE]
+        scaled = WORKLOADS[WORKLOAD].get("inputs") == "scaled"
+        w_norm = (1.0 + 0.02 * torch.randn(HIDDEN, generator=g, device=dev) if scaled
+                  else torch.ones(HIDDEN, device=dev))
+        self.norm = NormSpec(NORM_RMS, w_norm, None, 1e-5)
         self.runner = CheckpointRunner(dev)
         self.x, self.routers, self.active = [], [], []
         active = ROWS
         for k, layer in enumerate(LAYERS):
-            x = torch.randn(ROWS, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+            x = torch.randn(ROWS, HIDDEN, generator=g, device=dev)
+            if scaled:
+                x = x * (torch.rand(ROWS, 1, generator=g, device=dev) * 1.5 + 0.5)
+            x = x.to(dt)
             down = 0.02 * torch.randn(BOTTLENECK, HIDDEN, generator=g, device=dev)
             up = 0.02 * torch.randn(1, BOTTLENECK, generator=g, device=dev)
             z = workloads.prebias_logits_torch(x[:active], "rms", self.norm.weight, None, 1e-5,
@@ -174,15 +191,15 @@ class Workload:
             else:
                 exits = int(round(EXIT_FRACTIONS[k] * active))
             bias = workloads.bias_for_exit_fraction(z, exits / active, THRESHOLD)
-            self.routers.append(prepare_router(down, up, bias, self.norm, torch.bfloat16))
+            self.routers.append(prepare_router(down, up, bias, self.norm, dt))
             self.x.append(x)
             self.active.append(active)
             active -= exits
         self.positions0 = torch.arange(ROWS, device=dev, dtype=torch.int64)
         self.slots0 = torch.arange(ROWS, device=dev, dtype=torch.int32)
         self.count0 = torch.tensor([ROWS], dtype=torch.int32, device=dev)
-        self.out = torch.zeros(ROWS, HIDDEN, dtype=torch.bfloat16, device=dev)
-        self.compact = torch.empty(ROWS, HIDDEN, dtype=torch.bfloat16, device=dev)
+        self.out = torch.zeros(ROWS, HIDDEN, dtype=dt, device=dev)
+        self.compact = torch.empty(ROWS, HIDDEN, dtype=dt, device=dev)
         self.pos = [torch.empty(ROWS, dtype=torch.int64, device=dev) for _ in range(2)]
         self.slots = [torch.empty(ROWS, dtype=torch.int32, device=dev) for _ in range(2)]
         self.counts = torch.zeros(len(LAYERS), 2, dtype=torch.int32, device=dev)
@@ -283,28 +300,29 @@ def host_threads() -> int:
     return n
 
 
-def cpu_checkpoint_sample(x_bf16: np.ndarray, down: np.ndarray, up: np.ndarray, bias: float):
+def cpu_checkpoint_sample(x: np.ndarray, down: np.ndarray, up: np.ndarray, bias: float,
+                          norm_weight: np.ndarray):
     """The oracle on one checkpoint's rows (the reference's CPU path,
-    restated): returns seconds."""
+    restated): returns seconds.  x holds bf16 bit patterns (uint16) or fp32."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import tide_oracle as O
 
-    norm = {"kind": "rms", "weight": np.ones(x_bf16.shape[1], dtype=np.float32), "bias": None,
-            "eps": 1e-5}
-    out = np.zeros_like(x_bf16)
+    norm = {"kind": "rms", "weight": norm_weight, "bias": None, "eps": 1e-5}
+    out = np.zeros_like(x)
     t0 = time.perf_counter()
-    O.checkpoint(x_bf16, O.BF16, norm, down, up, bias, THRESHOLD,
-                 positions=np.arange(x_bf16.shape[0], dtype=np.int64),
-                 slots=np.arange(x_bf16.shape[0], dtype=np.int32), out_buffer=out)
+    O.checkpoint(x, O.F32 if x.dtype == np.float32 else O.BF16, norm, down, up, bias, THRESHOLD,
+                 positions=np.arange(x.shape[0], dtype=np.int64),
+                 slots=np.arange(x.shape[0], dtype=np.int32), out_buffer=out)
     return time.perf_counter() - t0
 
 
 def cpu_sample_inputs(wl: "Workload", rows: int):
-    x = wl.x[0][:rows].contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    x = wl.x[0][:rows].contiguous()
+    x = x.cpu().numpy() if x.dtype == torch.float32 else x.view(torch.int16).cpu().numpy().view(np.uint16)
     r = wl.routers[0]
     down = r.down_t.T.contiguous().cpu().numpy()
     up = r.up.cpu().numpy().reshape(1, -1)
-    return x, down, up, r.up_bias
+    return x, down, up, r.up_bias, wl.norm.weight.cpu().numpy()
 
 
 # ----------------------------------------------------------------- main
@@ -318,22 +336,22 @@ def run_reference(args, world, rank):
     wl = Workload(rank, 0)
     rows = min(4096, ROWS)
     cores = host_threads()
-    x, down, up, bias = cpu_sample_inputs(wl, rows)
+    x, down, up, bias, nw = cpu_sample_inputs(wl, rows)
     for _ in range(args.warmup):
-        cpu_checkpoint_sample(x, down, up, bias)
-    ts = [cpu_checkpoint_sample(x, down, up, bias) for _ in range(args.steps)]
+        cpu_checkpoint_sample(x, down, up, bias, nw)
+    ts = [cpu_checkpoint_sample(x, down, up, bias, nw) for _ in range(args.steps)]
     t = sum(ts)
     v = rows * args.steps / t
     line = {
         "impl": "reference", "metric": "router_compact_scatter_tokens_per_s", "value": v,
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * t / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
         "config": {"workload": WORKLOAD, "sample_rows_per_step": rows, "hidden": HIDDEN,
                    "bottleneck": BOTTLENECK,
                    "checkpoint": f"first router (layer {LAYERS[0]}), {EXIT_FRACTIONS[0]:.0%} exit"},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"one checkpoint ({rows} rows x {HIDDEN} bf16) per step"},
+                         "sample": f"one checkpoint ({rows} rows x {HIDDEN} {DTYPE}) per step"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -353,7 +371,8 @@ def main():
     args = ap.parse_args()
     wk = WORKLOADS[args.workload]
     globals().update(WORKLOAD=args.workload, LAYERS=wk["layers"], EXIT_FRACTIONS=wk["exit_fractions"],
-                     EXITS_OF=wk["of"], ROWS=args.rows if args.rows else wk["rows"])
+                     EXITS_OF=wk["of"], ROWS=args.rows if args.rows else wk["rows"],
+                     HIDDEN=wk.get("hidden", 4096), DTYPE=wk.get("dtype", "bf16"))
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
         run_reference(args, world, rank)
@@ -425,7 +444,7 @@ def main():
     global_counts = tdist.sum_counts(world, wl.counts).cpu()
     collectives = gather_timings(world, wl) if world > 1 else None
 
-    e = 2
+    e = 4 if DTYPE == "f32" else 2
     alg = [algorithmic_bytes(active[k], exits_per_stage[k], HIDDEN, e) for k in range(len(LAYERS))]
     achieved = alg[0] / (per_ck[0] / 1000.0) / 1e9  # the first (largest) checkpoint
     achieved_all = sum(alg) / (elapsed / args.steps) / 1e9
@@ -455,6 +474,11 @@ def main():
     host_counts = torch.empty_like(wl.counts, device="cpu").pin_memory()
 
     e_graph = wl.capture(dev_x)[0]
+    # one untimed step: the graph's first launch uploads it to the device
+    for k in range(len(LAYERS)):
+        dev_x[k][: active[k]].copy_(host_x[k], non_blocking=True)
+    e_graph.replay()
+    host_counts.copy_(wl.counts, non_blocking=True)
     barrier(world)
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -476,11 +500,11 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rows = min(4096, ROWS)
         cores = host_threads()
-        x, down, up, bias = cpu_sample_inputs(wl, rows)
-        cpu_checkpoint_sample(x, down, up, bias)
-        t = min(cpu_checkpoint_sample(x, down, up, bias) for _ in range(3))
+        x, down, up, bias, nw = cpu_sample_inputs(wl, rows)
+        cpu_checkpoint_sample(x, down, up, bias, nw)
+        t = min(cpu_checkpoint_sample(x, down, up, bias, nw) for _ in range(3))
         cpu = {"value": rows / t, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"oracle, one checkpoint of {rows} rows x {HIDDEN} bf16 "
+               "sample": f"oracle, one checkpoint of {rows} rows x {HIDDEN} {DTYPE} "
                          f"(layer-{LAYERS[0]} router), best of 3"}
 
     n_launch = sum(launches_per_checkpoint(p) for p in wl.paths.values()) * args.steps
@@ -489,7 +513,7 @@ def main():
             "metric": "router_compact_scatter_tokens_per_s", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
             "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "hidden": HIDDEN,
                        "bottleneck": BOTTLENECK, "checkpoint_layers": LAYERS,
                        f"exit_fractions_of_{EXITS_OF}": EXIT_FRACTIONS,

@@ -461,10 +461,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
             uint8_t *stg = ring + (size_t)s * stage_bytes;
             for (int c = 0; c < KC; ++c) {
+              if (LAYER && ks == 0 && c == 0) {
+                // the row's first column: 16-byte unit 0, at (0 ^ row) of the
+                // swizzle; read by every thread of the row before any of them
+                // writes its hi parts in place (a row's threads share a warp)
+                if (live) shift = *reinterpret_cast<const float *>(stg + (size_t)r * 128 + ((r & 7) << 4));
+                __syncwarp();
+              }
               if (live) {
                 uint8_t *row = stg + (size_t)c * x_bytes + (size_t)r * 128;
-                // the row's first column: 16-byte unit 0, at (0 ^ row) of the swizzle
-                if (LAYER && ks == 0 && c == 0) shift = *reinterpret_cast<const float *>(row + ((r & 7) << 4));
                 float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
                 for (int j = 0; j < upt; ++j) {
                   uint8_t *at = row + (((part * upt + j + r) & 7) << 4);
