@@ -186,6 +186,34 @@ def test_generate(tmp_path):
     assert out.shape[1] >= 5
 
 
+@pytest.mark.parametrize("n,H", [(1, 2048), (300, 800), (4096, 768), (5000, 4096), (64, 784)])
+def test_torch_op_router_fp32_tensor_cores(n, H):
+    """torch.ops.tide.fused_layernorm_route on fp32 rows takes the tensor-core
+    router (three tf32 products) when H % 32 == 0, and the SIMT router
+    otherwise (H = 784): scores within the fp32 bar of 1e-5 of the oracle and
+    of the C ABI's SIMT router, on router weights at the reference's scale of
+    0.02."""
+    from tests.gpu_helpers import lib, ptr, stream
+    from tide_b200 import _native, capi
+
+    ops = _native.ops()
+    g = torch.Generator().manual_seed(n + H)
+    x = (torch.randn(n, H, generator=g) * (torch.rand(n, 1, generator=g) * 1.5 + 0.5)).to(DEV)
+    nw = (1.0 + 0.02 * torch.randn(H, generator=g)).to(DEV)
+    dw = (0.02 * torch.randn(H, 128, generator=g)).to(DEV)
+    uw = (0.02 * torch.randn(128, 1, generator=g)).to(DEV)
+    s = ops.fused_layernorm_route(x, nw, dw, uw, 1e-5)
+    simt = torch.empty(n, device=DEV)
+    capi.check(lib(), lib().tide_fused_layernorm_route(capi.DTYPE_F32, ptr(x), ptr(nw), ptr(dw), ptr(uw),
+                                                       1e-5, ptr(simt), n, H, 128, stream()),
+               "fused_layernorm_route")
+    ref = O.fused_layernorm_route(storage_np(x), O.F32, nw.cpu().numpy(), dw.cpu().numpy(),
+                                  uw.cpu().numpy(), 1e-5)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(s.cpu().numpy(), ref, atol=1e-5, rtol=0)
+    np.testing.assert_allclose(s.cpu().numpy(), simt.cpu().numpy(), atol=1e-5, rtol=0)
+
+
 def test_torch_ops_reference_semantics():
     """torch.ops.tide.* with the reference's calling conventions
     (tests/test_kernels.py:64-186 of the reference), seeded."""
