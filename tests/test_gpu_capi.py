@@ -198,22 +198,24 @@ def test_checkpoint_device_row_count():
     assert np.array_equal(ck.positions_out.cpu().numpy()[: len(keep)], keep)
 
 
-@pytest.mark.parametrize("path", [capi.PATH_SIMT, capi.PATH_TC, capi.PATH_TC_SPLIT])
+@pytest.mark.parametrize("dtype,path", [(torch.bfloat16, capi.PATH_SIMT), (torch.bfloat16, capi.PATH_TC),
+                                        (torch.bfloat16, capi.PATH_TC_SPLIT),
+                                        (torch.float32, capi.PATH_TC_SPLIT)])
 @pytest.mark.parametrize("live", [0, 1, 63, 64, 65])
-def test_device_row_count_edges(path, live):
+def test_device_row_count_edges(dtype, path, live):
     """A live count on the device of 0 (an earlier checkpoint exited every
     row), 1, and around a 64-row tile, below a launch capacity of 1000 rows:
     nothing past the live rows is read or written; with no live rows the
-    counts are {0, 0} and every output stays untouched."""
+    counts are {0, 0} and every output stays untouched.  fp32 rows on the
+    split path (the tf32 router) too."""
     n_cap, H = 1000, 512
-    dtype = torch.bfloat16
     w = workloads.rows(n_cap, H, dtype, seed=70 + live, unit_norm_weight=False)
     x = w["x"].to(DEV)
     nw = w["norm_weight"].to(DEV)
     norm = oracle_norm("rms", nw, None, 1e-5)
     x_live = storage_np(x)[:live]
-    z = O.router_logits(O.final_norm(O.to_f32(storage_np(x), O.BF16), norm), w["down"].numpy(),
-                        w["up"].numpy())
+    z = O.router_logits(O.final_norm(O.to_f32(storage_np(x), TORCH2O[dtype]), norm),
+                        w["down"].numpy(), w["up"].numpy())
     bias = workloads.bias_for_exit_fraction(z, 0.4, THR)
     out = torch.zeros_like(x)
     out0 = storage_np(out).copy()
@@ -231,7 +233,7 @@ def test_device_row_count_edges(path, live):
         assert np.all(ck.exit_positions_out.cpu().numpy() == -7)
         assert np.array_equal(storage_np(out), out0)
         return
-    res = O.checkpoint(x_live, O.BF16, norm, w["down"].numpy(), w["up"].numpy(), bias, THR)
+    res = O.checkpoint(x_live, TORCH2O[dtype], norm, w["down"].numpy(), w["up"].numpy(), bias, THR)
     res["eps"] = 1e-5
     view = types.SimpleNamespace(
         x=ck.x[:live], scores_out=ck.scores_out[:live], counts=ck.counts, error_word=ck.error_word,
