@@ -493,6 +493,46 @@ def test_full_size_properties(path):
     assert int(out[untouched].abs().sum()) == 0
 
 
+def test_full_size_properties_fp32():
+    """32768 x 4096 fp32 rows on the split path (the tf32 router, three
+    products): counts add up, positions are a stable partition, survivors are
+    bit-exact copies, exits are the final norm of their row (<= 8 ulp against
+    a torch fp32 evaluation), decisions follow the scores, scores match a
+    torch fp32 router (no tf32) within 1e-5."""
+    assert not torch.backends.cuda.matmul.allow_tf32
+    n, H = 32768, 4096
+    w = workloads.rows(n, H, torch.float32, seed=78, device=DEV, unit_norm_weight=False)
+    x = w["x"]
+    nw = w["norm_weight"]
+    z = workloads.prebias_logits_torch(x, "rms", nw, None, 1e-5, w["down"], w["up"])
+    bias = workloads.bias_for_exit_fraction(z, 0.3, THR)
+    out = torch.zeros_like(x)
+    ck = Checkpoint(x, "rms", nw, None, 1e-5, w["down"], w["up"], bias, THR, out_buffer=out,
+                    path=capi.PATH_TC_SPLIT)
+    assert ck.path() == capi.PATH_TC_SPLIT
+    ck()
+    torch.cuda.synchronize()
+    assert int(ck.error_word.item()) == 0
+    s = ck.scores_out
+    assert float((s - torch.sigmoid(z + bias)).abs().max()) <= 1e-5
+    ex = s > THR
+    c = ck.counts.cpu().tolist()
+    assert c == [int((~ex).sum()), int(ex.sum())]
+    assert abs(c[1] - 0.3 * n) < 0.01 * n
+    keep_idx = torch.nonzero(~ex).flatten()
+    ex_idx = torch.nonzero(ex).flatten()
+    assert torch.equal(ck.positions_out[: c[0]], keep_idx)
+    assert torch.equal(ck.exit_positions_out[: c[1]], ex_idx)
+    assert torch.equal(ck.compact_out[: c[0]], x[keep_idx])
+    xe = x[ex_idx]
+    normed = nw * (xe * torch.rsqrt(xe.pow(2).mean(-1, keepdim=True) + 1e-5))
+    diff = (out[ex_idx].view(torch.int32).long() - normed.view(torch.int32).long()).abs()
+    assert int(diff.max()) <= 8
+    untouched = torch.ones(n, dtype=torch.bool, device=DEV)
+    untouched[ex_idx] = False
+    assert int(out[untouched].abs().sum()) == 0
+
+
 # the bandwidth sweep's shapes: N up to 1M rows, H 2048..8192, exit fractions
 # 0..0.9 (the largest case holds 3 x 16 GiB of rows on the device)
 SWEEP = [(65536, 2048, 0.0), (65536, 5120, 0.1), (16384, 8192, 0.5), (262144, 4096, 0.9),
