@@ -79,9 +79,10 @@ __device__ __forceinline__ float rsqrt_rn(float v) { return __fdiv_rn(1.0f, __fs
 // SiLU and sigmoid in fp32 (x * sigmoid(x), 1 / (1 + e^-x)).
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
-// Fast SiLU for the tensor-core paths (scores held to 1e-2): the hardware
-// exponential and the approximate division, ~1e-6 relative error and no
-// branches, so an unrolled loop of them keeps the MUFU pipe busy.  The
+// Fast SiLU for the fp32 tensor-core router (scores held to 1e-5): the
+// hardware exponential and the approximate division, a few 1e-6 relative at
+// most over the logits' range, and no branches, so an unrolled loop of them
+// keeps the MUFU pipe busy.  The
 // exponent is clamped at 80 (e^80 < 2^126, inside __fdividef's range); below
 // -80 SiLU is 0 to fp32 precision anyway.
 __device__ __forceinline__ float silu_fast(float x) {

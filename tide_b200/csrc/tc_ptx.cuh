@@ -101,11 +101,6 @@ __device__ __forceinline__ void bulk_store(void *dst, const void *src, uint32_t 
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
-// Wait until every committed bulk store of this thread has finished reading
-// its shared-memory source.
-__device__ __forceinline__ void bulk_wait_read_all() {
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
 // Wait until at most `n` (0..7) of this thread's committed bulk-store groups
 // are still reading their shared-memory sources.
 __device__ __forceinline__ void bulk_wait_read(int n) {
@@ -241,20 +236,6 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t local_smem_addr, uint32
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
   return r;
-}
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
-               "f"(c), "f"(d)
-               : "memory");
-}
-__device__ __forceinline__ void st_cluster_v2(uint32_t addr, float a, float b) {
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
-}
-// Arrive on an mbarrier of (possibly) another CTA of the cluster, releasing
-// this thread's prior writes at cluster scope.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
 }
 // Relaxed arrive: no ordering of this thread's earlier memory operations (use
 // after fence_cluster() when the arrival publishes data).
