@@ -75,6 +75,17 @@ DTYPE = "bf16"
 NCU_TRAFFIC_CKPT0 = {"rows": 32768, "path": "tc_split", "bytes": (269.5 + 63.3 + 221.3 + 209.0) * 1e6}
 
 
+def e2e_step_count(requested, h2d_bytes_nominal: int) -> int:
+    """Steps of the e2e region: as requested, else enough for about 2 GB of
+    host-to-device copies (at least 3, at most 200), so that a small
+    workload's region is not a few hundred microseconds of host jitter.  The
+    nominal bytes (rows x H x element size x checkpoints) are the same on
+    every rank."""
+    if requested is not None:
+        return int(requested)
+    return max(3, min(200, int(2e9 // max(int(h2d_bytes_nominal), 1))))
+
+
 def algorithmic_bytes(n: int, exits: int, h: int, e: int) -> int:
     """Bytes a single pass must move for one checkpoint of n rows: read every
     row and write it once (survivor to the dense buffer, exit to its
@@ -364,7 +375,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--path", default="auto", choices=["auto", "simt", "tc", "tc_split"])
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=None,
+                    help="e2e steps (default: about 2 GB of host->device copies, at least 3)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--rows", type=int, default=None, help="rows per GPU (profiling runs)")
@@ -473,6 +485,7 @@ def main():
     dev_x = [torch.empty_like(x) for x in wl.x]
     host_counts = torch.empty_like(wl.counts, device="cpu").pin_memory()
 
+    e2e_steps = e2e_step_count(args.e2e_steps, ROWS * HIDDEN * e * len(LAYERS))
     e_graph = wl.capture(dev_x)[0]
     # one untimed step: the graph's first launch uploads it to the device
     for k in range(len(LAYERS)):
@@ -483,7 +496,7 @@ def main():
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record()
-    for _ in range(args.e2e_steps):
+    for _ in range(e2e_steps):
         for k in range(len(LAYERS)):
             dev_x[k][: active[k]].copy_(host_x[k], non_blocking=True)
         e_graph.replay()
@@ -491,9 +504,9 @@ def main():
     e_end.record()
     torch.cuda.synchronize()
     e_el = max_over_ranks(world, e_start.elapsed_time(e_end) / 1000.0)
-    e2e = {"value": world * rows_per_step * args.e2e_steps / e_el, "unit": "tokens/s",
+    e2e = {"value": world * rows_per_step * e2e_steps / e_el, "unit": "tokens/s",
            "h2d_bytes_per_step": int(sum(x.numel() * x.element_size() for x in host_x)),
-           "d2h_bytes_per_step": int(host_counts.numel() * 4), "steps": args.e2e_steps}
+           "d2h_bytes_per_step": int(host_counts.numel() * 4), "steps": e2e_steps}
     del e_graph, step_graph, ck_graphs
 
     cpu = None
