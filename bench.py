@@ -1,34 +1,46 @@
 """Benchmark of the early-exit hot path (router -> compaction -> scatter).
 
-Workload per GPU ("llama8b_prefill_checkpoints"): the checkpoint sweep of a
-Llama-3.1-8B-architecture prefill batch of 16 x 2048 tokens = 32768 rows of
-H = 4096 bf16 hidden states, routers at layers 8/12/16/20/24/28 (RMSNorm
-eps 1e-5, router 4096 -> 128 -> 1) with biases placed so that 5/10/15/20/
-20/30 % of the batch exits at each checkpoint (everything by layer 28).
-Each checkpoint reads its own synthetic hidden-state tensor (rows N(0,1),
-the hidden states of the still-active tokens at that layer), scores it,
-compacts survivors (rows, int64 positions, int32 KV slots) into a dense
+Default workload per GPU ("llama8b_prefill_checkpoints"): the checkpoint
+sweep of a Llama-3.1-8B-architecture prefill batch of 16 x 2048 tokens =
+32768 rows of H = 4096 bf16 hidden states, routers at layers 8/12/16/20/24/28
+(RMSNorm eps 1e-5, router 4096 -> 128 -> 1) with biases placed so that
+5/10/15/20/20/30 % of the batch exits at each checkpoint (everything by layer
+28).  Each checkpoint reads its own synthetic hidden-state tensor (rows
+N(0,1), the hidden states of the still-active tokens at that layer), scores
+it, compacts survivors (rows, int64 positions, int32 KV slots) into a dense
 buffer and writes exits, final-normed, to their original positions.  Active
 counts chain on the device between checkpoints (no host sync).  One step =
 the six checkpoints.  Inputs (1.1 GiB per step) exceed the 126 MB L2, so no
-explicit flush is needed between steps.
+explicit flush is needed between steps.  The same run also measures the
+8B-architecture prefill through the engine (random-init Llama-3.1-8B
+architecture, bf16, batch 16 x 2048 split over the ranks): engine(input_ids)
+against the model's own forward, 3 warm-up and 10 timed calls each.
 
-Third workload ("kernel_fp32_4096x768", --workload): the reference's own
-kernel-level case, one checkpoint of 4096 fp32 rows of H = 768 (N(0,1) times
-a per-row scale U(0.5, 2)), RMSNorm weight N(1, 0.02), 30 % exits.
+Inputs: the first CAL_ROWS rows of every checkpoint's tensor and every
+router's weights come from a CPU torch.Generator, so the CPU reference arm
+sees bit-identical rows; the router biases are placed on those rows (both
+arms compute the same biases).  The rest of the rows are drawn on the device.
 
-Second workload ("qwen3_8b_decode_checkpoints", --workload): one decode step
-of a Qwen3-8B-architecture batch of 256 sequences, routers at layers
-3/7/.../31 (eight checkpoints, H = 4096), each exiting ~10 % of the rows
-still active; the small-batch regime where launch and latency, not HBM,
-set the time.
+Other workloads (--workload):
+  qwen3_8b_decode_checkpoints  one decode step of a Qwen3-8B-architecture
+      batch of 256 sequences, routers at layers 3/7/.../31 (eight
+      checkpoints, H = 4096), each exiting ~10 % of the rows still active;
+  kernel_fp32_4096x768  the reference's own kernel-level case, one
+      checkpoint of 4096 fp32 rows of H = 768 (N(0,1) times a per-row scale
+      U(0.5, 2)), RMSNorm weight N(1, 0.02), 30 % exits;
+  bandwidth_sweep  one checkpoint per (N, H, f): N in 1K..1M rows (powers of
+      4, split evenly over the ranks), H in {2048, 4096, 5120, 8192} bf16,
+      exit fraction f in {0, 0.1, 0.5, 0.9}; HBM GB/s against the measured
+      copy peak for each;
+  llama8b_prefill_engine  the engine prefill measurement alone.
 
 Multi-GPU: one process per GPU under torchrun; every rank processes its own
-batch (weak scaling, no data-path collective); timing is the max over ranks.
+batch (weak scaling).  The step's exit counts are all-gathered (NCCL) inside
+the timed region, overlapped with the next step on a second stream; timing
+is the max over ranks.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload llama8b_prefill_checkpoints|qwen3_8b_decode_checkpoints|
-                              kernel_fp32_4096x768]
+                  [--workload NAME] [--no-engine]
 """
 from __future__ import annotations
 
@@ -37,6 +49,7 @@ import json
 import os
 import statistics
 import sys
+import tempfile
 import threading
 import time
 from pathlib import Path
@@ -48,6 +61,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 THRESHOLD = 0.85
+SEED = 1234
+CAL_ROWS = 8192  # CPU-drawn rows per checkpoint: bias calibration and the CPU sample
 WORKLOADS = {
     # exits: fraction of the whole batch per checkpoint (the last takes the rest)
     "llama8b_prefill_checkpoints": {"rows": 16 * 2048, "layers": [8, 12, 16, 20, 24, 28],
@@ -58,8 +73,14 @@ WORKLOADS = {
                                     "exit_fractions": [0.10] * 8, "of": "active"},
     # one router over fp32 rows scaled per row, RMSNorm weight N(1, 0.02)
     "kernel_fp32_4096x768": {"rows": 4096, "layers": [0], "exit_fractions": [0.30],
-                             "of": "active", "hidden": 768, "dtype": "f32", "inputs": "scaled"},
+                             "of": "active", "hidden": 768, "dtype": "f32", "inputs": "k1"},
 }
+# workloads that are not a checkpoint sweep
+SWEEP_WORKLOAD = "bandwidth_sweep"
+ENGINE_WORKLOAD = "llama8b_prefill_engine"
+SWEEP_N = [1024, 4096, 16384, 65536, 262144, 1048576]
+SWEEP_H = [2048, 4096, 5120, 8192]
+SWEEP_F = [0.0, 0.1, 0.5, 0.9]
 DTYPE_NAMES = {"bf16": torch.bfloat16, "f32": torch.float32}
 WORKLOAD = "llama8b_prefill_checkpoints"
 LAYERS = WORKLOADS[WORKLOAD]["layers"]
@@ -69,21 +90,28 @@ ROWS, HIDDEN, BOTTLENECK = WORKLOADS[WORKLOAD]["rows"], 4096, 128
 DTYPE = "bf16"
 
 
+def configure(name: str, rows: int | None = None) -> None:
+    """Select a checkpoint-sweep workload (module globals used below)."""
+    wk = WORKLOADS[name]
+    globals().update(WORKLOAD=name, LAYERS=wk["layers"], EXIT_FRACTIONS=wk["exit_fractions"],
+                     EXITS_OF=wk["of"], ROWS=rows if rows else wk["rows"],
+                     HIDDEN=wk.get("hidden", 4096), DTYPE=wk.get("dtype", "bf16"))
+
+
 # DRAM bytes (read + write) of checkpoint 0's two kernels (router + mover),
 # 32768 rows x 4096 bf16, from the warm-cache ncu launch list of this
-# benchmark (profiles/launches__llama8b_prefill_checkpoints.md).
+# benchmark on the split path.
 NCU_TRAFFIC_CKPT0 = {"rows": 32768, "path": "tc_split", "bytes": (269.5 + 63.3 + 221.3 + 209.0) * 1e6}
 
 
-def e2e_step_count(requested, h2d_bytes_nominal: int) -> int:
+def e2e_step_count(requested, h2d_bytes_per_step: int) -> int:
     """Steps of the e2e region: as requested, else enough for about 2 GB of
     host-to-device copies (at least 3, at most 200), so that a small
     workload's region is not a few hundred microseconds of host jitter.  The
-    nominal bytes (rows x H x element size x checkpoints) are the same on
-    every rank."""
+    bytes are those one step actually copies."""
     if requested is not None:
         return int(requested)
-    return max(3, min(200, int(2e9 // max(int(h2d_bytes_nominal), 1))))
+    return max(3, min(200, int(2e9 // max(int(h2d_bytes_per_step), 1))))
 
 
 def algorithmic_bytes(n: int, exits: int, h: int, e: int) -> int:
@@ -92,6 +120,21 @@ def algorithmic_bytes(n: int, exits: int, h: int, e: int) -> int:
     position), fp32 score + u8 decision + int32 source index per row, read
     int64 position + int32 slot per row, write position + slot per survivor."""
     return n * 2 * h * e + 21 * n + 12 * (n - exits)
+
+
+def nominal_schedule(rows: int) -> tuple[list[int], list[int]]:
+    """(active rows, exits) per checkpoint of the workload's exit schedule."""
+    active, exits, a = [], [], rows
+    for k in range(len(LAYERS)):
+        if EXITS_OF == "batch":
+            e = int(round(EXIT_FRACTIONS[k] * rows)) if k < len(LAYERS) - 1 else a
+        else:
+            e = int(round(EXIT_FRACTIONS[k] * a))
+        e = min(e, a)
+        active.append(a)
+        exits.append(e)
+        a -= e
+    return active, exits
 
 
 # ----------------------------------------------------------------- clocks
@@ -154,7 +197,8 @@ class ClockSampler:
 def dist_setup(n_gpus: int):
     from tide_b200 import dist as tdist
 
-    return tdist.init("nccl" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else None)
+    return tdist.init("nccl" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else None,
+                      timeout_s=120.0)
 
 
 def barrier(world):
@@ -169,46 +213,72 @@ def max_over_ranks(world, v: float) -> float:
     return tdist.max_over_ranks(world, v)
 
 
+def norm_weight_cpu() -> torch.Tensor:
+    if WORKLOADS[WORKLOAD].get("inputs") == "k1":
+        from tide_b200 import workloads
+
+        return workloads.k1(n=ROWS, h=HIDDEN)["norm_weight"]
+    return torch.ones(HIDDEN)
+
+
+def checkpoint_setup(k: int, rank: int, active_nominal: int, exits_nominal: int) -> dict:
+    """The CPU-drawn part of checkpoint k on a rank: the first
+    min(CAL_ROWS, rows) rows of its hidden-state tensor (model dtype), its
+    router (down [B, H], up [1, B], fp32) and the scalar bias that makes the
+    nominal share of those rows (the first active_nominal of them) exit.
+    Both arms call this, so they see the same rows, weights and biases."""
+    from tide_b200 import workloads
+
+    dt = DTYPE_NAMES[DTYPE]
+    cal = min(CAL_ROWS, ROWS)
+    if WORKLOADS[WORKLOAD].get("inputs") == "k1":
+        w = workloads.k1(n=ROWS, h=HIDDEN, b=BOTTLENECK, seed=0)  # the reference's seed-0 draw
+        x, down, up = w["x"][:cal].to(dt), w["down"], w["up"]
+    else:
+        g = torch.Generator().manual_seed(SEED + 7919 * rank + 101 * k)
+        x = torch.randn(cal, HIDDEN, generator=g).to(dt)
+        down = 0.02 * torch.randn(BOTTLENECK, HIDDEN, generator=g)
+        up = 0.02 * torch.randn(1, BOTTLENECK, generator=g)
+    n_cal = min(cal, active_nominal)
+    z = workloads.prebias_logits_torch(x[:n_cal], "rms", norm_weight_cpu(), None, 1e-5, down, up)
+    frac = exits_nominal / active_nominal if active_nominal else 0.0
+    bias = workloads.bias_for_exit_fraction(z, frac, THRESHOLD)
+    return {"x_head": x, "down": down, "up": up, "bias": bias}
+
+
 class Workload:
     """Device-resident inputs and buffers of one rank's checkpoint sweep."""
 
     def __init__(self, rank: int, path: int):
-        from tide_b200 import workloads
-        from tide_b200.ops import CheckpointRunner, NormSpec, prepare_router
         from tide_b200.capi import NORM_RMS
+        from tide_b200.ops import CheckpointRunner, NormSpec, prepare_router
 
         dev = torch.device("cuda")
-        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        g = torch.Generator(device=dev).manual_seed(SEED + 31 * rank)
         self.path = path
         dt = DTYPE_NAMES[DTYPE]
-        scaled = WORKLOADS[WORKLOAD].get("inputs") == "scaled"
-        w_norm = (1.0 + 0.02 * torch.randn(HIDDEN, generator=g, device=dev) if scaled
-                  else torch.ones(HIDDEN, device=dev))
-        self.norm = NormSpec(NORM_RMS, w_norm, None, 1e-5)
+        self.norm = NormSpec(NORM_RMS, norm_weight_cpu().to(dev), None, 1e-5)
         self.runner = CheckpointRunner(dev)
-        self.x, self.routers, self.active = [], [], []
-        active = ROWS
-        for k, layer in enumerate(LAYERS):
-            x = torch.randn(ROWS, HIDDEN, generator=g, device=dev)
-            if scaled:
-                x = x * (torch.rand(ROWS, 1, generator=g, device=dev) * 1.5 + 0.5)
-            x = x.to(dt)
-            down = 0.02 * torch.randn(BOTTLENECK, HIDDEN, generator=g, device=dev)
-            up = 0.02 * torch.randn(1, BOTTLENECK, generator=g, device=dev)
-            z = workloads.prebias_logits_torch(x[:active], "rms", self.norm.weight, None, 1e-5,
-                                               down, up)
-            if EXITS_OF == "batch":
-                exits = int(round(EXIT_FRACTIONS[k] * ROWS)) if k < len(LAYERS) - 1 else active
+        self.x, self.routers, self.setups = [], [], []
+        self.active_nominal, self.exits_nominal = nominal_schedule(ROWS)
+        scaled = WORKLOADS[WORKLOAD].get("inputs") == "k1"
+        for k in range(len(LAYERS)):
+            s = checkpoint_setup(k, rank, self.active_nominal[k], self.exits_nominal[k])
+            head = s["x_head"].to(dev)
+            rest = ROWS - head.shape[0]
+            if rest > 0:
+                xr = torch.randn(rest, HIDDEN, generator=g, device=dev)
+                if scaled:
+                    xr = xr * (torch.rand(rest, 1, generator=g, device=dev) * 1.5 + 0.5)
+                x = torch.cat([head, xr.to(dt)])
             else:
-                exits = int(round(EXIT_FRACTIONS[k] * active))
-            bias = workloads.bias_for_exit_fraction(z, exits / active, THRESHOLD)
-            self.routers.append(prepare_router(down, up, bias, self.norm, dt))
+                x = head.contiguous()
+            self.routers.append(prepare_router(s["down"].to(dev), s["up"].to(dev), s["bias"],
+                                               self.norm, dt))
+            self.setups.append({"down": s["down"], "up": s["up"], "bias": s["bias"]})
             self.x.append(x)
-            self.active.append(active)
-            active -= exits
         self.positions0 = torch.arange(ROWS, device=dev, dtype=torch.int64)
         self.slots0 = torch.arange(ROWS, device=dev, dtype=torch.int32)
-        self.count0 = torch.tensor([ROWS], dtype=torch.int32, device=dev)
         self.out = torch.zeros(ROWS, HIDDEN, dtype=dt, device=dev)
         self.compact = torch.empty(ROWS, HIDDEN, dtype=dt, device=dev)
         self.pos = [torch.empty(ROWS, dtype=torch.int64, device=dev) for _ in range(2)]
@@ -216,7 +286,7 @@ class Workload:
         self.counts = torch.zeros(len(LAYERS), 2, dtype=torch.int32, device=dev)
         self.paths = {}  # path the library chose for each checkpoint
 
-    def checkpoint(self, k: int, xs=None):
+    def checkpoint(self, k: int, xs=None, scores_out=None):
         """Checkpoint k of the sweep: positions, slots and the live row count
         come from checkpoint k-1's outputs on the device."""
         xs = xs if xs is not None else self.x
@@ -227,7 +297,8 @@ class Workload:
         self.runner.run(xs[k], self.routers[k], self.norm, THRESHOLD, positions=pos_in,
                         slots=slot_in, out_buffer=self.out, compact_out=self.compact,
                         positions_out=self.pos[k % 2], slots_out=self.slots[k % 2],
-                        n_rows_dev=cnt, counts=self.counts[k], path=self.path)
+                        n_rows_dev=cnt, counts=self.counts[k], path=self.path,
+                        scores_out=scores_out)
         self.paths[k] = self.runner.last_path
 
     def step(self, xs=None):
@@ -271,33 +342,102 @@ def launches_per_checkpoint(path_used: int) -> int:
 PATH_NAMES = {1: "simt", 2: "tc_fused_single_pass", 3: "tc_split"}
 
 
+def parity_sample(wl: "Workload", active: list[int], rows: int = 2048) -> dict:
+    """Scores of the timed path against the oracle on the first `rows` rows of
+    every checkpoint (untimed calls with the same arguments plus a score
+    output): the largest score difference and the exit decisions that differ,
+    in total and outside the score tolerance around the threshold."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import tide_oracle as O
+
+    f32 = DTYPE == "f32"
+    tol = 1e-5 if f32 else 1e-2
+    odt = O.F32 if f32 else O.BF16
+    norm = {"kind": "rms", "weight": wl.norm.weight.cpu().numpy(), "bias": None, "eps": 1e-5}
+    res = {"rows_checked": 0, "score_tolerance": tol, "max_score_err": 0.0,
+           "decision_disagreements": 0, "disagreements_outside_tolerance": 0}
+    for k in range(len(LAYERS)):
+        n = active[k]
+        if n == 0:
+            continue
+        s = torch.full((n,), -1.0, device="cuda")
+        wl.checkpoint(k, scores_out=s)
+        torch.cuda.synchronize()
+        m = min(rows, n)
+        x = wl.x[k][:m]
+        xs = x.cpu().numpy() if f32 else x.view(torch.int16).cpu().numpy().view(np.uint16)
+        st = wl.setups[k]
+        ref = O.score_rows(xs, odt, norm, st["down"].numpy(), st["up"].numpy(), st["bias"])
+        got = s[:m].cpu().numpy()
+        dis = (got > THRESHOLD) != (ref > THRESHOLD)
+        res["rows_checked"] += m
+        res["max_score_err"] = max(res["max_score_err"], float(np.abs(got - ref).max()))
+        res["decision_disagreements"] += int(dis.sum())
+        res["disagreements_outside_tolerance"] += int((dis & (np.abs(ref - THRESHOLD) > tol)).sum())
+    return res
+
+
 def gather_timings(world: int, wl: "Workload", reps: int = 5) -> dict:
-    """The step's two collectives, timed on their own (not part of `value`):
-    the all-gather of every rank's exit counts and of every rank's output
-    rows (ncclAllGather over NVLink).  CUDA events, max over ranks."""
+    """The output-row collective, timed on its own: every rank's output rows
+    gathered to every rank (ncclAllGather over NVLink).  The path never
+    needs it (each rank's rows are consumed by its own lm_head); it is the
+    cost of a consumer that wants all rows in one place.  CUDA events, max
+    over ranks."""
     from tide_b200 import dist as tdist
 
     rows_out = torch.empty((world * ROWS, HIDDEN), dtype=wl.out.dtype, device=wl.out.device)
-    res = {}
-    for name, fn, nbytes in (
-            ("exit_counts", lambda: tdist.all_gather_counts(world, wl.counts),
-             wl.counts.numel() * 4),
-            ("output_rows", lambda: tdist.all_gather_rows(world, wl.out, rows_out),
-             wl.out.numel() * wl.out.element_size())):
-        fn()
-        torch.cuda.synchronize()
-        barrier(world)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(reps):
-            fn()
-        b.record()
-        torch.cuda.synchronize()
-        ms = max_over_ranks(world, a.elapsed_time(b) / reps)
-        res[name] = {"ms": ms, "bytes_per_rank": nbytes,
-                     "busbw_GBps": (world - 1) * nbytes / (ms / 1000.0) / 1e9}
+    nbytes = wl.out.numel() * wl.out.element_size()
+    tdist.all_gather_rows(world, wl.out, rows_out)
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        tdist.all_gather_rows(world, wl.out, rows_out)
+    b.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(world, a.elapsed_time(b) / reps)
     del rows_out
-    return res
+    return {"output_rows_all_gather": {"ms": ms, "bytes_per_rank": nbytes,
+                                       "busbw_GBps": (world - 1) * nbytes / (ms / 1000.0) / 1e9}}
+
+
+class CountsGather:
+    """The step's collective: every rank's {survivors, exits} per checkpoint
+    all-gathered (global ExitStats need them), on a second stream so that it
+    overlaps the next step.  Two staging buffers: step i's counts are copied
+    on the main stream, gathered on the side stream, and the copy into a
+    buffer waits for the gather that last read it."""
+
+    def __init__(self, world: int, counts: torch.Tensor):
+        self.world = world
+        self.side = torch.cuda.Stream()
+        self.stage = [torch.empty_like(counts) for _ in range(2)]
+        self.out = [torch.empty((world,) + tuple(counts.shape), dtype=counts.dtype,
+                                device=counts.device) for _ in range(2)]
+        self.done = [None, None]
+        self.i = 0
+
+    def after_step(self, counts: torch.Tensor) -> None:
+        import torch.distributed as dist
+
+        j = self.i % 2
+        main = torch.cuda.current_stream()
+        if self.done[j] is not None:
+            main.wait_event(self.done[j])
+        self.stage[j].copy_(counts)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        self.side.wait_event(ready)
+        with torch.cuda.stream(self.side):
+            dist.all_gather_into_tensor(self.out[j].view(-1), self.stage[j].view(-1))
+            ev = torch.cuda.Event()
+            ev.record(self.side)
+        self.done[j] = ev
+        self.i += 1
+
+    def finish(self) -> None:
+        torch.cuda.current_stream().wait_stream(self.side)
 
 
 # ----------------------------------------------------------------- CPU leg
@@ -308,64 +448,296 @@ def host_threads() -> int:
 
     n = os.cpu_count() or 1
     threadpool_limits(limits=n)
+    torch.set_num_threads(n)
     return n
 
 
-def cpu_checkpoint_sample(x: np.ndarray, down: np.ndarray, up: np.ndarray, bias: float,
-                          norm_weight: np.ndarray):
-    """The oracle on one checkpoint's rows (the reference's CPU path,
-    restated): returns seconds.  x holds bf16 bit patterns (uint16) or fp32."""
+def cpu_sweep_inputs(sample_rows: int) -> dict:
+    """The reference arm's inputs: rank 0's CPU-drawn rows, routers and
+    biases of every checkpoint (checkpoint_setup), as numpy."""
+    active, exits = nominal_schedule(ROWS)
+    cks = []
+    for k in range(len(LAYERS)):
+        s = checkpoint_setup(k, 0, active[k], exits[k])
+        x = s["x_head"][:sample_rows]
+        xs = x.numpy() if x.dtype == torch.float32 else x.view(torch.int16).numpy().view(np.uint16)
+        cks.append({"x": xs, "down": s["down"].numpy(), "up": s["up"].numpy(), "bias": s["bias"]})
+    return {"checkpoints": cks, "norm_weight": norm_weight_cpu().numpy()}
+
+
+def cpu_sweep_step(inp: dict) -> tuple[float, int]:
+    """One step of the workload on the host by the oracle (the reference's CPU
+    path, restated): every checkpoint on the sample's still-active rows, the
+    survivor count chaining into the next checkpoint as on the device.
+    Returns (seconds, rows routed)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import tide_oracle as O
 
-    norm = {"kind": "rms", "weight": norm_weight, "bias": None, "eps": 1e-5}
-    out = np.zeros_like(x)
+    odt = O.F32 if DTYPE == "f32" else O.BF16
+    norm = {"kind": "rms", "weight": inp["norm_weight"], "bias": None, "eps": 1e-5}
+    n = inp["checkpoints"][0]["x"].shape[0]
+    out = np.zeros_like(inp["checkpoints"][0]["x"])
+    routed = 0
+    positions = np.arange(n, dtype=np.int64)
+    slots = np.arange(n, dtype=np.int32)
     t0 = time.perf_counter()
-    O.checkpoint(x, O.F32 if x.dtype == np.float32 else O.BF16, norm, down, up, bias, THRESHOLD,
-                 positions=np.arange(x.shape[0], dtype=np.int64),
-                 slots=np.arange(x.shape[0], dtype=np.int32), out_buffer=out)
-    return time.perf_counter() - t0
+    for ck in inp["checkpoints"]:
+        if n == 0:
+            break
+        r = O.checkpoint(ck["x"][:n], odt, norm, ck["down"], ck["up"], ck["bias"], THRESHOLD,
+                         positions=positions[:n], slots=slots[:n], out_buffer=out)
+        out = r["out_buffer"]
+        positions, slots = r["positions"], r["slots"]
+        routed += n
+        n = r["n_survivors"]
+    return time.perf_counter() - t0, routed
 
 
-def cpu_sample_inputs(wl: "Workload", rows: int):
-    x = wl.x[0][:rows].contiguous()
-    x = x.cpu().numpy() if x.dtype == torch.float32 else x.view(torch.int16).cpu().numpy().view(np.uint16)
-    r = wl.routers[0]
-    down = r.down_t.T.contiguous().cpu().numpy()
-    up = r.up.cpu().numpy().reshape(1, -1)
-    return x, down, up, r.up_bias, wl.norm.weight.cpu().numpy()
+def cpu_baseline_sample(sample_rows: int, reps: int) -> dict:
+    cores = host_threads()
+    inp = cpu_sweep_inputs(sample_rows)
+    cpu_sweep_step(inp)
+    runs = [cpu_sweep_step(inp) for _ in range(reps)]
+    t, routed = min(runs, key=lambda r: r[0])
+    return {"value": routed / t, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"oracle on the first {sample_rows} rows of every checkpoint of "
+                      f"{WORKLOAD} ({routed} rows routed per step, same rows, routers and "
+                      f"biases as the device run), best of {reps}"}
 
 
 # ----------------------------------------------------------------- main
 def run_reference(args, world, rank):
     """--impl reference: the CPU restatement of the reference path (the
     reference is Python and cannot be built into a library), timed on the host
-    cores with every thread numpy's BLAS can use; rank 0 only."""
+    cores with every thread numpy's BLAS can use; rank 0 only.  It loads
+    nothing of tide_b200's native code: the rows, routers and biases come
+    from the CPU generator (checkpoint_setup) and go straight to the oracle."""
     if rank != 0:
         return
-    torch.cuda.set_device(0)
-    wl = Workload(rank, 0)
-    rows = min(4096, ROWS)
+    if WORKLOAD in (SWEEP_WORKLOAD, ENGINE_WORKLOAD):
+        configure("llama8b_prefill_checkpoints")
+    sample = min(2048, ROWS)
     cores = host_threads()
-    x, down, up, bias, nw = cpu_sample_inputs(wl, rows)
+    inp = cpu_sweep_inputs(sample)
     for _ in range(args.warmup):
-        cpu_checkpoint_sample(x, down, up, bias, nw)
-    ts = [cpu_checkpoint_sample(x, down, up, bias, nw) for _ in range(args.steps)]
-    t = sum(ts)
-    v = rows * args.steps / t
+        cpu_sweep_step(inp)
+    runs = [cpu_sweep_step(inp) for _ in range(args.steps)]
+    t = sum(r[0] for r in runs)
+    routed = sum(r[1] for r in runs)
+    v = routed / t
     line = {
         "impl": "reference", "metric": "router_compact_scatter_tokens_per_s", "value": v,
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * t / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample_rows_per_step": rows, "hidden": HIDDEN,
-                   "bottleneck": BOTTLENECK,
-                   "checkpoint": f"first router (layer {LAYERS[0]}), {EXIT_FRACTIONS[0]:.0%} exit"},
+        "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "hidden": HIDDEN,
+                   "bottleneck": BOTTLENECK, "checkpoint_layers": LAYERS,
+                   f"exit_fractions_of_{EXITS_OF}": EXIT_FRACTIONS,
+                   "sample_rows_per_checkpoint": sample, "rows_routed_per_step": routed // args.steps,
+                   "same_config": True,
+                   "note": "the same checkpoints, routers, biases and leading rows as the device "
+                           "run, on a bounded sample of each checkpoint's rows; tokens/s is rows "
+                           "routed per second"},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"one checkpoint ({rows} rows x {HIDDEN} {DTYPE}) per step"},
+                         "sample": f"first {sample} rows of every checkpoint, chained"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def engine_prefill(world: int, rank: int, reps: int = 10, warmup: int = 3) -> dict:
+    """8B-architecture prefill through the engine: a random-init bf16
+    Llama-3.1-8B-architecture model (32 layers, H 4096, 32/8 heads, head_dim
+    128, SwiGLU 14336, vocab 128256, RMSNorm eps 1e-5, RoPE theta 5e5),
+    routers at layers 8..28 whose biases exit 5/10/15/20/20/30 % of the
+    batch, input 16 x 2048 uniform random ids (seed 1) split by sequence
+    over the ranks.  Times engine(input_ids) (3 warm-up + 10 timed, the
+    reference's throughput protocol: batch * seq / time) and the model's own
+    forward on the same ids."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from tide_b200 import TIDEConfig
+    from tide_b200 import dist as tdist
+    from tide_b200 import workloads
+    from tide_b200.router import RouterCheckpoint, TokenRouter
+    from tide_b200.runtime import TIDERuntime
+
+    dev = torch.device("cuda")
+    layers, fracs = [8, 12, 16, 20, 24, 28], [0.05, 0.10, 0.15, 0.20, 0.20, 0.30]
+    B_all, S = 16, 2048
+    ids_all = torch.randint(0, 128256, (B_all, S), generator=torch.Generator().manual_seed(1))
+    b0, b1 = tdist.shard_range(B_all, world, rank)
+    ids = ids_all[b0:b1].to(dev)
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336,
+                      num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8,
+                      head_dim=128, rms_norm_eps=1e-5, rope_theta=500000.0,
+                      max_position_embeddings=8192, tie_word_embeddings=False)
+    torch.manual_seed(SEED)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = LlamaForCausalLM(cfg).eval()
+    finally:
+        torch.set_default_dtype(prev)
+    res = {"model": "Llama-3.1-8B architecture, random-init bf16", "global_batch": B_all,
+           "seq_len": S, "batch_per_rank": b1 - b0, "scaling": "strong", "timed_calls": reps,
+           "warmup_calls": warmup, "router_layers": layers, "exit_fractions_of_batch": fracs}
+    with torch.inference_mode():
+        # routers and biases: exit the scheduled share of the rows still active
+        hs = model(ids, output_hidden_states=True, logits_to_keep=1).hidden_states
+        g = torch.Generator().manual_seed(SEED + 5)
+        N = ids.numel()
+        exited = torch.zeros(N, dtype=torch.bool, device=dev)
+        routers = {}
+        nw = model.model.norm.weight.float()
+        for L, f in zip(layers, fracs):
+            r = TokenRouter(4096, 128, up_bias=True)
+            with torch.no_grad():
+                r.down.weight.normal_(0, 0.02, generator=g)
+                r.up.weight.normal_(0, 0.02, generator=g)
+            h = hs[L + 1].reshape(N, -1)
+            z = workloads.prebias_logits_torch(h, "rms", nw, None, 1e-5, r.down.weight.to(dev),
+                                               r.up.weight.to(dev))
+            active = (~exited).nonzero()[:, 0]
+            n_exit = int(round(f * N)) if L != layers[-1] else int(active.numel())
+            za = z[active]
+            bias = workloads.bias_for_exit_fraction(za, n_exit / max(1, active.numel()), THRESHOLD)
+            with torch.no_grad():
+                r.up.bias.fill_(bias)
+            exited[active[(za + bias) > workloads.logit(THRESHOLD)]] = True
+            routers[L] = r
+        del hs
+        tmp = Path(tempfile.mkdtemp(prefix="tide_bench_"))
+        RouterCheckpoint(routers, 4096, 128).save(tmp / "router.pt")
+        engine = TIDERuntime(model, tmp / "router.pt",
+                             config=TIDEConfig(exit_threshold=THRESHOLD, min_layers=0))
+
+        def timed(fn) -> float:
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            barrier(world)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(reps):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            return max_over_ranks(world, a.elapsed_time(b) / 1000.0)
+
+        t_engine = timed(lambda: engine(ids))
+        stats = tdist.global_stats(world, engine.last_stats)
+        t_hf = timed(lambda: model(ids).logits)
+    tokens = B_all * S * reps
+    res.update({"engine_tok_s": tokens / t_engine, "engine_ms_per_call": 1000 * t_engine / reps,
+                "hf_forward_tok_s": tokens / t_hf, "hf_forward_ms_per_call": 1000 * t_hf / reps,
+                "engine_mode": "post-hoc (every layer runs; the reference's semantics)",
+                "exit_rate": stats.exit_rate,
+                "exits_per_layer": {str(k): v for k, v in sorted(stats.exits_per_layer.items())}})
+    del engine, model
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_sweep(args, world, rank, local) -> None:
+    """--workload bandwidth_sweep: one checkpoint per (N, H, f), N split evenly
+    over the ranks; aggregate algorithmic GB/s (max device time over ranks)
+    against the measured copy peak."""
+    from tide_b200 import dist as tdist
+    from tide_b200 import workloads
+    from tide_b200.capi import NORM_RMS, PATH_AUTO
+    from tide_b200.ops import CheckpointRunner, NormSpec, prepare_router
+
+    dev = torch.device("cuda")
+    peak = load_peak()
+    hs = [int(h) for h in args.sweep_h.split(",")] if args.sweep_h else SWEEP_H
+    ns = [int(n) for n in args.sweep_n.split(",")] if args.sweep_n else SWEEP_N
+    fs = [float(f) for f in args.sweep_f.split(",")] if args.sweep_f else SWEEP_F
+    runner = CheckpointRunner(dev)
+    rows_out = []
+    with ClockSampler(local) as clocks:
+        for H in hs:
+            norm = NormSpec(NORM_RMS, torch.ones(H, device=dev), None, 1e-5)
+            gw = torch.Generator().manual_seed(SEED + H)
+            down = (0.02 * torch.randn(BOTTLENECK, H, generator=gw)).to(dev)
+            up = (0.02 * torch.randn(1, BOTTLENECK, generator=gw)).to(dev)
+            for N in ns:
+                r0, r1 = tdist.shard_range(N, world, rank)
+                n = r1 - r0
+                g = torch.Generator(device=dev).manual_seed(SEED + 17 * rank + N + H)
+                x = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+                for s0 in range(0, n, 65536):
+                    s1 = min(n, s0 + 65536)
+                    x[s0:s1] = torch.randn(s1 - s0, H, generator=g, device=dev).to(torch.bfloat16)
+                z = workloads.prebias_logits_torch(x[:65536], "rms", norm.weight, None, 1e-5, down, up)
+                out = torch.zeros_like(x)
+                comp = torch.empty_like(x)
+                pos_out = torch.empty(n, dtype=torch.int64, device=dev)
+                counts = torch.zeros(2, dtype=torch.int32, device=dev)
+                for f in fs:
+                    bias = workloads.bias_for_exit_fraction(z, f, THRESHOLD)
+                    router = prepare_router(down, up, bias, norm, torch.bfloat16)
+
+                    def call():
+                        runner.run(x, router, norm, THRESHOLD, out_buffer=out, compact_out=comp,
+                                   positions_out=pos_out, counts=counts, path=PATH_AUTO)
+
+                    for _ in range(2):
+                        call()
+                    torch.cuda.synchronize()
+                    path = runner.last_path
+                    exits = int(counts[1].item())
+                    est_ms = max(0.02, 2 * n * H * 2 / 5e12 * 1e3)
+                    reps = int(max(5, min(50, 100.0 / est_ms)))
+                    s = torch.cuda.Stream()
+                    s.wait_stream(torch.cuda.current_stream())
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.stream(s):
+                        with torch.cuda.graph(graph, stream=s):
+                            call()
+                    torch.cuda.current_stream().wait_stream(s)
+                    graph.replay()
+                    torch.cuda.synchronize()
+                    barrier(world)
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    for _ in range(reps):
+                        graph.replay()
+                    b.record()
+                    torch.cuda.synchronize()
+                    ms = max_over_ranks(world, a.elapsed_time(b) / reps)
+                    alg = world * algorithmic_bytes(n, exits, H, 2)  # ranks' shares are equal +-1 row
+                    gbs = alg / (ms / 1000.0) / 1e9
+                    rows_out.append({"N": N, "rows_per_gpu": n, "H": H, "f": f, "exits_rank0": exits,
+                                     "ms": ms, "GBps": gbs, "frac": gbs / (world * peak),
+                                     "tokens_per_s": N / (ms / 1000.0), "path": PATH_NAMES.get(path, path),
+                                     "reps": reps})
+                    del graph
+                runner.check_errors()
+                del x, out, comp, pos_out
+                torch.cuda.empty_cache()
+    if rank == 0:
+        head = [r for r in rows_out if r["H"] == 4096 and r["N"] == max(ns)
+                and abs(r["f"] - 0.1) < 1e-9] or rows_out[-1:]
+        v = head[0]["GBps"] if head else None
+        line = {"metric": "router_compact_scatter_hbm_GBps", "value": v, "unit": "GB/s",
+                "n_gpus": world, "steps": None, "warmup": 2, "ms_per_step": head[0]["ms"] if head else None,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic",
+                "config": {"workload": SWEEP_WORKLOAD, "N_total": ns, "H": hs, "exit_fractions": fs,
+                           "value_case": "H 4096, largest N, f 0.1", "peak_GBps_per_gpu": peak,
+                           "l2": "one checkpoint call per graph replay; rows above ~8K x 4096 exceed L2"},
+                "sweep": rows_out, "clocks": clocks.summary(),
+                "gpu_launches": None}
+        print(json.dumps(line), flush=True)
+
+
+def load_peak() -> float:
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"])
+    except Exception:
+        return 6650.0
 
 
 def main():
@@ -378,21 +750,42 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None,
                     help="e2e steps (default: about 2 GB of host->device copies, at least 3)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--no-engine", action="store_true", help="skip the engine prefill measurement")
+    ap.add_argument("--workload", default=WORKLOAD,
+                    choices=sorted(WORKLOADS) + [SWEEP_WORKLOAD, ENGINE_WORKLOAD])
     ap.add_argument("--rows", type=int, default=None, help="rows per GPU (profiling runs)")
+    ap.add_argument("--sweep-h", default=None, help="bandwidth_sweep: comma-separated H values")
+    ap.add_argument("--sweep-n", default=None, help="bandwidth_sweep: comma-separated N values")
+    ap.add_argument("--sweep-f", default=None, help="bandwidth_sweep: comma-separated exit fractions")
     args = ap.parse_args()
-    wk = WORKLOADS[args.workload]
-    globals().update(WORKLOAD=args.workload, LAYERS=wk["layers"], EXIT_FRACTIONS=wk["exit_fractions"],
-                     EXITS_OF=wk["of"], ROWS=args.rows if args.rows else wk["rows"],
-                     HIDDEN=wk.get("hidden", 4096), DTYPE=wk.get("dtype", "bf16"))
+    if args.workload in WORKLOADS:
+        configure(args.workload, args.rows)
+    else:
+        globals()["WORKLOAD"] = args.workload
     world, rank, local = dist_setup(args.gpus)
-    if args.impl == "reference":
-        run_reference(args, world, rank)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        elif args.workload == SWEEP_WORKLOAD:
+            run_sweep(args, world, rank, local)
+        elif args.workload == ENGINE_WORKLOAD:
+            eng = engine_prefill(world, rank)
+            if rank == 0:
+                print(json.dumps({"metric": "prefill_tokens_per_s", "value": eng["engine_tok_s"],
+                                  "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
+                                  "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                                  "data": "synthetic", "config": {"workload": ENGINE_WORKLOAD},
+                                  "prefill_engine": eng}), flush=True)
+        else:
+            run_checkpoints(args, world, rank, local)
+    finally:
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
-        return
 
+
+def run_checkpoints(args, world, rank, local) -> None:
+    from tide_b200 import dist as tdist
     from tide_b200.capi import PATH_AUTO, PATH_SIMT, PATH_TC, PATH_TC_SPLIT
 
     path = {"auto": PATH_AUTO, "simt": PATH_SIMT, "tc": PATH_TC, "tc_split": PATH_TC_SPLIT}[args.path]
@@ -400,7 +793,6 @@ def main():
     for _ in range(max(args.warmup, 3)):
         wl.step()
     torch.cuda.synchronize()
-    path_used = wl.runner.last_path
     counts = wl.counts.cpu()
     rows_per_step = int(counts.sum().item())
     exits_per_stage = counts[:, 1].tolist()
@@ -409,14 +801,21 @@ def main():
 
     step_graph = wl.capture()[0]
     ck_graphs = wl.capture(per_checkpoint=True, calls=CK_CALLS)
+    gather = CountsGather(world, wl.counts) if world > 1 else None
     for _ in range(2):
         step_graph.replay()
+        if gather:
+            gather.after_step(wl.counts)
         for g in ck_graphs:
             g.replay()
+    if gather:
+        gather.finish()
     torch.cuda.synchronize()
 
     # timed region: device-resident inputs, one graph launch per step on the
-    # current stream, CUDA events before the first and after the last
+    # current stream (plus, on several ranks, the all-gather of the step's
+    # exit counts on a second stream), CUDA events before the first launch
+    # and after the last step's collective
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
@@ -424,6 +823,10 @@ def main():
         t_start.record()
         for _ in range(args.steps):
             step_graph.replay()
+            if gather:
+                gather.after_step(wl.counts)
+        if gather:
+            gather.finish()
         t_end.record()
         torch.cuda.synchronize()
         # per-launch device time of each checkpoint's kernels (the roofline's
@@ -449,78 +852,90 @@ def main():
     counts_after = wl.counts.cpu()
     assert torch.equal(counts_after, counts), "graph replay changed the exit counts"
     wl.runner.check_errors()
-    from tide_b200 import dist as tdist
-
-    # every rank: global {survivors, exits} per checkpoint (host bookkeeping,
-    # outside the timed region)
-    global_counts = tdist.sum_counts(world, wl.counts).cpu()
+    global_counts = (gather.out[(gather.i - 1) % 2].sum(0).cpu() if gather
+                     else wl.counts.cpu().to(torch.int64))
     collectives = gather_timings(world, wl) if world > 1 else None
 
     e = 4 if DTYPE == "f32" else 2
     alg = [algorithmic_bytes(active[k], exits_per_stage[k], HIDDEN, e) for k in range(len(LAYERS))]
     achieved = alg[0] / (per_ck[0] / 1000.0) / 1e9  # the first (largest) checkpoint
     achieved_all = sum(alg) / (elapsed / args.steps) / 1e9
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except Exception:
-        pass
-    peak = peaks.get("hbm_gbs", 6650.0)
+    peak = load_peak()
     path_name = PATH_NAMES.get(wl.paths[0], wl.paths[0])
     traffic = (NCU_TRAFFIC_CKPT0["bytes"] if ROWS == NCU_TRAFFIC_CKPT0["rows"]
-               and path_name == NCU_TRAFFIC_CKPT0["path"] else None)
+               and path_name == NCU_TRAFFIC_CKPT0["path"] and WORKLOAD == "llama8b_prefill_checkpoints"
+               else None)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic,
-                "traffic_source": "ncu launch list (warm caches), profiles/" if traffic else None,
-                "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-                "kernel": f"checkpoint 0 ({ROWS} rows x {HIDDEN}), both kernels of the call",
+                "traffic_source": "ncu launch list of this workload (warm caches)" if traffic else None,
+                "peak_source": "measured" if (ROOT / "MEASURED_PEAKS.json").exists() else "fallback",
+                "kernel": f"checkpoint 0 ({ROWS} rows x {HIDDEN}), every kernel of the call",
                 "per_checkpoint_ms": per_ck, "per_checkpoint_reps": reps,
                 "per_checkpoint_calls_per_graph": CK_CALLS,
                 "achieved_all_checkpoints": achieved_all, "algorithmic_bytes_per_step": sum(alg)}
 
+    parity = parity_sample(wl, active) if rank == 0 else None
+
     # e2e through the public operator with host buffers: H2D of the step's
     # hidden states from pinned memory (the rows each checkpoint routes), the
-    # step graph, D2H of the counts
+    # step graph, D2H of the output rows, of the last checkpoint's survivors
+    # and of the counts
     host_x = [x[: active[k]].cpu().pin_memory() for k, x in enumerate(wl.x)]
     dev_x = [torch.empty_like(x) for x in wl.x]
     host_counts = torch.empty_like(wl.counts, device="cpu").pin_memory()
-
-    e2e_steps = e2e_step_count(args.e2e_steps, ROWS * HIDDEN * e * len(LAYERS))
+    host_out = torch.empty_like(wl.out, device="cpu").pin_memory()
+    n_last = int(counts[-1, 0].item())
+    host_surv = torch.empty((max(n_last, 1), HIDDEN), dtype=wl.compact.dtype).pin_memory()
+    h2d = int(sum(x.numel() * x.element_size() for x in host_x))
+    d2h = int(host_out.numel() * host_out.element_size() + n_last * HIDDEN * e
+              + host_counts.numel() * 4)
+    e2e_steps = e2e_step_count(args.e2e_steps, h2d)
     e_graph = wl.capture(dev_x)[0]
-    # one untimed step: the graph's first launch uploads it to the device
-    for k in range(len(LAYERS)):
-        dev_x[k][: active[k]].copy_(host_x[k], non_blocking=True)
-    e_graph.replay()
-    host_counts.copy_(wl.counts, non_blocking=True)
+
+    def e2e_step():
+        for k in range(len(LAYERS)):
+            dev_x[k][: active[k]].copy_(host_x[k], non_blocking=True)
+        e_graph.replay()
+        if gather:
+            gather.after_step(wl.counts)
+        host_out.copy_(wl.out, non_blocking=True)
+        if n_last:
+            host_surv[:n_last].copy_(wl.compact[:n_last], non_blocking=True)
+        host_counts.copy_(wl.counts, non_blocking=True)
+
+    e2e_step()  # untimed: the graph's first launch uploads it to the device
+    if gather:
+        gather.finish()
     barrier(world)
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record()
     for _ in range(e2e_steps):
-        for k in range(len(LAYERS)):
-            dev_x[k][: active[k]].copy_(host_x[k], non_blocking=True)
-        e_graph.replay()
-        host_counts.copy_(wl.counts, non_blocking=True)
+        e2e_step()
+    if gather:
+        gather.finish()
     e_end.record()
     torch.cuda.synchronize()
     e_el = max_over_ranks(world, e_start.elapsed_time(e_end) / 1000.0)
     e2e = {"value": world * rows_per_step * e2e_steps / e_el, "unit": "tokens/s",
-           "h2d_bytes_per_step": int(sum(x.numel() * x.element_size() for x in host_x)),
-           "d2h_bytes_per_step": int(host_counts.numel() * 4), "steps": e2e_steps}
-    del e_graph, step_graph, ck_graphs
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps}
+    del e_graph, step_graph, ck_graphs, host_out, dev_x
+
+    paths_used = [PATH_NAMES.get(wl.paths[k], wl.paths[k]) for k in range(len(LAYERS))]
+    n_launch = sum(launches_per_checkpoint(p) for p in wl.paths.values()) * args.steps
+    engine = None
+    if WORKLOAD == "llama8b_prefill_checkpoints" and not args.no_engine and args.rows is None:
+        del wl
+        torch.cuda.empty_cache()
+        try:
+            engine = engine_prefill(world, rank)
+        except Exception as exc:  # reported, not fatal: the checkpoint numbers stand
+            engine = {"error": f"{type(exc).__name__}: {exc}"[:400]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rows = min(4096, ROWS)
-        cores = host_threads()
-        x, down, up, bias, nw = cpu_sample_inputs(wl, rows)
-        cpu_checkpoint_sample(x, down, up, bias, nw)
-        t = min(cpu_checkpoint_sample(x, down, up, bias, nw) for _ in range(3))
-        cpu = {"value": rows / t, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"oracle, one checkpoint of {rows} rows x {HIDDEN} {DTYPE} "
-                         f"(layer-{LAYERS[0]} router), best of 3"}
+        cpu = cpu_baseline_sample(min(2048, ROWS), 3)
 
-    n_launch = sum(launches_per_checkpoint(p) for p in wl.paths.values()) * args.steps
     if rank == 0:
         line = {
             "metric": "router_compact_scatter_tokens_per_s", "value": value, "unit": "tokens/s",
@@ -533,20 +948,16 @@ def main():
                        "rows_routed_per_step": rows_per_step, "active_rows": active,
                        "exits": exits_per_stage,
                        "global_exits_all_ranks": global_counts[:, 1].tolist(),
-                       "path": path_name,
-                       "path_per_checkpoint": [PATH_NAMES.get(wl.paths[k], wl.paths[k])
-                                               for k in range(len(LAYERS))],
-                       "parallelism": f"dp{world} (row shards, no collective)",
+                       "path": path_name, "path_per_checkpoint": paths_used,
+                       "parallelism": (f"dp{world} (row shards; exit counts all-gathered every "
+                                       f"step inside the timed region)" if world > 1 else "dp1"),
                        "l2": "inputs 1.1 GiB/step > 126 MB L2, no flush"},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "parity": parity,
             "gpu_launches": n_launch, "clocks": clocks.summary(),
             "collectives_timed_separately": collectives,
-            "prefill_tokens_per_s": world * ROWS * args.steps / elapsed,
+            "prefill_engine": engine,
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

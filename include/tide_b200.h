@@ -105,8 +105,12 @@ int tide_batch_compact(int dtype, const void *input, const int32_t *exit_mask,
  * TIDE_NOALLOC_MAX_ROWS rows (65,792 bytes, held by every GPU that loads the
  * library until exit); larger n_tokens is rejected with TIDE_ERR_INVALID.  It
  * calls no allocator.  The first call on a device looks the array's address
- * up (make it before any stream capture).  All calls on a device share the
- * array: calls whose kernels overlap on the GPU race, so serialise them. */
+ * up (make it before any stream capture) and keeps it for the life of the
+ * process: after a cudaDeviceReset (or anything else that destroys and
+ * recreates the device's primary context) the kept address is stale, so do
+ * not call this entry point on that device again in the same process.  All
+ * calls on a device share the array: calls whose kernels overlap on the GPU
+ * race, so serialise them. */
 #define TIDE_NOALLOC_MAX_ROWS 1048576
 int tide_batch_compact_noalloc(int dtype, const void *input, const int32_t *exit_mask,
                                void *compacted, void *exited, int32_t *continue_indices,

@@ -1,11 +1,12 @@
 """Generate the golden vectors that pin the oracle to the reference.
 
 Runs the reference's own Python code (RightNow-AI/TIDE v0.2.1, imported from
-/root/reference/python; the reference is read, never modified) on seeded
+the `python/` folder of a checkout of it, named by the environment variable
+TIDE_REFERENCE_PYTHON; the reference is read, never modified) on seeded
 inputs from tide_b200.workloads and stores its outputs here as .npz files.
-The GPU box never runs this script: the fixtures are committed.
+Nothing that runs on a GPU runs this script: the fixtures are committed.
 
-  python tests/golden/make_golden.py
+  TIDE_REFERENCE_PYTHON=<reference checkout>/python python tests/golden/make_golden.py
 
 Reference code exercised:
   TIDE.router.TokenRouter / RouterCheckpoint      (router.py:11-52)
@@ -15,6 +16,7 @@ Reference code exercised:
 """
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -23,7 +25,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path("/root/reference/python")
+if "TIDE_REFERENCE_PYTHON" not in os.environ:
+    sys.exit("set TIDE_REFERENCE_PYTHON to the reference checkout's python/ folder")
+REF = Path(os.environ["TIDE_REFERENCE_PYTHON"])
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(REF))
 

@@ -4,6 +4,7 @@ import importlib.util
 from pathlib import Path
 
 import pytest
+import torch
 
 ROOT = Path(__file__).resolve().parents[1]
 
@@ -42,3 +43,42 @@ def test_e2e_step_count(bench):
     assert bench.e2e_step_count(None, 1) == 200
     assert bench.e2e_step_count(5, 1) == 5
     assert bench.e2e_step_count(1, 10 ** 12) == 1
+
+
+def test_nominal_schedule(bench):
+    bench.configure("llama8b_prefill_checkpoints")
+    active, exits = bench.nominal_schedule(32768)
+    assert active[0] == 32768 and sum(exits) == 32768  # everything exits by the last router
+    assert [round(e / 32768, 2) for e in exits[:-1]] == [0.05, 0.10, 0.15, 0.20, 0.20]
+    bench.configure("qwen3_8b_decode_checkpoints")
+    active, exits = bench.nominal_schedule(256)
+    assert all(e == round(0.1 * a) for a, e in zip(active, exits))
+    bench.configure("llama8b_prefill_checkpoints")
+
+
+def test_checkpoint_setup_is_shared_and_places_the_bias(bench):
+    """Both arms draw a checkpoint's leading rows, router and bias from the CPU
+    generator: the same call gives bit-identical results, and the bias exits
+    the scheduled share of the calibration rows."""
+    from tide_b200 import workloads
+
+    bench.configure("llama8b_prefill_checkpoints")
+    a = bench.checkpoint_setup(1, 0, 31130, 3277)
+    b = bench.checkpoint_setup(1, 0, 31130, 3277)
+    assert torch.equal(a["x_head"].view(torch.int16), b["x_head"].view(torch.int16))
+    assert torch.equal(a["down"], b["down"]) and a["bias"] == b["bias"]
+    z = workloads.prebias_logits_torch(a["x_head"], "rms", torch.ones(4096), None, 1e-5,
+                                       a["down"], a["up"])
+    frac = float(((z + a["bias"]) > workloads.logit(0.85)).float().mean())
+    assert abs(frac - 3277 / 31130) < 1e-3
+    c = bench.checkpoint_setup(1, 1, 31130, 3277)  # another rank: other rows
+    assert not torch.equal(a["x_head"].view(torch.int16), c["x_head"].view(torch.int16))
+
+
+def test_cpu_reference_step_chains_survivors(bench):
+    bench.configure("llama8b_prefill_checkpoints")
+    inp = bench.cpu_sweep_inputs(64)
+    t, routed = bench.cpu_sweep_step(inp)
+    assert t > 0 and 64 <= routed <= 6 * 64
+    t2, routed2 = bench.cpu_sweep_step(inp)
+    assert routed2 == routed  # deterministic

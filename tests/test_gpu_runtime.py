@@ -243,3 +243,64 @@ def test_torch_ops_reference_semantics():
         ops.exit_projection(x[:4, :256].contiguous(), torch.ones(256, device=DEV), pos[:4], out, 1e-6)
         ref = O.rms_norm(O.to_f32(storage_np(x[:4, :256]), TORCH2O[dtype]), np.ones(256, np.float32), 1e-6)
         np.testing.assert_allclose(out[pos[:4].long()].float().cpu().numpy(), ref, atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("H", [2048, 4096])
+@pytest.mark.parametrize("n", [1, 8, 32, 128, 5000])
+def test_torch_op_router_16bit_tensor_cores(n, H, dtype):
+    """torch.ops.tide.fused_layernorm_route on the reference runtime's own
+    inputs (runtime.py:120-126: rows and the final norm's weight in the model
+    dtype, pre-transposed fp32 router weights, eps 1e-6) at the reference
+    op test's shapes (tests/test_kernels.py:64-87) runs a tensor-core router
+    (fused single pass or split) and stays within the 1e-2 score bar of the
+    oracle; the observed margin is printed."""
+    from tide_b200 import _native, capi
+
+    ops = _native.ops()
+    g = torch.Generator().manual_seed(n * 7 + H)
+    x = torch.randn(n, H, generator=g).to(dtype).to(DEV)
+    nw = (1.0 + 0.02 * torch.randn(H, generator=g)).to(dtype).to(DEV)
+    dw = (0.02 * torch.randn(H, 128, generator=g)).to(DEV)
+    uw = (0.15 * torch.randn(128, 1, generator=g)).to(DEV)
+    s = ops.fused_layernorm_route(x, nw, dw, uw, 1e-6)
+    path = ops.last_route_path()
+    ref = O.fused_layernorm_route(storage_np(x), TORCH2O[dtype], nw.float().cpu().numpy(),
+                                  dw.cpu().numpy(), uw.cpu().numpy(), 1e-6)
+    err = float(np.abs(s.cpu().numpy() - ref).max())
+    print(f"n={n} H={H} {dtype}: path {path}, max score error {err:.2e}")
+    assert path in (capi.PATH_TC, capi.PATH_TC_SPLIT)
+    assert err <= 1e-2
+
+
+def test_torch_op_router_refolds_after_update_and_falls_back():
+    """The op's folded-weight cache: an in-place update of the router weights
+    (version bump) refolds; weights whose 16-bit rounding could move a score
+    by more than the bar (N(0,1) weights, as in the reference's op test) take
+    the fp32 SIMT router and stay exact to 1e-4."""
+    from tide_b200 import _native, capi
+
+    ops = _native.ops()
+    g = torch.Generator().manual_seed(11)
+    n, H = 256, 4096
+    x = torch.randn(n, H, generator=g).to(torch.bfloat16).to(DEV)
+    nw = torch.ones(H, device=DEV)
+    dw = (0.02 * torch.randn(H, 128, generator=g)).to(DEV)
+    uw = (0.15 * torch.randn(128, 1, generator=g)).to(DEV)
+
+    def ref():
+        return O.fused_layernorm_route(storage_np(x), O.BF16, nw.cpu().numpy(), dw.cpu().numpy(),
+                                       uw.cpu().numpy(), 1e-6)
+
+    s0 = ops.fused_layernorm_route(x, nw, dw, uw, 1e-6).cpu().numpy()
+    assert ops.last_route_path() in (capi.PATH_TC, capi.PATH_TC_SPLIT)
+    np.testing.assert_allclose(s0, ref(), atol=1e-2, rtol=0)
+    dw.mul_(-1.5)  # same tensor, new values
+    s1 = ops.fused_layernorm_route(x, nw, dw, uw, 1e-6).cpu().numpy()
+    np.testing.assert_allclose(s1, ref(), atol=1e-2, rtol=0)
+    assert np.abs(s1 - s0).max() > 1e-2
+    big = torch.randn(H, 128, generator=g).to(DEV)
+    ub = torch.randn(128, 1, generator=g).to(DEV)
+    s2 = ops.fused_layernorm_route(x, torch.randn(H, generator=g).to(DEV), big, ub, 1e-6)
+    assert ops.last_route_path() == capi.PATH_SIMT
+    assert torch.isfinite(s2).all()

@@ -64,6 +64,26 @@ def test_noalloc_matches_workspace_version_two_calls(dtype, H):
         assert np.array_equal(got[3].cpu().numpy(), keep)
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [capi.NOALLOC_MAX_ROWS, 0])
+def test_noalloc_at_its_limit_and_empty(n):
+    """The largest call the built-in scratch takes (its last status word in
+    use) and an empty call, each twice in a row, against the workspace
+    version and np.nonzero.  Rows of 4 fp32 values keep the limit case at
+    16 MB per tensor."""
+    g = torch.Generator().manual_seed(n + 1)
+    x = torch.randn(n, 4, generator=g).cuda()
+    mask = (torch.rand(n, generator=g) < 0.5).to(torch.int32).cuda()
+    ref = _split(x, mask, noalloc=False)
+    for _ in range(2):
+        got = _split(x, mask, noalloc=True)
+        assert got[0] == ref[0] == int((mask == 0).sum().item())
+        for a, b in zip(got[1:], ref[1:]):
+            assert torch.equal(a, b)
+        keep = np.nonzero(mask.cpu().numpy() == 0)[0]
+        assert np.array_equal(got[3].cpu().numpy(), keep)
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch():
     lib = _native.lib()
     n = capi.NOALLOC_MAX_ROWS + 1

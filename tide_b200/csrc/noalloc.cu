@@ -22,7 +22,10 @@
 // Host code only ever sees a stand-in for the array's name, not a device
 // address.  The first call on a device therefore looks the address up with
 // cudaGetSymbolAddress, with that device current, and caches it for later
-// calls.  That first call should happen before any stream capture.
+// calls.  That first call should happen before any stream capture.  The
+// cached address belongs to the device's primary context: a cudaDeviceReset
+// (or a release and re-creation of that context) makes it stale, and the
+// entry point must not be called on that device again in this process.
 #include <stdarg.h>
 #include <stdio.h>
 

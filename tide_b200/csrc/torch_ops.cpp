@@ -12,6 +12,10 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <cmath>
+#include <deque>
+#include <mutex>
+
 #include "tide_b200.h"
 
 namespace {
@@ -50,6 +54,128 @@ void *opt_mut(const std::optional<at::Tensor> &t) {
 
 // ---- reference operators ------------------------------------------------
 
+// Router weights in the tensor-core layout, folded once per (weights,
+// version, dtype) instead of on every call: the reference op re-casts its
+// weights on each call (torch_bindings.cpp:101-103); the runtime that calls
+// it passes the same parameters every time (python/TIDE/runtime.py:120-126).
+// Entries hold the source tensors, so a cached address cannot be reused by
+// another tensor while it is cached; an in-place update bumps the version
+// counter and refolds.
+struct FoldEntry {
+  at::Tensor down_src, norm_src, up_src;
+  uint32_t down_ver = 0, norm_ver = 0, up_ver = 0;
+  at::ScalarType fold_dtype;
+  at::Tensor folded, colsum, up;
+  // whether the folded weights' rounding keeps scores inside the score bar
+  // (always for fp32 folds; see fold_cached)
+  bool tc_ok = true;
+};
+
+std::mutex g_fold_mu;
+std::deque<FoldEntry> g_fold_cache;  // most recent at the front
+constexpr size_t kFoldCacheEntries = 64;
+thread_local int64_t g_last_route_path = 0;
+
+uint32_t version_of(const at::Tensor &t) {
+  return t.unsafeGetTensorImpl()->version_counter().current_version();
+}
+
+// Folded weights for (down_weight [H, B] pre-transposed, norm_weight [H],
+// up_weight [B]) in fold_dtype: W'[b, i] = down[i, b] * norm_weight[i].
+FoldEntry fold_cached(const at::Tensor &down_weight, const at::Tensor &norm_weight,
+                      const at::Tensor &up_weight, at::ScalarType fold_dtype, cudaStream_t s) {
+  std::lock_guard<std::mutex> lock(g_fold_mu);
+  for (auto it = g_fold_cache.begin(); it != g_fold_cache.end(); ++it) {
+    if (it->fold_dtype == fold_dtype && it->down_src.is_same(down_weight) &&
+        it->norm_src.is_same(norm_weight) && it->up_src.is_same(up_weight) &&
+        it->down_ver == version_of(down_weight) && it->norm_ver == version_of(norm_weight) &&
+        it->up_ver == version_of(up_weight)) {
+      FoldEntry e = *it;
+      if (it != g_fold_cache.begin()) {
+        g_fold_cache.erase(it);
+        g_fold_cache.push_front(e);
+      }
+      return e;
+    }
+  }
+  const int64_t H = down_weight.size(0), B = down_weight.size(1);
+  auto down = down_weight.to(at::kFloat).t().contiguous();  // [B, H], router.down.weight
+  auto nw = norm_weight.to(at::kFloat).contiguous();
+  auto f32 = down.options();
+  FoldEntry e;
+  e.down_src = down_weight;
+  e.norm_src = norm_weight;
+  e.up_src = up_weight;
+  e.down_ver = version_of(down_weight);
+  e.norm_ver = version_of(norm_weight);
+  e.up_ver = version_of(up_weight);
+  e.fold_dtype = fold_dtype;
+  e.folded = at::empty({B, H}, f32.dtype(fold_dtype));
+  e.colsum = at::empty({B}, f32);
+  e.up = up_weight.to(at::kFloat).reshape({-1}).contiguous();
+  TIDE_CHECK_OK(tide_router_fold(to_dtype(fold_dtype, "fused_layernorm_route"),
+                                 down.data_ptr<float>(), nw.data_ptr<float>(), nullptr, H, B,
+                                 nullptr, e.folded.data_ptr(), e.colsum.data_ptr<float>(), nullptr,
+                                 (tide_stream_t)s));
+  if (fold_dtype != at::kFloat) {
+    // A 16-bit W' rounds each weight by up to 2^-9 (bf16) or 2^-12 (fp16)
+    // relative.  For RMS-normed rows (unit mean square) the router's output
+    // logit then moves by a zero-mean error of standard deviation
+    //   sigma = sqrt(sum_b up_b^2 * ||W'_b - W'_b(fp32)||^2),
+    // and a score, sigmoid of that logit, by at most sigma / 4 per unit.
+    // The tensor cores take these weights only when six sigma stays inside
+    // the 1e-2 score bar; otherwise (e.g. N(0,1) weights, as in the
+    // reference's own op test) the fp32 SIMT router runs.
+    auto exact = at::empty({B, H}, f32);
+    auto cs = at::empty({B}, f32);
+    TIDE_CHECK_OK(tide_router_fold(TIDE_DTYPE_F32, down.data_ptr<float>(), nw.data_ptr<float>(),
+                                   nullptr, H, B, nullptr, exact.data_ptr(), cs.data_ptr<float>(),
+                                   nullptr, (tide_stream_t)s));
+    auto err2 = (e.folded.to(at::kFloat) - exact).pow(2).sum(1);  // [B]
+    const double sigma = std::sqrt((e.up.pow(2) * err2).sum().item<double>());
+    e.tc_ok = std::isfinite(sigma) && 6.0 * sigma / 4.0 <= 1e-2;
+  }
+  g_fold_cache.push_front(e);
+  while (g_fold_cache.size() > kFoldCacheEntries) g_fold_cache.pop_back();
+  return e;
+}
+
+// Scores of `input` on a tensor-core path: one checkpoint with a threshold
+// no score can pass, so no row exits and nothing moves.  Returns the path
+// taken, or 0 when neither tensor-core path takes these arguments.
+int route_tensor_cores(const at::Tensor &input, const at::Tensor &norm_weight, const FoldEntry &fe,
+                       double eps, at::Tensor &scores, cudaStream_t s) {
+  const int64_t n = input.size(0), H = input.size(1), B = fe.folded.size(0);
+  auto nw = norm_weight.to(at::kFloat).contiguous();
+  auto counts = at::empty({2}, input.options().dtype(at::kInt));
+  tide_checkpoint_args a{};
+  a.dtype = to_dtype(input.scalar_type(), "fused_layernorm_route");
+  a.norm_type = TIDE_NORM_RMS;
+  a.path = TIDE_PATH_AUTO;
+  a.n_rows = n;
+  a.hidden_dim = H;
+  a.bottleneck_dim = B;
+  a.n_total = n;
+  a.x = input.data_ptr();
+  a.norm_weight = nw.data_ptr<float>();
+  a.eps = (float)eps;
+  a.up_bias = 0.f;
+  a.folded = fe.folded.data_ptr();
+  a.colsum = fe.colsum.data_ptr<float>();
+  a.up = fe.up.data_ptr<float>();
+  a.threshold = 2.0f;  // scores lie in [0, 1]
+  a.scores_out = scores.data_ptr<float>();
+  a.counts_out = counts.data_ptr<int32_t>();
+  auto ws = at::empty({(int64_t)tide_checkpoint_workspace_size(&a)}, input.options().dtype(at::kByte));
+  a.workspace = ws.data_ptr();
+  a.workspace_bytes = (size_t)ws.numel();
+  // (the path check validates the whole argument block, workspace included)
+  const int path = tide_checkpoint_select_path(&a);
+  if (path != TIDE_PATH_TC && path != TIDE_PATH_TC_SPLIT) return 0;
+  TIDE_CHECK_OK(tide_checkpoint(&a, (tide_stream_t)s));
+  return path;
+}
+
 at::Tensor fused_layernorm_route(const at::Tensor &input, const at::Tensor &norm_weight,
                                  const at::Tensor &down_weight, const at::Tensor &up_weight,
                                  double eps) {
@@ -65,56 +191,35 @@ at::Tensor fused_layernorm_route(const at::Tensor &input, const at::Tensor &norm
   TORCH_CHECK(down_weight.size(0) == H, "down_weight must be [D, B]");
   TORCH_CHECK(up_weight.numel() == B, "up_weight must have B elements");
   const c10::cuda::CUDAGuard guard(input.device());
-  auto nw = norm_weight.to(at::kFloat).contiguous();
-  auto dw = down_weight.to(at::kFloat).contiguous();
-  auto uw = up_weight.to(at::kFloat).contiguous();
+  const int dtype = to_dtype(input.scalar_type(), "fused_layernorm_route");
   auto scores = at::empty({n}, input.options().dtype(at::kFloat));
-  if (input.scalar_type() == at::kFloat && n > 0 && H % 32 == 0 && B <= 256) {
-    // fp32 rows: the tensor-core router (three tf32 products per K step,
-    // scores within the fp32 bar), 3-5x faster than the SIMT router.  The
-    // weights are folded on each call (one small kernel), and one checkpoint
-    // runs with a threshold no score can pass: no row exits, nothing moves.
-    auto down = dw.t().contiguous();  // [B, H]
-    auto f32 = input.options().dtype(at::kFloat);
-    auto folded = at::empty({B, H}, f32);
-    auto colsum = at::empty({B}, f32);
-    TIDE_CHECK_OK(tide_router_fold(TIDE_DTYPE_F32, down.data_ptr<float>(), nw.data_ptr<float>(),
-                                   nullptr, H, B, nullptr, folded.data_ptr(),
-                                   colsum.data_ptr<float>(), nullptr, cur_stream(input)));
-    auto counts = at::empty({2}, input.options().dtype(at::kInt));
-    tide_checkpoint_args a{};
-    a.dtype = TIDE_DTYPE_F32;
-    a.norm_type = TIDE_NORM_RMS;
-    a.path = TIDE_PATH_TC_SPLIT;
-    a.n_rows = n;
-    a.hidden_dim = H;
-    a.bottleneck_dim = B;
-    a.n_total = n;
-    a.x = input.data_ptr();
-    a.norm_weight = nw.data_ptr<float>();
-    a.eps = (float)eps;
-    a.up_bias = 0.f;
-    a.folded = folded.data_ptr();
-    a.colsum = colsum.data_ptr<float>();
-    a.up = uw.data_ptr<float>();
-    a.threshold = 2.0f;  // scores lie in [0, 1]
-    a.scores_out = scores.data_ptr<float>();
-    a.counts_out = counts.data_ptr<int32_t>();
-    auto ws = at::empty({(int64_t)tide_checkpoint_workspace_size(&a)}, input.options().dtype(at::kByte));
-    a.workspace = ws.data_ptr();
-    a.workspace_bytes = (size_t)ws.numel();
-    // (the path check validates the whole argument block, workspace included)
-    if (tide_checkpoint_select_path(&a) == TIDE_PATH_TC_SPLIT) {
-      TIDE_CHECK_OK(tide_checkpoint(&a, cur_stream(input)));
+  const bool f32 = dtype == TIDE_DTYPE_F32;
+  const cudaStream_t s = at::cuda::getCurrentCUDAStream(input.device().index()).stream();
+  if (n > 0 && B <= 256 && H % (f32 ? 32 : 64) == 0) {
+    // The tensor-core routers: kind::f16 MMAs on the rows' own 16-bit type
+    // (the single-pass cluster kernel up to a few thousand rows, the split
+    // router above), three kind::tf32 products for fp32 rows.  The weights
+    // are folded once (cached above) in the rows' type.
+    const FoldEntry fe = fold_cached(down_weight, norm_weight, up_weight, input.scalar_type(), s);
+    const int path = fe.tc_ok ? route_tensor_cores(input, norm_weight, fe, eps, scores, s) : 0;
+    if (path) {
+      g_last_route_path = path;
       return scores;
     }
   }
-  TIDE_CHECK_OK(tide_fused_layernorm_route(to_dtype(input.scalar_type(), "fused_layernorm_route"),
-                                           input.data_ptr(), nw.data_ptr<float>(),
+  auto nw = norm_weight.to(at::kFloat).contiguous();
+  auto dw = down_weight.to(at::kFloat).contiguous();
+  auto uw = up_weight.to(at::kFloat).contiguous();
+  TIDE_CHECK_OK(tide_fused_layernorm_route(dtype, input.data_ptr(), nw.data_ptr<float>(),
                                            dw.data_ptr<float>(), uw.data_ptr<float>(), (float)eps,
-                                           scores.data_ptr<float>(), n, H, B, cur_stream(input)));
+                                           scores.data_ptr<float>(), n, H, B, (tide_stream_t)s));
+  g_last_route_path = TIDE_PATH_SIMT;
   return scores;
 }
+
+// The path the calling thread's last fused_layernorm_route took
+// (TIDE_PATH_SIMT, _TC or _TC_SPLIT; 0 before the first call).
+int64_t last_route_path() { return g_last_route_path; }
 
 std::vector<at::Tensor> batch_compact(const at::Tensor &input, const at::Tensor &exit_mask) {
   check_cuda_contig(input, "input");
@@ -363,6 +468,7 @@ TORCH_LIBRARY(tide, m) {
   m.def("router_fold(Tensor down, Tensor norm_weight, Tensor? norm_bias, ScalarType fold_dtype) "
         "-> Tensor[]");
   m.def("checkpoint_workspace_size(int n_rows, int hidden_dim) -> int", &checkpoint_workspace_size);
+  m.def("last_route_path() -> int", &last_route_path);
   m.def("checkpoint(Tensor x, Tensor? n_rows_dev, Tensor norm_weight, Tensor? norm_bias, "
         "int norm_type, float eps, Tensor down_t, Tensor? folded, Tensor? colsum, "
         "Tensor? bias_proj, Tensor up, float up_bias, float threshold, Tensor? positions, "
