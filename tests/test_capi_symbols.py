@@ -151,3 +151,15 @@ def test_path_selection():
     assert sel(path=capi.PATH_SIMT) == capi.PATH_SIMT
     assert sel(path=capi.PATH_TC, hidden_dim=4000) == -capi.ERR_UNSUPPORTED
     assert b"multiple of 64" in lib.tide_last_error()
+
+
+def test_testhooks_library_mirrors_the_product_surface():
+    """The test build (one look-back tile that never publishes, short wait
+    bounds) loads without a GPU and exports the same C ABI."""
+    from tide_b200 import build
+
+    lib = ctypes.CDLL(str(build.TEST_LIB))
+    capi.declare(lib)
+    for n in declared_functions():
+        assert hasattr(lib, n), n
+    assert lib.tide_abi_version() == 1

@@ -25,6 +25,12 @@ INCLUDE = ROOT / "include"
 BUILD = ROOT / "_build"
 LIB = PKG / "libtide_b200.so"
 EXT = PKG / "_C.so"
+# The same kernels built with one test hook: tile TEST_TILE of every stable
+# partition never publishes its look-back status, and look-back waits give up
+# after a short bound, so tests can make a bounded device wait run out
+# (TIDE_DEVERR_TIMEOUT) without any fault.  Only tests load it.
+TEST_LIB = PKG / "libtide_b200_testhooks.so"
+TEST_TILE = 3
 
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
@@ -58,20 +64,29 @@ def _headers() -> list[Path]:
     return [CSRC / h for h in HEADERS] + [INCLUDE / "tide_b200.h"]
 
 
-def build_lib(verbose: bool = False, force: bool = False) -> Path:
-    BUILD.mkdir(exist_ok=True)
-    objs = []
-    jobs = []
+def _lib_jobs(build_dir: Path, extra: list[str], force: bool) -> tuple[list[Path], list[list[str]]]:
+    build_dir.mkdir(parents=True, exist_ok=True)
+    objs, jobs = [], []
     for src in CU_SOURCES:
         s = CSRC / src
-        o = BUILD / (src + ".o")
+        o = build_dir / (src + ".o")
         objs.append(o)
         if force or not _newer(o, [s, *_headers(), Path(__file__)]):
-            jobs.append([NVCC, *NVCC_FLAGS, "-c", str(s), "-o", str(o)])
-    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
-        list(ex.map(lambda c: _run(c, verbose), jobs))
+            jobs.append([NVCC, *NVCC_FLAGS, *extra, "-c", str(s), "-o", str(o)])
+    return objs, jobs
+
+
+def build_lib(verbose: bool = False, force: bool = False) -> Path:
+    """libtide_b200.so and its test-hook twin, compiled in parallel."""
+    objs, jobs = _lib_jobs(BUILD, [], force)
+    tobjs, tjobs = _lib_jobs(BUILD / "testhooks", [f"-DTIDE_TEST_UNPUBLISHED_TILE={TEST_TILE}"], force)
+    all_jobs = jobs + tjobs
+    with ThreadPoolExecutor(max_workers=max(1, min(len(all_jobs), os.cpu_count() or 1))) as ex:
+        list(ex.map(lambda c: _run(c, verbose), all_jobs))
     if force or jobs or not _newer(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs)], verbose)
+    if force or tjobs or not _newer(TEST_LIB, tobjs):
+        _run([NVCC, *ARCH, "-shared", "-o", str(TEST_LIB), *map(str, tobjs)], verbose)
     return LIB
 
 

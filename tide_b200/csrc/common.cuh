@@ -115,7 +115,27 @@ constexpr uint64_t kCountMask = (1ull << 31) - 1;
 // Spin bound for a look-back wait.  A predecessor tile is always held by a
 // running CTA (tiles are handed out in ticket order), so this only expires
 // if the device is wedged; the kernel then flags TIDE_DEVERR_TIMEOUT.
+//
+// The test build of the library (libtide_b200_testhooks.so, compiled with
+// TIDE_TEST_UNPUBLISHED_TILE=t) makes that happen on purpose without any
+// fault: tile t computes its own prefix but never publishes its status, so
+// the look-back of the tiles after it waits on a word nothing sets, gives up
+// after a short bound and reports TIDE_DEVERR_TIMEOUT.  The product build
+// has no such tile.
+#ifdef TIDE_TEST_UNPUBLISHED_TILE
+constexpr int kSpinLimit = 1 << 12;
+#else
 constexpr int kSpinLimit = 1 << 24;
+#endif
+
+__device__ __forceinline__ bool unpublished_test_tile(uint32_t tile) {
+#ifdef TIDE_TEST_UNPUBLISHED_TILE
+  return tile == (uint32_t)(TIDE_TEST_UNPUBLISHED_TILE);
+#else
+  (void)tile;
+  return false;
+#endif
+}
 
 __device__ __forceinline__ uint64_t pack_status(uint64_t flag, uint32_t keep, uint32_t exits) {
   return flag | ((uint64_t)exits << 31) | (uint64_t)keep;
@@ -140,13 +160,14 @@ __device__ __forceinline__ bool lookback(uint64_t *status, uint32_t tile, uint32
                                          uint32_t exits, uint32_t *keep_before,
                                          uint32_t *exits_before) {
   uint32_t kb = 0, eb = 0;
+  const bool publish = !unpublished_test_tile(tile);
   if (tile == 0) {
-    st_status(&status[0], pack_status(kFlagPrefix, keep, exits));
+    if (publish) st_status(&status[0], pack_status(kFlagPrefix, keep, exits));
     *keep_before = 0;
     *exits_before = 0;
     return true;
   }
-  st_status(&status[tile], pack_status(kFlagAggregate, keep, exits));
+  if (publish) st_status(&status[tile], pack_status(kFlagAggregate, keep, exits));
   int64_t j = (int64_t)tile - 1;
   bool ok = true;
   while (j >= 0) {
@@ -162,7 +183,7 @@ __device__ __forceinline__ bool lookback(uint64_t *status, uint32_t tile, uint32
     if ((s >> 62) == 2) break;
     --j;
   }
-  st_status(&status[tile], pack_status(kFlagPrefix, kb + keep, eb + exits));
+  if (publish) st_status(&status[tile], pack_status(kFlagPrefix, kb + keep, eb + exits));
   *keep_before = kb;
   *exits_before = eb;
   return ok;
@@ -182,6 +203,7 @@ __device__ __forceinline__ bool warp_lookback(uint64_t *status, uint32_t tile, u
                                               uint32_t *exits_before) {
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
+  publish = publish && !unpublished_test_tile(tile);
   if (publish && lane == 0)
     st_status(&status[tile], pack_status(tile == 0 ? kFlagPrefix : kFlagAggregate, keep, exits));
   uint32_t kb = 0, eb = 0;
@@ -214,7 +236,7 @@ __device__ __forceinline__ bool warp_lookback(uint64_t *status, uint32_t tile, u
     if (incl) break;
   }
   if (publish && lane == 0 && tile != 0)
-    st_status(&status[tile], pack_status(kFlagPrefix, kb + keep, eb + exits));
+    if (publish) st_status(&status[tile], pack_status(kFlagPrefix, kb + keep, eb + exits));
   *keep_before = kb;
   *exits_before = eb;
   return ok;
