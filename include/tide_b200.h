@@ -139,6 +139,27 @@ int tide_norm_scatter(int dtype, int norm_type, const void *rows, const int64_t 
                       float eps, int64_t n_rows, int64_t hidden_dim, int64_t n_total,
                       int32_t *error_word, tide_stream_t stream);
 
+/* Rows of a full tensor picked through an index, for a live row count kept
+ * on the device (checkpoint k-1's counts_out), so that checkpoints chain
+ * without a host read-back.  i runs over [0, *n_rows_dev) (clamped to
+ * n_rows; [0, n_rows) when n_rows_dev is NULL); an index outside [0, n_src)
+ * skips the row and sets TIDE_DEVERR_POSITION.
+ * tide_gather_rows:       dst[i] = src[index[i]], src [n_src, H]: the still-
+ *                         active rows of a later layer's hidden states, the
+ *                         `hidden[~exited]` of python/TIDE/runtime.py:172-174
+ *                         (and of scheduler.py:98 in the live loop).
+ * tide_norm_at_positions: out[positions[i]] = final_norm(src[positions[i]]),
+ *                         src and out [n_total, H]: the rows that never exit,
+ *                         python/TIDE/runtime.py:183-187. */
+int tide_gather_rows(int dtype, const void *src, int64_t n_src, const int64_t *index,
+                     const int32_t *n_rows_dev, int64_t n_rows, int64_t hidden_dim, void *dst,
+                     int32_t *error_word, tide_stream_t stream);
+int tide_norm_at_positions(int dtype, int norm_type, const void *src, const int64_t *positions,
+                           const int32_t *n_rows_dev, int64_t n_rows, int64_t hidden_dim,
+                           int64_t n_total, void *output_buffer, const float *norm_weight,
+                           const float *norm_bias, float eps, int32_t *error_word,
+                           tide_stream_t stream);
+
 /* ---- router preparation (once per router) ------------------------------ */
 
 /* From the router's down.weight [B, H] fp32 and the final norm's weight (and

@@ -224,15 +224,19 @@ def checkpoint(x: np.ndarray, dtype: str, norm: dict, down, up, up_bias: float,
 
 
 def forward_posthoc(all_hidden: list[np.ndarray], dtype: str, norm: dict,
-                    routers: dict[int, dict], threshold: float, min_layers: int):
+                    routers: dict[int, dict], threshold: float, min_layers: int,
+                    detail: bool = False):
     """The post-hoc exit loop of TIDERuntime.forward, python/TIDE/runtime.py:
     163-188, on the flattened hidden states all_hidden[l] [N, H] (index 0 =
     embeddings, index l+1 = output of decoder layer l).  routers maps a layer
     index to {"down", "up", "up_bias"}.  Returns (output_buffer in storage
-    dtype, exits_per_layer, remaining_tokens)."""
+    dtype, exits_per_layer, remaining_tokens); with detail=True also a dict
+    with each token's exit layer (-1: never) and every router's scores."""
     n, h = all_hidden[-1].shape
     out = np.zeros((n, h), dtype=all_hidden[-1].dtype)
     exited = np.zeros(n, dtype=bool)
+    exit_layer = np.full(n, -1, dtype=np.int64)
+    scores: dict[int, np.ndarray] = {}
     exits_per_layer: dict[int, int] = {}
     for layer in sorted(routers):
         if layer < min_layers:
@@ -240,16 +244,21 @@ def forward_posthoc(all_hidden: list[np.ndarray], dtype: str, norm: dict,
         hid = all_hidden[layer + 1]
         r = routers[layer]
         s = score_rows(hid, dtype, norm, r["down"], r["up"], r.get("up_bias", 0.0))
+        scores[layer] = s
         new = exit_decision(s, threshold, exited)
         if new.any():
             normed = from_f32(final_norm(to_f32(hid, dtype), norm), dtype)
             out[new] = normed[new]
             exited |= new
+            exit_layer[new] = layer
             exits_per_layer[layer] = int(new.sum())
     remaining = ~exited
     if remaining.any():
         normed = from_f32(final_norm(to_f32(all_hidden[-1], dtype), norm), dtype)
         out[remaining] = normed[remaining]
+    if detail:
+        return out, exits_per_layer, int(remaining.sum()), {"exit_layer": exit_layer,
+                                                            "scores": scores}
     return out, exits_per_layer, int(remaining.sum())
 
 

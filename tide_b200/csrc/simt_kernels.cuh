@@ -468,6 +468,57 @@ __global__ void scatter_rows_kernel(const T *__restrict__ src, const int32_t *__
   norm_row<T, VEC>(s, d, H, lane, mean, rstd, norm_type, w, bias);
 }
 
+// ------------------------------------------------------- indexed rows
+// Rows addressed through an index with a live count kept on the device, so
+// that checkpoints chain without reading the count back:
+//   gather (NORM = false):       dst[i] = src[idx[i]]
+//   norm in place (NORM = true): dst[idx[i]] = final_norm(src[idx[i]])
+// for i < live, live = *n_dev clamped to [0, n_cap] (n_cap without n_dev).
+// One warp per row, grid-stride over the capacity.
+template <typename T, bool VEC, bool NORM>
+__global__ void indexed_rows_kernel(const T *__restrict__ src, const int64_t *__restrict__ idx,
+                                    const int32_t *__restrict__ n_dev, int64_t n_cap, int64_t H,
+                                    int64_t n_src, T *__restrict__ dst, int norm_type,
+                                    const float *__restrict__ w, const float *__restrict__ bias,
+                                    float eps, int32_t *err) {
+  const int lane = threadIdx.x & 31;
+  int64_t live = n_cap;
+  if (n_dev) {
+    const int64_t nd = (int64_t)__ldg(n_dev);
+    if (nd < 0 || nd > n_cap) {
+      if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(err, TIDE_DEVERR_COUNT);
+    }
+    live = nd < 0 ? 0 : (nd > n_cap ? n_cap : nd);
+  }
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t i = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); i < live; i += warps) {
+    const int64_t p = idx[i];
+    if (p < 0 || p >= n_src) {
+      if (lane == 0) raise_error(err, TIDE_DEVERR_POSITION);
+      continue;
+    }
+    const T *s = src + p * H;
+    if (!NORM) {
+      copy_row<T, VEC>(s, dst + i * H, H, lane);
+      continue;
+    }
+    float mean = 0.f;
+    if (norm_type == TIDE_NORM_LAYER) {
+      float sum = 0.f;
+      for (int64_t k = lane; k < H; k += 32) sum += Elem<T>::to_f(s[k]);
+      mean = warp_sum(sum) / (float)H;
+    }
+    float ss = 0.f;
+    for (int64_t k = lane; k < H; k += 32) {
+      const float dv = Elem<T>::to_f(s[k]) - mean;
+      ss = fmaf(dv, dv, ss);
+    }
+    ss = warp_sum(ss);
+    const float rstd = rsqrt_rn(ss / (float)H + eps);
+    norm_row<T, VEC>(s, dst + p * H, H, lane, mean, rstd, norm_type, w, bias);
+  }
+}
+
 // ---------------------------------------------------------- weight fold
 // One CTA per router unit b.
 template <typename TF>

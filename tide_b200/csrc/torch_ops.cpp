@@ -320,6 +320,62 @@ void norm_scatter(const at::Tensor &rows, const at::Tensor &positions,
                                   cur_stream(rows)));
 }
 
+void gather_rows(const at::Tensor &src, const at::Tensor &index,
+                 const std::optional<at::Tensor> &n_rows_dev, const at::Tensor &dst,
+                 const std::optional<at::Tensor> &error_word) {
+  check_cuda_contig(src, "src");
+  check_cuda_contig(index, "index");
+  check_cuda_contig(dst, "dst");
+  TORCH_CHECK(src.dim() == 2 && dst.dim() == 2 && src.size(1) == dst.size(1), "expected [*, H] rows");
+  TORCH_CHECK(src.scalar_type() == dst.scalar_type(), "src/dst dtype differ");
+  TORCH_CHECK(index.scalar_type() == at::kLong, "index must be int64");
+  const int64_t n = index.numel();
+  TORCH_CHECK(dst.size(0) >= n, "dst has fewer rows than index entries");
+  if (n_rows_dev.has_value() && n_rows_dev->defined())
+    TORCH_CHECK(n_rows_dev->is_cuda() && n_rows_dev->scalar_type() == at::kInt, "n_rows_dev must be int32");
+  if (error_word.has_value() && error_word->defined())
+    TORCH_CHECK(error_word->is_cuda() && error_word->scalar_type() == at::kInt, "error_word must be int32");
+  const c10::cuda::CUDAGuard guard(src.device());
+  TIDE_CHECK_OK(tide_gather_rows(to_dtype(src.scalar_type(), "gather_rows"), src.data_ptr(), src.size(0),
+                                 index.data_ptr<int64_t>(),
+                                 static_cast<const int32_t *>(opt_ptr(n_rows_dev)), n, src.size(1),
+                                 dst.data_ptr(), static_cast<int32_t *>(opt_mut(error_word)),
+                                 cur_stream(src)));
+}
+
+void norm_at_positions(const at::Tensor &src, const at::Tensor &positions,
+                       const std::optional<at::Tensor> &n_rows_dev, const at::Tensor &output_buffer,
+                       const at::Tensor &norm_weight, const std::optional<at::Tensor> &norm_bias,
+                       int64_t norm_type, double eps, const std::optional<at::Tensor> &error_word) {
+  check_cuda_contig(src, "src");
+  check_cuda_contig(positions, "positions");
+  check_cuda_contig(output_buffer, "output_buffer");
+  check_cuda_contig(norm_weight, "norm_weight");
+  TORCH_CHECK(src.dim() == 2 && output_buffer.dim() == 2 && src.sizes() == output_buffer.sizes(),
+              "src and output_buffer must both be [N_total, H]");
+  TORCH_CHECK(src.scalar_type() == output_buffer.scalar_type(), "src/output_buffer dtype differ");
+  TORCH_CHECK(positions.scalar_type() == at::kLong, "positions must be int64");
+  const int64_t H = src.size(1);
+  TORCH_CHECK(norm_weight.scalar_type() == at::kFloat && norm_weight.numel() == H,
+              "norm_weight must be fp32 [H]");
+  const float *nb = nullptr;
+  if (norm_bias.has_value() && norm_bias->defined()) {
+    check_cuda_contig(*norm_bias, "norm_bias");
+    TORCH_CHECK(norm_bias->scalar_type() == at::kFloat && norm_bias->numel() == H,
+                "norm_bias must be fp32 [H]");
+    nb = norm_bias->data_ptr<float>();
+  }
+  if (n_rows_dev.has_value() && n_rows_dev->defined())
+    TORCH_CHECK(n_rows_dev->is_cuda() && n_rows_dev->scalar_type() == at::kInt, "n_rows_dev must be int32");
+  const c10::cuda::CUDAGuard guard(src.device());
+  TIDE_CHECK_OK(tide_norm_at_positions(to_dtype(src.scalar_type(), "norm_at_positions"), (int)norm_type,
+                                       src.data_ptr(), positions.data_ptr<int64_t>(),
+                                       static_cast<const int32_t *>(opt_ptr(n_rows_dev)),
+                                       positions.numel(), H, src.size(0), output_buffer.data_ptr(),
+                                       norm_weight.data_ptr<float>(), nb, (float)eps,
+                                       static_cast<int32_t *>(opt_mut(error_word)), cur_stream(src)));
+}
+
 // ---- router fold and fused checkpoint ----------------------------------
 
 std::vector<at::Tensor> router_fold(const at::Tensor &down, const at::Tensor &norm_weight,
@@ -465,6 +521,11 @@ TORCH_LIBRARY(tide, m) {
         "Tensor(a!) output_buffer, float eps) -> ()");
   m.def("norm_scatter(Tensor rows, Tensor positions, Tensor(a!) output_buffer, "
         "Tensor norm_weight, Tensor? norm_bias, int norm_type, float eps) -> ()");
+  m.def("gather_rows(Tensor src, Tensor index, Tensor? n_rows_dev, Tensor(a!) dst, "
+        "Tensor(b!)? error_word) -> ()");
+  m.def("norm_at_positions(Tensor src, Tensor positions, Tensor? n_rows_dev, "
+        "Tensor(a!) output_buffer, Tensor norm_weight, Tensor? norm_bias, int norm_type, float eps, "
+        "Tensor(b!)? error_word) -> ()");
   m.def("router_fold(Tensor down, Tensor norm_weight, Tensor? norm_bias, ScalarType fold_dtype) "
         "-> Tensor[]");
   m.def("checkpoint_workspace_size(int n_rows, int hidden_dim) -> int", &checkpoint_workspace_size);
@@ -484,6 +545,8 @@ TORCH_LIBRARY_IMPL(tide, CUDA, m) {
   m.impl("exit_scatter", &exit_scatter);
   m.impl("exit_projection", &exit_projection);
   m.impl("norm_scatter", &norm_scatter);
+  m.impl("gather_rows", &gather_rows);
+  m.impl("norm_at_positions", &norm_at_positions);
   m.impl("router_fold", &router_fold);
   m.impl("checkpoint", &checkpoint);
 }

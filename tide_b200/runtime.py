@@ -66,6 +66,8 @@ class TIDERuntime(nn.Module):
         self._prepared: Dict[tuple, PreparedRouter] = {}
         self._runner = CheckpointRunner(dev)
         self.last_stats: Optional[ExitStats] = None
+        self.last_exit_layer: Optional[torch.Tensor] = None
+        self._events = []
         # TIDEConfig.profile (declared by the reference, config.py:21, never
         # read there): NVTX ranges around every checkpoint and the device time
         # of each, in milliseconds, after a forward
@@ -106,90 +108,142 @@ class TIDERuntime(nn.Module):
         except TypeError:
             return self.model(input_ids, **kw)
 
+    def _checkpoint_chain(self, hidden_at, N: int, H: int, dtype: torch.dtype, final: torch.Tensor,
+                          out_buf: torch.Tensor, slots: Optional[torch.Tensor] = None):
+        """The post-hoc exit loop on N rows (runtime.py:163-188): for every
+        router layer L >= min_layers, in order, route the still-active rows
+        of hidden_at(L) ([N, H], row index = token position), write the
+        exiting ones final-normed to out_buf at their positions and compact
+        the positions (and KV slots) of the survivors; then final-norm the
+        rows that never exit from `final`.  The live count chains on the
+        device from checkpoint to checkpoint: nothing is read back here.
+        Returns (layers, counts [n_layers, 2] device, exit position buffers,
+        error word)."""
+        ops = _native.ops()
+        layers = [L for L in sorted(self.routers) if L >= self.config.min_layers]
+        dev = out_buf.device
+        counts = torch.zeros(len(layers), 2, dtype=torch.int32, device=dev)
+        pos = [torch.empty(N, dtype=torch.int64, device=dev) for _ in range(2)]
+        slot_buf = ([torch.empty(N, dtype=torch.int32, device=dev) for _ in range(2)]
+                    if slots is not None else [None, None])
+        exit_pos = [torch.empty(N, dtype=torch.int64, device=dev) for _ in layers]
+        xbuf = torch.empty(N, H, dtype=dtype, device=dev) if len(layers) > 1 else None
+        err = self._runner.error_word
+        thr = self.config.exit_threshold
+        prof = bool(self.config.profile)
+        events = []
+        pos_in, slot_in, cnt = None, slots, None
+        for k, layer in enumerate(layers):
+            if prof:
+                torch.cuda.nvtx.range_push(f"tide.checkpoint.layer{layer}")
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record()
+            hidden = hidden_at(layer)
+            if k == 0:
+                x = hidden
+            else:  # the still-active rows of this layer, by position, count on the device
+                ops.gather_rows(hidden, pos_in, cnt, xbuf, err)
+                x = xbuf
+            self._runner.run(x, self._router(layer, dtype), self._norm, thr, positions=pos_in,
+                             slots=slot_in, out_buffer=out_buf, positions_out=pos[k % 2],
+                             slots_out=slot_buf[k % 2], exit_positions_out=exit_pos[k],
+                             n_rows_dev=cnt, counts=counts[k])
+            if prof:
+                ev[1].record()
+                torch.cuda.nvtx.range_pop()
+                events.append((f"checkpoint.layer{layer}", ev))
+            pos_in, slot_in, cnt = pos[k % 2], slot_buf[k % 2], counts[k, :1]
+        if prof:
+            torch.cuda.nvtx.range_push("tide.finalize")
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        if pos_in is None:
+            pos_in = torch.arange(N, dtype=torch.int64, device=dev)
+        n = self._norm
+        ops.norm_at_positions(final, pos_in, cnt, out_buf, n.weight, n.bias, n.kind, n.eps, err)
+        if prof:
+            ev[1].record()
+            torch.cuda.nvtx.range_pop()
+            events.append(("finalize", ev))
+        self._events = events
+        return layers, counts, exit_pos, (pos_in, slot_in)
+
+    def _read_back(self, layers, counts, exit_pos, N: int, shape) -> ExitStats:
+        """The forward's one host synchronisation: the exit counts and the
+        device error word together; then ExitStats (layers with no exit are
+        not recorded, runtime.py:176-180) and the per-token exit layer."""
+        err = self._runner.error_word
+        host = torch.cat([counts.reshape(-1), err]).cpu().tolist()
+        if host[-1]:
+            self._runner.error_word.zero_()
+            raise RuntimeError(f"tide_b200 kernel reported device error bits 0x{host[-1]:x} "
+                               "(1: position out of range, 2: wait timeout, 4: bad row count)")
+        stats = ExitStats(total_tokens=N)
+        exit_layer = torch.full((N,), -1, dtype=torch.int32, device=counts.device)
+        remaining = N
+        for k, layer in enumerate(layers):
+            n_surv, n_exit = host[2 * k], host[2 * k + 1]
+            if n_exit > 0:
+                stats.exits_per_layer[layer] = n_exit
+                exit_layer.index_fill_(0, exit_pos[k][:n_exit], layer)
+            remaining = n_surv
+        stats.remaining_tokens = remaining
+        self.last_exit_layer = exit_layer.view(shape)
+        if self.config.profile:
+            torch.cuda.synchronize()
+            self.last_timings = {name: a.elapsed_time(b) for name, (a, b) in self._events}
+        return stats
+
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
                 logits_to_keep: int = 0, **kwargs) -> torch.Tensor:
         """Post-hoc early exit over the model's hidden states (reference
-        runtime.py:134-192): logits [B, S, V].  `logits_to_keep` > 0 keeps
-        only the last that many positions ([B, logits_to_keep, V]), so lm_head
-        runs on the rows whose logits are used, e.g. 1 before sampling."""
+        runtime.py:134-192): logits [B, S, V].  One host synchronisation per
+        call (the exit counts, after every kernel is queued).  After a call,
+        last_stats holds the ExitStats and last_exit_layer [B, S] the layer
+        each token exited at (-1: ran every layer).  `logits_to_keep` > 0
+        keeps only the last that many positions ([B, logits_to_keep, V]), so
+        lm_head runs on the rows whose logits are used, e.g. 1 before
+        sampling."""
         B, S = input_ids.shape
         out = self._hidden_states(input_ids, attention_mask)
         hs = out.hidden_states
         H = hs[-1].shape[-1]
         dtype = hs[-1].dtype
-        dev = hs[-1].device
         N = B * S
-        out_buf = torch.zeros(N, H, device=dev, dtype=dtype)
-        stats = ExitStats(total_tokens=N)
-        positions = torch.arange(N, device=dev, dtype=torch.int64)
-        spare = torch.empty_like(positions)
-        n_active = N
-        thr = self.config.exit_threshold
-        prof = bool(self.config.profile)
-        events = []
-        for layer in sorted(self.routers):
-            if layer < self.config.min_layers or n_active == 0:
-                continue
-            if prof:
-                torch.cuda.nvtx.range_push(f"tide.checkpoint.layer{layer}")
-                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                ev[0].record()
-            hidden = hs[layer + 1].reshape(N, H)
-            x = hidden if n_active == N else hidden.index_select(0, positions[:n_active])
-            counts = self._runner.run(x.contiguous(), self._router(layer, dtype), self._norm, thr,
-                                      positions=positions[:n_active], out_buffer=out_buf,
-                                      positions_out=spare)
-            if prof:
-                ev[1].record()
-                torch.cuda.nvtx.range_pop()
-                events.append((f"checkpoint.layer{layer}", ev))
-            n_surv, n_exit = (int(v) for v in counts.tolist())
-            if n_exit > 0:
-                stats.exits_per_layer[layer] = n_exit
-            positions, spare = spare, positions
-            n_active = n_surv
-        if n_active > 0:
-            if prof:
-                torch.cuda.nvtx.range_push("tide.finalize")
-                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                ev[0].record()
-            final = hs[-1].reshape(N, H)
-            rows = final if n_active == N else final.index_select(0, positions[:n_active])
-            self._runner.norm_scatter(rows.contiguous(), positions[:n_active], out_buf, self._norm)
-            if prof:
-                ev[1].record()
-                torch.cuda.nvtx.range_pop()
-                events.append(("finalize", ev))
-        stats.remaining_tokens = n_active
-        self._runner.check_errors()
-        self.last_stats = stats
-        if prof:
-            torch.cuda.synchronize()
-            self.last_timings = {name: a.elapsed_time(b) for name, (a, b) in events}
+        out_buf = torch.zeros(N, H, device=hs[-1].device, dtype=dtype)
+        layers, counts, exit_pos, _ = self._checkpoint_chain(
+            lambda L: hs[L + 1].reshape(N, H), N, H, dtype, hs[-1].reshape(N, H), out_buf)
         rows = out_buf.view(B, S, H)
         if logits_to_keep > 0:
             rows = rows[:, -logits_to_keep:, :]
-        return self._lm_head(rows)
+        logits = self._lm_head(rows)
+        self.last_stats = self._read_back(layers, counts, exit_pos, N, (B, S))
+        return logits
 
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 512,
                  temperature: float = 1.0, top_k: int = 50, top_p: float = 0.9,
-                 **kwargs) -> torch.Tensor:
-        """Autoregressive decode with the reference's whole-batch exit rule
-        (runtime.py:223-313): every step runs all layers; the earliest
-        checkpoint at which every row's score passes the threshold supplies
-        the next-token logits via lm_head(final_norm(h)).  Generation stops
-        when every sampled token equals `eos_token_id` (default 2, the
-        reference's fixed id, runtime.py:257)."""
+                 per_row_exit: bool = False, **kwargs) -> torch.Tensor:
+        """Autoregressive decode (runtime.py:223-313).  Every step runs all
+        layers (the reference's post-hoc design).  With the reference's rule
+        (default) the earliest checkpoint at which every row's score passes
+        the threshold supplies all rows' next-token logits via
+        lm_head(final_norm(h)).  With per_row_exit=True each row exits on its
+        own: the step's rows go through the same checkpoint chain as a
+        prefill (positions and KV slot ids of the survivors compacted on the
+        device at every checkpoint), and each row's logits come from its own
+        exit layer.  Generation stops when every sampled token equals
+        `eos_token_id` (default 2, the reference's fixed id, runtime.py:257)."""
         eos = kwargs.get("eos_token_id", 2)
         B = input_ids.shape[0]
+        dev = input_ids.device
         n_layers = len(self._layers)
         generated = input_ids.clone()
         gen_stats = ExitStats(total_tokens=0)
         pre = self.model(generated, use_cache=True, return_dict=True)
         past = pre.past_key_values
         next_logits = pre.logits[:, -1, :]
-        positions = torch.arange(B, device=input_ids.device, dtype=torch.int64)
+        slots = torch.arange(B, device=dev, dtype=torch.int32)
         for _ in range(max_new_tokens):
             nxt = sample_next_token(next_logits, temperature, top_k, top_p)
             generated = torch.cat([generated, nxt], dim=-1)
@@ -200,20 +254,30 @@ class TIDERuntime(nn.Module):
                              output_hidden_states=True)
             past = out.past_key_values
             hs = out.hidden_states
-            exit_layer = None
-            exit_hidden = None
+            if per_row_exit:
+                H = hs[-1].shape[-1]
+                out_buf = torch.zeros(B, H, device=dev, dtype=hs[-1].dtype)
+                layers, counts, exit_pos, _ = self._checkpoint_chain(
+                    lambda L: hs[L + 1][:, -1, :].contiguous(), B, H, hs[-1].dtype,
+                    hs[-1][:, -1, :].contiguous(), out_buf, slots=slots)
+                next_logits = self._lm_head(out_buf)
+                st = self._read_back(layers, counts, exit_pos, B, (B,))
+                for layer, c in st.exits_per_layer.items():
+                    gen_stats.exits_per_layer[layer] = gen_stats.exits_per_layer.get(layer, 0) + c
+                gen_stats.remaining_tokens += st.remaining_tokens
+                continue
+            exit_layer, exit_hidden = None, None
             for layer in sorted(self.routers):
                 if layer < self.config.min_layers:
                     continue
-                h = hs[layer + 1][:, -1, :].contiguous()
-                counts = self._runner.run(h, self._router(layer, h.dtype), self._norm,
-                                          self.config.exit_threshold)
-                if int(counts[1].item()) == B:  # every row exits: (scores > thr).all()
-                    exit_layer, exit_hidden = layer, h
+                h = hs[layer + 1][:, -1, :]
+                if bool((self._score_router(h, layer) > self.config.exit_threshold).all()):
+                    exit_layer, exit_hidden = layer, h.contiguous()
                     break
             if exit_layer is not None:
                 normed = torch.empty_like(exit_hidden)
-                self._runner.norm_scatter(exit_hidden, positions, normed, self._norm)
+                self._runner.norm_scatter(exit_hidden, torch.arange(B, device=dev), normed,
+                                          self._norm)
                 next_logits = self._lm_head(normed)
                 gen_stats.exits_per_layer[exit_layer] = gen_stats.exits_per_layer.get(exit_layer, 0) + B
             else:
