@@ -628,13 +628,21 @@ def engine_prefill(world: int, rank: int, reps: int = 10, warmup: int = 3) -> di
 
         t_engine = timed(lambda: engine(ids))
         stats = tdist.global_stats(world, engine.last_stats)
+        t_live = timed(lambda: engine(ids, live=True))
+        live_stats = tdist.global_stats(world, engine.last_stats)
         t_hf = timed(lambda: model(ids).logits)
     tokens = B_all * S * reps
     res.update({"engine_tok_s": tokens / t_engine, "engine_ms_per_call": 1000 * t_engine / reps,
                 "hf_forward_tok_s": tokens / t_hf, "hf_forward_ms_per_call": 1000 * t_hf / reps,
                 "engine_mode": "post-hoc (every layer runs; the reference's semantics)",
                 "exit_rate": stats.exit_rate,
-                "exits_per_layer": {str(k): v for k, v in sorted(stats.exits_per_layer.items())}})
+                "exits_per_layer": {str(k): v for k, v in sorted(stats.exits_per_layer.items())},
+                "live_tok_s": tokens / t_live, "live_ms_per_call": 1000 * t_live / reps,
+                "live_mode": "layers after each checkpoint on the active tokens only; exited "
+                             "tokens' K/V zero-padded",
+                "live_exit_rate": live_stats.exit_rate,
+                "live_exits_per_layer": {str(k): v for k, v in
+                                         sorted(live_stats.exits_per_layer.items())}})
     del engine, model
     torch.cuda.empty_cache()
     return res

@@ -1,6 +1,10 @@
 """TIDEConfig: the reference's configuration dataclass (python/TIDE/config.py:
-9-33), same fields, defaults and YAML layout.  The hot path reads
-exit_threshold and min_layers."""
+9-33), same fields, defaults and YAML layout, plus one field of its own:
+live_compaction (default off, the reference's post-hoc forward) runs the
+layers after each checkpoint on the still-active tokens only
+(tide_b200/live.py), with exited tokens' K/V handled as kv_cache_strategy
+says ("zero_pad", the reference's default and the one implemented).  The hot
+path reads exit_threshold, min_layers, live_compaction and profile."""
 from __future__ import annotations
 
 from dataclasses import asdict, dataclass
@@ -22,6 +26,7 @@ class TIDEConfig:
     convergence_threshold: float = 0.98
     kv_cache_strategy: str = "zero_pad"
     profile: bool = False
+    live_compaction: bool = False
 
     def save(self, path: str | Path) -> None:
         path = Path(path)

@@ -1,0 +1,204 @@
+"""Live early exit: after each checkpoint the later layers run only on the
+tokens that are still active.
+
+The reference evaluates its routers post hoc: every layer runs on every
+token and the exit buffer is assembled afterwards (python/TIDE/runtime.py:
+151-188).  Its scheduler (python/TIDE/scheduler.py:39-120) and config
+(`compaction_threshold`, `kv_cache_strategy`, python/TIDE/config.py:14-20)
+describe the live variant without running it.  Here it runs: at each router
+layer the checkpoint kernel scores the active rows, writes the exiting ones
+final-normed to the output buffer and compacts the survivors (rows and
+positions) into the dense buffer that the next layer takes as its input.
+
+Exited tokens stay visible to the attention of later layers through the
+reference's declared K/V policy, "zero_pad" (python/TIDE/runtime.py:194-221):
+from the layer after its exit on, a token's key and value are zeros (not
+masked).  Attention itself runs over the whole [batch, seq] layout (zeros
+in the exited rows), so its cost does not shrink; the projections and the
+MLP, which dominate a layer, run on the active rows only.
+
+Supported layer families: Llama-style decoder layers (q/k/v/o projections,
+optional per-head q/k RMSNorm as in Qwen3, rotary embeddings, gated MLP) and
+GPT-2 blocks.  Inputs without padding only.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+def _attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos: Optional[torch.Tensor],
+            B: int, S: int, scale: float) -> torch.Tensor:
+    """Causal attention of the active rows q/k/v [n, heads, d] (token index
+    b * S + s in `pos`; None = all B * S tokens in order) over the whole
+    [B, S] layout, exited tokens' keys and values being zeros.  Returns
+    [n, heads_q * d]."""
+    n, nh, d = q.shape
+    nkv = k.shape[1]
+    if pos is not None:
+        qf = q.new_zeros(B * S, nh, d)
+        kf = k.new_zeros(B * S, nkv, d)
+        vf = v.new_zeros(B * S, nkv, d)
+        qf.index_copy_(0, pos, q)
+        kf.index_copy_(0, pos, k)
+        vf.index_copy_(0, pos, v)
+        q, k, v = qf, kf, vf
+    o = F.scaled_dot_product_attention(q.view(B, S, nh, d).transpose(1, 2),
+                                       k.view(B, S, nkv, d).transpose(1, 2),
+                                       v.view(B, S, nkv, d).transpose(1, 2),
+                                       is_causal=True, scale=scale, enable_gqa=nh != nkv)
+    o = o.transpose(1, 2).reshape(B * S, nh * d)
+    return o if pos is None else o.index_select(0, pos)
+
+
+class _LlamaFamily:
+    """Llama / Qwen3 / Mistral-style decoder layers (HF modules' weights)."""
+
+    def __init__(self, model: nn.Module):
+        inner = model.model
+        self.embed = inner.embed_tokens
+        self.rotary = inner.rotary_emb
+        self.layers = inner.layers
+        self.norm = inner.norm
+        cfg = model.config
+        if getattr(cfg, "sliding_window", None) and getattr(cfg, "use_sliding_window", True) \
+                and "mistral" in type(model).__name__.lower():
+            raise NotImplementedError("sliding-window attention is not supported in live mode")
+
+    def embed_tokens(self, ids: torch.Tensor) -> torch.Tensor:
+        return self.embed(ids).reshape(ids.numel(), -1)
+
+    def layer(self, i: int, h: torch.Tensor, pos: Optional[torch.Tensor], seq_pos: torch.Tensor,
+              B: int, S: int) -> torch.Tensor:
+        layer = self.layers[i]
+        attn = layer.self_attn
+        d = attn.head_dim
+        n = h.shape[0]
+        x = layer.input_layernorm(h)
+        q = attn.q_proj(x).view(n, -1, d)
+        k = attn.k_proj(x).view(n, -1, d)
+        v = attn.v_proj(x).view(n, -1, d)
+        if getattr(attn, "q_norm", None) is not None:
+            q = attn.q_norm(q)
+            k = attn.k_norm(k)
+        cos, sin = self.rotary(v, seq_pos.view(1, -1))
+        cos, sin = cos[0].unsqueeze(1), sin[0].unsqueeze(1)
+        q = q * cos + _rotate_half(q) * sin
+        k = k * cos + _rotate_half(k) * sin
+        o = _attend(q, k, v, pos, B, S, float(attn.scaling))
+        h = h + attn.o_proj(o)
+        return h + layer.mlp(layer.post_attention_layernorm(h))
+
+
+class _GPT2Family:
+    """GPT-2 blocks (fused c_attn, learned absolute positions)."""
+
+    def __init__(self, model: nn.Module):
+        tr = model.transformer
+        self.wte, self.wpe = tr.wte, tr.wpe
+        self.layers = tr.h
+        self.norm = tr.ln_f
+
+    def embed_tokens(self, ids: torch.Tensor) -> torch.Tensor:
+        B, S = ids.shape
+        p = torch.arange(S, device=ids.device)
+        return (self.wte(ids) + self.wpe(p)[None]).reshape(B * S, -1)
+
+    def layer(self, i: int, h: torch.Tensor, pos: Optional[torch.Tensor], seq_pos: torch.Tensor,
+              B: int, S: int) -> torch.Tensor:
+        blk = self.layers[i]
+        attn = blk.attn
+        n, H = h.shape
+        nh = attn.num_heads
+        d = H // nh
+        q, k, v = attn.c_attn(blk.ln_1(h)).split(H, dim=1)
+        scale = (d ** -0.5) if attn.scale_attn_weights else 1.0
+        if getattr(attn, "scale_attn_by_inverse_layer_idx", False):
+            scale /= float(i + 1)
+        o = _attend(q.view(n, nh, d), k.view(n, nh, d), v.view(n, nh, d), pos, B, S, scale)
+        h = h + attn.c_proj(o)
+        return h + blk.mlp(blk.ln_2(h))
+
+
+def family_of(model: nn.Module):
+    """The live executor for a model's layer family, or NotImplementedError."""
+    inner = getattr(model, "model", None)
+    layers = getattr(inner, "layers", None)
+    if layers is not None and len(layers) and hasattr(layers[0], "self_attn") \
+            and hasattr(layers[0].self_attn, "q_proj") and hasattr(inner, "rotary_emb"):
+        return _LlamaFamily(model)
+    tr = getattr(model, "transformer", None)
+    if tr is not None and hasattr(tr, "h") and len(tr.h) and hasattr(tr.h[0].attn, "c_attn"):
+        return _GPT2Family(model)
+    raise NotImplementedError(f"live early exit does not know the layers of {type(model).__name__}")
+
+
+@torch.no_grad()
+def live_forward(runtime, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor],
+                 on_checkpoint: Optional[Callable[[int, int], None]] = None):
+    """The live forward of TIDERuntime (see the module docstring): returns
+    (out_buf [B*S, H] of final-normed rows at their token positions,
+    ExitStats, exit_layer [B*S] int32).  One host read-back of the survivor
+    count per checkpoint (the next layers' shapes depend on it)."""
+    from tide_b200.scheduler import ExitStats
+
+    if attention_mask is not None and not bool(attention_mask.bool().all()):
+        raise NotImplementedError("live early exit takes inputs without padding")
+    fam = runtime._live_family()
+    B, S = input_ids.shape
+    N = B * S
+    dev = input_ids.device
+    h = fam.embed_tokens(input_ids)
+    H = h.shape[1]
+    dtype = h.dtype
+    seq_all = torch.arange(S, device=dev).repeat(B)
+    out_buf = torch.zeros(N, H, dtype=dtype, device=dev)
+    exit_layer = torch.full((N,), -1, dtype=torch.int32, device=dev)
+    stats = ExitStats(total_tokens=N)
+    routers = {L for L in runtime.routers if L >= runtime.config.min_layers}
+    thr = runtime.config.exit_threshold
+    pos = None  # all tokens, in order
+    pos_out = [torch.empty(N, dtype=torch.int64, device=dev) for _ in range(2)]
+    exit_pos = torch.empty(N, dtype=torch.int64, device=dev)
+    counts = torch.zeros(2, dtype=torch.int32, device=dev)
+    n_ck = 0
+    for i in range(len(fam.layers)):
+        seq_pos = seq_all if pos is None else pos % S
+        h = fam.layer(i, h, pos, seq_pos, B, S)
+        if i not in routers:
+            continue
+        nxt = pos_out[n_ck % 2]
+        comp = torch.empty_like(h)
+        runtime._runner.run(h, runtime._router(i, dtype), runtime._norm, thr, positions=pos,
+                            out_buffer=out_buf, compact_out=comp, positions_out=nxt,
+                            exit_positions_out=exit_pos, counts=counts)
+        n_surv, n_exit = (int(v) for v in counts.tolist())
+        n_ck += 1
+        if n_exit:
+            stats.exits_per_layer[i] = n_exit
+            exit_layer.index_fill_(0, exit_pos[:n_exit], i)
+        if on_checkpoint is not None:
+            on_checkpoint(i, n_surv)
+        pos = nxt[:n_surv]
+        h = comp[:n_surv]  # the survivors, compacted by the kernel: the next layer's input
+        if n_surv == 0:
+            break
+    n_rem = h.shape[0]
+    stats.remaining_tokens = n_rem
+    if n_rem:
+        # as the post-hoc path: the model's last hidden state (its final norm
+        # applied, as HF reports it), final-normed once more
+        last = fam.norm(h).contiguous()
+        if pos is None:
+            pos = torch.arange(N, device=dev)
+        runtime._runner.norm_scatter(last, pos, out_buf, runtime._norm)
+    runtime._runner.check_errors()
+    return out_buf, stats, exit_layer

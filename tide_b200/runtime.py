@@ -68,6 +68,7 @@ class TIDERuntime(nn.Module):
         self.last_stats: Optional[ExitStats] = None
         self.last_exit_layer: Optional[torch.Tensor] = None
         self._events = []
+        self._family = None
         # TIDEConfig.profile (declared by the reference, config.py:21, never
         # read there): NVTX ranges around every checkpoint and the device time
         # of each, in milliseconds, after a forward
@@ -194,17 +195,38 @@ class TIDERuntime(nn.Module):
             self.last_timings = {name: a.elapsed_time(b) for name, (a, b) in self._events}
         return stats
 
+    def _live_family(self):
+        if self._family is None:
+            from tide_b200.live import family_of
+
+            self._family = family_of(self.model)
+        return self._family
+
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
-                logits_to_keep: int = 0, **kwargs) -> torch.Tensor:
-        """Post-hoc early exit over the model's hidden states (reference
-        runtime.py:134-192): logits [B, S, V].  One host synchronisation per
-        call (the exit counts, after every kernel is queued).  After a call,
+                logits_to_keep: int = 0, live: Optional[bool] = None, **kwargs) -> torch.Tensor:
+        """Early-exit forward: logits [B, S, V].  By default the reference's
+        post-hoc exit over the model's hidden states (runtime.py:134-192),
+        with one host synchronisation per call (the exit counts, after every
+        kernel is queued).  With live=True (or config.live_compaction) the
+        layers after each checkpoint run only on the tokens still active
+        (tide_b200/live.py; logits then differ from the post-hoc ones by
+        design, through the exited tokens' zero-padded K/V).  After a call,
         last_stats holds the ExitStats and last_exit_layer [B, S] the layer
         each token exited at (-1: ran every layer).  `logits_to_keep` > 0
         keeps only the last that many positions ([B, logits_to_keep, V]), so
         lm_head runs on the rows whose logits are used, e.g. 1 before
         sampling."""
         B, S = input_ids.shape
+        if live if live is not None else self.config.live_compaction:
+            from tide_b200.live import live_forward
+
+            out_buf, stats, exit_layer = live_forward(self, input_ids, attention_mask)
+            rows = out_buf.view(B, S, -1)
+            if logits_to_keep > 0:
+                rows = rows[:, -logits_to_keep:, :]
+            self.last_stats = stats
+            self.last_exit_layer = exit_layer.view(B, S)
+            return self._lm_head(rows)
         out = self._hidden_states(input_ids, attention_mask)
         hs = out.hidden_states
         H = hs[-1].shape[-1]
