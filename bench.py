@@ -360,7 +360,7 @@ def parity_sample(wl: "Workload", active: list[int], rows: int = 2048) -> dict:
         n = active[k]
         if n == 0:
             continue
-        s = torch.full((n,), -1.0, device="cuda")
+        s = torch.full((wl.x[k].shape[0],), -1.0, device="cuda")  # capacity rows
         wl.checkpoint(k, scores_out=s)
         torch.cuda.synchronize()
         m = min(rows, n)

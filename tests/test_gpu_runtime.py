@@ -99,9 +99,11 @@ def tuned_routers(path, model, ids, layers, fractions, threshold, bottleneck=64,
             r.down.weight.normal_(0, down_std, generator=g)
             r.up.weight.normal_(0, up_std, generator=g)
         h = hs[L + 1].reshape(N, H)
-        z = workloads.prebias_logits_torch(h, kind, fn.weight.float(),
-                                           None if kind == "rms" else fn.bias.float(), eps,
-                                           r.down.weight.to(h.device), r.up.weight.to(h.device)).cpu()
+        with torch.no_grad():
+            z = workloads.prebias_logits_torch(h, kind, fn.weight.float(),
+                                               None if kind == "rms" else fn.bias.float(), eps,
+                                               r.down.weight.to(h.device),
+                                               r.up.weight.to(h.device)).cpu()
         active = (~exited).nonzero()[:, 0]
         bias = workloads.bias_for_exit_fraction(z[active], f, threshold)
         with torch.no_grad():

@@ -6,10 +6,15 @@ squeezed to [N].  The file written by RouterCheckpoint.save is the
 reference's layout (router.py:28-38):
     {"hidden_dim": int, "bottleneck_dim": int,
      "router_layers": {layer_idx: {"down.weight": [B, H], "up.weight": [1, B]}}}
-One optional key is understood on top of it: "up.bias" ([1]) in a layer's
-state dict, a scalar added before the sigmoid.  Files without it (every file
-the reference writes) load unchanged and mean a zero bias.  Layer keys may be
-ints or strings, as in router.py:47.
+Optional keys understood on top of it, in a layer's state dict:
+  "up.bias" ([1]): a scalar added before the sigmoid;
+  "exit_proj.weight" ([H, H]) and "exit_proj.bias" ([H]): the learned exit
+    projection of the reference's declared "Mode B" (csrc/kernels/
+    exit_projection.cu:5-8, TIDEConfig.exit_strategy = "learned"): an exiting
+    token's output row is exit_proj(final_norm(h)) instead of final_norm(h).
+Files without them (every file the reference writes) load unchanged and mean
+a zero bias and no projection.  Layer keys may be ints or strings, as in
+router.py:47.
 """
 from __future__ import annotations
 
@@ -22,11 +27,13 @@ import torch.nn as nn
 
 
 class TokenRouter(nn.Module):
-    def __init__(self, hidden_dim: int, bottleneck_dim: int = 128, up_bias: bool = False):
+    def __init__(self, hidden_dim: int, bottleneck_dim: int = 128, up_bias: bool = False,
+                 exit_proj: bool = False, exit_proj_bias: bool = False):
         super().__init__()
         self.down = nn.Linear(hidden_dim, bottleneck_dim, bias=False)
         self.up = nn.Linear(bottleneck_dim, 1, bias=up_bias)
         self.act = nn.SiLU()
+        self.exit_proj = nn.Linear(hidden_dim, hidden_dim, bias=exit_proj_bias) if exit_proj else None
 
     def forward(self, hidden_state: torch.Tensor) -> torch.Tensor:
         return torch.sigmoid(self.up(self.act(self.down(hidden_state)))).squeeze(-1)
@@ -55,7 +62,8 @@ class RouterCheckpoint:
         h, b = int(state["hidden_dim"]), int(state["bottleneck_dim"])
         routers: Dict[int, TokenRouter] = {}
         for key, sd in state["router_layers"].items():
-            r = TokenRouter(h, b, up_bias="up.bias" in sd)
+            r = TokenRouter(h, b, up_bias="up.bias" in sd, exit_proj="exit_proj.weight" in sd,
+                            exit_proj_bias="exit_proj.bias" in sd)
             r.load_state_dict(sd)
             routers[int(key)] = r.to(device)
         return cls(routers=routers, hidden_dim=h, bottleneck_dim=b)

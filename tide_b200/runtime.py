@@ -69,6 +69,8 @@ class TIDERuntime(nn.Module):
         self.last_exit_layer: Optional[torch.Tensor] = None
         self._events = []
         self._family = None
+        self._host_counts: list = []
+        self._learned_exits()  # reject an unknown exit_strategy now
         # TIDEConfig.profile (declared by the reference, config.py:21, never
         # read there): NVTX ranges around every checkpoint and the device time
         # of each, in milliseconds, after a forward
@@ -193,7 +195,37 @@ class TIDERuntime(nn.Module):
         if self.config.profile:
             torch.cuda.synchronize()
             self.last_timings = {name: a.elapsed_time(b) for name, (a, b) in self._events}
+        self._host_counts = host
         return stats
+
+    def _learned_exits(self) -> bool:
+        """TIDEConfig.exit_strategy: "identity" (the reference's Mode A: an
+        exiting row is final_norm(h)) or "learned" (its declared Mode B,
+        csrc/kernels/exit_projection.cu:5-8: exit_proj(final_norm(h)) with
+        the router file's per-layer exit_proj weights)."""
+        strategy = self.config.exit_strategy
+        if strategy not in ("identity", "learned"):
+            raise ValueError(f"exit_strategy {strategy!r}: expected 'identity' or 'learned'")
+        return strategy == "learned"
+
+    def _project_exits(self, out_buf: torch.Tensor, layer: int, positions: torch.Tensor) -> None:
+        """Mode B for the rows that exited at `layer` (their positions in
+        out_buf, already final-normed there): gathered by the gather kernel,
+        projected by one GEMM, written back in place."""
+        r = self.routers[layer]
+        if r.exit_proj is None or positions.numel() == 0:
+            return
+        key = ("proj", layer, out_buf.dtype)
+        if key not in self._prepared:
+            w = r.exit_proj.weight.detach().to(out_buf.device, out_buf.dtype).contiguous()
+            b = (r.exit_proj.bias.detach().to(out_buf.device, out_buf.dtype)
+                 if r.exit_proj.bias is not None else None)
+            self._prepared[key] = (w, b)
+        w, b = self._prepared[key]
+        rows = torch.empty(positions.numel(), out_buf.shape[1], dtype=out_buf.dtype,
+                           device=out_buf.device)
+        _native.ops().gather_rows(out_buf, positions, None, rows, self._runner.error_word)
+        out_buf.index_copy_(0, positions, torch.nn.functional.linear(rows, w, b))
 
     def _live_family(self):
         if self._family is None:
@@ -221,6 +253,9 @@ class TIDERuntime(nn.Module):
             from tide_b200.live import live_forward
 
             out_buf, stats, exit_layer = live_forward(self, input_ids, attention_mask)
+            if self._learned_exits():
+                for layer in stats.exits_per_layer:
+                    self._project_exits(out_buf, layer, (exit_layer == layer).nonzero()[:, 0])
             rows = out_buf.view(B, S, -1)
             if logits_to_keep > 0:
                 rows = rows[:, -logits_to_keep:, :]
@@ -238,9 +273,14 @@ class TIDERuntime(nn.Module):
         rows = out_buf.view(B, S, H)
         if logits_to_keep > 0:
             rows = rows[:, -logits_to_keep:, :]
-        logits = self._lm_head(rows)
+        if not self._learned_exits():
+            logits = self._lm_head(rows)  # queued before the read-back
+            self.last_stats = self._read_back(layers, counts, exit_pos, N, (B, S))
+            return logits
         self.last_stats = self._read_back(layers, counts, exit_pos, N, (B, S))
-        return logits
+        for k, layer in enumerate(layers):
+            self._project_exits(out_buf, layer, exit_pos[k][: self._host_counts[2 * k + 1]])
+        return self._lm_head(rows)
 
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 512,
@@ -282,8 +322,12 @@ class TIDERuntime(nn.Module):
                 layers, counts, exit_pos, _ = self._checkpoint_chain(
                     lambda L: hs[L + 1][:, -1, :].contiguous(), B, H, hs[-1].dtype,
                     hs[-1][:, -1, :].contiguous(), out_buf, slots=slots)
-                next_logits = self._lm_head(out_buf)
                 st = self._read_back(layers, counts, exit_pos, B, (B,))
+                if self._learned_exits():
+                    for k, layer in enumerate(layers):
+                        self._project_exits(out_buf, layer,
+                                            exit_pos[k][: self._host_counts[2 * k + 1]])
+                next_logits = self._lm_head(out_buf)
                 for layer, c in st.exits_per_layer.items():
                     gen_stats.exits_per_layer[layer] = gen_stats.exits_per_layer.get(layer, 0) + c
                 gen_stats.remaining_tokens += st.remaining_tokens
@@ -298,8 +342,10 @@ class TIDERuntime(nn.Module):
                     break
             if exit_layer is not None:
                 normed = torch.empty_like(exit_hidden)
-                self._runner.norm_scatter(exit_hidden, torch.arange(B, device=dev), normed,
-                                          self._norm)
+                every = torch.arange(B, device=dev)
+                self._runner.norm_scatter(exit_hidden, every, normed, self._norm)
+                if self._learned_exits():
+                    self._project_exits(normed, exit_layer, every)
                 next_logits = self._lm_head(normed)
                 gen_stats.exits_per_layer[exit_layer] = gen_stats.exits_per_layer.get(exit_layer, 0) + B
             else:
