@@ -502,3 +502,50 @@ def test_torch_op_router_refolds_after_update_and_falls_back():
     s2 = ops.fused_layernorm_route(x, torch.randn(H, generator=g).to(DEV), big, ub, 1e-6)
     assert ops.last_route_path() == capi.PATH_SIMT
     assert torch.isfinite(s2).all()
+
+
+def test_learned_exit_projection(tmp_path):
+    """exit_strategy 'learned' (the reference's declared Mode B): an exiting
+    row is exit_proj(final_norm(h)), the projection taken from the router
+    file; rows that never exit keep final_norm(h).  Against the oracle's
+    post-hoc loop with the projection applied to its exit rows (normed rows
+    rounded to the model dtype, weights in the model dtype, fp32 sums)."""
+    model = llama()
+    ids = torch.randint(0, 512, (2, 40), generator=torch.Generator().manual_seed(12)).to(DEV)
+    routers = tuned_routers(tmp_path / "r0.pt", model, ids, [1, 2], [0.3, 0.3], 0.7)
+    g = torch.Generator().manual_seed(13)
+    for r in routers.values():
+        r.exit_proj = torch.nn.Linear(256, 256, bias=True)
+        with torch.no_grad():
+            r.exit_proj.weight.normal_(0, 0.06, generator=g)
+            r.exit_proj.bias.normal_(0, 0.1, generator=g)
+    RouterCheckpoint(routers, 256, 64).save(tmp_path / "router.pt")
+    rt = TIDERuntime(model, tmp_path / "router.pt",
+                     config=TIDEConfig(exit_threshold=0.7, min_layers=0, exit_strategy="learned"))
+    with torch.no_grad():
+        logits = rt(ids)
+        out = model(ids, output_hidden_states=True, return_dict=True)
+    hs = [storage_np(h.reshape(-1, h.shape[-1])) for h in out.hidden_states]
+    norm = norm_of(rt._final_norm, "rms")
+    r_np = {L: {"down": r.down.weight.detach().numpy(), "up": r.up.weight.detach().numpy(),
+                "up_bias": float(r.up.bias.detach())} for L, r in routers.items()}
+    buf, _, _, det = O.forward_posthoc(hs, O.BF16, norm, r_np, 0.7, 0, detail=True)
+    for L, r in routers.items():
+        sel = det["exit_layer"] == L
+        w = O.to_f32(O.from_f32(r.exit_proj.weight.detach().numpy(), O.BF16), O.BF16)
+        b = O.to_f32(O.from_f32(r.exit_proj.bias.detach().numpy(), O.BF16), O.BF16)
+        buf[sel] = O.from_f32(O.to_f32(buf[sel], O.BF16) @ w.T + b, O.BF16)
+    ref = rt._lm_head(torch.from_numpy(buf.view(np.int16)).view(torch.bfloat16).to(DEV).view(2, 40, -1))
+    ours = rt.last_exit_layer.reshape(-1).cpu().numpy()
+    assert (ours >= 0).sum() > 0
+    same = torch.from_numpy(ours == det["exit_layer"]).to(DEV).view(2, 40)
+    assert int(same.sum()) >= 78
+    torch.testing.assert_close(logits[same].float(), ref[same].float(), atol=5e-2, rtol=5e-2)
+    # identity (Mode A) differs exactly on the exit rows
+    rt_a = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.7,
+                                                                         min_layers=0))
+    with torch.no_grad():
+        plain = rt_a(ids)
+    exited = torch.from_numpy(ours >= 0).to(DEV).view(2, 40)
+    assert torch.equal(plain[~exited], logits[~exited])
+    assert not torch.allclose(plain[exited].float(), logits[exited].float(), atol=1e-2)
