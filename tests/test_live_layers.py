@@ -53,7 +53,7 @@ def hf_layer(model, fam, i, h_full, keep, B, S):
     cache = ZeroPadKV(keep)
     x = h_full.view(B, S, -1)
     if hasattr(model, "model"):
-        pos_ids = torch.arange(S)[None]
+        pos_ids = torch.arange(S, device=x.device)[None]
         pe = model.model.rotary_emb(x, pos_ids)
         out = model.model.layers[i](x, attention_mask=None, position_ids=pos_ids,
                                     past_key_values=cache, use_cache=False, position_embeddings=pe)
