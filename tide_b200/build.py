@@ -38,7 +38,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-O3",
                      "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{CSRC}"]
 
-CU_SOURCES = ["capi.cu", "tc_checkpoint.cu", "tc_fused.cu", "move_bulk.cu", "noalloc.cu"]
+CU_SOURCES = ["capi.cu", "tc_checkpoint.cu", "tc_route_pair.cu", "tc_fused.cu", "move_bulk.cu",
+              "noalloc.cu"]
 HEADERS = ["common.cuh", "move_bulk.cuh", "simt_kernels.cuh", "tc_checkpoint.cuh", "tc_ptx.cuh"]
 
 

@@ -54,6 +54,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "tc_checkpoint.cuh"
@@ -686,10 +688,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+}  // namespace
+
 // A [rows, cols] row-major matrix of `dtype` (TIDE_DTYPE_*), read in boxes
 // of 128 bytes of a row (64 16-bit or 32 fp32 columns) by box_rows rows.
-bool make_tmap(CUtensorMap *m, const void *base, int dtype, uint64_t rows, uint64_t cols,
-               uint32_t box_rows) {
+bool tc_make_tmap(CUtensorMap *m, const void *base, int dtype, uint64_t rows, uint64_t cols,
+                  uint32_t box_rows) {
   auto enc = encode_fn();
   if (!enc) return false;
   const uint64_t esize = dtype == TIDE_DTYPE_F32 ? 4 : 2;
@@ -704,6 +708,24 @@ bool make_tmap(CUtensorMap *m, const void *base, int dtype, uint64_t rows, uint6
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+namespace {
+
+bool make_tmap(CUtensorMap *m, const void *base, int dtype, uint64_t rows, uint64_t cols,
+               uint32_t box_rows) {
+  return tc_make_tmap(m, base, dtype, rows, cols, box_rows);
+}
+
+// Which router the split path runs for 16-bit rows of router width 128: the
+// paired-CTA kernel (default) or the single-CTA one (TIDE_ROUTER=single).
+bool pair_router_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("TIDE_ROUTER");
+    v = (e && strcmp(e, "single") == 0) ? 0 : 1;
+  }
+  return v == 1;
 }
 
 // 128-unit blocks of W' (the MMA's M), each with a 256-column accumulator;
@@ -749,6 +771,11 @@ size_t tc_workspace_bytes(int64_t) { return 0; }
 int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_stats,
                     void *zero, size_t zero_bytes, cudaStream_t stream, char *err,
                     size_t err_len) {
+  if (pair_router_enabled() && tc_pair_supported(a)) {
+    const int rc = tc_route_pair_launch(a, scores, row_stats, zero, zero_bytes, stream, err, err_len);
+    if (rc != TIDE_ERR_UNSUPPORTED) return rc;
+    err[0] = '\0';  // no CTA pair fits on this device: the single-CTA router runs
+  }
   const int dt = a->dtype;
   const int B = (int)a->bottleneck_dim;
   const int w_rows = B < kTcM ? B : kTcM;

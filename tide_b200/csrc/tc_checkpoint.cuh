@@ -3,9 +3,16 @@
 
 #include <stddef.h>
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace tide {
+
+// Tensor map of a [rows, cols] row-major matrix of a TIDE_DTYPE_*, read in
+// boxes of 128 bytes of a row by box_rows rows, with the 128-byte swizzle.
+bool tc_make_tmap(CUtensorMap *m, const void *base, int dtype, uint64_t rows, uint64_t cols,
+                  uint32_t box_rows);
 
 bool tc_supported(const tide_checkpoint_args *a);
 const char *tc_unsupported_reason(const tide_checkpoint_args *a);
@@ -15,6 +22,12 @@ size_t tc_workspace_bytes(int64_t n_rows);
 // workspace of the mover launched after it.
 int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_stats, void *zero,
                     size_t zero_bytes, cudaStream_t s, char *err, size_t err_len);
+
+// Paired-CTA router (tc_route_pair.cu): 16-bit rows, router width 128.
+// tc_route_launch takes it by default where it applies.
+bool tc_pair_supported(const tide_checkpoint_args *a);
+int tc_route_pair_launch(const tide_checkpoint_args *a, float *scores, float2 *row_stats,
+                         void *zero, size_t zero_bytes, cudaStream_t s, char *err, size_t err_len);
 
 // Single-pass fused cluster kernel (tc_fused.cu).
 bool fused_supported(const tide_checkpoint_args *a);
