@@ -648,6 +648,48 @@ def engine_prefill(world: int, rank: int, reps: int = 10, warmup: int = 3) -> di
     return res
 
 
+def decode_checkpoints(world: int, rank: int, steps: int = 200) -> dict:
+    """The decode-size regime next to the prefill one: one step of the
+    qwen3_8b_decode_checkpoints workload (256 rows of H 4096 bf16 through
+    eight checkpoints at layers 3..31, ~10 % of the active rows exiting at
+    each, positions and KV slot ids compacted on the device), as a CUDA graph
+    replayed `steps` times; rows routed per second, summed over ranks."""
+    saved = {k: globals()[k] for k in ("WORKLOAD", "LAYERS", "EXIT_FRACTIONS", "EXITS_OF", "ROWS",
+                                       "HIDDEN", "DTYPE")}
+    try:
+        configure("qwen3_8b_decode_checkpoints")
+        from tide_b200.capi import PATH_AUTO
+
+        wl = Workload(rank, PATH_AUTO)
+        for _ in range(3):
+            wl.step()
+        torch.cuda.synchronize()
+        counts = wl.counts.cpu()
+        rows = int(counts.sum().item())
+        g = wl.capture()[0]
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        t = max_over_ranks(world, a.elapsed_time(b) / 1000.0)
+        wl.runner.check_errors()
+        res = {"workload": WORKLOAD, "rows_per_gpu": ROWS, "checkpoint_layers": LAYERS,
+               "rows_routed_per_step": rows, "exits": counts[:, 1].tolist(), "steps": steps,
+               "us_per_step": 1e6 * t / steps, "rows_per_s": world * rows * steps / t,
+               "paths": [PATH_NAMES.get(v, v) for v in wl.paths.values()],
+               "gpu_launches_per_step": sum(launches_per_checkpoint(v) for v in wl.paths.values())}
+        del g, wl
+        return res
+    finally:
+        globals().update(saved)
+
+
 def run_sweep(args, world, rank, local) -> None:
     """--workload bandwidth_sweep: one checkpoint per (N, H, f), N split evenly
     over the ranks; aggregate algorithmic GB/s (max device time over ranks)
@@ -931,14 +973,16 @@ def run_checkpoints(args, world, rank, local) -> None:
 
     paths_used = [PATH_NAMES.get(wl.paths[k], wl.paths[k]) for k in range(len(LAYERS))]
     n_launch = sum(launches_per_checkpoint(p) for p in wl.paths.values()) * args.steps
-    engine = None
-    if WORKLOAD == "llama8b_prefill_checkpoints" and not args.no_engine and args.rows is None:
+    engine = decode = None
+    if WORKLOAD == "llama8b_prefill_checkpoints" and args.rows is None:
         del wl
         torch.cuda.empty_cache()
-        try:
-            engine = engine_prefill(world, rank)
-        except Exception as exc:  # reported, not fatal: the checkpoint numbers stand
-            engine = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+        decode = decode_checkpoints(world, rank)
+        if not args.no_engine:
+            try:
+                engine = engine_prefill(world, rank)
+            except Exception as exc:  # reported, not fatal: the checkpoint numbers stand
+                engine = {"error": f"{type(exc).__name__}: {exc}"[:400]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -964,6 +1008,7 @@ def run_checkpoints(args, world, rank, local) -> None:
             "gpu_launches": n_launch, "clocks": clocks.summary(),
             "collectives_timed_separately": collectives,
             "prefill_engine": engine,
+            "decode_checkpoints": decode,
         }
         print(json.dumps(line), flush=True)
 

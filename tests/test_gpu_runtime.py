@@ -26,6 +26,16 @@ def llama(dtype=torch.bfloat16, layers=4, hidden=256):
     return LlamaForCausalLM(cfg).to(DEV, dtype).eval()
 
 
+def qwen3(dtype=torch.bfloat16, layers=4, hidden=256):
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    cfg = Qwen3Config(vocab_size=512, hidden_size=hidden, intermediate_size=2 * hidden,
+                      num_hidden_layers=layers, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=hidden // 4, rms_norm_eps=1e-6, max_position_embeddings=256)
+    torch.manual_seed(0)
+    return Qwen3ForCausalLM(cfg).to(DEV, dtype).eval()
+
+
 def gpt2(dtype=torch.float16, layers=4, hidden=256):
     from transformers import GPT2Config, GPT2LMHeadModel
 
@@ -356,13 +366,15 @@ def _oracle_generate(model, rt, ids, routers, threshold, steps, per_row):
     return gen, exits
 
 
-@pytest.mark.parametrize("per_row", [False, True])
-def test_generate_greedy_matches_oracle(tmp_path, per_row):
+@pytest.mark.parametrize("family,per_row", [("llama", False), ("llama", True), ("qwen3", True)])
+def test_generate_greedy_matches_oracle(tmp_path, family, per_row):
     """Greedy decode (temperature 0) of an fp32 model against the oracle's
     decode: the same tokens and the same exit counts.  Whole-batch rule:
-    routers that every row passes at layer 1 on most steps.  Per-row rule:
-    routers that split the rows between layers 1, 2 and no exit."""
-    model = llama(dtype=torch.float32)
+    routers that every row passes at layer 1 on most steps.  Per-row rule
+    (Llama, and the Qwen3 architecture with its QK-norm): routers that split
+    the rows between layers 1, 2 and no exit, positions and KV slot ids
+    compacted on the device at every checkpoint of every step."""
+    model = (llama if family == "llama" else qwen3)(dtype=torch.float32)
     ids = torch.randint(0, 512, (4, 6), generator=torch.Generator().manual_seed(8)).to(DEV)
     if per_row:
         routers = tuned_routers(tmp_path / "router.pt", model, ids, [1, 2], [0.4, 0.4], 0.6)
