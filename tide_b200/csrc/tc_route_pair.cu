@@ -26,19 +26,24 @@
 //   warps 0, 2  TMA producers: per stage KC K chunks, warp 0 arms the stage
 //               and loads this CTA's half of W' [64 units x 64 cols], warp 2
 //               the x rows [rows x 64 cols] (boxes of 128, 64, 32 rows);
-//   warp 1      CTA 0: TMEM (cta_group::2) and the MMAs of the pair;
-//               CTA 1: TMEM, and relays "this CTA's stage landed" to CTA 0;
+//   warp 1      TMEM (cta_group::2, both CTAs); in CTA 0 the pair's MMAs;
 //   warps 4-11  row statistics from the x chunks (one row per thread);
 //   warps 8-15  epilogue: warp 8 + 4m + q reads TMEM lanes 32q..32q+31 of
 //               M block m (rows 128m + 32q + lane), all 128 units.
-// Barriers: a stage's `full` barrier in CTA 0 completes when CTA 0's own
-// bytes have landed and CTA 1 has relayed that its bytes have; each CTA's
-// `empty` barrier takes the MMA completion (one commit multicast to both
-// CTAs) and its eight statistics warps; the accumulator's `acc_full` is a
-// multicast commit as well, and CTA 0's `acc_empty` counts the epilogue
+// Barriers: both CTAs' copies of a stage complete on CTA 0's `full` barrier
+// (CTA 1 issues its copies with the cta_group::2 form, naming CTA 0's
+// barrier), which CTA 0 arms for the pair's bytes; the MMA issuer waits on
+// it alone.  One commit per stage, multicast to both CTAs' `mdone`, says
+// the MMAs have read the stage.  The statistics warps read a stage after
+// `full` (CTA 0) or after `mdone` (CTA 1, which cannot see CTA 0's barrier)
+// and arrive on their CTA's `empty`; a producer refills a stage once its
+// CTA's `mdone` and `empty` have completed.  The accumulator's `acc_full` is
+// a multicast commit as well, and CTA 0's `acc_empty` counts the epilogue
 // warps of both CTAs.  Every wait is bounded; on expiry the CTA raises
-// TIDE_DEVERR_TIMEOUT, stops, drains what it issued and meets its peer at
-// the final cluster barrier before TMEM is released.
+// TIDE_DEVERR_TIMEOUT and stops, and the two meet at the final cluster
+// barrier before TMEM is released (a CTA whose peer stopped reaches it only
+// after one of its own waits has run out, long after any copy it issued has
+// landed).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdio.h>
@@ -112,6 +117,16 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
 }
+// 2-D tiled load into this CTA's shared memory whose completion is counted
+// on a barrier of the leading CTA of the pair (a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_to_lead(void *dst, const void *tmap, uint32_t lead_bar,
+                                                    int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(ptx::smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(lead_bar), "r"(c0), "r"(c1)
+      : "memory");
+}
 // Release-arrive on a barrier of the peer CTA (a shared::cluster address):
 // this thread's earlier accesses happen before the peer's wait returns.
 __device__ __forceinline__ void arrive_remote(uint32_t cluster_addr) {
@@ -166,9 +181,10 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
   const uint32_t rank = ptx::cluster_rank();  // 0: issues the pair's MMAs
   const bool lead = rank == 0;
 
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-  uint64_t *empty = full + kMaxStages;
-  uint64_t *acc_full = empty + kMaxStages;  // [2]
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // CTA 0: both CTAs' copies
+  uint64_t *empty = full + kMaxStages;                  // this CTA's statistics warps
+  uint64_t *mdone = empty + kMaxStages;                 // the pair's MMAs read the stage
+  uint64_t *acc_full = mdone + kMaxStages;  // [2]
   uint64_t *acc_empty = acc_full + 2;       // [2] (CTA 0: both CTAs' epilogues)
   uint64_t *stat_full = acc_empty + 2;      // [2]
   uint64_t *stat_empty = stat_full + 2;     // [2]
@@ -181,16 +197,16 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
   float *s_cs = s_up + kN;
   float *s_bp = s_cs + kN;
   float *s_stat = s_bp + kN;  // [2 slots][256 rows][rstd, mean]
-  static_assert((2 * kMaxStages + 9) * 8 + 16 + 3 * kN * 4 + 2 * 256 * 2 * 4 <= kAux,
+  static_assert((3 * kMaxStages + 9) * 8 + 16 + 3 * kN * 4 + 2 * 256 * 2 * 4 <= kAux,
                 "auxiliary shared-memory area");
   uint8_t *ring = smem + kAux;
   const int k_chunks = p.H / kK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMaxStages; ++s) {
-      // CTA 0: its own arming + CTA 1's relay; CTA 1: its own arming
-      ptx::mbar_init(&full[s], lead ? 2 : 1);
-      ptx::mbar_init(&empty[s], 1 + 8);  // the MMA commit + 8 statistics warps
+      ptx::mbar_init(&full[s], 1);   // CTA 0's arming (for the pair's bytes)
+      ptx::mbar_init(&empty[s], 8);  // 8 statistics warps
+      ptx::mbar_init(&mdone[s], 1);  // one commit of the pair's MMAs
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&acc_full[a], 1);
@@ -255,9 +271,12 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
     // ------------------------------------------------ TMA producers
     if (lane == 0) {
       const bool arm = warp == 0;
+      const uint32_t lead_full0 = ptx::map_to_rank(ptx::smem_u32(&full[0]), 0);
       uint32_t it = 0;
       for (int64_t pu0 = pu_begin; pu0 < pu_end && !*abort_flag; pu0 += kPairUnits) {
         const PairTile tl = pair_tile(pu0, pu_end, rank);
+        const PairTile t0 = pair_tile(pu0, pu_end, 0), t1 = pair_tile(pu0, pu_end, 1);
+        const uint32_t pair_bytes = (uint32_t)KC * ((uint32_t)(t0.nu + t1.nu) * kUnit * 128 + 2 * w_bytes);
         const int nu = tl.nu;
         const int n_big = nu / (128 / kUnit);
         const bool mid = (nu % (128 / kUnit)) >= 64 / kUnit;
@@ -265,31 +284,33 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
         const int u_small = u_mid + (mid ? 64 / kUnit : 0);
         for (int ks = 0; ks < k_stages; ++ks, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
-          if (it >= (uint32_t)S && !ptx::mbar_wait_cluster(&empty[s], ph ^ 1u, abort_flag)) {
+          if (it >= (uint32_t)S && !(ptx::mbar_wait_cluster(&mdone[s], ph ^ 1u, abort_flag) &&
+                                     ptx::mbar_wait(&empty[s], ph ^ 1u, abort_flag))) {
             raise_error(p.err, TIDE_DEVERR_TIMEOUT);
             *abort_flag = 1;
             break;
           }
           uint8_t *st = ring + (size_t)s * stage_bytes;
+          const uint32_t bar = lead_full0 + (uint32_t)s * 8u;  // CTA 0's full[s]
           if (arm) {
-            ptx::mbar_expect_tx(&full[s], (uint32_t)KC * ((uint32_t)nu * kUnit * 128 + w_bytes));
+            if (lead) ptx::mbar_expect_tx(&full[s], pair_bytes);
             for (int c = 0; c < KC; ++c)
-              ptx::tma_load_2d(st + w_off + (size_t)c * w_bytes, &tmap_w, &full[s],
-                               (ks * KC + c) * kK, (int)rank * kHalfN);
+              pair::tma_load_2d_to_lead(st + w_off + (size_t)c * w_bytes, &tmap_w, bar,
+                                        (ks * KC + c) * kK, (int)rank * kHalfN);
             *issued = it + 1;
           } else {
             for (int c = 0; c < KC; ++c) {
               const int col = (ks * KC + c) * kK;
               uint8_t *xc = st + (size_t)c * x_bytes;
               for (int j = 0; j < n_big; ++j)
-                ptx::tma_load_2d(xc + (size_t)j * 128 * 128, &tmap_x_big, &full[s], col,
-                                 (int)((tl.u0 + j * (128 / kUnit)) * kUnit));
+                pair::tma_load_2d_to_lead(xc + (size_t)j * 128 * 128, &tmap_x_big, bar, col,
+                                          (int)((tl.u0 + j * (128 / kUnit)) * kUnit));
               if (mid)
-                ptx::tma_load_2d(xc + (size_t)u_mid * kUnit * 128, &tmap_x_mid, &full[s], col,
-                                 (int)((tl.u0 + u_mid) * kUnit));
+                pair::tma_load_2d_to_lead(xc + (size_t)u_mid * kUnit * 128, &tmap_x_mid, bar, col,
+                                          (int)((tl.u0 + u_mid) * kUnit));
               if (u_small < nu)
-                ptx::tma_load_2d(xc + (size_t)u_small * kUnit * 128, &tmap_x, &full[s], col,
-                                 (int)((tl.u0 + u_small) * kUnit));
+                pair::tma_load_2d_to_lead(xc + (size_t)u_small * kUnit * 128, &tmap_x, bar, col,
+                                          (int)((tl.u0 + u_small) * kUnit));
             }
             *issued_x = it + 1;
           }
@@ -332,7 +353,7 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
               }
             }
           }
-          pair::commit_both(&empty[s]);
+          pair::commit_both(&mdone[s]);
         }
         if (!ok) break;
         pair::commit_both(&acc_full[acc]);
@@ -342,22 +363,6 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
         *abort_flag = 1;
       }
       pair::commit_both(drain);  // every MMA of the pair has finished once it completes
-    } else if (lane == 0) {
-      // ------------------------------- CTA 1: relay its landed stages
-      const uint32_t lead_full0 = ptx::map_to_rank(ptx::smem_u32(&full[0]), 0);
-      uint32_t it = 0;
-      bool ok = true;
-      for (int64_t pu0 = pu_begin; pu0 < pu_end && ok && !*abort_flag; pu0 += kPairUnits) {
-        for (int ks = 0; ks < k_stages; ++ks, ++it) {
-          const uint32_t s = it % S, ph = (it / S) & 1u;
-          if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
-          pair::arrive_remote(lead_full0 + (uint32_t)s * 8u);
-        }
-      }
-      if (!ok) {
-        raise_error(p.err, TIDE_DEVERR_TIMEOUT);
-        *abort_flag = 1;
-      }
     }
   } else if (warp >= 4) {
     // ------------------------------------- row statistics and epilogue
@@ -397,7 +402,13 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
         float ss0 = 0.f, ss1 = 0.f, sx0 = 0.f, sx1 = 0.f;
         for (int ks = 0; ks < k_stages; ++ks, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
-          if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+          // CTA 0 reads a stage once it has landed; CTA 1 once the MMAs
+          // have read it (its copies complete on CTA 0's barrier)
+          if (!(lead ? ptx::mbar_wait_cluster(&full[s], ph, abort_flag)
+                     : ptx::mbar_wait_cluster(&mdone[s], ph, abort_flag))) {
+            ok = false;
+            break;
+          }
           if (live) {
             for (int c = 0; c < KC; ++c) {
               const uint8_t *row = ring + (size_t)s * stage_bytes + (size_t)c * x_bytes + (size_t)t * 128;
@@ -490,14 +501,15 @@ __global__ void __launch_bounds__(pair::kThreads, 1)
   }
 
   __syncthreads();
-  if (threadIdx.x == 0 && *abort_flag) {
-    // drain this CTA's TMA loads still in flight
+  if (threadIdx.x == 0 && *abort_flag && lead) {
+    // drain the pair's TMA loads still in flight (they complete on CTA 0's
+    // barriers; phases CTA 0 never armed give up after the bound)
     const uint32_t n_issued = *issued > *issued_x ? *issued : *issued_x;
     volatile int never = 0;
     for (int s = 0; s < S; ++s) {
       if ((uint32_t)s >= n_issued) break;
       const uint32_t count = (n_issued - (uint32_t)s + (uint32_t)S - 1) / (uint32_t)S;
-      ptx::mbar_wait(&full[s], (count - 1) & 1u, &never);
+      ptx::mbar_wait_cluster(&full[s], (count - 1) & 1u, &never);
     }
   }
   if (threadIdx.x == 32) {
