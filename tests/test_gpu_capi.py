@@ -753,3 +753,22 @@ def test_fused_layernorm_route_reference_op():
                                       dt_.cpu().numpy(), ut.cpu().numpy(), 1e-6)
         torch.cuda.synchronize()
         np.testing.assert_allclose(s.cpu().numpy(), ref, atol=2e-3, rtol=0)
+
+
+def test_paired_router_parity_in_its_own_process():
+    """The paired-CTA router (tcgen05.mma cta_group::2, TIDE_ROUTER=pair) on
+    the split path's parity cases (golden vectors, tile geometry of 1 to 8
+    units per CTA, the 32768 x 4096 properties), in a fresh process with the
+    switch set."""
+    import os
+    import subprocess
+    import sys
+
+    from tests.conftest import ROOT
+
+    env = dict(os.environ, TIDE_ROUTER="pair")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", str(ROOT / "tests" / "test_gpu_capi.py"),
+                        "-k", "golden and TC_SPLIT or split_router or full_size_properties"],
+                       cwd=str(ROOT), env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    assert " passed" in r.stdout

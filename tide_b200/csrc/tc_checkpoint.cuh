@@ -24,7 +24,7 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
                     size_t zero_bytes, cudaStream_t s, char *err, size_t err_len);
 
 // Paired-CTA router (tc_route_pair.cu): 16-bit rows, router width 128.
-// tc_route_launch takes it by default where it applies.
+// tc_route_launch takes it where it applies when TIDE_ROUTER=pair.
 bool tc_pair_supported(const tide_checkpoint_args *a);
 int tc_route_pair_launch(const tide_checkpoint_args *a, float *scores, float2 *row_stats,
                          void *zero, size_t zero_bytes, cudaStream_t s, char *err, size_t err_len);
