@@ -627,9 +627,9 @@ def engine_prefill(world: int, rank: int, reps: int = 10, warmup: int = 3) -> di
             return max_over_ranks(world, a.elapsed_time(b) / 1000.0)
 
         t_engine = timed(lambda: engine(ids))
-        stats = tdist.global_stats(world, engine.last_stats)
+        stats = tdist.global_stats(world, engine.last_stats, layers)
         t_live = timed(lambda: engine(ids, live=True))
-        live_stats = tdist.global_stats(world, engine.last_stats)
+        live_stats = tdist.global_stats(world, engine.last_stats, layers)
         t_hf = timed(lambda: model(ids).logits)
     tokens = B_all * S * reps
     res.update({"engine_tok_s": tokens / t_engine, "engine_ms_per_call": 1000 * t_engine / reps,

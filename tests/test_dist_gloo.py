@@ -42,6 +42,12 @@ def _collectives(rank: int, world: int, port: int, q) -> None:
                    remaining_tokens=100 * (r + 1) - (r + 3))
     g = td.global_stats(w, st)
     out["stats"] = (g.total_tokens, dict(g.exits_per_layer), g.remaining_tokens, g.summary())
+    # ranks that recorded different layers (a layer with no exit on a rank is
+    # not recorded there): summed over the full router layer list
+    st2 = ExitStats(total_tokens=10, exits_per_layer={8: 3} if r == 0 else {8: 1, 12: 2},
+                    remaining_tokens=7 if r == 0 else 7)
+    g2 = td.global_stats(w, st2, layers=[8, 12, 16])
+    out["stats_uneven"] = (g2.total_tokens, dict(g2.exits_per_layer), g2.remaining_tokens)
     rows = torch.full((3, 4), float(r), dtype=torch.bfloat16)
     out["rows"] = td.all_gather_rows(w, rows).float().tolist()
     out["gcounts"] = td.all_gather_counts(w, torch.tensor([[r, 2 * r]], dtype=torch.int32)).tolist()
@@ -115,6 +121,7 @@ def test_two_rank_collectives():
         total, exits, remaining, text = d["stats"]
         assert total == 300 and exits == {4: 3, 8: 4} and remaining == 300 - 7
         assert text.startswith("Total tokens: 300, Exited: 7")
+        assert d["stats_uneven"] == (20, {8: 4, 12: 2}, 14)
         assert d["rows"] == [[0.0] * 4] * 3 + [[1.0] * 4] * 3
         assert d["gcounts"] == [[[0, 0]], [[1, 2]]]
 

@@ -79,15 +79,19 @@ def sum_counts(world: int, counts: torch.Tensor) -> torch.Tensor:
     return t.to(counts.device, counts.dtype)
 
 
-def global_stats(world: int, stats: ExitStats) -> ExitStats:
-    """ExitStats summed over ranks (same fields, same summary text).  Every
-    rank must pass stats with the same set of checkpoint layers."""
-    layers = sorted(stats.exits_per_layer)
+def global_stats(world: int, stats: ExitStats, layers=None) -> ExitStats:
+    """ExitStats summed over ranks (same fields, same summary text).  `layers`
+    lists every checkpoint layer (the same list on every rank: a rank records
+    only the layers where some of its tokens exited, so its own keys can
+    differ from another rank's); without it every rank must pass stats with
+    the same keys.  Layers with no exit on any rank are left out, as in a
+    single process."""
+    layers = sorted(layers) if layers is not None else sorted(stats.exits_per_layer)
     local = torch.tensor([stats.total_tokens, stats.remaining_tokens]
-                         + [stats.exits_per_layer[k] for k in layers], dtype=torch.int64)
+                         + [stats.exits_per_layer.get(k, 0) for k in layers], dtype=torch.int64)
     tot = sum_counts(world, local).tolist()
     return ExitStats(total_tokens=int(tot[0]), remaining_tokens=int(tot[1]),
-                     exits_per_layer={k: int(v) for k, v in zip(layers, tot[2:])})
+                     exits_per_layer={k: int(v) for k, v in zip(layers, tot[2:]) if v})
 
 
 def shard_range(n: int, world: int, rank: int) -> Tuple[int, int]:
