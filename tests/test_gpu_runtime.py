@@ -561,3 +561,27 @@ def test_learned_exit_projection(tmp_path):
     exited = torch.from_numpy(ours >= 0).to(DEV).view(2, 40)
     assert torch.equal(plain[~exited], logits[~exited])
     assert not torch.allclose(plain[exited].float(), logits[exited].float(), atol=1e-2)
+
+
+@pytest.mark.parametrize("per_row", [False, True])
+def test_generate_from_a_prefilled_cache(tmp_path, per_row):
+    """generate(past_key_values=cache) with the context already in the cache
+    (all but the last prompt token) gives the tokens and exit counts of a
+    generate that prefills the whole prompt itself."""
+    from transformers import DynamicCache
+
+    model = qwen3(dtype=torch.float32)
+    ids = torch.randint(0, 512, (4, 9), generator=torch.Generator().manual_seed(21)).to(DEV)
+    routers = tuned_routers(tmp_path / "router.pt", model, ids, [1, 2], [0.4, 0.4], 0.6)
+    rt = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.6,
+                                                                       min_layers=0))
+    a = rt.generate(ids, max_new_tokens=6, temperature=0, per_row_exit=per_row, eos_token_id=-1)
+    sa = rt.last_stats
+    cache = DynamicCache(config=model.config)
+    with torch.no_grad():
+        model(ids[:, :-1], past_key_values=cache, use_cache=True)
+    b = rt.generate(ids, max_new_tokens=6, temperature=0, per_row_exit=per_row, eos_token_id=-1,
+                    past_key_values=cache)
+    assert torch.equal(a, b)
+    assert rt.last_stats == sa
+    assert sa.total_exited + sa.remaining_tokens == sa.total_tokens

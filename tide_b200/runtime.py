@@ -285,7 +285,7 @@ class TIDERuntime(nn.Module):
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 512,
                  temperature: float = 1.0, top_k: int = 50, top_p: float = 0.9,
-                 per_row_exit: bool = False, **kwargs) -> torch.Tensor:
+                 per_row_exit: bool = False, past_key_values=None, **kwargs) -> torch.Tensor:
         """Autoregressive decode (runtime.py:223-313).  Every step runs all
         layers (the reference's post-hoc design).  With the reference's rule
         (default) the earliest checkpoint at which every row's score passes
@@ -294,18 +294,29 @@ class TIDERuntime(nn.Module):
         own: the step's rows go through the same checkpoint chain as a
         prefill (positions and KV slot ids of the survivors compacted on the
         device at every checkpoint), and each row's logits come from its own
-        exit layer.  Generation stops when every sampled token equals
-        `eos_token_id` (default 2, the reference's fixed id, runtime.py:257)."""
+        exit layer; the exit counts of every step add up on the device and
+        are read back once, after the last step.  Generation stops when every
+        sampled token equals `eos_token_id` (default 2, the reference's fixed
+        id, runtime.py:257).  `past_key_values`: a model cache that already
+        holds the context (e.g. an HF StaticCache); the model then runs only
+        on input_ids[:, -1:] to start, instead of a prefill of input_ids."""
         eos = kwargs.get("eos_token_id", 2)
         B = input_ids.shape[0]
         dev = input_ids.device
         n_layers = len(self._layers)
         generated = input_ids.clone()
         gen_stats = ExitStats(total_tokens=0)
-        pre = self.model(generated, use_cache=True, return_dict=True)
+        if past_key_values is None:
+            pre = self.model(generated, use_cache=True, return_dict=True)
+        else:
+            pre = self.model(generated[:, -1:], past_key_values=past_key_values, use_cache=True,
+                             return_dict=True)
         past = pre.past_key_values
         next_logits = pre.logits[:, -1, :]
         slots = torch.arange(B, device=dev, dtype=torch.int32)
+        learned = self._learned_exits()
+        step_counts = None  # per-row exits: {survivors, exits} per checkpoint, summed on the device
+        row_layers: list = []
         for _ in range(max_new_tokens):
             nxt = sample_next_token(next_logits, temperature, top_k, top_p)
             generated = torch.cat([generated, nxt], dim=-1)
@@ -322,15 +333,18 @@ class TIDERuntime(nn.Module):
                 layers, counts, exit_pos, _ = self._checkpoint_chain(
                     lambda L: hs[L + 1][:, -1, :].contiguous(), B, H, hs[-1].dtype,
                     hs[-1][:, -1, :].contiguous(), out_buf, slots=slots)
-                st = self._read_back(layers, counts, exit_pos, B, (B,))
-                if self._learned_exits():
+                row_layers = layers
+                if learned:  # the projection's GEMM shapes need the counts now
+                    st = self._read_back(layers, counts, exit_pos, B, (B,))
                     for k, layer in enumerate(layers):
                         self._project_exits(out_buf, layer,
                                             exit_pos[k][: self._host_counts[2 * k + 1]])
+                    for layer, c in st.exits_per_layer.items():
+                        gen_stats.exits_per_layer[layer] = gen_stats.exits_per_layer.get(layer, 0) + c
+                    gen_stats.remaining_tokens += st.remaining_tokens
+                else:
+                    step_counts = counts.to(torch.int64) if step_counts is None else step_counts + counts
                 next_logits = self._lm_head(out_buf)
-                for layer, c in st.exits_per_layer.items():
-                    gen_stats.exits_per_layer[layer] = gen_stats.exits_per_layer.get(layer, 0) + c
-                gen_stats.remaining_tokens += st.remaining_tokens
                 continue
             exit_layer, exit_hidden = None, None
             for layer in sorted(self.routers):
@@ -351,6 +365,12 @@ class TIDERuntime(nn.Module):
             else:
                 next_logits = out.logits[:, -1, :]
                 gen_stats.remaining_tokens += B
+        if step_counts is not None:  # the one read-back of the per-row exit counts
+            host = step_counts.cpu().tolist()
+            for layer, (n_surv, n_exit) in zip(row_layers, host):
+                if n_exit:
+                    gen_stats.exits_per_layer[layer] = gen_stats.exits_per_layer.get(layer, 0) + n_exit
+            gen_stats.remaining_tokens += host[-1][0] if host else gen_stats.total_tokens
         self._runner.check_errors()
         self.last_stats = gen_stats
         if gen_stats.total_tokens > 0:
