@@ -78,6 +78,7 @@ WORKLOADS = {
 # workloads that are not a checkpoint sweep
 SWEEP_WORKLOAD = "bandwidth_sweep"
 ENGINE_WORKLOAD = "llama8b_prefill_engine"
+DECODE_WORKLOAD = "qwen3_8b_decode_generate"
 SWEEP_N = [1024, 4096, 16384, 65536, 262144, 1048576]
 SWEEP_H = [2048, 4096, 5120, 8192]
 SWEEP_F = [0.0, 0.1, 0.5, 0.9]
@@ -514,7 +515,7 @@ def run_reference(args, world, rank):
     from the CPU generator (checkpoint_setup) and go straight to the oracle."""
     if rank != 0:
         return
-    if WORKLOAD in (SWEEP_WORKLOAD, ENGINE_WORKLOAD):
+    if WORKLOAD in (SWEEP_WORKLOAD, ENGINE_WORKLOAD, DECODE_WORKLOAD):
         configure("llama8b_prefill_checkpoints")
     sample = min(2048, ROWS)
     cores = host_threads()
@@ -690,6 +691,110 @@ def decode_checkpoints(world: int, rank: int, steps: int = 200) -> dict:
         globals().update(saved)
 
 
+def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
+                    ctx: int = 1024) -> dict:
+    """Config 4 at model level: a random-init bf16 Qwen3-8B-architecture
+    model (36 layers, H 4096, 32/8 heads, head_dim 128, MLP 12288, vocab
+    151936, QK-norm), a decode batch of 256 sequences per rank whose KV cache
+    holds 1024 positions of N(0,1) keys and values, routers at layers
+    3, 7, ..., 31 whose biases exit ~10 % of the rows still active at each,
+    and 128 new tokens through engine.generate(per_row_exit=True) (greedy):
+    every row exits on its own, positions and KV slot ids compacted on the
+    device at every checkpoint of every step.  Timed beside the model's own
+    greedy loop on the same cache (both run every layer: the reference's
+    post-hoc decode).  tokens/s = batch * steps / time, summed over ranks."""
+    from transformers import Qwen3Config, Qwen3ForCausalLM, StaticCache
+
+    from tide_b200 import TIDEConfig
+    from tide_b200 import dist as tdist
+    from tide_b200 import workloads
+    from tide_b200.router import RouterCheckpoint, TokenRouter
+    from tide_b200.runtime import TIDERuntime
+
+    dev = torch.device("cuda")
+    layers = list(range(3, 35, 4))  # 3..31: every fourth layer short of the last
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=4096, intermediate_size=12288,
+                      num_hidden_layers=36, num_attention_heads=32, num_key_value_heads=8,
+                      head_dim=128, rms_norm_eps=1e-6, rope_theta=1e6,
+                      max_position_embeddings=40960, tie_word_embeddings=False)
+    torch.manual_seed(SEED + 3)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = Qwen3ForCausalLM(cfg).eval()
+    finally:
+        torch.set_default_dtype(prev)
+    res = {"model": "Qwen3-8B architecture, random-init bf16", "batch_per_rank": batch,
+           "kv_context": ctx, "new_tokens": steps, "router_layers": layers,
+           "exit_fraction_of_active_per_checkpoint": 0.10, "scaling": "weak"}
+    g = torch.Generator(device=dev).manual_seed(SEED + 11 + rank)
+    cache = StaticCache(config=cfg, max_cache_len=ctx + 2 * steps + 16)
+    with torch.inference_mode():
+        for li in range(cfg.num_hidden_layers):
+            k = torch.randn(batch, 8, ctx, 128, generator=g, device=dev).to(torch.bfloat16)
+            v = torch.randn(batch, 8, ctx, 128, generator=g, device=dev).to(torch.bfloat16)
+            cache.update(k, v, li, {"cache_position": torch.arange(ctx, device=dev)})
+            del k, v
+        tok = torch.randint(0, cfg.vocab_size, (batch, 1), generator=g, device=dev)
+        # router biases from one decode step's hidden states
+        hs = model(tok, past_key_values=cache, use_cache=True, output_hidden_states=True).hidden_states
+        gw = torch.Generator().manual_seed(SEED + 13)
+        nw = model.model.norm.weight.float()
+        exited = torch.zeros(batch, dtype=torch.bool, device=dev)
+        routers = {}
+        for L in layers:
+            r = TokenRouter(4096, 128, up_bias=True)
+            with torch.no_grad():
+                r.down.weight.normal_(0, 0.02, generator=gw)
+                r.up.weight.normal_(0, 0.02, generator=gw)
+            z = workloads.prebias_logits_torch(hs[L + 1][:, -1, :], "rms", nw, None, 1e-6,
+                                               r.down.weight.to(dev), r.up.weight.to(dev))
+            active = (~exited).nonzero()[:, 0]
+            bias = workloads.bias_for_exit_fraction(z[active], 0.10, THRESHOLD)
+            with torch.no_grad():
+                r.up.bias.fill_(bias)
+            exited[active[(z[active] + bias) > workloads.logit(THRESHOLD)]] = True
+            routers[L] = r
+        del hs
+        tmp = Path(tempfile.mkdtemp(prefix="tide_bench_"))
+        RouterCheckpoint(routers, 4096, 128).save(tmp / "router.pt")
+        engine = TIDERuntime(model, tmp / "router.pt",
+                             config=TIDEConfig(exit_threshold=THRESHOLD, min_layers=0))
+        engine.generate(tok, max_new_tokens=3, temperature=0, per_row_exit=True,
+                        past_key_values=cache, eos_token_id=-1)  # warm-up
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        engine.generate(tok, max_new_tokens=steps, temperature=0, per_row_exit=True,
+                        past_key_values=cache, eos_token_id=-1)
+        b.record()
+        torch.cuda.synchronize()
+        t_eng = max_over_ranks(world, a.elapsed_time(b) / 1000.0)
+        stats = tdist.global_stats(world, engine.last_stats, layers)
+        # the model's own greedy loop on the same cache
+        nxt = tok
+        torch.cuda.synchronize()
+        barrier(world)
+        a.record()
+        for _ in range(steps):
+            out = model(nxt, past_key_values=cache, use_cache=True)
+            nxt = out.logits[:, -1, :].argmax(-1, keepdim=True)
+        b.record()
+        torch.cuda.synchronize()
+        t_hf = max_over_ranks(world, a.elapsed_time(b) / 1000.0)
+    tokens = world * batch * steps
+    res.update({"engine_tok_s": tokens / t_eng, "engine_ms_per_step": 1000 * t_eng / (steps + 1),
+                "hf_greedy_tok_s": tokens / t_hf, "hf_ms_per_step": 1000 * t_hf / steps,
+                "mode": "per-row exits, post-hoc (every layer runs)",
+                "exit_rate": stats.exit_rate,
+                "exits_per_layer": {str(k): v for k, v in sorted(stats.exits_per_layer.items())}})
+    del engine, model, cache
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_sweep(args, world, rank, local) -> None:
     """--workload bandwidth_sweep: one checkpoint per (N, H, f), N split evenly
     over the ranks; aggregate algorithmic GB/s (max device time over ranks)
@@ -802,7 +907,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-engine", action="store_true", help="skip the engine prefill measurement")
     ap.add_argument("--workload", default=WORKLOAD,
-                    choices=sorted(WORKLOADS) + [SWEEP_WORKLOAD, ENGINE_WORKLOAD])
+                    choices=sorted(WORKLOADS) + [SWEEP_WORKLOAD, ENGINE_WORKLOAD, DECODE_WORKLOAD])
     ap.add_argument("--rows", type=int, default=None, help="rows per GPU (profiling runs)")
     ap.add_argument("--sweep-h", default=None, help="bandwidth_sweep: comma-separated H values")
     ap.add_argument("--sweep-n", default=None, help="bandwidth_sweep: comma-separated N values")
@@ -818,6 +923,14 @@ def main():
             run_reference(args, world, rank)
         elif args.workload == SWEEP_WORKLOAD:
             run_sweep(args, world, rank, local)
+        elif args.workload == DECODE_WORKLOAD:
+            dg = decode_generate(world, rank)
+            if rank == 0:
+                print(json.dumps({"metric": "decode_tokens_per_s", "value": dg["engine_tok_s"],
+                                  "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
+                                  "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                                  "data": "synthetic", "config": {"workload": DECODE_WORKLOAD},
+                                  "decode_generate": dg}), flush=True)
         elif args.workload == ENGINE_WORKLOAD:
             eng = engine_prefill(world, rank)
             if rank == 0:
@@ -973,7 +1086,7 @@ def run_checkpoints(args, world, rank, local) -> None:
 
     paths_used = [PATH_NAMES.get(wl.paths[k], wl.paths[k]) for k in range(len(LAYERS))]
     n_launch = sum(launches_per_checkpoint(p) for p in wl.paths.values()) * args.steps
-    engine = decode = None
+    engine = decode = decode_gen = None
     if WORKLOAD == "llama8b_prefill_checkpoints" and args.rows is None:
         del wl
         torch.cuda.empty_cache()
@@ -983,6 +1096,10 @@ def run_checkpoints(args, world, rank, local) -> None:
                 engine = engine_prefill(world, rank)
             except Exception as exc:  # reported, not fatal: the checkpoint numbers stand
                 engine = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+            try:
+                decode_gen = decode_generate(world, rank)
+            except Exception as exc:
+                decode_gen = {"error": f"{type(exc).__name__}: {exc}"[:400]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1009,6 +1126,7 @@ def run_checkpoints(args, world, rank, local) -> None:
             "collectives_timed_separately": collectives,
             "prefill_engine": engine,
             "decode_checkpoints": decode,
+            "decode_generate": decode_gen,
         }
         print(json.dumps(line), flush=True)
 
