@@ -703,7 +703,7 @@ def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
     device at every checkpoint of every step.  Timed beside the model's own
     greedy loop on the same cache (both run every layer: the reference's
     post-hoc decode).  tokens/s = batch * steps / time, summed over ranks."""
-    from transformers import Qwen3Config, Qwen3ForCausalLM, StaticCache
+    from transformers import DynamicCache, Qwen3Config, Qwen3ForCausalLM
 
     from tide_b200 import TIDEConfig
     from tide_b200 import dist as tdist
@@ -729,7 +729,9 @@ def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
            "kv_context": ctx, "new_tokens": steps, "router_layers": layers,
            "exit_fraction_of_active_per_checkpoint": 0.10, "scaling": "weak"}
     g = torch.Generator(device=dev).manual_seed(SEED + 11 + rank)
-    cache = StaticCache(config=cfg, max_cache_len=ctx + 2 * steps + 16)
+    # (HF's DynamicCache: 75 ms per step here, against 193 ms for its StaticCache,
+    # whose per-layer updates copy the whole cache)
+    cache = DynamicCache(config=cfg)
     with torch.inference_mode():
         for li in range(cfg.num_hidden_layers):
             k = torch.randn(batch, 8, ctx, 128, generator=g, device=dev).to(torch.bfloat16)
