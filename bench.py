@@ -698,18 +698,22 @@ def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
     151936, QK-norm), a decode batch of 256 sequences per rank whose KV cache
     holds 1024 positions of N(0,1) keys and values, routers at layers
     3, 7, ..., 31 whose biases exit ~10 % of the rows still active at each,
-    and 128 new tokens through engine.generate(per_row_exit=True) (greedy):
-    every row exits on its own, positions and KV slot ids compacted on the
-    device at every checkpoint of every step.  Timed beside the model's own
-    greedy loop on the same cache (both run every layer: the reference's
-    post-hoc decode).  tokens/s = batch * steps / time, summed over ranks."""
+    and 128 greedy tokens.  Timed three ways, each on its own copy of that
+    cache: the live decoder with per-row exits (tide_b200.live.LiveDecoder:
+    after a row exits its later layers are skipped, the survivors' KV slot ids
+    compacted by the checkpoint kernel), the same decoder with no exit (every
+    checkpoint still runs), and the model's own greedy loop on HF's
+    DynamicCache (every layer for every row, as in the reference's decode).
+    tokens/s = batch * steps / time, summed over ranks."""
     from transformers import DynamicCache, Qwen3Config, Qwen3ForCausalLM
 
     from tide_b200 import TIDEConfig
     from tide_b200 import dist as tdist
     from tide_b200 import workloads
+    from tide_b200.live import LiveDecoder
     from tide_b200.router import RouterCheckpoint, TokenRouter
     from tide_b200.runtime import TIDERuntime
+    from tide_b200.scheduler import ExitStats
 
     dev = torch.device("cuda")
     layers = list(range(3, 35, 4))  # 3..31: every fourth layer short of the last
@@ -728,19 +732,30 @@ def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
     res = {"model": "Qwen3-8B architecture, random-init bf16", "batch_per_rank": batch,
            "kv_context": ctx, "new_tokens": steps, "router_layers": layers,
            "exit_fraction_of_active_per_checkpoint": 0.10, "scaling": "weak"}
-    g = torch.Generator(device=dev).manual_seed(SEED + 11 + rank)
-    # (HF's DynamicCache: 75 ms per step here, against 193 ms for its StaticCache,
-    # whose per-layer updates copy the whole cache)
-    cache = DynamicCache(config=cfg)
+    tok0 = torch.randint(0, cfg.vocab_size, (batch,),
+                         generator=torch.Generator(device=dev).manual_seed(SEED + 7 + rank),
+                         device=dev)
+
+    def timed(fn) -> float:
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(world, a.elapsed_time(b) / 1000.0)
+
     with torch.inference_mode():
+        # routers placed on one step's hidden states (the model's own decode)
+        cal = DynamicCache(config=cfg)
+        g = torch.Generator(device=dev).manual_seed(SEED + 11 + rank)
         for li in range(cfg.num_hidden_layers):
-            k = torch.randn(batch, 8, ctx, 128, generator=g, device=dev).to(torch.bfloat16)
-            v = torch.randn(batch, 8, ctx, 128, generator=g, device=dev).to(torch.bfloat16)
-            cache.update(k, v, li, {"cache_position": torch.arange(ctx, device=dev)})
-            del k, v
-        tok = torch.randint(0, cfg.vocab_size, (batch, 1), generator=g, device=dev)
-        # router biases from one decode step's hidden states
-        hs = model(tok, past_key_values=cache, use_cache=True, output_hidden_states=True).hidden_states
+            cal.update(torch.randn(batch, 8, 64, 128, generator=g, device=dev).to(torch.bfloat16),
+                       torch.randn(batch, 8, 64, 128, generator=g, device=dev).to(torch.bfloat16), li)
+        hs = model(tok0[:, None], past_key_values=cal, use_cache=True,
+                   output_hidden_states=True).hidden_states
+        del cal
         gw = torch.Generator().manual_seed(SEED + 13)
         nw = model.model.norm.weight.float()
         exited = torch.zeros(batch, dtype=torch.bool, device=dev)
@@ -763,35 +778,52 @@ def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
         RouterCheckpoint(routers, 4096, 128).save(tmp / "router.pt")
         engine = TIDERuntime(model, tmp / "router.pt",
                              config=TIDEConfig(exit_threshold=THRESHOLD, min_layers=0))
-        engine.generate(tok, max_new_tokens=3, temperature=0, per_row_exit=True,
-                        past_key_values=cache, eos_token_id=-1)  # warm-up
-        torch.cuda.synchronize()
-        barrier(world)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        engine.generate(tok, max_new_tokens=steps, temperature=0, per_row_exit=True,
-                        past_key_values=cache, eos_token_id=-1)
-        b.record()
-        torch.cuda.synchronize()
-        t_eng = max_over_ranks(world, a.elapsed_time(b) / 1000.0)
-        stats = tdist.global_stats(world, engine.last_stats, layers)
-        # the model's own greedy loop on the same cache
-        nxt = tok
-        torch.cuda.synchronize()
-        barrier(world)
-        a.record()
-        for _ in range(steps):
-            out = model(nxt, past_key_values=cache, use_cache=True)
-            nxt = out.logits[:, -1, :].argmax(-1, keepdim=True)
-        b.record()
-        torch.cuda.synchronize()
-        t_hf = max_over_ranks(world, a.elapsed_time(b) / 1000.0)
+
+        def live_run(threshold: float, stats):
+            engine.config.exit_threshold = threshold
+            dec = LiveDecoder(engine, batch, ctx + steps + 8)
+            dec.fill_random(ctx, torch.Generator(device=dev).manual_seed(SEED + 17 + rank))
+            tok = tok0
+            for _ in range(3):  # warm-up steps
+                tok = dec.step(tok).argmax(-1)
+
+            def loop():
+                t = tok
+                for _ in range(steps):
+                    t = dec.step(t, stats).argmax(-1)
+
+            t_run = timed(loop)
+            del dec
+            torch.cuda.empty_cache()
+            return t_run
+
+        st_live = ExitStats()
+        t_live = live_run(THRESHOLD, st_live)
+        t_noexit = live_run(2.0, None)  # scores lie in [0, 1]: no row exits
+        engine.config.exit_threshold = THRESHOLD
+        cache = DynamicCache(config=cfg)
+        g = torch.Generator(device=dev).manual_seed(SEED + 17 + rank)
+        for li in range(cfg.num_hidden_layers):
+            cache.update(torch.randn(batch, 8, ctx, 128, generator=g, device=dev).to(torch.bfloat16),
+                         torch.randn(batch, 8, ctx, 128, generator=g, device=dev).to(torch.bfloat16), li)
+        nxt = tok0[:, None]
+        for _ in range(3):
+            nxt = model(nxt, past_key_values=cache, use_cache=True).logits[:, -1, :].argmax(-1, keepdim=True)
+
+        def hf_loop():
+            t = nxt
+            for _ in range(steps):
+                t = model(t, past_key_values=cache, use_cache=True).logits[:, -1, :].argmax(-1, keepdim=True)
+
+        t_hf = timed(hf_loop)
+        stats = tdist.global_stats(world, st_live, layers)
     tokens = world * batch * steps
-    res.update({"engine_tok_s": tokens / t_eng, "engine_ms_per_step": 1000 * t_eng / (steps + 1),
+    res.update({"live_tok_s": tokens / t_live, "live_ms_per_step": 1000 * t_live / steps,
+                "live_no_exit_tok_s": tokens / t_noexit, "live_no_exit_ms_per_step": 1000 * t_noexit / steps,
                 "hf_greedy_tok_s": tokens / t_hf, "hf_ms_per_step": 1000 * t_hf / steps,
-                "mode": "per-row exits, post-hoc (every layer runs)",
-                "exit_rate": stats.exit_rate,
-                "exits_per_layer": {str(k): v for k, v in sorted(stats.exits_per_layer.items())}})
+                "hf_cache": "DynamicCache (HF's StaticCache measured 193 ms per step here)",
+                "live_exit_rate": stats.exit_rate,
+                "live_exits_per_layer": {str(k): v for k, v in sorted(stats.exits_per_layer.items())}})
     del engine, model, cache
     torch.cuda.empty_cache()
     return res
@@ -928,7 +960,7 @@ def main():
         elif args.workload == DECODE_WORKLOAD:
             dg = decode_generate(world, rank)
             if rank == 0:
-                print(json.dumps({"metric": "decode_tokens_per_s", "value": dg["engine_tok_s"],
+                print(json.dumps({"metric": "decode_tokens_per_s", "value": dg["live_tok_s"],
                                   "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
                                   "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                                   "data": "synthetic", "config": {"workload": DECODE_WORKLOAD},

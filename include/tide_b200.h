@@ -160,6 +160,22 @@ int tide_norm_at_positions(int dtype, int norm_type, const void *src, const int6
                            const float *norm_bias, float eps, int32_t *error_word,
                            tide_stream_t stream);
 
+/* Decode attention over a KV cache addressed by slot: for each of the n_rows
+ * rows still active in a decode step (their slot ids as compacted by
+ * tide_checkpoint's slots_out),
+ *   out[i, h] = softmax_j(scale * q[i, h] . K[slots[i], h/G, j]) . V[slots[i], h/G, j],
+ *   j in [0, length), G = n_q_heads / n_kv_heads (at most 8), head_dim 128.
+ * q, out [n_rows, n_q_heads, 128]; K, V caches [n_slots, n_kv_heads, max_len, 128],
+ * bf16 or fp16.  Positions a sequence skipped hold zeros and count like any
+ * other (the "zero_pad" K/V policy of python/TIDE/runtime.py:194-221).  It
+ * replaces, for the rows that have not exited, the attention of the HF model
+ * call inside the reference's decode loop (runtime.py:266-273).  A slot
+ * outside [0, n_slots) skips its row and sets TIDE_DEVERR_POSITION. */
+int tide_decode_attention(int dtype, const void *q, const void *k_cache, const void *v_cache,
+                          const int32_t *slots, void *out, int64_t n_rows, int64_t n_q_heads,
+                          int64_t n_kv_heads, int64_t head_dim, int64_t n_slots, int64_t max_len,
+                          int64_t length, float scale, int32_t *error_word, tide_stream_t stream);
+
 /* ---- router preparation (once per router) ------------------------------ */
 
 /* From the router's down.weight [B, H] fp32 and the final norm's weight (and

@@ -101,3 +101,108 @@ def test_live_matches_dense_emulation(tmp_path, dtype):
     if len(differ) == 0:
         atol = 1e-3 if dtype == torch.float32 else 5e-2
         torch.testing.assert_close(logits.float(), ref.float(), atol=atol, rtol=atol)
+
+
+@pytest.mark.parametrize("G,L", [(4, 1), (4, 17), (4, 1025), (8, 300), (1, 64), (2, 5000)])
+def test_decode_attention_matches_torch(G, L):
+    """tide_decode_attention over slot-addressed caches against an fp32 torch
+    softmax attention of the gathered rows (bf16 in and out)."""
+    from tide_b200 import _native
+
+    ops = _native.ops()
+    n, hkv, d, n_slots = 37, 2, 128, 50
+    hq, max_len = G * hkv, L + 3
+    g = torch.Generator(device=DEV).manual_seed(G * 10007 + L)
+    kc = torch.randn(n_slots, hkv, max_len, d, generator=g, device=DEV).to(torch.bfloat16)
+    vc = torch.randn(n_slots, hkv, max_len, d, generator=g, device=DEV).to(torch.bfloat16)
+    q = torch.randn(n, hq, d, generator=g, device=DEV).to(torch.bfloat16)
+    slots = torch.randperm(n_slots, generator=torch.Generator().manual_seed(L))[:n].to(torch.int32).to(DEV)
+    out = torch.empty_like(q)
+    scale = d ** -0.5
+    ops.decode_attention(q, kc, vc, slots, out, L, scale, None)
+    K = kc[slots.long(), :, :L].float().repeat_interleave(G, dim=1)
+    V = vc[slots.long(), :, :L].float().repeat_interleave(G, dim=1)
+    p = torch.softmax(torch.einsum("nhd,nhld->nhl", q.float(), K) * scale, dim=-1)
+    ref = torch.einsum("nhl,nhld->nhd", p, V)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
+
+
+def test_decode_attention_flags_a_slot_outside_the_cache():
+    from tide_b200 import _native
+
+    ops = _native.ops()
+    kc = torch.zeros(4, 1, 8, 128, dtype=torch.bfloat16, device=DEV)
+    q = torch.ones(3, 2, 128, dtype=torch.bfloat16, device=DEV)
+    out = torch.full_like(q, 5.0)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    slots = torch.tensor([0, 4, 2], dtype=torch.int32, device=DEV)
+    ops.decode_attention(q, kc, kc, slots, out, 8, 0.1, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & 1
+    assert torch.all(out[1] == 5.0) and torch.all(out[0] == 0.0) and torch.all(out[2] == 0.0)
+
+
+def _qwen3_hd128():
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
+                      num_attention_heads=2, num_key_value_heads=1, head_dim=128,
+                      rms_norm_eps=1e-6, max_position_embeddings=256)
+    torch.manual_seed(0)
+    return Qwen3ForCausalLM(cfg).to(DEV, torch.bfloat16).eval()
+
+
+def test_live_decoder_first_step_matches_posthoc(tmp_path):
+    """One decode step of the live decoder (layers skipped per row after its
+    exit) against the post-hoc chain on the model's own hidden states: on the
+    first step a row's computation up to its exit reads only its own cache,
+    so both give the same logits and exit layers (bf16, within tolerance)."""
+    from tide_b200.live import LiveDecoder
+    from tide_b200.scheduler import ExitStats
+
+    model = _qwen3_hd128()
+    B, S = 6, 12
+    ids = torch.randint(0, 512, (B, S), generator=torch.Generator().manual_seed(17)).to(DEV)
+    tuned_routers(tmp_path / "router.pt", model, ids, [1, 2], [0.3, 0.3], 0.6)
+    rt = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.6,
+                                                                       min_layers=0))
+    dec = LiveDecoder(rt, B, S + 4)
+    with torch.no_grad():
+        first = dec.prefill(ids)
+        pre = model(ids, use_cache=True)
+    torch.testing.assert_close(first.float(), pre.logits[:, -1].float(), atol=5e-2, rtol=5e-2)
+    nxt = first.argmax(-1)
+    st = ExitStats()
+    live_logits = dec.step(nxt, st)
+    live_exit = dec.last_exit_layer.clone()
+    with torch.no_grad():
+        out = model(nxt[:, None], past_key_values=pre.past_key_values, use_cache=True,
+                    output_hidden_states=True)
+        hs = out.hidden_states
+        H = hs[-1].shape[-1]
+        out_buf = torch.zeros(B, H, dtype=hs[-1].dtype, device=DEV)
+        layers, counts, exit_pos, _ = rt._checkpoint_chain(
+            lambda L: hs[L + 1][:, -1, :].contiguous(), B, H, hs[-1].dtype,
+            hs[-1][:, -1, :].contiguous(), out_buf)
+        rt._read_back(layers, counts, exit_pos, B, (B,))
+        ref_logits = rt._lm_head(out_buf)
+    same = live_exit == rt.last_exit_layer
+    assert int(same.sum()) >= B - 1
+    assert st.total_tokens == B and st.total_exited + st.remaining_tokens == B
+    torch.testing.assert_close(live_logits[same].float(), ref_logits[same].float(), atol=6e-2,
+                               rtol=6e-2)
+
+
+def test_generate_live_skips_layers_per_row(tmp_path):
+    """generate(live=True): greedy tokens with per-row exits that skip the
+    later layers; exit counts add up and rows exit."""
+    model = _qwen3_hd128()
+    ids = torch.randint(0, 512, (4, 10), generator=torch.Generator().manual_seed(23)).to(DEV)
+    tuned_routers(tmp_path / "router.pt", model, ids, [1, 2], [0.4, 0.4], 0.6)
+    rt = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.6,
+                                                                       min_layers=0))
+    out = rt.generate(ids, max_new_tokens=6, temperature=0, live=True, eos_token_id=-1)
+    assert out.shape == (4, 16)
+    st = rt.last_stats
+    assert st.total_tokens == 4 * 6 and st.total_exited + st.remaining_tokens == st.total_tokens
+    assert st.total_exited > 0

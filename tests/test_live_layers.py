@@ -91,3 +91,45 @@ def test_live_embedding_matches_model():
         with torch.no_grad():
             hs = model(ids, output_hidden_states=True).hidden_states
             torch.testing.assert_close(fam.embed_tokens(ids), hs[0].reshape(18, -1))
+
+
+class CaptureKV:
+    """A stand-in for the HF cache that keeps the keys and values it is given."""
+
+    def __init__(self):
+        self.k = self.v = None
+
+    def update(self, k, v, layer_idx, cache_kwargs=None):
+        self.k, self.v = k, v
+        return k, v
+
+    def get_seq_length(self, layer_idx=0):
+        return 0
+
+
+@pytest.mark.parametrize("kind", ["llama", "qwen3"])
+def test_prefill_layer_stores_the_models_keys_and_values(kind):
+    """The live decoder's prefill layer gives the model layer's output and
+    stores, per sequence slot and position, the keys and values the model's
+    attention uses (after rotary embedding and, for Qwen3, the k-norm)."""
+    model = tiny_llama(qk_norm=kind == "qwen3")
+    fam = family_of(model)
+    B, S = 3, 7
+    ids = torch.randint(0, 97, (B, S), generator=torch.Generator().manual_seed(4))
+    nkv, d = fam.kv_heads(), fam.head_dim()
+    kc = torch.zeros(B + 2, nkv, 12, d)
+    vc = torch.zeros_like(kc)
+    with torch.no_grad():
+        h = fam.embed_tokens(ids)
+        ours = fam.prefill_layer(0, h, B, S, kc, vc)
+        cap = CaptureKV()
+        x = h.view(B, S, -1)
+        pos_ids = torch.arange(S)[None]
+        pe = model.model.rotary_emb(x, pos_ids)
+        ref = model.model.layers[0](x, attention_mask=None, position_ids=pos_ids,
+                                    past_key_values=cap, use_cache=False, position_embeddings=pe)
+        ref = ref[0] if isinstance(ref, tuple) else ref
+    torch.testing.assert_close(ours, ref.reshape(B * S, -1), atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(kc[:B, :, :S], cap.k, atol=1e-6, rtol=1e-6)
+    torch.testing.assert_close(vc[:B, :, :S], cap.v, atol=1e-6, rtol=1e-6)
+    assert torch.all(kc[B:] == 0) and torch.all(kc[:, :, S:] == 0)

@@ -376,6 +376,36 @@ void norm_at_positions(const at::Tensor &src, const at::Tensor &positions,
                                        static_cast<int32_t *>(opt_mut(error_word)), cur_stream(src)));
 }
 
+void decode_attention(const at::Tensor &q, const at::Tensor &k_cache, const at::Tensor &v_cache,
+                      const std::optional<at::Tensor> &slots, const at::Tensor &out, int64_t length,
+                      double scale, const std::optional<at::Tensor> &error_word) {
+  check_cuda_contig(q, "q");
+  check_cuda_contig(k_cache, "k_cache");
+  check_cuda_contig(v_cache, "v_cache");
+  check_cuda_contig(out, "out");
+  TORCH_CHECK(q.dim() == 3 && out.sizes() == q.sizes(), "q and out must be [n, heads, head_dim]");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes(),
+              "caches must be [slots, kv_heads, max_len, head_dim]");
+  TORCH_CHECK(q.scalar_type() == k_cache.scalar_type() && v_cache.scalar_type() == q.scalar_type() &&
+              out.scalar_type() == q.scalar_type(), "q, caches and out must share a dtype");
+  TORCH_CHECK(k_cache.size(3) == q.size(2), "head_dim differs");
+  const int32_t *sl = nullptr;
+  if (slots.has_value() && slots->defined()) {
+    check_cuda_contig(*slots, "slots");
+    TORCH_CHECK(slots->scalar_type() == at::kInt && slots->numel() >= q.size(0),
+                "slots must be int32 with one entry per row");
+    sl = slots->data_ptr<int32_t>();
+  }
+  if (error_word.has_value() && error_word->defined())
+    TORCH_CHECK(error_word->is_cuda() && error_word->scalar_type() == at::kInt, "error_word must be int32");
+  const c10::cuda::CUDAGuard guard(q.device());
+  TIDE_CHECK_OK(tide_decode_attention(to_dtype(q.scalar_type(), "decode_attention"), q.data_ptr(),
+                                      k_cache.data_ptr(), v_cache.data_ptr(), sl, out.data_ptr(),
+                                      q.size(0), q.size(1), k_cache.size(1), q.size(2),
+                                      k_cache.size(0), k_cache.size(2), length, (float)scale,
+                                      static_cast<int32_t *>(opt_mut(error_word)), cur_stream(q)));
+}
+
 // ---- router fold and fused checkpoint ----------------------------------
 
 std::vector<at::Tensor> router_fold(const at::Tensor &down, const at::Tensor &norm_weight,
@@ -526,6 +556,8 @@ TORCH_LIBRARY(tide, m) {
   m.def("norm_at_positions(Tensor src, Tensor positions, Tensor? n_rows_dev, "
         "Tensor(a!) output_buffer, Tensor norm_weight, Tensor? norm_bias, int norm_type, float eps, "
         "Tensor(b!)? error_word) -> ()");
+  m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor? slots, Tensor(a!) out, "
+        "int length, float scale, Tensor(b!)? error_word) -> ()");
   m.def("router_fold(Tensor down, Tensor norm_weight, Tensor? norm_bias, ScalarType fold_dtype) "
         "-> Tensor[]");
   m.def("checkpoint_workspace_size(int n_rows, int hidden_dim) -> int", &checkpoint_workspace_size);
@@ -547,6 +579,7 @@ TORCH_LIBRARY_IMPL(tide, CUDA, m) {
   m.impl("norm_scatter", &norm_scatter);
   m.impl("gather_rows", &gather_rows);
   m.impl("norm_at_positions", &norm_at_positions);
+  m.impl("decode_attention", &decode_attention);
   m.impl("router_fold", &router_fold);
   m.impl("checkpoint", &checkpoint);
 }

@@ -98,6 +98,66 @@ class _LlamaFamily:
         return h + layer.mlp(layer.post_attention_layernorm(h))
 
 
+    # ---- decode with a KV cache addressed by slot (LiveDecoder)
+    def kv_heads(self) -> int:
+        a = self.layers[0].self_attn
+        return a.k_proj.out_features // a.head_dim
+
+    def head_dim(self) -> int:
+        return self.layers[0].self_attn.head_dim
+
+    def _qkv(self, layer, h: torch.Tensor, seq_pos: torch.Tensor):
+        attn = layer.self_attn
+        d = attn.head_dim
+        n = h.shape[0]
+        x = layer.input_layernorm(h)
+        q = attn.q_proj(x).view(n, -1, d)
+        k = attn.k_proj(x).view(n, -1, d)
+        v = attn.v_proj(x).view(n, -1, d)
+        if getattr(attn, "q_norm", None) is not None:
+            q = attn.q_norm(q)
+            k = attn.k_norm(k)
+        cos, sin = self.rotary(v, seq_pos.view(1, -1))
+        cos, sin = cos[0].unsqueeze(1), sin[0].unsqueeze(1)
+        return q * cos + _rotate_half(q) * sin, k * cos + _rotate_half(k) * sin, v
+
+    def prefill_layer(self, i: int, h: torch.Tensor, B: int, S: int, kc: torch.Tensor,
+                      vc: torch.Tensor) -> torch.Tensor:
+        """Layer i on every token of B sequences of S positions ([B*S, H]),
+        storing its keys and values in slots 0..B-1, positions 0..S-1."""
+        layer = self.layers[i]
+        attn = layer.self_attn
+        seq = torch.arange(S, device=h.device).repeat(B)
+        q, k, v = self._qkv(layer, h, seq)
+        nkv, d = k.shape[1], k.shape[2]
+        kc[:B, :, :S] = k.view(B, S, nkv, d).transpose(1, 2)
+        vc[:B, :, :S] = v.view(B, S, nkv, d).transpose(1, 2)
+        o = _attend(q, k, v, None, B, S, float(attn.scaling))
+        h = h + attn.o_proj(o)
+        return h + layer.mlp(layer.post_attention_layernorm(h))
+
+    def decode_layer(self, i: int, h: torch.Tensor, slots: torch.Tensor, pos: int,
+                     kc: torch.Tensor, vc: torch.Tensor, err: torch.Tensor) -> torch.Tensor:
+        """Layer i for one new token of each active row ([n, H]), whose
+        sequences sit in cache `slots` (int32) and have `pos` earlier
+        positions: its key and value are written at `pos`, attention reads
+        positions 0..pos of those slots only (tide_decode_attention)."""
+        from tide_b200 import _native
+
+        layer = self.layers[i]
+        attn = layer.self_attn
+        n = h.shape[0]
+        q, k, v = self._qkv(layer, h, torch.full((n,), pos, device=h.device, dtype=torch.long))
+        idx = slots.long()
+        kc[idx, :, pos] = k.to(kc.dtype)
+        vc[idx, :, pos] = v.to(vc.dtype)
+        o = torch.empty_like(q)
+        _native.ops().decode_attention(q.contiguous(), kc, vc, slots, o, pos + 1,
+                                       float(attn.scaling), err)
+        h = h + attn.o_proj(o.view(n, -1))
+        return h + layer.mlp(layer.post_attention_layernorm(h))
+
+
 class _GPT2Family:
     """GPT-2 blocks (fused c_attn, learned absolute positions)."""
 
@@ -202,3 +262,96 @@ def live_forward(runtime, input_ids: torch.Tensor, attention_mask: Optional[torc
         runtime._runner.norm_scatter(last, pos, out_buf, runtime._norm)
     runtime._runner.check_errors()
     return out_buf, stats, exit_layer
+
+
+class LiveDecoder:
+    """Decode with per-row early exit that skips layers: after each checkpoint
+    of a step, the later layers run only on the rows still active, their KV
+    slot ids compacted by the checkpoint kernel, and attention reads only those
+    slots (tide_decode_attention).  A row that exits leaves zeros in the cache
+    at that position for every later layer (the reference's "zero_pad",
+    python/TIDE/runtime.py:194-221).  Each row's logits come from its own exit
+    layer (final norm, lm_head); the rows that never exit take the model's
+    last layer, normalised as in the post-hoc path.  One host read-back per
+    checkpoint (the next layers' shapes).  Llama-family layers with a head
+    dimension of 128, bf16 or fp16."""
+
+    def __init__(self, runtime, n_slots: int, max_len: int):
+        fam = runtime._live_family()
+        if not isinstance(fam, _LlamaFamily) or fam.head_dim() != 128:
+            raise NotImplementedError("the live decoder takes Llama-family layers with head_dim 128")
+        self.rt, self.fam = runtime, fam
+        p = next(runtime.model.parameters())
+        if p.dtype not in (torch.bfloat16, torch.float16):
+            raise NotImplementedError("the live decoder takes bf16 or fp16 models")
+        shape = (n_slots, fam.kv_heads(), max_len, fam.head_dim())
+        self.k = [torch.zeros(shape, dtype=p.dtype, device=p.device) for _ in fam.layers]
+        self.v = [torch.zeros(shape, dtype=p.dtype, device=p.device) for _ in fam.layers]
+        self.n_slots, self.max_len, self.length = n_slots, max_len, 0
+        self.err = runtime._runner.error_word
+
+    def fill_random(self, length: int, generator: torch.Generator) -> None:
+        """Positions 0..length-1 of every slot hold N(0,1) keys and values."""
+        for kc, vc in zip(self.k, self.v):
+            for c in (kc, vc):
+                c[:, :, :length] = torch.randn(c[:, :, :length].shape, generator=generator,
+                                               device=c.device).to(c.dtype)
+        self.length = length
+
+    @torch.no_grad()
+    def prefill(self, input_ids: torch.Tensor) -> torch.Tensor:
+        """Every layer on the prompt (no exits), filling slots 0..B-1; returns
+        the last position's logits [B, V] (the model's own)."""
+        B, S = input_ids.shape
+        h = self.fam.embed_tokens(input_ids)
+        for i in range(len(self.fam.layers)):
+            h = self.fam.prefill_layer(i, h, B, S, self.k[i], self.v[i])
+        self.length = S
+        last = self.fam.norm(h.view(B, S, -1)[:, -1, :])
+        return self.rt._lm_head(last)
+
+    @torch.no_grad()
+    def step(self, tokens: torch.Tensor, stats=None) -> torch.Tensor:
+        """One decode step for tokens [B] (slot i holds sequence i): the next
+        logits [B, V].  `stats` (an ExitStats) gets this step's exits."""
+        rt, fam = self.rt, self.fam
+        B = tokens.shape[0]
+        pos = self.length
+        if pos >= self.max_len:
+            raise RuntimeError("the live decoder's cache is full")
+        dev = tokens.device
+        h = fam.embed_tokens(tokens.view(B, 1))
+        dtype = h.dtype
+        out_buf = torch.zeros(B, h.shape[1], dtype=dtype, device=dev)
+        rows = torch.arange(B, device=dev)
+        slots = torch.arange(B, device=dev, dtype=torch.int32)
+        routers = {L for L in rt.routers if L >= rt.config.min_layers}
+        counts = torch.zeros(2, dtype=torch.int32, device=dev)
+        exit_pos = torch.empty(B, dtype=torch.int64, device=dev)
+        self.last_exit_layer = torch.full((B,), -1, dtype=torch.int32, device=dev)
+        for i in range(len(fam.layers)):
+            h = fam.decode_layer(i, h, slots, pos, self.k[i], self.v[i], self.err)
+            if i not in routers:
+                continue
+            comp = torch.empty_like(h)
+            rows_out = torch.empty_like(rows)
+            slots_out = torch.empty_like(slots)
+            rt._runner.run(h, rt._router(i, dtype), rt._norm, rt.config.exit_threshold,
+                           positions=rows, slots=slots, out_buffer=out_buf, compact_out=comp,
+                           positions_out=rows_out, slots_out=slots_out,
+                           exit_positions_out=exit_pos, counts=counts)
+            n_surv, n_exit = (int(c) for c in counts.tolist())
+            if n_exit:
+                self.last_exit_layer.index_fill_(0, exit_pos[:n_exit], i)
+                if stats is not None:
+                    stats.exits_per_layer[i] = stats.exits_per_layer.get(i, 0) + n_exit
+            h, rows, slots = comp[:n_surv], rows_out[:n_surv], slots_out[:n_surv]
+            if n_surv == 0:
+                break
+        if h.shape[0]:
+            rt._runner.norm_scatter(fam.norm(h).contiguous(), rows, out_buf, rt._norm)
+        if stats is not None:
+            stats.total_tokens += B
+            stats.remaining_tokens += h.shape[0]
+        self.length += 1
+        return rt._lm_head(out_buf)

@@ -285,7 +285,8 @@ class TIDERuntime(nn.Module):
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 512,
                  temperature: float = 1.0, top_k: int = 50, top_p: float = 0.9,
-                 per_row_exit: bool = False, past_key_values=None, **kwargs) -> torch.Tensor:
+                 per_row_exit: bool = False, past_key_values=None, live: bool = False,
+                 **kwargs) -> torch.Tensor:
         """Autoregressive decode (runtime.py:223-313).  Every step runs all
         layers (the reference's post-hoc design).  With the reference's rule
         (default) the earliest checkpoint at which every row's score passes
@@ -299,13 +300,31 @@ class TIDERuntime(nn.Module):
         sampled token equals `eos_token_id` (default 2, the reference's fixed
         id, runtime.py:257).  `past_key_values`: a model cache that already
         holds the context (e.g. an HF StaticCache); the model then runs only
-        on input_ids[:, -1:] to start, instead of a prefill of input_ids."""
+        on input_ids[:, -1:] to start, instead of a prefill of input_ids.
+        With live=True each row exits on its own and the layers after its
+        exit are skipped for it (tide_b200.live.LiveDecoder: its own KV cache
+        addressed by slot, exited rows' later keys and values zero-padded);
+        Llama-family models with head_dim 128, bf16/fp16."""
         eos = kwargs.get("eos_token_id", 2)
         B = input_ids.shape[0]
         dev = input_ids.device
         n_layers = len(self._layers)
         generated = input_ids.clone()
         gen_stats = ExitStats(total_tokens=0)
+        if live:
+            from tide_b200.live import LiveDecoder
+
+            dec = LiveDecoder(self, B, input_ids.shape[1] + max_new_tokens + 1)
+            next_logits = dec.prefill(input_ids)
+            for _ in range(max_new_tokens):
+                nxt = sample_next_token(next_logits, temperature, top_k, top_p)
+                generated = torch.cat([generated, nxt], dim=-1)
+                if bool((nxt == eos).all()):
+                    break
+                next_logits = dec.step(nxt[:, 0], gen_stats)
+            self._runner.check_errors()
+            self.last_stats = gen_stats
+            return generated
         if past_key_values is None:
             pre = self.model(generated, use_cache=True, return_dict=True)
         else:
