@@ -698,13 +698,15 @@ def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
     151936, QK-norm), a decode batch of 256 sequences per rank whose KV cache
     holds 1024 positions of N(0,1) keys and values, routers at layers
     3, 7, ..., 31 whose biases exit ~10 % of the rows still active at each,
-    and 128 greedy tokens.  Timed three ways, each on its own copy of that
+    and 128 greedy tokens.  Timed four ways, each on its own copy of that
     cache: the live decoder with per-row exits (tide_b200.live.LiveDecoder:
-    after a row exits its later layers are skipped, the survivors' KV slot ids
-    compacted by the checkpoint kernel), the same decoder with no exit (every
-    checkpoint still runs), and the model's own greedy loop on HF's
-    DynamicCache (every layer for every row, as in the reference's decode).
-    tokens/s = batch * steps / time, summed over ranks."""
+    after a row exits its later attention and cache writes are skipped, the
+    survivors' KV slot ids compacted by the checkpoint kernel; each step one
+    CUDA graph replay), the same decoder launching its kernels one by one
+    (no graph), the graph decoder with no exit (every checkpoint still
+    runs), and the model's own greedy loop on HF's DynamicCache (every layer
+    for every row, as in the reference's decode).  tokens/s = batch * steps
+    / time, summed over ranks."""
     from transformers import DynamicCache, Qwen3Config, Qwen3ForCausalLM
 
     from tide_b200 import TIDEConfig
@@ -779,13 +781,14 @@ def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
         engine = TIDERuntime(model, tmp / "router.pt",
                              config=TIDEConfig(exit_threshold=THRESHOLD, min_layers=0))
 
-        def live_run(threshold: float, stats):
+        def live_run(threshold: float, stats, graph: bool = True):
             engine.config.exit_threshold = threshold
-            dec = LiveDecoder(engine, batch, ctx + steps + 8)
+            dec = LiveDecoder(engine, batch, ctx + steps + 8, graph=graph)
             dec.fill_random(ctx, torch.Generator(device=dev).manual_seed(SEED + 17 + rank))
             tok = tok0
-            for _ in range(3):  # warm-up steps
+            for _ in range(3):  # warm-up steps (the first records the step's graph)
                 tok = dec.step(tok).argmax(-1)
+            dec.read_stats(ExitStats())
 
             def loop():
                 t = tok
@@ -793,14 +796,13 @@ def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
                     t = dec.step(t, stats).argmax(-1)
 
             t_run = timed(loop)
+            dec.read_stats(stats if stats is not None else ExitStats())
             del dec
             torch.cuda.empty_cache()
             return t_run
 
-        st_live = ExitStats()
-        t_live = live_run(THRESHOLD, st_live)
-        t_noexit = live_run(2.0, None)  # scores lie in [0, 1]: no row exits
-        engine.config.exit_threshold = THRESHOLD
+        # the model's own loop first, on a fresh allocator (its cache grows
+        # by concatenation every step)
         cache = DynamicCache(config=cfg)
         g = torch.Generator(device=dev).manual_seed(SEED + 17 + rank)
         for li in range(cfg.num_hidden_layers):
@@ -816,15 +818,23 @@ def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
                 t = model(t, past_key_values=cache, use_cache=True).logits[:, -1, :].argmax(-1, keepdim=True)
 
         t_hf = timed(hf_loop)
+        del cache
+        torch.cuda.empty_cache()
+        st_live = ExitStats()
+        t_live = live_run(THRESHOLD, st_live)
+        t_eager = live_run(THRESHOLD, None, graph=False)
+        t_noexit = live_run(2.0, None)  # scores lie in [0, 1]: no row exits
+        engine.config.exit_threshold = THRESHOLD
         stats = tdist.global_stats(world, st_live, layers)
     tokens = world * batch * steps
     res.update({"live_tok_s": tokens / t_live, "live_ms_per_step": 1000 * t_live / steps,
+                "live_eager_tok_s": tokens / t_eager, "live_eager_ms_per_step": 1000 * t_eager / steps,
                 "live_no_exit_tok_s": tokens / t_noexit, "live_no_exit_ms_per_step": 1000 * t_noexit / steps,
                 "hf_greedy_tok_s": tokens / t_hf, "hf_ms_per_step": 1000 * t_hf / steps,
                 "hf_cache": "DynamicCache (HF's StaticCache measured 193 ms per step here)",
                 "live_exit_rate": stats.exit_rate,
                 "live_exits_per_layer": {str(k): v for k, v in sorted(stats.exits_per_layer.items())}})
-    del engine, model, cache
+    del engine, model
     torch.cuda.empty_cache()
     return res
 

@@ -170,11 +170,47 @@ int tide_norm_at_positions(int dtype, int norm_type, const void *src, const int6
  * other (the "zero_pad" K/V policy of python/TIDE/runtime.py:194-221).  It
  * replaces, for the rows that have not exited, the attention of the HF model
  * call inside the reference's decode loop (runtime.py:266-273).  A slot
- * outside [0, n_slots) skips its row and sets TIDE_DEVERR_POSITION. */
+ * outside [0, n_slots) skips its row and sets TIDE_DEVERR_POSITION.
+ * n_rows_dev (optional, device int32): only rows below it are computed (the
+ * live count a checkpoint wrote).  length_dev (optional, device int32): the
+ * length is read from the device, clamped to [1, length]; `length` then only
+ * bounds it (shared memory is sized for it).  Both keep a decode step free of
+ * host values, so it can be captured in a CUDA graph. */
 int tide_decode_attention(int dtype, const void *q, const void *k_cache, const void *v_cache,
-                          const int32_t *slots, void *out, int64_t n_rows, int64_t n_q_heads,
-                          int64_t n_kv_heads, int64_t head_dim, int64_t n_slots, int64_t max_len,
-                          int64_t length, float scale, int32_t *error_word, tide_stream_t stream);
+                          const int32_t *slots, void *out, int64_t n_rows,
+                          const int32_t *n_rows_dev, int64_t n_q_heads, int64_t n_kv_heads,
+                          int64_t head_dim, int64_t n_slots, int64_t max_len, int64_t length,
+                          const int32_t *length_dev, float scale, int32_t *error_word,
+                          tide_stream_t stream);
+
+/* Append one decode position to a KV cache addressed by slot:
+ *   K[slots[i], h, pos, :] = k_new[i, h, :],  V[...] = v_new[i, h, :]
+ * for i below the live row count (*n_rows_dev clamped to [0, n_rows]; n_rows
+ * when NULL) and pos = *position_dev when given, else `position`.  k_new,
+ * v_new [n_rows, n_kv_heads, 128]; caches as tide_decode_attention's.  A
+ * position outside [0, max_len) or a slot outside [0, n_slots) writes
+ * nothing for the rows concerned and sets TIDE_DEVERR_POSITION.  With the
+ * checkpoint's compacted slot ids it stores the keys and values of the rows
+ * still active in a decode step; an exited row's entry at that position
+ * keeps the zeros it was created with (the reference's "zero_pad",
+ * python/TIDE/runtime.py:194-221). */
+int tide_kv_append(int dtype, const void *k_new, const void *v_new, const int32_t *slots,
+                   const int32_t *n_rows_dev, int64_t n_rows, int64_t n_kv_heads,
+                   int64_t head_dim, void *k_cache, void *v_cache, int64_t n_slots,
+                   int64_t max_len, int64_t position, const int32_t *position_dev,
+                   int32_t *error_word, tide_stream_t stream);
+
+/* tide_norm_scatter with the row count on the device:
+ *   output_buffer[positions[i]] = final_norm(rows[i]),  i < *n_rows_dev
+ * (clamped to [0, n_rows]; n_rows when NULL).  The finalize step
+ * (python/TIDE/scheduler.py:102-120) for survivors whose count a checkpoint
+ * left on the device.  A position outside [0, n_total) skips its row and
+ * sets TIDE_DEVERR_POSITION. */
+int tide_norm_scatter_rows(int dtype, int norm_type, const void *rows, const int64_t *positions,
+                           const int32_t *n_rows_dev, int64_t n_rows, int64_t hidden_dim,
+                           int64_t n_total, void *output_buffer, const float *norm_weight,
+                           const float *norm_bias, float eps, int32_t *error_word,
+                           tide_stream_t stream);
 
 /* ---- router preparation (once per router) ------------------------------ */
 

@@ -127,6 +127,34 @@ def test_decode_attention_matches_torch(G, L):
     torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
 
 
+def test_decode_attention_reads_row_count_and_length_from_the_device():
+    """n_rows_dev: rows at and past it are left alone; length_dev: the length
+    read on the device (clamped to [1, length]) against the torch reference
+    at that length."""
+    from tide_b200 import _native
+
+    ops = _native.ops()
+    n, hkv, G, d, n_slots, max_len = 37, 2, 4, 128, 40, 1100
+    g = torch.Generator(device=DEV).manual_seed(77)
+    kc = torch.randn(n_slots, hkv, max_len, d, generator=g, device=DEV).to(torch.bfloat16)
+    vc = torch.randn(n_slots, hkv, max_len, d, generator=g, device=DEV).to(torch.bfloat16)
+    q = torch.randn(n, G * hkv, d, generator=g, device=DEV).to(torch.bfloat16)
+    slots = torch.randperm(n_slots, generator=torch.Generator().manual_seed(3))[:n]
+    slots = slots.to(torch.int32).to(DEV)
+    scale = d ** -0.5
+    for live, L in [(20, 300), (0, 5), (37, 1025), (1, 1)]:
+        out = torch.full_like(q, 5.0)
+        n_dev = torch.tensor([live], dtype=torch.int32, device=DEV)
+        len_dev = torch.tensor([L], dtype=torch.int32, device=DEV)
+        ops.decode_attention(q, kc, vc, slots, out, 1025, scale, None, n_dev, len_dev)
+        K = kc[slots.long(), :, :L].float().repeat_interleave(G, dim=1)
+        V = vc[slots.long(), :, :L].float().repeat_interleave(G, dim=1)
+        p = torch.softmax(torch.einsum("nhd,nhld->nhl", q.float(), K) * scale, dim=-1)
+        ref = torch.einsum("nhl,nhld->nhd", p, V)
+        torch.testing.assert_close(out[:live].float(), ref[:live], atol=2e-2, rtol=2e-2)
+        assert torch.all(out[live:] == 5.0)
+
+
 def test_decode_attention_flags_a_slot_outside_the_cache():
     from tide_b200 import _native
 
@@ -152,11 +180,13 @@ def _qwen3_hd128():
     return Qwen3ForCausalLM(cfg).to(DEV, torch.bfloat16).eval()
 
 
-def test_live_decoder_first_step_matches_posthoc(tmp_path):
+@pytest.mark.parametrize("graph", [False, True])
+def test_live_decoder_first_step_matches_posthoc(tmp_path, graph):
     """One decode step of the live decoder (layers skipped per row after its
     exit) against the post-hoc chain on the model's own hidden states: on the
     first step a row's computation up to its exit reads only its own cache,
-    so both give the same logits and exit layers (bf16, within tolerance)."""
+    so both give the same logits and exit layers (bf16, within tolerance).
+    With graph=True the step is the replay of its captured CUDA graph."""
     from tide_b200.live import LiveDecoder
     from tide_b200.scheduler import ExitStats
 
@@ -166,15 +196,16 @@ def test_live_decoder_first_step_matches_posthoc(tmp_path):
     tuned_routers(tmp_path / "router.pt", model, ids, [1, 2], [0.3, 0.3], 0.6)
     rt = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.6,
                                                                        min_layers=0))
-    dec = LiveDecoder(rt, B, S + 4)
+    dec = LiveDecoder(rt, B, S + 4, graph=graph)
     with torch.no_grad():
         first = dec.prefill(ids)
         pre = model(ids, use_cache=True)
     torch.testing.assert_close(first.float(), pre.logits[:, -1].float(), atol=5e-2, rtol=5e-2)
     nxt = first.argmax(-1)
     st = ExitStats()
-    live_logits = dec.step(nxt, st)
+    live_logits = dec.step(nxt, st).clone()
     live_exit = dec.last_exit_layer.clone()
+    dec.read_stats(st)
     with torch.no_grad():
         out = model(nxt[:, None], past_key_values=pre.past_key_values, use_cache=True,
                     output_hidden_states=True)
@@ -206,3 +237,134 @@ def test_generate_live_skips_layers_per_row(tmp_path):
     st = rt.last_stats
     assert st.total_tokens == 4 * 6 and st.total_exited + st.remaining_tokens == st.total_tokens
     assert st.total_exited > 0
+
+
+def _decoder_case(tmp_path, B=5, S=9):
+    model = _qwen3_hd128()
+    ids = torch.randint(0, 512, (B, S), generator=torch.Generator().manual_seed(29)).to(DEV)
+    tuned_routers(tmp_path / "router.pt", model, ids, [1, 2], [0.35, 0.35], 0.6)
+    rt = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.6,
+                                                                       min_layers=0))
+    return model, rt, ids
+
+
+def test_live_decoder_graph_replays_the_eager_step(tmp_path):
+    """Four decode steps, captured once and replayed, against the same steps
+    launched kernel by kernel: the same logits, exit layers and caches, and
+    the exit counts read back once agree."""
+    from tide_b200.live import LiveDecoder
+    from tide_b200.scheduler import ExitStats
+
+    model, rt, ids = _decoder_case(tmp_path)
+    B, S = ids.shape
+    runs = []
+    for graph in (False, True):
+        dec = LiveDecoder(rt, B, S + 6, graph=graph)
+        st = ExitStats()
+        with torch.no_grad():
+            tok = dec.prefill(ids).argmax(-1)
+            logits, layers = [], []
+            for _ in range(4):
+                lg = dec.step(tok, st)
+                logits.append(lg.float().clone())
+                layers.append(dec.last_exit_layer.clone())
+                tok = lg.argmax(-1)
+        dec.read_stats(st)
+        runs.append((logits, layers, st, dec))
+    (l0, e0, s0, d0), (l1, e1, s1, d1) = runs
+    for a, b in zip(l0, l1):
+        torch.testing.assert_close(a, b, atol=1e-3, rtol=1e-3)
+    for a, b in zip(e0, e1):
+        assert torch.equal(a, b)
+    assert s0.total_tokens == s1.total_tokens == 4 * B
+    assert s0.exits_per_layer == s1.exits_per_layer and s0.remaining_tokens == s1.remaining_tokens
+    assert s1.total_exited + s1.remaining_tokens == 4 * B and s1.total_exited > 0
+    for i in range(len(d0.k)):
+        torch.testing.assert_close(d0.k[i].float(), d1.k[i].float(), atol=1e-3, rtol=1e-3)
+
+
+def test_live_decoder_zero_pads_the_layers_after_an_exit(tmp_path):
+    """After a step, a row that exited at layer e holds this position's key
+    and value in the caches of layers 0..e and zeros above (the reference's
+    "zero_pad"); a row that never exited holds them in every layer."""
+    from tide_b200.live import LiveDecoder
+    from tide_b200.scheduler import ExitStats
+
+    model, rt, ids = _decoder_case(tmp_path, B=8)
+    B, S = ids.shape
+    dec = LiveDecoder(rt, B, S + 4, graph=True)
+    st = ExitStats()
+    with torch.no_grad():
+        tok = dec.prefill(ids).argmax(-1)
+        dec.step(tok, st)
+    dec.read_stats(st)
+    exit_layer = dec.last_exit_layer.cpu().tolist()
+    assert any(e >= 0 for e in exit_layer)
+    n_layers = len(dec.k)
+    for r, e in enumerate(exit_layer):
+        top = n_layers - 1 if e < 0 else e
+        for i in range(n_layers):
+            written = bool(dec.k[i][r, :, S].abs().sum() > 0) and bool(dec.v[i][r, :, S].abs().sum() > 0)
+            assert written == (i <= top), (r, e, i)
+
+
+def test_kv_append_writes_the_live_rows_at_the_device_position():
+    from tide_b200 import _native
+
+    ops = _native.ops()
+    n, hkv, d, n_slots, max_len = 11, 3, 128, 16, 20
+    g = torch.Generator(device=DEV).manual_seed(5)
+    kn = torch.randn(n, hkv, d, generator=g, device=DEV).to(torch.float16)
+    vn = torch.randn(n, hkv, d, generator=g, device=DEV).to(torch.float16)
+    slots = torch.randperm(n_slots, generator=torch.Generator().manual_seed(1))[:n].to(torch.int32).to(DEV)
+    kc = torch.zeros(n_slots, hkv, max_len, d, dtype=torch.float16, device=DEV)
+    vc = torch.zeros_like(kc)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    live, pos = 7, 13
+    ops.kv_append(kn, vn, slots, torch.tensor([live], dtype=torch.int32, device=DEV), kc, vc, 0,
+                  torch.tensor([pos], dtype=torch.int32, device=DEV), err)
+    ek, ev = torch.zeros_like(kc), torch.zeros_like(vc)
+    ek[slots[:live].long(), :, pos] = kn[:live]
+    ev[slots[:live].long(), :, pos] = vn[:live]
+    assert torch.equal(kc, ek) and torch.equal(vc, ev) and int(err.item()) == 0
+    ops.kv_append(kn, vn, slots, None, kc, vc, 0, torch.tensor([max_len], dtype=torch.int32,
+                                                              device=DEV), err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & 1 and torch.equal(kc, ek)  # a position past the cache: nothing written
+
+
+@pytest.mark.parametrize("dtype,kind", [(torch.bfloat16, "rms"), (torch.float16, "layer"),
+                                        (torch.float32, "rms")])
+def test_norm_scatter_rows_with_a_device_count(dtype, kind):
+    """output[positions[i]] = final_norm(rows[i]) for i below the device count,
+    against the oracle's norm scatter of those rows (<= 1 ulp of the output
+    type); rows past the count leave the buffer alone."""
+    from tide_b200 import _native
+    from tide_b200.capi import NORM_LAYER, NORM_RMS
+
+    ops = _native.ops()
+    n, H, total, live = 40, 768, 64, 23
+    g = torch.Generator().manual_seed(8)
+    rows = torch.randn(n, H, generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(H, generator=g)).float()
+    b = (0.1 * torch.randn(H, generator=g)).float() if kind == "layer" else None
+    pos = torch.randperm(total, generator=g)[:n]
+    out = torch.full((total, H), 7.0, dtype=dtype)
+    ref = out.clone()
+    dt = TORCH2O[dtype]
+    norm = {"kind": kind, "weight": w.numpy(), "bias": None if b is None else b.numpy(), "eps": 1e-5}
+    normed = O.from_f32(O.final_norm(O.to_f32(storage_np(rows[:live]), dt), norm), dt)
+    if dt == O.BF16:
+        ref[pos[:live]] = torch.from_numpy(normed.view(np.int16)).view(torch.bfloat16)
+    else:
+        ref[pos[:live]] = torch.from_numpy(normed)
+    dev_out = out.to(DEV)
+    ops.norm_scatter_rows(rows.to(DEV), pos.to(DEV), torch.tensor([live], dtype=torch.int32, device=DEV),
+                          dev_out, w.to(DEV), None if b is None else b.to(DEV),
+                          NORM_LAYER if kind == "layer" else NORM_RMS, 1e-5, None)
+    got = dev_out.cpu()
+    untouched = sorted(set(range(total)) - set(pos[:live].tolist()))
+    assert torch.equal(got[untouched], out[untouched])
+    ulp = torch.finfo(dtype).eps  # 1 ulp (16-bit), 8 ulp (fp32: another summation order)
+    k = 8 if dtype == torch.float32 else 1
+    torch.testing.assert_close(got.float(), ref.float(), atol=4 * k * ulp, rtol=k * ulp)

@@ -47,8 +47,12 @@ PROTOTYPES = {
     "tide_gather_rows": (C.c_int, [C.c_int, p, i64, p, p, i64, i64, p, p, p]),
     "tide_norm_at_positions": (C.c_int, [C.c_int, C.c_int, p, p, p, i64, i64, i64, p, p, p, f32,
                                          p, p]),
-    "tide_decode_attention": (C.c_int, [C.c_int, p, p, p, p, p, i64, i64, i64, i64, i64, i64, i64,
-                                        f32, p, p]),
+    "tide_decode_attention": (C.c_int, [C.c_int, p, p, p, p, p, i64, p, i64, i64, i64, i64, i64,
+                                        i64, p, f32, p, p]),
+    "tide_kv_append": (C.c_int, [C.c_int, p, p, p, p, i64, i64, i64, p, p, i64, i64, i64, p,
+                                 p, p]),
+    "tide_norm_scatter_rows": (C.c_int, [C.c_int, C.c_int, p, p, p, i64, i64, i64, p, p, p, f32,
+                                         p, p]),
     "tide_router_fold": (C.c_int, [C.c_int, p, p, p, i64, i64, p, p, p, p, p]),
     "tide_checkpoint_workspace_size": (sz, [C.POINTER(CheckpointArgs)]),
     "tide_checkpoint": (C.c_int, [C.POINTER(CheckpointArgs), p]),

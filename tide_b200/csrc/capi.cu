@@ -88,14 +88,19 @@ template <typename T, bool VEC> struct ScatterLaunch {
 };
 
 template <typename T, bool VEC> struct IndexedLaunch {
+  // norm: 0 gather, 1 norm in place at idx, 2 norm scatter (src row i to idx[i])
   static void run(const void *src, const int64_t *idx, const int32_t *n_dev, int64_t n_cap,
-                  int64_t H, int64_t n_src, void *dst, bool norm, int norm_type, const float *w,
+                  int64_t H, int64_t n_src, void *dst, int norm, int norm_type, const float *w,
                   const float *b, float eps, int32_t *err, cudaStream_t s) {
     const int warps_per_block = 8;
     int64_t blocks = (n_cap + warps_per_block - 1) / warps_per_block;
     if (blocks > 148 * 16) blocks = 148 * 16;  // grid-stride beyond 16 blocks per SM
     if (blocks < 1) blocks = 1;
-    if (norm)
+    if (norm == 2)
+      tide::indexed_rows_kernel<T, VEC, true, true><<<(unsigned)blocks, 32 * warps_per_block, 0, s>>>(
+          static_cast<const T *>(src), idx, n_dev, n_cap, H, n_src, static_cast<T *>(dst),
+          norm_type, w, b, eps, err);
+    else if (norm)
       tide::indexed_rows_kernel<T, VEC, true><<<(unsigned)blocks, 32 * warps_per_block, 0, s>>>(
           static_cast<const T *>(src), idx, n_dev, n_cap, H, n_src, static_cast<T *>(dst),
           norm_type, w, b, eps, err);
@@ -286,7 +291,7 @@ int tide_gather_rows(int dtype, const void *src, int64_t n_src, const int64_t *i
   if (!src || !index || !dst) return fail(TIDE_ERR_INVALID, "gather_rows: NULL pointer");
   const bool vec = rows_vectorizable(dtype, hidden_dim, {src, dst});
   dispatch_rows<IndexedLaunch>(dtype, vec, src, index, n_rows_dev, n_rows, hidden_dim, n_src, dst,
-                               false, (int)TIDE_NORM_RMS, (const float *)nullptr,
+                               0, (int)TIDE_NORM_RMS, (const float *)nullptr,
                                (const float *)nullptr, 0.f, error_word, (cudaStream_t)stream);
   return check_launch("gather_rows");
 }
@@ -306,10 +311,31 @@ int tide_norm_at_positions(int dtype, int norm_type, const void *src, const int6
     return fail(TIDE_ERR_INVALID, "norm_at_positions: NULL pointer");
   const bool vec = rows_vectorizable(dtype, hidden_dim, {src, output_buffer});
   dispatch_rows<IndexedLaunch>(dtype, vec, src, positions, n_rows_dev, n_rows, hidden_dim, n_total,
-                               output_buffer, true, norm_type, norm_weight,
+                               output_buffer, 1, norm_type, norm_weight,
                                norm_type == TIDE_NORM_LAYER ? norm_bias : (const float *)nullptr,
                                eps, error_word, (cudaStream_t)stream);
   return check_launch("norm_at_positions");
+}
+
+int tide_norm_scatter_rows(int dtype, int norm_type, const void *rows, const int64_t *positions,
+                           const int32_t *n_rows_dev, int64_t n_rows, int64_t hidden_dim,
+                           int64_t n_total, void *output_buffer, const float *norm_weight,
+                           const float *norm_bias, float eps, int32_t *error_word,
+                           tide_stream_t stream) {
+  if (!valid_dtype(dtype)) return fail(TIDE_ERR_INVALID, "norm_scatter_rows: bad dtype %d", dtype);
+  if (norm_type != TIDE_NORM_RMS && norm_type != TIDE_NORM_LAYER)
+    return fail(TIDE_ERR_INVALID, "norm_scatter_rows: bad norm_type %d", norm_type);
+  if (n_rows < 0 || n_total < 0 || hidden_dim <= 0)
+    return fail(TIDE_ERR_INVALID, "norm_scatter_rows: bad sizes");
+  if (n_rows == 0) return TIDE_OK;
+  if (!rows || !positions || !output_buffer || !norm_weight)
+    return fail(TIDE_ERR_INVALID, "norm_scatter_rows: NULL pointer");
+  const bool vec = rows_vectorizable(dtype, hidden_dim, {rows, output_buffer});
+  dispatch_rows<IndexedLaunch>(dtype, vec, rows, positions, n_rows_dev, n_rows, hidden_dim, n_total,
+                               output_buffer, 2, norm_type, norm_weight,
+                               norm_type == TIDE_NORM_LAYER ? norm_bias : (const float *)nullptr,
+                               eps, error_word, (cudaStream_t)stream);
+  return check_launch("norm_scatter_rows");
 }
 
 int tide_router_fold(int fold_dtype, const float *down, const float *norm_weight,

@@ -1,5 +1,6 @@
 // Decode attention over a KV cache addressed by slot, for the rows still
-// active after the early-exit checkpoints of a decode step.
+// active after the early-exit checkpoints of a decode step, and the append of
+// a step's keys and values to that cache.
 //
 // The checkpoint kernels compact the surviving rows of a step together with
 // their KV slot ids; the layers after a checkpoint then run on those rows
@@ -14,154 +15,454 @@
 //   o[i, h, :] = sum_j softmax_j(scale * q[i, h, :] . K[s_i, h / G, j, :]) V[s_i, h / G, j, :]
 //   for j in [0, L), s_i = slots[i], G = query heads per KV head.
 //
-// One CTA per (active row, KV head), 128 threads, head_dim 128.  Pass 1:
-// every thread scores whole key rows (256 bytes each, positions t, t+128, ...)
-// against the G query heads held in shared memory, keeping the scores in
-// shared memory.  Pass 2: max and sum per query head.  Pass 3: warp g owns
-// query head g (G <= 4) or two of them (G = 8), each lane four output
-// dimensions, and walks the value rows once (a warp reads a 256-byte value
-// row per position).  fp32 throughout; output in the cache's 16-bit type.
+// Split over the positions (flash decoding): a thread-block cluster of S CTAs
+// per (active row, KV head), CTA s taking the blocks of 128 positions s,
+// s + S, s + 2S, ...  A CTA (128 threads) walks its blocks with a running
+// maximum and sum per query head:
+//   scores   on the tensor cores (mma.sync m16n8k16, 16-bit operands, fp32
+//            accumulators): the G query heads as the rows of A, 8 key rows
+//            as B, four tiles per warp; a key row comes in as four 16-byte
+//            loads by the four lanes that hold it in B;
+//   softmax  one warp per query head: block maximum, rescale factor, the
+//            block's probabilities and their sum;
+//   P V      warp w takes 32 consecutive positions of the block, each lane
+//            four output dimensions of all G heads; a warp reads one 256-byte
+//            value row per position from shared memory.
+// The S partial results (running max m_s, sum l_s, unnormalised output a_s)
+// are combined through distributed shared memory: after a cluster barrier
+// CTA r computes its share of the G*128 outputs as
+//   o = sum_s e^(m_s - M) a_s / sum_s e^(m_s - M) l_s,   M = max_s m_s,
+// and a second barrier keeps every CTA's shared memory alive until all have
+// read it.  Exponentials are base 2 on log2(e)-scaled scores.  fp32
+// throughout; output in the cache's 16-bit type.
+//
+// Loads: a block's keys and the query go to registers (16 + 4 loads of 16
+// bytes per lane, all issued before the first is used) and its values to
+// shared memory by one bulk copy (32 KB), so that a block is fetched in one
+// round trip; a CTA's next block is requested after its P V.  The wait for the values is bounded: on expiry the
+// kernel raises TIDE_DEVERR_TIMEOUT and still meets its cluster's barriers.
+//
+// The active row count and the length may live on the device (a
+// checkpoint's counts, the decode position), so that a decode step needs no
+// host value and can be captured in a CUDA graph.  Rows at or past the live
+// count return at once, so the attention of a step costs what its active
+// rows read.
+#include <cooperative_groups.h>
 #include <math.h>
 #include <stdio.h>
 
+#include <type_traits>
+
 #include "common.cuh"
+#include "tc_ptx.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tide {
 
 namespace dattn {
-constexpr int kD = 128;
-constexpr int kThreads = 128;
-constexpr int kMaxG = 8;
+constexpr int kD = 128;        // head dimension
+constexpr int kThreads = 128;  // 4 warps
+constexpr int kBlock = 128;    // positions per block
+constexpr int kMaxSplit = 8;   // CTAs per cluster (portable cluster size)
+#ifndef TIDE_DATTN_MIN_BLOCKS
+#define TIDE_DATTN_MIN_BLOCKS 3
+#endif
+constexpr int kMinBlocks = TIDE_DATTN_MIN_BLOCKS;  // resident CTAs per SM the registers allow
+#ifndef TIDE_DATTN_TARGET_CTAS
+#define TIDE_DATTN_TARGET_CTAS 2368
+#endif
+constexpr int64_t kTargetCtas = TIDE_DATTN_TARGET_CTAS;  // grid size the split aims at
+constexpr float kLog2e = 1.4426950408889634f;
 }  // namespace dattn
 
+__device__ __forceinline__ uint4 ld_nc16(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Tensor-core tile of the scores: D[16 x 8] += A[16 x 16] * B[16 x 8],
+// A = query heads (rows; G <= 8 real, the rest zero), B = 8 key rows,
+// 16-bit operands, fp32 accumulators (mma.sync m16n8k16).
 template <typename T>
-__global__ void __launch_bounds__(dattn::kThreads)
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                          uint32_t b1) {
+  if constexpr (std::is_same<T, __half>::value)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+template <typename T, int G>
+__global__ void __launch_bounds__(dattn::kThreads, dattn::kMinBlocks)
     decode_attention_kernel(const T *__restrict__ q, const T *__restrict__ kc,
                             const T *__restrict__ vc, const int32_t *__restrict__ slots,
-                            T *__restrict__ o, int n_rows, int hq, int hkv, int64_t n_slots,
-                            int64_t max_len, int L, float scale, int32_t *err) {
+                            T *__restrict__ o, int n_rows, const int32_t *__restrict__ n_dev,
+                            int hq, int hkv, int64_t n_slots, int64_t max_len, int Lmax,
+                            const int32_t *__restrict__ len_dev, float scale, int32_t *err) {
   using namespace dattn;
-  extern __shared__ float sm[];
-  const int G = hq / hkv;
-  float *s_q = sm;                 // [G][128]
-  float *s_p = sm + G * kD;        // [G][L] scores, then probabilities
-  __shared__ float s_red[kMaxG][4];
-  __shared__ float s_max[kMaxG], s_sum[kMaxG];
-  const int row = blockIdx.x / hkv, kvh = blockIdx.x % hkv;
+  extern __shared__ __align__(128) unsigned char dyn_smem[];
+  T *s_v = reinterpret_cast<T *>(dyn_smem);        // [128 positions][128]: the block's values
+  __shared__ __align__(16) float s_p[G][kBlock];   // block scores, then probabilities
+  __shared__ __align__(16) float s_a[4][G][kD];    // per-warp partial outputs; [0] = the CTA's
+  __shared__ float s_m[G], s_l[G], s_alpha[G];
+  __shared__ __align__(8) uint64_t bar_v;
+  __shared__ int s_abort;
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = (int)cluster.num_blocks();
+  const int split = (int)cluster.block_rank();
+  const int64_t unit = (int64_t)blockIdx.x / S;  // row * hkv + kv head
+  const int row = (int)(unit / hkv), kvh = (int)(unit % hkv);
+  // Every early return below depends on (row, kv head) only, so a whole
+  // cluster leaves together and no CTA waits at a barrier for one that left.
   if (row >= n_rows) return;
+  if (n_dev && row >= __ldg(n_dev)) return;  // past the live row count
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t slot = slots ? (int64_t)slots[row] : row;
+  const int64_t slot = slots ? (int64_t)__ldg(slots + row) : row;
   if (slot < 0 || slot >= n_slots) {  // a slot outside the cache: the row is skipped
-    if (threadIdx.x == 0) raise_error(err, TIDE_DEVERR_POSITION);
+    if (tid == 0 && split == 0) raise_error(err, TIDE_DEVERR_POSITION);
     return;
   }
+  const int L = len_dev ? min(max(__ldg(len_dev), 1), Lmax) : Lmax;
   const T *kb = kc + ((slot * hkv + kvh) * max_len) * kD;
   const T *vb = vc + ((slot * hkv + kvh) * max_len) * kD;
-  for (int i = tid; i < G * kD; i += kThreads)
-    s_q[i] = Elem<T>::to_f(q[((int64_t)row * hq + kvh * G) * kD + i]) * scale;
-  __syncthreads();
 
-  // pass 1: scores
-  float mx[kMaxG];
+  if (tid == 0) {
+    ptx::mbar_init(&bar_v, 1);
+    ptx::fence_mbar_init();
+    s_abort = 0;
+  }
+  if (tid < G) {
+    s_m[tid] = -INFINITY;
+    s_l[tid] = 0.f;
+  }
+  __syncthreads();
+  const uint64_t pol = l2_evict_first_policy();  // the cache is read once per step
+  auto load_values = [&](int b) {
+    const uint32_t bytes = (uint32_t)min(kBlock, L - b) * kD * (uint32_t)sizeof(T);
+    ptx::mbar_expect_tx(&bar_v, bytes);
+    ptx::bulk_load(s_v, vb + (int64_t)b * kD, bytes, &bar_v, pol);
+  };
+  // Keys: lane (n = lane / 4, t = lane % 4) of warp w holds, for n-tile it,
+  // 32 dims of block position w*32 + it*8 + n as four 16-byte chunks, chunk c
+  // = dims (c*4 + t)*8 .. +8.  They are the B fragments of the score tiles:
+  // k-step 2c + h takes the chunk's words 2h and 2h+1.  The query's A
+  // fragments use the same dims for row n (query head n < G), so each tile's
+  // k order is a permutation shared by both operands.
+  const int t4 = lane & 3, n8 = lane >> 2;
+  uint4 kv[4][4];
+  auto load_keys = [&](int b) {
+    const int nb = min(kBlock, L - b);
 #pragma unroll
-  for (int g = 0; g < kMaxG; ++g) mx[g] = -INFINITY;
-  for (int j = tid; j < L; j += kThreads) {
-    const uint4 *kr = reinterpret_cast<const uint4 *>(kb + (int64_t)j * kD);
-    float acc[kMaxG];
+    for (int it = 0; it < 4; ++it) {
+      const int t = warp * 32 + it * 8 + n8;
+      if (t < nb) {
+        const T *kr = kb + (int64_t)(b + t) * kD;
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) acc[g] = 0.f;
-#pragma unroll 4
-    for (int c = 0; c < kD / 8; ++c) {
-      const uint4 v = kr[c];
-      float f[8];
-      unpack16<T>(v, f);
+        for (int c = 0; c < 4; ++c) kv[it][c] = ld_nc16(kr + (c * 4 + t4) * 8);
+      } else {
 #pragma unroll
-      for (int g = 0; g < kMaxG; ++g) {
-        if (g >= G) break;
-        const float *qg = s_q + g * kD + c * 8;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[g] = fmaf(qg[e], f[e], acc[g]);
+        for (int c = 0; c < 4; ++c) kv[it][c] = make_uint4(0, 0, 0, 0);
       }
     }
+  };
+  // one round trip for a block: the values by bulk copy, the keys and the
+  // query to registers
+  if (tid == 0 && split * kBlock < L) load_values(split * kBlock);
+  if (split * kBlock < L) load_keys(split * kBlock);
+  uint4 qf[4];
+  if (n8 < G) {
+    const T *qr = q + ((int64_t)row * hq + kvh * G + n8) * kD;
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
-      if (g >= G) break;
-      s_p[g * L + j] = acc[g];
-      mx[g] = fmaxf(mx[g], acc[g]);
-    }
+    for (int c = 0; c < 4; ++c) qf[c] = *reinterpret_cast<const uint4 *>(qr + (c * 4 + t4) * 8);
+  } else {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) qf[c] = make_uint4(0, 0, 0, 0);
   }
-  // pass 2: max and sum per query head
-#pragma unroll
-  for (int g = 0; g < kMaxG; ++g) {
-    if (g >= G) break;
-    float m = mx[g];
-    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if (lane == 0) s_red[g][warp] = m;
-  }
-  __syncthreads();
-  if (tid < G) s_max[tid] = fmaxf(fmaxf(s_red[tid][0], s_red[tid][1]), fmaxf(s_red[tid][2], s_red[tid][3]));
-  __syncthreads();
-  float sum[kMaxG];
-#pragma unroll
-  for (int g = 0; g < kMaxG; ++g) sum[g] = 0.f;
-  for (int j = tid; j < L; j += kThreads) {
-#pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
-      if (g >= G) break;
-      const float e = __expf(s_p[g * L + j] - s_max[g]);
-      s_p[g * L + j] = e;
-      sum[g] += e;
-    }
-  }
-#pragma unroll
-  for (int g = 0; g < kMaxG; ++g) {
-    if (g >= G) break;
-    float sg = sum[g];
-    for (int off = 16; off; off >>= 1) sg += __shfl_xor_sync(0xffffffffu, sg, off);
-    if (lane == 0) s_red[g][warp] = sg;
-  }
-  __syncthreads();
-  if (tid < G) s_sum[tid] = (s_red[tid][0] + s_red[tid][1]) + (s_red[tid][2] + s_red[tid][3]);
-  __syncthreads();
+  const float qs = scale * kLog2e;
+  uint32_t phase = 0;
+  int late_phase = -1;  // the phase of a wait that expired, if any
 
-  // pass 3: o = P V; warp w serves query heads w, w + 4 (G = 8), lane four dims
-  for (int g = warp; g < G; g += kThreads / 32) {
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    const float *pg = s_p + g * L;
-#pragma unroll 4
-    for (int j = 0; j < L; ++j) {
-      const uint2 v = *reinterpret_cast<const uint2 *>(vb + (int64_t)j * kD + lane * 4);
-      const T *e4 = reinterpret_cast<const T *>(&v);
-      float f[4];
+  float acc[G][4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) f[e] = Elem<T>::to_f(e4[e]);
-      const float pj = pg[j];
-      a0 = fmaf(pj, f[0], a0);
-      a1 = fmaf(pj, f[1], a1);
-      a2 = fmaf(pj, f[2], a2);
-      a3 = fmaf(pj, f[3], a3);
+  for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
+
+  // blocks split, split + S, ... of 128 positions (none when S exceeds the
+  // block count: that CTA's partial result is empty)
+  for (int b0 = split * kBlock; b0 < L; b0 += S * kBlock) {
+    const int nb = min(kBlock, L - b0);
+    // scores: four 16 x 8 tiles per warp, eight k-steps each
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        mma_16816<T>(d, qf[c].x, qf[c].y, kv[it][c].x, kv[it][c].y);
+        mma_16816<T>(d, qf[c].z, qf[c].w, kv[it][c].z, kv[it][c].w);
+      }
+      // d[0], d[1]: head n8 at block positions w*32 + it*8 + 2*t4 + {0, 1}
+      if (n8 < G) {
+        const int t = warp * 32 + it * 8 + 2 * t4;
+        *reinterpret_cast<float2 *>(&s_p[n8][t]) =
+            make_float2(t < nb ? d[0] * qs : -INFINITY, t + 1 < nb ? d[1] * qs : -INFINITY);
+      }
     }
-    const float inv = 1.0f / s_sum[g];
-    T *og = o + ((int64_t)row * hq + kvh * G + g) * kD + lane * 4;
-    og[0] = Elem<T>::from_f(a0 * inv);
-    og[1] = Elem<T>::from_f(a1 * inv);
-    og[2] = Elem<T>::from_f(a2 * inv);
-    og[3] = Elem<T>::from_f(a3 * inv);
+    __syncthreads();
+    // softmax of the block, one warp per query head
+    for (int g = warp; g < G; g += kThreads / 32) {
+      float v[4], mx = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[k] = s_p[g][lane + 32 * k];
+        mx = fmaxf(mx, v[k]);
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_old = s_m[g];
+      const float m_new = fmaxf(m_old, mx);  // finite: the block holds a position
+      float sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float p = exp2f(v[k] - m_new);  // -inf (past the range) -> 0
+        s_p[g][lane + 32 * k] = p;
+        sum += p;
+      }
+      sum = warp_sum(sum);
+      __syncwarp();
+      if (lane == 0) {
+        const float alpha = exp2f(m_old - m_new);  // 0 on the first block
+        s_alpha[g] = alpha;
+        s_l[g] = s_l[g] * alpha + sum;
+        s_m[g] = m_new;
+      }
+    }
+    __syncthreads();
+    // P V: warp w takes block positions w*32 .. w*32+31, each lane four
+    // output dimensions of all G heads
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float a = s_alpha[g];
+      acc[g][0] *= a;
+      acc[g][1] *= a;
+      acc[g][2] *= a;
+      acc[g][3] *= a;
+    }
+    // the block's values in shared memory (bounded wait; on expiry the
+    // error is raised and the block's output is not to be used)
+    if (!ptx::mbar_wait(&bar_v, phase, &s_abort)) {
+      if (lane == 0) raise_error(err, TIDE_DEVERR_TIMEOUT);
+      s_abort = 1;
+      late_phase = (int)phase;
+    }
+    phase ^= 1u;
+    const int p0 = warp * 32, p1 = min(nb, p0 + 32);
+    for (int t0 = p0; t0 < p1; t0 += 4) {
+      float4 pg[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) pg[g] = *reinterpret_cast<const float4 *>(&s_p[g][t0]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (t0 + u < p1) {
+          const uint2 vv = *reinterpret_cast<const uint2 *>(s_v + (t0 + u) * kD + lane * 4);
+          const T *e4 = reinterpret_cast<const T *>(&vv);
+          const float f0 = Elem<T>::to_f(e4[0]), f1 = Elem<T>::to_f(e4[1]);
+          const float f2 = Elem<T>::to_f(e4[2]), f3 = Elem<T>::to_f(e4[3]);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float p = u == 0 ? pg[g].x : u == 1 ? pg[g].y : u == 2 ? pg[g].z : pg[g].w;
+            acc[g][0] = fmaf(p, f0, acc[g][0]);
+            acc[g][1] = fmaf(p, f1, acc[g][1]);
+            acc[g][2] = fmaf(p, f2, acc[g][2]);
+            acc[g][3] = fmaf(p, f3, acc[g][3]);
+          }
+        }
+      }
+    }
+    __syncthreads();  // s_p, s_alpha and the values are rewritten by the next block
+    if (b0 + S * kBlock < L) {
+      if (tid == 0) load_values(b0 + S * kBlock);
+      load_keys(b0 + S * kBlock);
+    }
+  }
+
+  if (late_phase >= 0 && tid == 0) {  // a copy may still be landing: wait for it once more
+    volatile int none = 0;
+    ptx::mbar_wait(&bar_v, (uint32_t)late_phase, &none);
+  }
+  // this CTA's unnormalised output: sum of the four warps' partials
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+    *reinterpret_cast<float4 *>(&s_a[warp][g][lane * 4]) =
+        make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+    s_a[0][g][tid] = (s_a[0][g][tid] + s_a[1][g][tid]) + (s_a[2][g][tid] + s_a[3][g][tid]);
+
+  cluster.sync();  // every CTA's m, l and output are in its shared memory
+  constexpr int kOut = G * kD;
+  const int share = (kOut + S - 1) / S;
+  const int e_end = min(kOut, (split + 1) * share);
+  for (int e = split * share + tid; e < e_end; e += kThreads) {
+    const int g = e / kD, d = e % kD;
+    float m[kMaxSplit], l[kMaxSplit], a[kMaxSplit];
+#pragma unroll
+    for (int r = 0; r < kMaxSplit; ++r) {  // independent remote reads, issued together
+      if (r < S) {
+        m[r] = cluster.map_shared_rank(&s_m[0], r)[g];
+        l[r] = cluster.map_shared_rank(&s_l[0], r)[g];
+        a[r] = cluster.map_shared_rank(&s_a[0][0][0], r)[g * kD + d];
+      } else {
+        m[r] = -INFINITY;
+        l[r] = a[r] = 0.f;
+      }
+    }
+    float M = m[0];  // CTA 0 always holds block 0: finite
+#pragma unroll
+    for (int r = 1; r < kMaxSplit; ++r) M = fmaxf(M, m[r]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxSplit; ++r) {
+      const float w = exp2f(m[r] - M);  // a CTA without positions: 0
+      den = fmaf(w, l[r], den);
+      num = fmaf(w, a[r], num);
+    }
+    o[((int64_t)row * hq + kvh * G + g) * kD + d] = Elem<T>::from_f(num / den);
+  }
+  cluster.sync();  // no CTA leaves while another still reads its shared memory
+}
+
+// Append one decode position: k/v_new [n_rows, hkv, 128] go to
+// cache[slots[i], :, pos, :] for i below the live row count.  One warp per
+// (row, KV head), 8 bytes per lane.
+template <typename T>
+__global__ void kv_append_kernel(const T *__restrict__ k_new, const T *__restrict__ v_new,
+                                 const int32_t *__restrict__ slots, const int32_t *__restrict__ n_dev,
+                                 int64_t n_rows, int hkv, T *__restrict__ kc, T *__restrict__ vc,
+                                 int64_t n_slots, int64_t max_len, int64_t pos,
+                                 const int32_t *__restrict__ pos_dev, int32_t *err) {
+  const int lane = threadIdx.x & 31;
+  int64_t live = n_rows;
+  if (n_dev) live = min((int64_t)max(__ldg(n_dev), 0), n_rows);
+  const int64_t p = pos_dev ? (int64_t)__ldg(pos_dev) : pos;
+  if (p < 0 || p >= max_len) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && live > 0) raise_error(err, TIDE_DEVERR_POSITION);
+    return;
+  }
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); w < live * hkv;
+       w += warps) {
+    const int64_t i = w / hkv;
+    const int h = (int)(w % hkv);
+    const int64_t slot = slots ? (int64_t)slots[i] : i;
+    if (slot < 0 || slot >= n_slots) {
+      if (lane == 0) raise_error(err, TIDE_DEVERR_POSITION);
+      continue;
+    }
+    const int64_t src = (i * hkv + h) * dattn::kD + lane * 4;
+    const int64_t dst = ((slot * hkv + h) * max_len + p) * dattn::kD + lane * 4;
+    *reinterpret_cast<uint2 *>(kc + dst) = *reinterpret_cast<const uint2 *>(k_new + src);
+    *reinterpret_cast<uint2 *>(vc + dst) = *reinterpret_cast<const uint2 *>(v_new + src);
   }
 }
+
+void set_last_error(const char *msg);
 
 }  // namespace tide
 
-namespace tide {
-void set_last_error(const char *msg);
+namespace {
+
+template <typename T, int G>
+cudaError_t launch_attention(const void *q, const void *k_cache, const void *v_cache,
+                             const int32_t *slots, void *out, int64_t n_rows,
+                             const int32_t *n_rows_dev, int hq, int hkv, int64_t n_slots,
+                             int64_t max_len, int length, const int32_t *length_dev, float scale,
+                             int32_t *error_word, int splits, cudaStream_t s) {
+  const size_t dyn = tide::dattn::kBlock * tide::dattn::kD * sizeof(T);
+  static bool attr_set = false;  // per instantiation: static + dynamic exceed 48 KB at G = 8
+  if (!attr_set) {
+    const cudaError_t e = cudaFuncSetAttribute(tide::decode_attention_kernel<T, G>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)dyn);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(n_rows * hkv * splits), 1, 1);
+  cfg.blockDim = dim3(tide::dattn::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = dyn;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, tide::decode_attention_kernel<T, G>, static_cast<const T *>(q),
+                            static_cast<const T *>(k_cache), static_cast<const T *>(v_cache),
+                            slots, static_cast<T *>(out), (int)n_rows, n_rows_dev, hq, hkv,
+                            n_slots, max_len, length, length_dev, scale, error_word);
 }
+
+template <typename T>
+cudaError_t launch_attention_g(int G, const void *q, const void *k_cache, const void *v_cache,
+                               const int32_t *slots, void *out, int64_t n_rows,
+                               const int32_t *n_rows_dev, int hq, int hkv, int64_t n_slots,
+                               int64_t max_len, int length, const int32_t *length_dev,
+                               float scale, int32_t *error_word, int splits, cudaStream_t s) {
+  switch (G) {
+    case 1:
+      return launch_attention<T, 1>(q, k_cache, v_cache, slots, out, n_rows, n_rows_dev, hq, hkv,
+                                    n_slots, max_len, length, length_dev, scale, error_word,
+                                    splits, s);
+    case 2:
+      return launch_attention<T, 2>(q, k_cache, v_cache, slots, out, n_rows, n_rows_dev, hq, hkv,
+                                    n_slots, max_len, length, length_dev, scale, error_word,
+                                    splits, s);
+    case 4:
+      return launch_attention<T, 4>(q, k_cache, v_cache, slots, out, n_rows, n_rows_dev, hq, hkv,
+                                    n_slots, max_len, length, length_dev, scale, error_word,
+                                    splits, s);
+    default:
+      return launch_attention<T, 8>(q, k_cache, v_cache, slots, out, n_rows, n_rows_dev, hq, hkv,
+                                    n_slots, max_len, length, length_dev, scale, error_word,
+                                    splits, s);
+  }
+}
+
+int report(cudaError_t e, const char *what) {
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString(e));
+    tide::set_last_error(buf);
+    return TIDE_ERR_CUDA;
+  }
+  return TIDE_OK;
+}
+
+}  // namespace
 
 extern "C" int tide_decode_attention(int dtype, const void *q, const void *k_cache,
                                      const void *v_cache, const int32_t *slots, void *out,
-                                     int64_t n_rows, int64_t n_q_heads, int64_t n_kv_heads,
-                                     int64_t head_dim, int64_t n_slots, int64_t max_len,
-                                     int64_t length, float scale, int32_t *error_word,
-                                     tide_stream_t stream) {
+                                     int64_t n_rows, const int32_t *n_rows_dev,
+                                     int64_t n_q_heads, int64_t n_kv_heads, int64_t head_dim,
+                                     int64_t n_slots, int64_t max_len, int64_t length,
+                                     const int32_t *length_dev, float scale,
+                                     int32_t *error_word, tide_stream_t stream) {
   using namespace tide;
   if (dtype != TIDE_DTYPE_BF16 && dtype != TIDE_DTYPE_F16) {
     tide::set_last_error("decode_attention: dtype must be bf16 or fp16");
@@ -171,10 +472,12 @@ extern "C" int tide_decode_attention(int dtype, const void *q, const void *k_cac
     tide::set_last_error("decode_attention: head_dim must be 128");
     return TIDE_ERR_UNSUPPORTED;
   }
+  const int64_t G = n_kv_heads > 0 ? n_q_heads / n_kv_heads : 0;
   if (n_rows < 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads != 0 ||
-      n_q_heads / n_kv_heads > dattn::kMaxG || length < 1 || length > max_len || n_slots < 1 ||
-      (!slots && n_rows > n_slots)) {
-    tide::set_last_error("decode_attention: bad sizes (heads, length)");
+      (G != 1 && G != 2 && G != 4 && G != 8) || length < 1 || length > max_len ||
+      length > INT32_MAX || n_slots < 1 || (!slots && n_rows > n_slots) ||
+      n_rows * n_kv_heads * dattn::kMaxSplit > INT32_MAX) {
+    tide::set_last_error("decode_attention: bad sizes (heads: G of 1, 2, 4 or 8; length)");
     return TIDE_ERR_INVALID;
   }
   if (n_rows == 0) return TIDE_OK;
@@ -182,39 +485,73 @@ extern "C" int tide_decode_attention(int dtype, const void *q, const void *k_cac
     tide::set_last_error("decode_attention: NULL pointer");
     return TIDE_ERR_INVALID;
   }
-  const int G = (int)(n_q_heads / n_kv_heads);
-  const size_t smem = (size_t)G * (dattn::kD + (size_t)length) * sizeof(float);
-  if (smem > 200 * 1024) {
-    tide::set_last_error("decode_attention: length too long for the scores in shared memory");
-    return TIDE_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+       reinterpret_cast<uintptr_t>(q)) & 15) {
+    tide::set_last_error("decode_attention: q and the caches must be 16-byte aligned");
+    return TIDE_ERR_INVALID;
   }
-  const int64_t grid = n_rows * n_kv_heads;
+  // Positions split over a cluster of up to 8 CTAs (at most one per block of
+  // 128): as few as keep about kTargetCtas CTAs in the grid, since every
+  // CTA pays a fixed cost (its first round trip, the cluster combine).
+  const int64_t blocks = (length + dattn::kBlock - 1) / dattn::kBlock;
+  const int64_t units = n_rows * n_kv_heads;
+  int64_t splits = dattn::kTargetCtas > 0 ? (dattn::kTargetCtas + units - 1) / units : blocks;
+  if (splits > blocks) splits = blocks;
+  if (splits > dattn::kMaxSplit) splits = dattn::kMaxSplit;
+  if (splits < 1) splits = 1;
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;
-  if (dtype == TIDE_DTYPE_BF16) {
-    e = cudaFuncSetAttribute(decode_attention_kernel<__nv_bfloat16>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e == cudaSuccess)
-      decode_attention_kernel<__nv_bfloat16><<<(unsigned)grid, dattn::kThreads, smem, s>>>(
-          static_cast<const __nv_bfloat16 *>(q), static_cast<const __nv_bfloat16 *>(k_cache),
-          static_cast<const __nv_bfloat16 *>(v_cache), slots, static_cast<__nv_bfloat16 *>(out),
-          (int)n_rows, (int)n_q_heads, (int)n_kv_heads, n_slots, max_len, (int)length, scale,
-          error_word);
-  } else {
-    e = cudaFuncSetAttribute(decode_attention_kernel<__half>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e == cudaSuccess)
-      decode_attention_kernel<__half><<<(unsigned)grid, dattn::kThreads, smem, s>>>(
-          static_cast<const __half *>(q), static_cast<const __half *>(k_cache),
-          static_cast<const __half *>(v_cache), slots, static_cast<__half *>(out), (int)n_rows,
-          (int)n_q_heads, (int)n_kv_heads, n_slots, max_len, (int)length, scale, error_word);
+  if (dtype == TIDE_DTYPE_BF16)
+    e = launch_attention_g<__nv_bfloat16>((int)G, q, k_cache, v_cache, slots, out, n_rows,
+                                          n_rows_dev, (int)n_q_heads, (int)n_kv_heads, n_slots,
+                                          max_len, (int)length, length_dev, scale, error_word,
+                                          (int)splits, s);
+  else
+    e = launch_attention_g<__half>((int)G, q, k_cache, v_cache, slots, out, n_rows, n_rows_dev,
+                                   (int)n_q_heads, (int)n_kv_heads, n_slots, max_len, (int)length,
+                                   length_dev, scale, error_word, (int)splits, s);
+  return report(e, "decode_attention");
+}
+
+extern "C" int tide_kv_append(int dtype, const void *k_new, const void *v_new,
+                              const int32_t *slots, const int32_t *n_rows_dev, int64_t n_rows,
+                              int64_t n_kv_heads, int64_t head_dim, void *k_cache, void *v_cache,
+                              int64_t n_slots, int64_t max_len, int64_t position,
+                              const int32_t *position_dev, int32_t *error_word,
+                              tide_stream_t stream) {
+  using namespace tide;
+  if (dtype != TIDE_DTYPE_BF16 && dtype != TIDE_DTYPE_F16) {
+    tide::set_last_error("kv_append: dtype must be bf16 or fp16");
+    return TIDE_ERR_UNSUPPORTED;
   }
-  if (e == cudaSuccess) e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    char buf[256];
-    snprintf(buf, sizeof(buf), "decode_attention: %s", cudaGetErrorString(e));
-    tide::set_last_error(buf);
-    return TIDE_ERR_CUDA;
+  if (head_dim != dattn::kD) {
+    tide::set_last_error("kv_append: head_dim must be 128");
+    return TIDE_ERR_UNSUPPORTED;
   }
-  return TIDE_OK;
+  if (n_rows < 0 || n_kv_heads <= 0 || n_slots < 1 || max_len < 1 ||
+      (!position_dev && (position < 0 || position >= max_len)) || (!slots && n_rows > n_slots)) {
+    tide::set_last_error("kv_append: bad sizes or position");
+    return TIDE_ERR_INVALID;
+  }
+  if (n_rows == 0) return TIDE_OK;
+  if (!k_new || !v_new || !k_cache || !v_cache) {
+    tide::set_last_error("kv_append: NULL pointer");
+    return TIDE_ERR_INVALID;
+  }
+  const int64_t warps = n_rows * n_kv_heads;
+  int64_t blocks = (warps + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == TIDE_DTYPE_BF16)
+    kv_append_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16 *>(k_new), static_cast<const __nv_bfloat16 *>(v_new),
+        slots, n_rows_dev, n_rows, (int)n_kv_heads, static_cast<__nv_bfloat16 *>(k_cache),
+        static_cast<__nv_bfloat16 *>(v_cache), n_slots, max_len, position, position_dev,
+        error_word);
+  else
+    kv_append_kernel<__half><<<(unsigned)blocks, 256, 0, s>>>(
+        static_cast<const __half *>(k_new), static_cast<const __half *>(v_new), slots, n_rows_dev,
+        n_rows, (int)n_kv_heads, static_cast<__half *>(k_cache), static_cast<__half *>(v_cache),
+        n_slots, max_len, position, position_dev, error_word);
+  return report(cudaSuccess, "kv_append");
 }

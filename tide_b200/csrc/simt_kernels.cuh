@@ -471,11 +471,13 @@ __global__ void scatter_rows_kernel(const T *__restrict__ src, const int32_t *__
 // ------------------------------------------------------- indexed rows
 // Rows addressed through an index with a live count kept on the device, so
 // that checkpoints chain without reading the count back:
-//   gather (NORM = false):       dst[i] = src[idx[i]]
-//   norm in place (NORM = true): dst[idx[i]] = final_norm(src[idx[i]])
-// for i < live, live = *n_dev clamped to [0, n_cap] (n_cap without n_dev).
-// One warp per row, grid-stride over the capacity.
-template <typename T, bool VEC, bool NORM>
+//   gather (NORM = false):                 dst[i] = src[idx[i]]
+//   norm in place (NORM, SRC_I = false):   dst[idx[i]] = final_norm(src[idx[i]])
+//   norm scatter (NORM, SRC_I = true):     dst[idx[i]] = final_norm(src[i])
+// for i < live, live = *n_dev clamped to [0, n_cap] (n_cap without n_dev);
+// idx[i] is checked against n_src.  One warp per row, grid-stride over the
+// capacity.
+template <typename T, bool VEC, bool NORM, bool SRC_I = false>
 __global__ void indexed_rows_kernel(const T *__restrict__ src, const int64_t *__restrict__ idx,
                                     const int32_t *__restrict__ n_dev, int64_t n_cap, int64_t H,
                                     int64_t n_src, T *__restrict__ dst, int norm_type,
@@ -497,7 +499,7 @@ __global__ void indexed_rows_kernel(const T *__restrict__ src, const int64_t *__
       if (lane == 0) raise_error(err, TIDE_DEVERR_POSITION);
       continue;
     }
-    const T *s = src + p * H;
+    const T *s = src + (SRC_I ? i : p) * H;
     if (!NORM) {
       copy_row<T, VEC>(s, dst + i * H, H, lane);
       continue;

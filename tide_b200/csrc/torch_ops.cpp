@@ -378,7 +378,9 @@ void norm_at_positions(const at::Tensor &src, const at::Tensor &positions,
 
 void decode_attention(const at::Tensor &q, const at::Tensor &k_cache, const at::Tensor &v_cache,
                       const std::optional<at::Tensor> &slots, const at::Tensor &out, int64_t length,
-                      double scale, const std::optional<at::Tensor> &error_word) {
+                      double scale, const std::optional<at::Tensor> &error_word,
+                      const std::optional<at::Tensor> &n_rows_dev,
+                      const std::optional<at::Tensor> &length_dev) {
   check_cuda_contig(q, "q");
   check_cuda_contig(k_cache, "k_cache");
   check_cuda_contig(v_cache, "v_cache");
@@ -398,12 +400,85 @@ void decode_attention(const at::Tensor &q, const at::Tensor &k_cache, const at::
   }
   if (error_word.has_value() && error_word->defined())
     TORCH_CHECK(error_word->is_cuda() && error_word->scalar_type() == at::kInt, "error_word must be int32");
+  for (const auto *t : {&n_rows_dev, &length_dev})
+    if (t->has_value() && (*t)->defined())
+      TORCH_CHECK((*t)->is_cuda() && (*t)->scalar_type() == at::kInt, "device counts must be int32");
   const c10::cuda::CUDAGuard guard(q.device());
   TIDE_CHECK_OK(tide_decode_attention(to_dtype(q.scalar_type(), "decode_attention"), q.data_ptr(),
                                       k_cache.data_ptr(), v_cache.data_ptr(), sl, out.data_ptr(),
-                                      q.size(0), q.size(1), k_cache.size(1), q.size(2),
-                                      k_cache.size(0), k_cache.size(2), length, (float)scale,
+                                      q.size(0), static_cast<const int32_t *>(opt_ptr(n_rows_dev)),
+                                      q.size(1), k_cache.size(1), q.size(2), k_cache.size(0),
+                                      k_cache.size(2), length,
+                                      static_cast<const int32_t *>(opt_ptr(length_dev)), (float)scale,
                                       static_cast<int32_t *>(opt_mut(error_word)), cur_stream(q)));
+}
+
+void norm_scatter_rows(const at::Tensor &rows, const at::Tensor &positions,
+                       const std::optional<at::Tensor> &n_rows_dev, const at::Tensor &output_buffer,
+                       const at::Tensor &norm_weight, const std::optional<at::Tensor> &norm_bias,
+                       int64_t norm_type, double eps, const std::optional<at::Tensor> &error_word) {
+  check_cuda_contig(rows, "rows");
+  check_cuda_contig(positions, "positions");
+  check_cuda_contig(output_buffer, "output_buffer");
+  check_cuda_contig(norm_weight, "norm_weight");
+  TORCH_CHECK(rows.dim() == 2 && output_buffer.dim() == 2 && rows.size(1) == output_buffer.size(1),
+              "rows [n, H] and output_buffer [N_total, H]");
+  TORCH_CHECK(rows.scalar_type() == output_buffer.scalar_type(), "rows/output_buffer dtype differ");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && positions.numel() >= rows.size(0),
+              "positions must be int64 with one entry per row");
+  const int64_t H = rows.size(1);
+  TORCH_CHECK(norm_weight.scalar_type() == at::kFloat && norm_weight.numel() == H,
+              "norm_weight must be fp32 [H]");
+  const float *nb = nullptr;
+  if (norm_bias.has_value() && norm_bias->defined()) {
+    check_cuda_contig(*norm_bias, "norm_bias");
+    TORCH_CHECK(norm_bias->scalar_type() == at::kFloat && norm_bias->numel() == H,
+                "norm_bias must be fp32 [H]");
+    nb = norm_bias->data_ptr<float>();
+  }
+  if (n_rows_dev.has_value() && n_rows_dev->defined())
+    TORCH_CHECK(n_rows_dev->is_cuda() && n_rows_dev->scalar_type() == at::kInt, "n_rows_dev must be int32");
+  const c10::cuda::CUDAGuard guard(rows.device());
+  TIDE_CHECK_OK(tide_norm_scatter_rows(to_dtype(rows.scalar_type(), "norm_scatter_rows"), (int)norm_type,
+                                       rows.data_ptr(), positions.data_ptr<int64_t>(),
+                                       static_cast<const int32_t *>(opt_ptr(n_rows_dev)), rows.size(0),
+                                       H, output_buffer.size(0), output_buffer.data_ptr(),
+                                       norm_weight.data_ptr<float>(), nb, (float)eps,
+                                       static_cast<int32_t *>(opt_mut(error_word)), cur_stream(rows)));
+}
+
+void kv_append(const at::Tensor &k_new, const at::Tensor &v_new, const std::optional<at::Tensor> &slots,
+               const std::optional<at::Tensor> &n_rows_dev, const at::Tensor &k_cache,
+               const at::Tensor &v_cache, int64_t position, const std::optional<at::Tensor> &position_dev,
+               const std::optional<at::Tensor> &error_word) {
+  check_cuda_contig(k_new, "k_new");
+  check_cuda_contig(v_new, "v_new");
+  check_cuda_contig(k_cache, "k_cache");
+  check_cuda_contig(v_cache, "v_cache");
+  TORCH_CHECK(k_new.dim() == 3 && v_new.sizes() == k_new.sizes(), "k_new, v_new must be [n, kv_heads, d]");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes(),
+              "caches must be [slots, kv_heads, max_len, head_dim]");
+  TORCH_CHECK(k_cache.size(1) == k_new.size(1) && k_cache.size(3) == k_new.size(2),
+              "kv_heads / head_dim differ");
+  TORCH_CHECK(k_new.scalar_type() == k_cache.scalar_type() && v_new.scalar_type() == k_cache.scalar_type() &&
+              v_cache.scalar_type() == k_cache.scalar_type(), "new rows and caches must share a dtype");
+  const int32_t *sl = nullptr;
+  if (slots.has_value() && slots->defined()) {
+    check_cuda_contig(*slots, "slots");
+    TORCH_CHECK(slots->scalar_type() == at::kInt && slots->numel() >= k_new.size(0),
+                "slots must be int32 with one entry per row");
+    sl = slots->data_ptr<int32_t>();
+  }
+  for (const auto *t : {&n_rows_dev, &position_dev, &error_word})
+    if (t->has_value() && (*t)->defined())
+      TORCH_CHECK((*t)->is_cuda() && (*t)->scalar_type() == at::kInt, "device words must be int32");
+  const c10::cuda::CUDAGuard guard(k_new.device());
+  TIDE_CHECK_OK(tide_kv_append(to_dtype(k_new.scalar_type(), "kv_append"), k_new.data_ptr(),
+                               v_new.data_ptr(), sl, static_cast<const int32_t *>(opt_ptr(n_rows_dev)),
+                               k_new.size(0), k_new.size(1), k_new.size(2), k_cache.data_ptr(),
+                               v_cache.data_ptr(), k_cache.size(0), k_cache.size(2), position,
+                               static_cast<const int32_t *>(opt_ptr(position_dev)),
+                               static_cast<int32_t *>(opt_mut(error_word)), cur_stream(k_new)));
 }
 
 // ---- router fold and fused checkpoint ----------------------------------
@@ -557,7 +632,13 @@ TORCH_LIBRARY(tide, m) {
         "Tensor(a!) output_buffer, Tensor norm_weight, Tensor? norm_bias, int norm_type, float eps, "
         "Tensor(b!)? error_word) -> ()");
   m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor? slots, Tensor(a!) out, "
-        "int length, float scale, Tensor(b!)? error_word) -> ()");
+        "int length, float scale, Tensor(b!)? error_word, Tensor? n_rows_dev=None, "
+        "Tensor? length_dev=None) -> ()");
+  m.def("norm_scatter_rows(Tensor rows, Tensor positions, Tensor? n_rows_dev, "
+        "Tensor(a!) output_buffer, Tensor norm_weight, Tensor? norm_bias, int norm_type, float eps, "
+        "Tensor(b!)? error_word) -> ()");
+  m.def("kv_append(Tensor k_new, Tensor v_new, Tensor? slots, Tensor? n_rows_dev, Tensor(a!) k_cache, "
+        "Tensor(b!) v_cache, int position, Tensor? position_dev, Tensor(c!)? error_word) -> ()");
   m.def("router_fold(Tensor down, Tensor norm_weight, Tensor? norm_bias, ScalarType fold_dtype) "
         "-> Tensor[]");
   m.def("checkpoint_workspace_size(int n_rows, int hidden_dim) -> int", &checkpoint_workspace_size);
@@ -580,6 +661,8 @@ TORCH_LIBRARY_IMPL(tide, CUDA, m) {
   m.impl("gather_rows", &gather_rows);
   m.impl("norm_at_positions", &norm_at_positions);
   m.impl("decode_attention", &decode_attention);
+  m.impl("norm_scatter_rows", &norm_scatter_rows);
+  m.impl("kv_append", &kv_append);
   m.impl("router_fold", &router_fold);
   m.impl("checkpoint", &checkpoint);
 }

@@ -136,24 +136,30 @@ class _LlamaFamily:
         h = h + attn.o_proj(o)
         return h + layer.mlp(layer.post_attention_layernorm(h))
 
-    def decode_layer(self, i: int, h: torch.Tensor, slots: torch.Tensor, pos: int,
-                     kc: torch.Tensor, vc: torch.Tensor, err: torch.Tensor) -> torch.Tensor:
-        """Layer i for one new token of each active row ([n, H]), whose
-        sequences sit in cache `slots` (int32) and have `pos` earlier
-        positions: its key and value are written at `pos`, attention reads
-        positions 0..pos of those slots only (tide_decode_attention)."""
+    def decode_layer(self, i: int, h: torch.Tensor, slots: torch.Tensor, n_live: torch.Tensor,
+                     pos: torch.Tensor, length: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor,
+                     err: torch.Tensor) -> torch.Tensor:
+        """Layer i for one new token of each row of h [B, H], of which the
+        first n_live (device int32 [1]) are active; their sequences sit in
+        cache `slots` (int32 [B]).  Their keys and values go to position
+        `pos` (device int32 [1]) of those slots (tide_kv_append); attention
+        reads positions [0, length) of those slots only (tide_decode_attention,
+        length = pos + 1 on the device).  Rows past n_live go through the
+        projections and the MLP (the GEMMs read the weights once whatever the
+        row count of a decode batch) but neither write the cache nor attend;
+        their outputs are not used."""
         from tide_b200 import _native
 
+        ops = _native.ops()
         layer = self.layers[i]
         attn = layer.self_attn
         n = h.shape[0]
-        q, k, v = self._qkv(layer, h, torch.full((n,), pos, device=h.device, dtype=torch.long))
-        idx = slots.long()
-        kc[idx, :, pos] = k.to(kc.dtype)
-        vc[idx, :, pos] = v.to(vc.dtype)
+        q, k, v = self._qkv(layer, h, pos.long().expand(n).contiguous())
+        ops.kv_append(k.to(kc.dtype).contiguous(), v.to(vc.dtype).contiguous(), slots, n_live,
+                      kc, vc, 0, pos, err)
         o = torch.empty_like(q)
-        _native.ops().decode_attention(q.contiguous(), kc, vc, slots, o, pos + 1,
-                                       float(attn.scaling), err)
+        ops.decode_attention(q.contiguous(), kc, vc, slots, o, kc.shape[2], float(attn.scaling),
+                             err, n_live, length)
         h = h + attn.o_proj(o.view(n, -1))
         return h + layer.mlp(layer.post_attention_layernorm(h))
 
@@ -264,6 +270,27 @@ def live_forward(runtime, input_ids: torch.Tensor, attention_mask: Optional[torc
     return out_buf, stats, exit_layer
 
 
+class _StepBuffers:
+    """The fixed-size device buffers of one decode step of B rows."""
+
+    def __init__(self, B: int, H: int, dtype: torch.dtype, dev: torch.device, checkpoints):
+        self.B = B
+        self.tokens = torch.zeros(B, dtype=torch.long, device=dev)
+        self.rows0 = torch.arange(B, dtype=torch.long, device=dev)
+        self.slots0 = torch.arange(B, dtype=torch.int32, device=dev)
+        self.n0 = torch.full((1,), B, dtype=torch.int32, device=dev)
+        self.out_buf = torch.zeros(B, H, dtype=dtype, device=dev)
+        self.exit_layer = torch.full((B + 1,), -1, dtype=torch.int32, device=dev)  # [B]: sink
+        self.ck = {i: (torch.empty(B, H, dtype=dtype, device=dev),           # compacted rows
+                       torch.empty(B, dtype=torch.long, device=dev),         # their positions
+                       torch.empty(B, dtype=torch.int32, device=dev),        # their KV slots
+                       torch.empty(B, dtype=torch.long, device=dev),         # exit positions
+                       torch.zeros(2, dtype=torch.int32, device=dev))        # {survivors, exits}
+                   for i in checkpoints}
+        self.graph = None
+        self.logits = None
+
+
 class LiveDecoder:
     """Decode with per-row early exit that skips layers: after each checkpoint
     of a step, the later layers run only on the rows still active, their KV
@@ -272,11 +299,20 @@ class LiveDecoder:
     at that position for every later layer (the reference's "zero_pad",
     python/TIDE/runtime.py:194-221).  Each row's logits come from its own exit
     layer (final norm, lm_head); the rows that never exit take the model's
-    last layer, normalised as in the post-hoc path.  One host read-back per
-    checkpoint (the next layers' shapes).  Llama-family layers with a head
-    dimension of 128, bf16 or fp16."""
+    last layer, normalised as in the post-hoc path.
 
-    def __init__(self, runtime, n_slots: int, max_len: int):
+    A step reads nothing back: the live row count stays on the device from
+    checkpoint to checkpoint (attention, the cache append and the final
+    scatter read it there), buffers keep the batch's size, and the decode
+    position is a device word.  The exit counts add up on the device until
+    read_stats().  So a step can be captured: with graph=True the first step
+    of a batch size is recorded as a CUDA graph and every later step replays
+    it (one launch per step).  Llama-family layers with a head dimension of
+    128, bf16 or fp16."""
+
+    def __init__(self, runtime, n_slots: int, max_len: int, graph: bool = False):
+        from tide_b200.ops import CheckpointRunner
+
         fam = runtime._live_family()
         if not isinstance(fam, _LlamaFamily) or fam.head_dim() != 128:
             raise NotImplementedError("the live decoder takes Llama-family layers with head_dim 128")
@@ -284,11 +320,31 @@ class LiveDecoder:
         p = next(runtime.model.parameters())
         if p.dtype not in (torch.bfloat16, torch.float16):
             raise NotImplementedError("the live decoder takes bf16 or fp16 models")
+        self.dev, self.dtype = p.device, p.dtype
         shape = (n_slots, fam.kv_heads(), max_len, fam.head_dim())
         self.k = [torch.zeros(shape, dtype=p.dtype, device=p.device) for _ in fam.layers]
         self.v = [torch.zeros(shape, dtype=p.dtype, device=p.device) for _ in fam.layers]
-        self.n_slots, self.max_len, self.length = n_slots, max_len, 0
-        self.err = runtime._runner.error_word
+        self.n_slots, self.max_len, self._length = n_slots, max_len, 0
+        self.pos = torch.zeros(1, dtype=torch.int32, device=p.device)
+        # its own checkpoint workspace and error word: a captured step keeps
+        # their addresses, which a prefill elsewhere must not reallocate
+        self.runner = CheckpointRunner(p.device)
+        self.err = self.runner.error_word
+        self.graph = graph
+        self._bufs = {}
+        self.exits_dev = torch.zeros(len(fam.layers), dtype=torch.int64, device=p.device)
+        self.remaining_dev = torch.zeros(1, dtype=torch.int64, device=p.device)
+        self.last_exit_layer = None
+
+    @property
+    def length(self) -> int:
+        """Positions held by every slot (the next token's position)."""
+        return self._length
+
+    @length.setter
+    def length(self, value: int) -> None:
+        self._length = int(value)
+        self.pos.fill_(self._length)
 
     def fill_random(self, length: int, generator: torch.Generator) -> None:
         """Positions 0..length-1 of every slot hold N(0,1) keys and values."""
@@ -310,48 +366,105 @@ class LiveDecoder:
         last = self.fam.norm(h.view(B, S, -1)[:, -1, :])
         return self.rt._lm_head(last)
 
+    def _checkpoints(self):
+        rt = self.rt
+        return sorted(L for L in rt.routers if L >= rt.config.min_layers)
+
+    def _body(self, b: _StepBuffers) -> torch.Tensor:
+        """One step on b.tokens; every shape fixed by the batch size."""
+        from tide_b200 import _native
+
+        rt, fam, B = self.rt, self.fam, b.B
+        norm = rt._norm
+        h = fam.embed_tokens(b.tokens.view(B, 1))
+        length = self.pos + 1
+        rows, slots, n_live = b.rows0, b.slots0, b.n0
+        b.exit_layer.fill_(-1)
+        thr = rt.config.exit_threshold
+        for i in range(len(fam.layers)):
+            h = fam.decode_layer(i, h, slots, n_live, self.pos, length, self.k[i], self.v[i],
+                                 self.err)
+            if i not in b.ck:
+                continue
+            comp, rows_out, slots_out, exit_pos, counts = b.ck[i]
+            self.runner.run(h, rt._router(i, self.dtype), norm, thr, positions=rows, slots=slots,
+                            n_rows_dev=n_live, out_buffer=b.out_buf, compact_out=comp,
+                            positions_out=rows_out, slots_out=slots_out,
+                            exit_positions_out=exit_pos, counts=counts)
+            # this checkpoint's exits: their layer, at their positions; the
+            # entries past the exit count point at the sink entry B
+            sink = torch.where(b.rows0 < counts[1], exit_pos, B)
+            b.exit_layer.index_fill_(0, sink, i)
+            self.exits_dev[i] += counts[1]
+            h, rows, slots, n_live = comp, rows_out, slots_out, counts[0:1]
+        # the rows that never exit: the model's last hidden state (its final
+        # norm applied, as HF reports it), final-normed once more
+        last = fam.norm(h).contiguous()
+        _native.ops().norm_scatter_rows(last, rows, n_live, b.out_buf, norm.weight, norm.bias,
+                                        norm.kind, norm.eps, self.err)
+        self.remaining_dev += n_live
+        self.pos += 1
+        return rt._lm_head(b.out_buf)
+
+    def _capture(self, b: _StepBuffers) -> None:
+        """Record b's step as a CUDA graph.  One eager step first (library
+        handles, workspaces, folded routers), on a side stream; its effects
+        are undone (the position's cache entries, the counters) before the
+        capture, which runs nothing."""
+        p = self._length
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            self._body(b)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        for kc, vc in zip(self.k, self.v):
+            kc[:, :, p].zero_()
+            vc[:, :, p].zero_()
+        self.length = p
+        self.exits_dev.zero_()
+        self.remaining_dev.zero_()
+        b.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(b.graph):
+            b.logits = self._body(b)
+
     @torch.no_grad()
     def step(self, tokens: torch.Tensor, stats=None) -> torch.Tensor:
         """One decode step for tokens [B] (slot i holds sequence i): the next
-        logits [B, V].  `stats` (an ExitStats) gets this step's exits."""
-        rt, fam = self.rt, self.fam
+        logits [B, V] (with graph=True, a buffer the next step overwrites).
+        `stats` (an ExitStats) counts the step's tokens; its exits stay on
+        the device until read_stats()."""
         B = tokens.shape[0]
-        pos = self.length
-        if pos >= self.max_len:
+        if self._length >= self.max_len:
             raise RuntimeError("the live decoder's cache is full")
-        dev = tokens.device
-        h = fam.embed_tokens(tokens.view(B, 1))
-        dtype = h.dtype
-        out_buf = torch.zeros(B, h.shape[1], dtype=dtype, device=dev)
-        rows = torch.arange(B, device=dev)
-        slots = torch.arange(B, device=dev, dtype=torch.int32)
-        routers = {L for L in rt.routers if L >= rt.config.min_layers}
-        counts = torch.zeros(2, dtype=torch.int32, device=dev)
-        exit_pos = torch.empty(B, dtype=torch.int64, device=dev)
-        self.last_exit_layer = torch.full((B,), -1, dtype=torch.int32, device=dev)
-        for i in range(len(fam.layers)):
-            h = fam.decode_layer(i, h, slots, pos, self.k[i], self.v[i], self.err)
-            if i not in routers:
-                continue
-            comp = torch.empty_like(h)
-            rows_out = torch.empty_like(rows)
-            slots_out = torch.empty_like(slots)
-            rt._runner.run(h, rt._router(i, dtype), rt._norm, rt.config.exit_threshold,
-                           positions=rows, slots=slots, out_buffer=out_buf, compact_out=comp,
-                           positions_out=rows_out, slots_out=slots_out,
-                           exit_positions_out=exit_pos, counts=counts)
-            n_surv, n_exit = (int(c) for c in counts.tolist())
-            if n_exit:
-                self.last_exit_layer.index_fill_(0, exit_pos[:n_exit], i)
-                if stats is not None:
-                    stats.exits_per_layer[i] = stats.exits_per_layer.get(i, 0) + n_exit
-            h, rows, slots = comp[:n_surv], rows_out[:n_surv], slots_out[:n_surv]
-            if n_surv == 0:
-                break
-        if h.shape[0]:
-            rt._runner.norm_scatter(fam.norm(h).contiguous(), rows, out_buf, rt._norm)
+        if B > self.n_slots:
+            raise ValueError("more rows than cache slots")
+        b = self._bufs.get(B)
+        if b is None:
+            H = self.fam.embed.embedding_dim
+            b = self._bufs[B] = _StepBuffers(B, H, self.dtype, self.dev, self._checkpoints())
+        b.tokens.copy_(tokens.reshape(B))
+        if self.graph:
+            if b.graph is None:
+                self._capture(b)
+            b.graph.replay()
+            logits = b.logits
+        else:
+            logits = self._body(b)
+        self._length += 1
+        self.last_exit_layer = b.exit_layer[:B]
         if stats is not None:
             stats.total_tokens += B
-            stats.remaining_tokens += h.shape[0]
-        self.length += 1
-        return rt._lm_head(out_buf)
+        return logits
+
+    def read_stats(self, stats) -> None:
+        """Add the exits and the never-exiting rows counted on the device
+        since the last call to `stats` (one read-back) and reset them; also
+        raises if a kernel flagged a device error."""
+        per_layer = self.exits_dev.tolist()
+        stats.remaining_tokens += int(self.remaining_dev.item())
+        for i, c in enumerate(per_layer):
+            if c:
+                stats.exits_per_layer[i] = stats.exits_per_layer.get(i, 0) + int(c)
+        self.exits_dev.zero_()
+        self.remaining_dev.zero_()
+        self.runner.check_errors()

@@ -303,7 +303,8 @@ class TIDERuntime(nn.Module):
         on input_ids[:, -1:] to start, instead of a prefill of input_ids.
         With live=True each row exits on its own and the layers after its
         exit are skipped for it (tide_b200.live.LiveDecoder: its own KV cache
-        addressed by slot, exited rows' later keys and values zero-padded);
+        addressed by slot, exited rows' later keys and values zero-padded,
+        each step one CUDA graph replay unless live_graph=False);
         Llama-family models with head_dim 128, bf16/fp16."""
         eos = kwargs.get("eos_token_id", 2)
         B = input_ids.shape[0]
@@ -314,7 +315,8 @@ class TIDERuntime(nn.Module):
         if live:
             from tide_b200.live import LiveDecoder
 
-            dec = LiveDecoder(self, B, input_ids.shape[1] + max_new_tokens + 1)
+            dec = LiveDecoder(self, B, input_ids.shape[1] + max_new_tokens + 1,
+                              graph=kwargs.get("live_graph", True))
             next_logits = dec.prefill(input_ids)
             for _ in range(max_new_tokens):
                 nxt = sample_next_token(next_logits, temperature, top_k, top_p)
@@ -322,6 +324,7 @@ class TIDERuntime(nn.Module):
                 if bool((nxt == eos).all()):
                     break
                 next_logits = dec.step(nxt[:, 0], gen_stats)
+            dec.read_stats(gen_stats)  # the one read-back of the exit counts
             self._runner.check_errors()
             self.last_stats = gen_stats
             return generated
