@@ -98,7 +98,7 @@ def test_operators_have_no_cpu_kernel():
 
 def test_path_selection():
     """bf16/fp16 with folded weights: up to a row count set per hidden size
-    from measured crossovers (3584 rows at H = 4096) the fused single-pass
+    from measured crossovers (5120 rows at H = 4096) the fused single-pass
     kernel when the router is 128 wide and a weight slice of H stays
     resident; above that, or when the fused kernel does not apply, the
     tensor-core split path (H % 64 == 0, B <= 256).  fp32 rows with folded
@@ -114,9 +114,9 @@ def test_path_selection():
         a = capi.CheckpointArgs(**base)
         return lib.tide_checkpoint_select_path(ctypes.byref(a))
 
-    assert sel() == capi.PATH_TC                               # up to 3584 rows: fused single pass
-    assert sel(n_rows=3584, n_total=3584) == capi.PATH_TC
-    assert sel(n_rows=3585, n_total=3585) == capi.PATH_TC_SPLIT
+    assert sel() == capi.PATH_TC                               # up to 5120 rows: fused single pass
+    assert sel(n_rows=5120, n_total=5120) == capi.PATH_TC
+    assert sel(n_rows=5121, n_total=5121) == capi.PATH_TC_SPLIT
     assert sel(n_rows=32768, n_total=32768) == capi.PATH_TC_SPLIT
     assert sel(dtype=capi.DTYPE_F16) == capi.PATH_TC
     assert sel(n_rows=32768, n_total=32768, dtype=capi.DTYPE_F16) == capi.PATH_TC_SPLIT
@@ -133,17 +133,18 @@ def test_path_selection():
     assert sel(bottleneck_dim=64) == capi.PATH_TC_SPLIT       # fused kernel: 128 units only
     assert sel(hidden_dim=8192, path=capi.PATH_TC) == capi.PATH_TC        # 16-CTA clusters, 8-chunk slices
     assert sel(hidden_dim=5120) == capi.PATH_TC                              # 16-CTA clusters, 5-chunk slices
-    assert sel(hidden_dim=5120, n_rows=2560, n_total=2560) == capi.PATH_TC
-    assert sel(hidden_dim=5120, n_rows=2561, n_total=2561) == capi.PATH_TC_SPLIT
-    assert sel(hidden_dim=8192, n_rows=5120, n_total=5120) == capi.PATH_TC
-    assert sel(hidden_dim=8192, n_rows=5121, n_total=5121) == capi.PATH_TC_SPLIT
-    assert sel(hidden_dim=768, n_rows=4608, n_total=4608) == capi.PATH_TC     # GPT-2 width: SIMT mover on the split path
-    assert sel(hidden_dim=768, n_rows=4609, n_total=4609) == capi.PATH_TC_SPLIT
-    assert sel(hidden_dim=1024, n_rows=1024, n_total=1024) == capi.PATH_TC
-    assert sel(hidden_dim=1024, n_rows=1025, n_total=1025) == capi.PATH_TC_SPLIT
-    assert sel(hidden_dim=2048, n_rows=2560, n_total=2560) == capi.PATH_TC
-    assert sel(hidden_dim=2048, n_rows=2561, n_total=2561) == capi.PATH_TC_SPLIT
-    assert sel(hidden_dim=512, n_rows=1025, n_total=1025) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=5120, n_rows=3584, n_total=3584) == capi.PATH_TC
+    assert sel(hidden_dim=5120, n_rows=3585, n_total=3585) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=8192, n_rows=5632, n_total=5632) == capi.PATH_TC
+    assert sel(hidden_dim=8192, n_rows=5633, n_total=5633) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=768, n_rows=8192, n_total=8192) == capi.PATH_TC     # GPT-2 width: SIMT mover on the split path
+    assert sel(hidden_dim=768, n_rows=8193, n_total=8193) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=1024, n_rows=128, n_total=128) == capi.PATH_TC_SPLIT  # 2 KB rows: split wins
+    assert sel(hidden_dim=1024, path=capi.PATH_TC) == capi.PATH_TC
+    assert sel(hidden_dim=2048, n_rows=4096, n_total=4096) == capi.PATH_TC
+    assert sel(hidden_dim=2048, n_rows=4097, n_total=4097) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=512, n_rows=128, n_total=128) == capi.PATH_TC_SPLIT
+    assert sel(hidden_dim=512, path=capi.PATH_TC) == capi.PATH_TC
     assert sel(hidden_dim=16384, path=capi.PATH_TC) == capi.PATH_TC_SPLIT  # slice too large to stay resident
     assert sel(hidden_dim=768, path=capi.PATH_TC) == capi.PATH_TC   # cluster of 2
     assert sel(path=capi.PATH_TC_SPLIT) == capi.PATH_TC_SPLIT

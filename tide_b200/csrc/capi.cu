@@ -386,9 +386,10 @@ int tide_checkpoint_select_path(const tide_checkpoint_args *a) {
     return -TIDE_ERR_UNSUPPORTED;
   }
   // automatic choice, from measured latencies: the fused single pass (one
-  // launch, ~21 us at 256 rows) up to a row count that depends on the hidden
-  // size (3584 rows at H <= 4096), the split path above it (its router
-  // streams all of W' through each CTA, a floor of ~38 us at H = 4096).
+  // launch, ~20 us at 256 rows) up to a row count that depends on the hidden
+  // size (5120 rows at H = 4096; none at H = 512 and 1024, where the split
+  // path wins from 128 rows), the split path above it (its router streams
+  // all of W' through each CTA, a floor of ~35 us at H = 4096).
   // SIMT otherwise.
   if (a->n_rows <= tide::fused_auto_max_rows(a->hidden_dim) && tide::fused_supported(a))
     return TIDE_PATH_TC;

@@ -39,8 +39,9 @@
 // Loads: a block's keys and the query go to registers (16 + 4 loads of 16
 // bytes per lane, all issued before the first is used) and its values to
 // shared memory by one bulk copy (32 KB), so that a block is fetched in one
-// round trip; a CTA's next block is requested after its P V.  The wait for the values is bounded: on expiry the
-// kernel raises TIDE_DEVERR_TIMEOUT and still meets its cluster's barriers.
+// round trip; a CTA's next block is requested after its P V.  The wait for
+// the values is bounded: on expiry the kernel raises TIDE_DEVERR_TIMEOUT and
+// still meets its cluster's barriers.
 //
 // The active row count and the length may live on the device (a
 // checkpoint's counts, the decode position), so that a decode step needs no

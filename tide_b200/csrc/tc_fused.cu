@@ -27,13 +27,15 @@
 // strict threshold, normed exit scatter), python/TIDE/scheduler.py:89-100
 // (stable compaction of rows and positions).
 //
-// Warp roles (512 threads):
+// Warp roles (768 threads):
 //   warp 0        TMA producer (resident W' slice once, then the x ring)
 //   warp 1        TMEM owner, MMA issuer
 //   warps 4-7     row statistics from the ring (two threads per row)
 //   warps 8-11    epilogue (tcgen05.ld of D_c), partial exchange, owner
-//                 reduction, decision and broadcast
-//   warps 12-15   write-out: look-back and the row moves
+//                 reduction, decision and broadcast (even local tiles)
+//   warps 12-15   write-out: look-back and the row moves (even local tiles)
+//   warps 16-19   epilogue of the odd local tiles
+//   warps 20-23   write-out of the odd local tiles
 // Every wait is bounded; on expiry the CTA raises TIDE_DEVERR_TIMEOUT,
 // stops, drains its in-flight copies and MMAs and meets its cluster at the
 // final barrier.
@@ -54,7 +56,11 @@ namespace fused {
 constexpr int kRows = 64;        // rows per tile (MMA N)
 constexpr int kUnits = 128;      // router units (MMA M)
 constexpr int kChunk = 64;       // columns per chunk (128 bytes of 16-bit data)
-constexpr int kThreads = 512;
+// G groups (1 or 2) of epilogue and write-out warps take alternate tiles of
+// a cluster: each stage is a chain of exchanges with the other CTAs (a few us
+// of latency, little work), so a second chain in flight raises the rate.
+constexpr int kMaxGroups = 2;
+__host__ __device__ constexpr int threads_for(int G) { return 256 + 256 * G; }
 constexpr int kStages = 10;
 constexpr int kMaxSliceChunks = 8;  // W' slice <= 8 chunks = 128 KB
 constexpr uint32_t kTmemCols = 128;  // two 64-column fp32 accumulators
@@ -95,14 +101,14 @@ struct Layout {
   uint32_t w, ring, slots, slot_ss, info, stat, wn, bn, up, cs, bp, red, own, wg2, pos, bars, end;
 };
 
-__host__ __device__ inline Layout layout(int slice_chunks, int C) {
+__host__ __device__ inline Layout layout(int slice_chunks, int C, int G) {
   Layout L;
   uint32_t o = 0;
   L.w = o;       o += (uint32_t)slice_chunks * kUnits * kChunk * 2;  // resident W' slice
   L.ring = o;    o += (uint32_t)kStages * kRows * kChunk * 2;        // x chunks
   L.slots = o;   o += 0;                                             // (exchange is in L2)
   L.slot_ss = o; o += 0;
-  L.info = o;    o += kRows * 16;                                     // this tile's decisions
+  L.info = o;    o += G * kRows * 16;                                 // [group] the tile's decisions
   L.stat = o;    o += 2u * 2 * kRows * 2 * 4;                         // [2 bufs][2 halves][64][ss, sx]
   const uint32_t slice = (uint32_t)slice_chunks * kChunk;
   L.wn = o;      o += slice * 4;
@@ -110,10 +116,10 @@ __host__ __device__ inline Layout layout(int slice_chunks, int C) {
   L.up = o;      o += kUnits * 4;
   L.cs = o;      o += kUnits * 4;
   L.bp = o;      o += kUnits * 4;
-  L.red = o;     o += 4u * kRows * 4;                                 // [4 warps][64/C]
-  L.own = o;     o += 2u * kRows * 4;                                 // rstd, mean of owned rows
-  L.wg2 = o;     o += 256 + kRows * 4;                                // ranks, prefix, flags
-  L.pos = o;     o += kRows * 8;                                      // positions of the tile's rows
+  L.red = o;     o += G * 4u * kRows * 4;                             // [group][4 warps][64/C]
+  L.own = o;     o += G * 2u * kRows * 4;                             // [group] rstd, mean of owned rows
+  L.wg2 = o;     o += G * (256 + kRows * 4);                          // [group] ranks, prefix, flags
+  L.pos = o;     o += G * kRows * 8;                                  // [group] positions of the tile's rows
   o = (o + 15u) & ~15u;
   L.bars = o;    o += 64 * 8;
   L.end = o;
@@ -180,8 +186,8 @@ __device__ __forceinline__ bool lookback_read(const uint64_t *status, uint32_t t
   return true;
 }
 
-template <bool BF16, int C>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool BF16, int C, int G>
+__global__ void __launch_bounds__(threads_for(G), 1)
     fused_checkpoint_kernel(const __grid_constant__ CUtensorMap tmap_x,
                             const __grid_constant__ CUtensorMap tmap_w, Params p) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -191,26 +197,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Layout L = layout(p.slice_chunks, C);
+  constexpr int kThreads = threads_for(G);
+  const Layout L = layout(p.slice_chunks, C, G);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
-  float4 *info = reinterpret_cast<float4 *>(smem + L.info);  // [64] decisions of the tile
+  const int grp = (int)(threadIdx.x >> 5) >= 8 ? ((int)(threadIdx.x >> 5) - 8) >> 3 : 0;  // group
+  float4 *info = reinterpret_cast<float4 *>(smem + L.info) + grp * kRows;  // [64] decisions of the tile
   float *stat = reinterpret_cast<float *>(smem + L.stat);
   float *s_wn = reinterpret_cast<float *>(smem + L.wn);
   float *s_bn = reinterpret_cast<float *>(smem + L.bn);
   float *s_up = reinterpret_cast<float *>(smem + L.up);
   float *s_cs = reinterpret_cast<float *>(smem + L.cs);
   float *s_bp = reinterpret_cast<float *>(smem + L.bp);
-  float *s_red = reinterpret_cast<float *>(smem + L.red);
-  uint32_t *wg2 = reinterpret_cast<uint32_t *>(smem + L.wg2);
+  float *s_red = reinterpret_cast<float *>(smem + L.red) + grp * 4 * kRows;
+  uint32_t *wg2 = reinterpret_cast<uint32_t *>(smem + L.wg2);  // [0..2]: CTA-wide words
+  uint32_t *wgg = wg2 + grp * (64 + kRows);                     // this group's words
   uint32_t *tmem_slot = wg2;              // [0]
   volatile int *abort_flag = reinterpret_cast<volatile int *>(wg2 + 1);
   uint32_t *issued = wg2 + 2;
-  uint32_t *s_prefix = wg2 + 4;           // [4]: keep_before, exits_before, keep_t, exit_t
-  uint32_t *s_rank = wg2 + 64;            // [64] rank of each row among its kind
-  volatile int *s_stop1 = reinterpret_cast<volatile int *>(wg2 + 16);  // epilogue group
-  volatile int *s_stop2 = reinterpret_cast<volatile int *>(wg2 + 17);  // write-out group
-  int64_t *s_pos = reinterpret_cast<int64_t *>(smem + L.pos);         // [64] tile positions
-  float *s_rstd = reinterpret_cast<float *>(smem + L.own);            // [R] owned rows
+  uint32_t *s_prefix = wgg + 4;           // [4]: keep_before, exits_before, keep_t, exit_t
+  uint32_t *s_rank = wgg + 64;            // [64] rank of each row among its kind
+  volatile int *s_stop1 = reinterpret_cast<volatile int *>(wgg + 16);  // epilogue group
+  volatile int *s_stop2 = reinterpret_cast<volatile int *>(wgg + 17);  // write-out group
+  int64_t *s_pos = reinterpret_cast<int64_t *>(smem + L.pos) + grp * kRows;  // [64] tile positions
+  float *s_rstd = reinterpret_cast<float *>(smem + L.own) + grp * 2 * kRows;  // [R] owned rows
   float *s_mean = s_rstd + kRows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = ptx::cluster_rank();
@@ -251,8 +260,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(&bars[kDrain], 1);
     *abort_flag = 0;
     *issued = 0;
-    *s_stop1 = 0;
-    *s_stop2 = 0;
+    for (int g = 0; g < G; ++g) {
+      wg2[g * (64 + kRows) + 16] = 0;  // s_stop1, s_stop2 of every group
+      wg2[g * (64 + kRows) + 17] = 0;
+    }
     ptx::fence_mbar_init();
     ptx::fence_proxy_async();
   }
@@ -397,18 +408,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       raise_error(p.err, TIDE_DEVERR_TIMEOUT);
       *abort_flag = 1;
     }
-  } else if (warp >= 8 && warp < 12) {
+  } else if (warp >= 8 && (warp & 7) < 4) {
     // ---------------------- epilogue, partial exchange, owner reduction
+    // (group grp: warps 8-11 or 16-19, the tiles with t_local % 2 == grp)
     // All 128 threads pass every named barrier of an iteration; a failed
     // wait only turns the rest of the iteration's work off (ok = false) and
     // the group stops together at the iteration's end (s_stop1).
-    const int t = threadIdx.x - 256;   // 0..127 = router unit b = TMEM lane
+    const int t = threadIdx.x - 256 - 256 * grp;  // 0..127 = router unit b = TMEM lane
+    const int bar_id = 1 + 2 * grp;
     const int q = warp & 3;            // TMEM lane quarter of this warp
     float *xP = p.xchg + (size_t)cluster_id * (size_t)p.xchg_stride;
     float *xS = xP + 2 * C * kRows * kUnits;
     float4 *xI = reinterpret_cast<float4 *>(xS + 2 * C * kRows * 2);
-    int t_local = 0;
-    for (int tile = cluster_id; tile < n_tiles; tile += n_clusters, ++t_local) {
+    for (int tile = cluster_id + grp * n_clusters, t_local = grp; tile < n_tiles;
+         tile += G * n_clusters, t_local += G) {
       bool ok = true;
       const int buf = t_local & 1;
       const uint32_t ph2 = (uint32_t)(t_local >> 1) & 1u;
@@ -424,25 +437,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (ok && lane == 0) ptx::mbar_arrive(&bars[kStatEmpty + buf]);
       // (2) this CTA's partial D_c[b, 0..63] from TMEM
-      float d[kRows];
+      // (3) publish the partials: xP[buf][rank][r][b], coalesced over b,
+      // read from TMEM in two halves of 32 rows (registers)
       if (ok) ok = ptx::mbar_wait(&bars[kAccFull + buf], ph2, abort_flag);
+      if (ok && t_local >= 2)
+        ok = ptx::mbar_wait_cluster(&bars[kSlotFree + buf], ph2 ^ 1u, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         ptx::tc_fence_after();
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kRows);
-        ptx::tmem_ld32(taddr, d);
-        ptx::tmem_ld32(taddr + 32u, d + 32);
+        float *dst = xP + ((size_t)(buf * C + (int)rank) * kRows) * kUnits + t;
+#pragma unroll
+        for (int half = 0; half < kRows / 32; ++half) {
+          float d[32];
+          ptx::tmem_ld32(taddr + 32u * half, d);
+#pragma unroll
+          for (int r = 0; r < 32; ++r) __stcg(dst + (size_t)(half * 32 + r) * kUnits, d[r]);
+        }
         ptx::tc_fence_before();
       }
       __syncwarp();
       if (ok && lane == 0) ptx::mbar_arrive(&bars[kAccEmpty + buf]);
-      // (3) publish the partials: xP[buf][rank][r][b], coalesced over b
-      if (ok && t_local >= 2)
-        ok = ptx::mbar_wait_cluster(&bars[kSlotFree + buf], ph2 ^ 1u, abort_flag);
       if (ok) {
-        float *dst = xP + ((size_t)(buf * C + (int)rank) * kRows) * kUnits + t;
-#pragma unroll
-        for (int r = 0; r < kRows; ++r) __stcg(dst + (size_t)r * kUnits, d[r]);
         if (t < kRows) {
           float *sd = xS + ((size_t)(buf * C + (int)rank) * kRows + t) * 2;
           __stcg(sd, ss_part);
@@ -479,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         s_mean[t] = mean;
       }
       if (!ok) *s_stop1 = 1;
-      ptx::named_sync(1, 128);
+      ptx::named_sync(bar_id, 128);
       ok = !*s_stop1;
       if (ok) {
         float acc[R];
@@ -499,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) s_red[q * R + rr] = v;
         }
       }
-      ptx::named_sync(1, 128);
+      ptx::named_sync(bar_id, 128);
       // every partial of this buffer has been read: sources may refill it
       // (the loads have returned: a relaxed signal orders nothing else)
       if (ok && t == 0)
@@ -526,29 +542,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok || *abort_flag) *s_stop1 = 1;
-      ptx::named_sync(1, 128);
+      ptx::named_sync(bar_id, 128);
       if (*s_stop1) break;
     }
     if (*s_stop1) {
       raise_error(p.err, TIDE_DEVERR_TIMEOUT);
       *abort_flag = 1;
     }
-  } else if (warp >= 12) {
+  } else if (warp >= 8) {
     // -------------------------------------------- look-back, row moves
-    const int t = threadIdx.x - 384;  // 0..127
+    // (group grp: warps 12-15 or 20-23, the tiles with t_local % 2 == grp)
+    const int t = threadIdx.x - 384 - 256 * grp;  // 0..127
+    const int bar_id = 2 + 2 * grp;
     const int w4 = t >> 5;            // 0..3
-    int t_local = 0;
     const T *x = static_cast<const T *>(p.x);
     const int vec_per_row = slice / 8;  // 16-byte vectors of this CTA's slice (<= 64)
     const float4 *xI2 = reinterpret_cast<const float4 *>(
         p.xchg + (size_t)cluster_id * (size_t)p.xchg_stride + 2 * C * kRows * kUnits + 2 * C * kRows * 2);
-    for (int tile = cluster_id; tile < n_tiles; tile += n_clusters, ++t_local) {
+    for (int tile = cluster_id + grp * n_clusters, t_local = grp; tile < n_tiles;
+         tile += G * n_clusters, t_local += G) {
       const int buf = t_local & 1;
       const uint32_t ph2 = (uint32_t)(t_local >> 1) & 1u;
       bool ok = ptx::mbar_wait_cluster(&bars[kInfoFull + buf], ph2, abort_flag);
       if (ok && t < kRows) info[t] = __ldcg(&xI2[buf * kRows + t]);
       if (!ok) *s_stop2 = 1;
-      ptx::named_sync(2, 128);
+      ptx::named_sync(bar_id, 128);
       if (*s_stop2) break;
       // the decisions are copied: every owner may reuse this buffer
       if (t == 0)
@@ -569,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           s_prefix[8 + w4 * 2 + 1] = __popc(eb);
         }
       }
-      ptx::named_sync(2, 128);
+      ptx::named_sync(bar_id, 128);
       if (t < kRows && t >= 32) {
         const int st = (int)info[t].w;
         s_rank[t] += st == 1 ? s_prefix[8] : s_prefix[9];
@@ -600,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      ptx::named_sync(2, 128);
+      ptx::named_sync(bar_id, 128);
       const uint32_t keep_before = s_prefix[0], exits_before = s_prefix[1];
       // token bookkeeping (rank 0 only)
       if (rank == 0 && t < kRows) {
@@ -614,12 +632,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           p.exit_pos_out[(int64_t)exits_before + s_rank[t]] = s_pos[t];
         }
       }
-      // row moves: warp w4 handles rows w4*16 .. w4*16+15 in two batches of 8
-      for (int batch = 0; batch < 2; ++batch) {
-        const int r0 = w4 * 16 + batch * 8;
-        uint4 v[8][2];
+      // row moves: warp w4 handles rows w4*16 .. w4*16+15 in batches of kMoveBatch
+      constexpr int kMoveBatch = G == 1 ? 8 : 4;  // registers: 128 per thread with one group, 80 with two
+      for (int batch = 0; batch < 16 / kMoveBatch; ++batch) {
+        const int r0 = w4 * 16 + batch * kMoveBatch;
+        uint4 v[kMoveBatch][2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < kMoveBatch; ++i) {
           const int r = r0 + i;
           const int st = (int)info[r].w;
           const int64_t row = (int64_t)tile * kRows + r;
@@ -631,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < kMoveBatch; ++i) {
           const int r = r0 + i;
           const float4 in = info[r];
           const int st = (int)in.w;
@@ -675,9 +694,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      ptx::named_sync(2, 128);
+      ptx::named_sync(bar_id, 128);
       if (*abort_flag) *s_stop2 = 1;
-      ptx::named_sync(2, 128);
+      ptx::named_sync(bar_id, 128);
       if (*s_stop2) break;
     }
     if (*s_stop2) {
@@ -752,10 +771,42 @@ int fused_cluster_size(int64_t H) {
   return 0;
 }
 
-size_t fused_smem_bytes(int64_t H) {
+size_t fused_smem_bytes(int64_t H, int G) {
   const int c = fused_cluster_size(H);
   if (!c) return 0;
-  return 1024 + fused::layout((int)(H / c / fused::kChunk), c).end;
+  return 1024 + fused::layout((int)(H / c / fused::kChunk), c, G).end;
+}
+
+// Epilogue / write-out groups: TIDE_FUSED_GROUPS=1 or 2 forces a count.
+// Otherwise one up to 1024 rows (a launch of a few tiles per cluster is one
+// chain long, and the second group only adds its setup) and two above, where
+// a second group's shared memory fits.  Measured at H = 4096, 10 % exits:
+// 1024 rows 26.7 us either way, 2048 rows 32.3 (one) against 30.9 us (two),
+// 4096 rows 43.5 against 39.6 us.
+int fused_groups(int64_t H, int64_t n_rows) {
+  static int forced = -1;
+  if (forced < 0) {
+    const char *e = getenv("TIDE_FUSED_GROUPS");
+    forced = (e && (e[0] == '1' || e[0] == '2') && e[1] == 0) ? e[0] - '0' : 0;
+  }
+  if (forced) return forced;
+  if (n_rows <= 1024) return 1;
+  return fused_smem_bytes(H, 2) <= (size_t)fused::kSmemBudget ? 2 : 1;
+}
+
+template <bool BF16, int G>
+const void *fused_fn_g(int C) {
+  switch (C) {
+    case 1: return (const void *)fused::fused_checkpoint_kernel<BF16, 1, G>;
+    case 2: return (const void *)fused::fused_checkpoint_kernel<BF16, 2, G>;
+    case 4: return (const void *)fused::fused_checkpoint_kernel<BF16, 4, G>;
+    case 8: return (const void *)fused::fused_checkpoint_kernel<BF16, 8, G>;
+    default: return (const void *)fused::fused_checkpoint_kernel<BF16, 16, G>;
+  }
+}
+const void *fused_fn(bool bf16, int C, int G) {
+  if (bf16) return G == 2 ? fused_fn_g<true, 2>(C) : fused_fn_g<true, 1>(C);
+  return G == 2 ? fused_fn_g<false, 2>(C) : fused_fn_g<false, 1>(C);
 }
 
 }  // namespace
@@ -765,7 +816,9 @@ const char *fused_unsupported_reason(const tide_checkpoint_args *a) {
   if (!a->folded) return "no folded router weights";
   if (a->bottleneck_dim != fused::kUnits) return "bottleneck_dim is not 128";
   if (!fused_cluster_size(a->hidden_dim)) return "hidden_dim has no cluster split with a resident weight slice";
-  if (fused_smem_bytes(a->hidden_dim) > (size_t)fused::kSmemBudget) return "shared memory budget";
+  if (fused_smem_bytes(a->hidden_dim, fused_groups(a->hidden_dim, a->n_rows)) >
+      (size_t)fused::kSmemBudget)
+    return "shared memory budget";
   if (a->norm_type == TIDE_NORM_LAYER && !a->colsum) return "LayerNorm needs colsum";
   if (((uintptr_t)a->x | (uintptr_t)a->folded | (uintptr_t)a->out_buffer |
        (uintptr_t)a->compact_out) & 15u)
@@ -777,26 +830,29 @@ const char *fused_unsupported_reason(const tide_checkpoint_args *a) {
 
 bool fused_supported(const tide_checkpoint_args *a) { return fused_unsupported_reason(a) == nullptr; }
 
-// Measured crossovers against the split path (bf16, 10-50 % exits), by
-// cluster size:
-//   1 CTA  (H <= 512):  the split path wins from 1536 rows.
+// Measured crossovers against the split path (bf16, 10 % exits, one
+// epilogue / write-out group up to 1024 rows and two above), by cluster size:
+//   1 CTA  (H <= 512):  the split path wins at every size from 128 rows
+//          (25.3 against 20.9 us at H = 512, 128 rows).
 //   2 CTAs (H 768-1024): rows under 2 KB (H = 768) leave the split path the
-//          SIMT mover, and the fused pass wins up to 4096 rows (loses from
-//          5120); with 2 KB rows (H = 1024) the split path wins from 1536.
-//   4 CTAs (H = 2048):  fused up to 2048 rows, split from 3072.
-//   8 CTAs (H = 4096):  fused up to 3072 rows, split from 4096.
-//   16 CTAs: H = 5120 fused up to 2048 rows, split from 3072; H = 8192, whose
+//          SIMT mover, and the fused pass wins up to 8192 rows (30.0 against
+//          30.1 us); with 2 KB rows (H = 1024) the split path wins from 128.
+//   4 CTAs (H = 2048):  fused up to 4096 rows (29.1 against 30.7 us), split
+//          from 4608.
+//   8 CTAs (H = 4096):  fused up to 5120 rows (45.2 against 46.9 us), split
+//          from 6144 (52.2 against 48.6 us).
+//   16 CTAs: H = 5120 fused up to 3584 rows, split from 4096; H = 8192, whose
 //          split router streams 2 MiB of W' through each CTA, fused up to
-//          4096, split from 6144.
+//          5120 (77.3 against 86.2 us); the two are level at 6144.
 int64_t fused_auto_max_rows(int64_t H) {
   const int C = fused_cluster_size(H);
   switch (C) {
     case 0: return 0;
-    case 1: return 1024;
-    case 2: return H * 2 < 2048 ? 4608 : 1024;
-    case 4: return 2560;
-    case 8: return 3584;
-    default: return H >= 8192 ? 5120 : 2560;
+    case 1: return 0;
+    case 2: return H * 2 < 2048 ? 8192 : 0;
+    case 4: return 4096;
+    case 8: return 5120;
+    default: return H >= 8192 ? 5632 : 3584;
   }
 }
 
@@ -867,36 +923,30 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
   p.xchg_stride = fused::xchg_floats(C);
   p.err = a->error_word;
 
-  const void *fn = nullptr;
-  switch (C) {
-    case 1: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 1> : (const void *)fused::fused_checkpoint_kernel<false, 1>; break;
-    case 2: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 2> : (const void *)fused::fused_checkpoint_kernel<false, 2>; break;
-    case 4: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 4> : (const void *)fused::fused_checkpoint_kernel<false, 4>; break;
-    case 8: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 8> : (const void *)fused::fused_checkpoint_kernel<false, 8>; break;
-    default: fn = bf16 ? (const void *)fused::fused_checkpoint_kernel<true, 16> : (const void *)fused::fused_checkpoint_kernel<false, 16>; break;
-  }
+  const int G = fused_groups(a->hidden_dim, a->n_rows);
+  const void *fn = fused_fn(bf16, C, G);
   // per device: the attributes and the occupancy belong to a device's context
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  static bool attr_set[64][2][kMaxCluster + 1] = {};
-  if (!attr_set[dev][bf16][C]) {
+  static bool attr_set[64][2][kMaxCluster + 1][fused::kMaxGroups + 1] = {};
+  if (!attr_set[dev][bf16][C][G]) {
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, fused::kSmemBudget);
     if (e == cudaSuccess && C > 8) e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) {
       snprintf(err, err_len, "fused checkpoint: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return TIDE_ERR_CUDA;
     }
-    attr_set[dev][bf16][C] = true;
+    attr_set[dev][bf16][C][G] = true;
   }
-  const size_t smem = fused_smem_bytes(a->hidden_dim);
+  const size_t smem = fused_smem_bytes(a->hidden_dim, G);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)C;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(fused::kThreads, 1, 1);
+  cfg.blockDim = dim3((unsigned)fused::threads_for(G), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
@@ -905,8 +955,8 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
   // so a look-back never waits on a tile whose cluster is not running.  A
   // device that cannot hold one cluster of this size reports
   // TIDE_ERR_UNSUPPORTED before anything is launched.
-  static int max_clusters[64][2][kMaxCluster + 1] = {};
-  if (!max_clusters[dev][bf16][C]) {
+  static int max_clusters[64][2][kMaxCluster + 1][fused::kMaxGroups + 1] = {};
+  if (!max_clusters[dev][bf16][C][G]) {
     cfg.gridDim = dim3((unsigned)C, 1, 1);
     int mc = 0;
     e = cudaOccupancyMaxActiveClusters(&mc, fn, &cfg);
@@ -916,24 +966,15 @@ int fused_checkpoint_launch(const tide_checkpoint_args *a, cudaStream_t stream, 
                cudaGetErrorString(e));
       return TIDE_ERR_UNSUPPORTED;
     }
-    max_clusters[dev][bf16][C] = mc;
+    max_clusters[dev][bf16][C][G] = mc;
   }
   const int64_t tiles = (a->n_rows + fused::kRows - 1) / fused::kRows;
-  int64_t g = tiles < max_clusters[dev][bf16][C] ? tiles : max_clusters[dev][bf16][C];
+  const int mcl = max_clusters[dev][bf16][C][G];
+  int64_t g = tiles < mcl ? tiles : mcl;
   if (g > 160 / C) g = 160 / C;  // the workspace holds 160 / C exchange areas
   cfg.gridDim = dim3((unsigned)(g * C), 1, 1);
-  switch (C) {
-    case 1: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 1>, tx, tw, p)
-                     : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 1>, tx, tw, p); break;
-    case 2: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 2>, tx, tw, p)
-                     : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 2>, tx, tw, p); break;
-    case 4: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 4>, tx, tw, p)
-                     : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 4>, tx, tw, p); break;
-    case 8: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 8>, tx, tw, p)
-                     : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 8>, tx, tw, p); break;
-    default: e = bf16 ? cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<true, 16>, tx, tw, p)
-                      : cudaLaunchKernelEx(&cfg, fused::fused_checkpoint_kernel<false, 16>, tx, tw, p); break;
-  }
+  void *args[] = {&tx, &tw, &p};
+  e = cudaLaunchKernelExC(&cfg, fn, args);
   if (e != cudaSuccess) {
     snprintf(err, err_len, "fused checkpoint launch: %s", cudaGetErrorString(e));
     return TIDE_ERR_CUDA;
