@@ -79,6 +79,7 @@ WORKLOADS = {
 SWEEP_WORKLOAD = "bandwidth_sweep"
 ENGINE_WORKLOAD = "llama8b_prefill_engine"
 DECODE_WORKLOAD = "qwen3_8b_decode_generate"
+ATTN_WORKLOAD = "qwen3_8b_decode_attention"
 SWEEP_N = [1024, 4096, 16384, 65536, 262144, 1048576]
 SWEEP_H = [2048, 4096, 5120, 8192]
 SWEEP_F = [0.0, 0.1, 0.5, 0.9]
@@ -515,7 +516,7 @@ def run_reference(args, world, rank):
     from the CPU generator (checkpoint_setup) and go straight to the oracle."""
     if rank != 0:
         return
-    if WORKLOAD in (SWEEP_WORKLOAD, ENGINE_WORKLOAD, DECODE_WORKLOAD):
+    if WORKLOAD in (SWEEP_WORKLOAD, ENGINE_WORKLOAD, DECODE_WORKLOAD, ATTN_WORKLOAD):
         configure("llama8b_prefill_checkpoints")
     sample = min(2048, ROWS)
     cores = host_threads()
@@ -839,6 +840,61 @@ def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
     return res
 
 
+def decode_attention_bench(world: int, rank: int, steps: int, warmup: int) -> dict:
+    """The live decoder's attention kernel alone (tide_decode_attention), at
+    the decode workload's shapes: 256 rows, Qwen3-8B heads (32 query / 8 KV,
+    head_dim 128), a 1024-position bf16 cache addressed by slot (permuted
+    slots), the live row count and the length on the device; with 256, 128
+    and 64 of the rows active (what the exits leave).  The cache (1.2 GB)
+    is larger than L2.  Algorithmic bytes per launch: the active rows' keys
+    and values (2 * 8 * 1024 * 128 * 2 bytes per row) plus their q and
+    output rows.  Times: CUDA events around `steps` launches after
+    `warmup`."""
+    from tide_b200 import _native
+
+    ops = _native.ops()
+    dev = torch.device("cuda")
+    B, hq, hkv, d, L, max_len = 256, 32, 8, 128, 1024, 1152
+    g = torch.Generator(device=dev).manual_seed(SEED + 31 + rank)
+    kc = torch.randn(B, hkv, max_len, d, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(B, hkv, max_len, d, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(B, hq, d, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    slots = torch.randperm(B, generator=torch.Generator().manual_seed(SEED)).to(torch.int32).to(dev)
+    len_dev = torch.tensor([L], dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    peak = load_peak()
+    cases = []
+    for live in (256, 128, 64):
+        n_dev = torch.tensor([live], dtype=torch.int32, device=dev)
+
+        def call():
+            ops.decode_attention(q, kc, vc, slots, out, max_len, d ** -0.5, err, n_dev, len_dev)
+
+        for _ in range(max(warmup, 3)):
+            call()
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            call()
+        b.record()
+        torch.cuda.synchronize()
+        sec = max_over_ranks(world, a.elapsed_time(b) / 1000.0 / steps)
+        nbytes = live * hkv * L * d * 2 * 2 + 2 * live * hq * d * 2
+        gbps = nbytes / sec / 1e9
+        cases.append({"active_rows": live, "us_per_launch": sec * 1e6, "bytes": nbytes,
+                      "GBps": gbps, "frac": gbps / peak})
+    if int(err.item()):
+        raise RuntimeError(f"decode attention raised device error bits {int(err.item())}")
+    del kc, vc
+    torch.cuda.empty_cache()
+    return {"rows": B, "q_heads": hq, "kv_heads": hkv, "head_dim": d, "positions": L,
+            "peak_GBps": peak, "cases": cases,
+            "note": "cache larger than L2 (1.2 GB); one launch per timed call"}
+
+
 def run_sweep(args, world, rank, local) -> None:
     """--workload bandwidth_sweep: one checkpoint per (N, H, f), N split evenly
     over the ranks; aggregate algorithmic GB/s (max device time over ranks)
@@ -951,7 +1007,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-engine", action="store_true", help="skip the engine prefill measurement")
     ap.add_argument("--workload", default=WORKLOAD,
-                    choices=sorted(WORKLOADS) + [SWEEP_WORKLOAD, ENGINE_WORKLOAD, DECODE_WORKLOAD])
+                    choices=sorted(WORKLOADS) + [SWEEP_WORKLOAD, ENGINE_WORKLOAD, DECODE_WORKLOAD,
+                                                 ATTN_WORKLOAD])
     ap.add_argument("--rows", type=int, default=None, help="rows per GPU (profiling runs)")
     ap.add_argument("--sweep-h", default=None, help="bandwidth_sweep: comma-separated H values")
     ap.add_argument("--sweep-n", default=None, help="bandwidth_sweep: comma-separated N values")
@@ -975,6 +1032,18 @@ def main():
                                   "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                                   "data": "synthetic", "config": {"workload": DECODE_WORKLOAD},
                                   "decode_generate": dg}), flush=True)
+        elif args.workload == ATTN_WORKLOAD:
+            da = decode_attention_bench(world, rank, args.steps, args.warmup)
+            if rank == 0:
+                full = da["cases"][0]
+                print(json.dumps({"metric": "decode_attention_GBps", "value": full["GBps"] * world,
+                                  "unit": "GB/s", "n_gpus": world, "higher_is_better": True,
+                                  "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                                  "data": "synthetic", "config": {"workload": ATTN_WORKLOAD},
+                                  "roofline": {"bound": "hbm", "achieved": full["GBps"],
+                                               "peak": da["peak_GBps"], "unit": "GB/s",
+                                               "frac": full["frac"], "traffic": None},
+                                  "decode_attention": da}), flush=True)
         elif args.workload == ENGINE_WORKLOAD:
             eng = engine_prefill(world, rank)
             if rank == 0:
