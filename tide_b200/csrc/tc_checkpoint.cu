@@ -85,6 +85,12 @@ constexpr int kTcMaxStages = 12;
 constexpr int kTcMaxKc = TIDE_ROUTER_MAX_KC;
 constexpr int kTcMinStages = TIDE_ROUTER_MIN_STAGES;
 constexpr int kTcSmemBudget = 227 * 1024;
+// fp32 tile width in 32-row units: narrower tiles at larger H leave TMEM
+// room for more K-group accumulators (2 at 256 rows, 4 at 128, 8 at 64), so
+// the fp32 score error stays under 1e-5 to H = 8192 (the error of one
+// accumulator grows with the K depth).
+__host__ __device__ inline int f32_tile_units(int H) { return H <= 2048 ? 8 : (H <= 4096 ? 4 : 2); }
+constexpr int kF32OneGroupMaxH = 1024;  // fp32 rows up to this H keep one K accumulator
 constexpr int kTcAux = 12288;     // barriers, flags, per-unit vectors, row statistics, partials
 static_assert((3 * kTcMaxStages + 9) * 8 + 16 + 3 * 256 * 4 + 2 * 256 * 2 * 4 + 4 * 256 * 4 +
                       8 * 4 <= kTcAux,
@@ -174,7 +180,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int NA = p.n_acc, AT = p.a_tiles;
   // a K chunk is 128 bytes of a row: 64 16-bit or 32 fp32 columns
   constexpr int kCols = F32 ? 32 : kTcK;
-  constexpr int kTileMax = kTcTileUnits;  // units per tile
+  // units per tile; fp32 tiles are narrower at larger H, so that TMEM holds
+  // several K-group accumulators (below)
+  const int kTileMax = F32 ? f32_tile_units(p.H) : kTcTileUnits;
   // fp32 stages are twice as large: two of them (two K chunks each on thin
   // tiles; 256-row tiles) measured faster than more, smaller stages
   constexpr int kMinStages = F32 ? 2 : kTcMinStages;
@@ -270,6 +278,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int S_fit = (int)(p.ring_bytes / stage_bytes);
   const int S = S_fit > kTcMaxStages ? kTcMaxStages : S_fit;
   const int k_stages = k_chunks / KC;
+  // fp32: the K range is cut into KG groups, each accumulated from zero in
+  // its own TMEM accumulator and summed in fp32 by the epilogue.  The
+  // tensor core's fp32 accumulation loses about an ulp of the running sum per
+  // MMA (measured: the score error of one accumulator over K grows linearly
+  // with H, 5e-6 at H = 4096 and 1.4e-5 at 8192 for default-scale weights);
+  // KG independent partial sums divide that by KG.  16-bit rows keep one,
+  // and so do fp32 rows up to H = 1024 (4e-7 with one accumulator), which
+  // keep two accumulator sets to overlap consecutive tiles instead.
+  const bool k_groups = F32 && p.H > kF32OneGroupMaxH;
+  const int acc_stride = k_groups ? tile_units * kTcUnit : kTcTileRows;  // TMEM columns per accumulator
+  int KG = 1;
+  if (k_groups) {
+    KG = 512 / (NA * AT * acc_stride);
+    KG = KG > 8 ? 8 : KG;
+    KG = KG > k_stages ? k_stages : KG;
+    KG = KG < 1 ? 1 : KG;
+  }
 
   uint32_t tmem_base = 0;
   // the setup group: warps 1 and 3-15 (warps 0 and 2 are the producers)
@@ -375,8 +400,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * AT * kTcTileRows);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * AT * KG * acc_stride);
         for (int ks = 0; ks < k_stages; ++ks, ++it) {
+          const int kg = ks * KG / k_stages;  // K group of this stage
+          const bool group_start = ks == 0 || (ks - 1) * KG / k_stages != kg;
           const uint32_t s = it % S, ph = (it / S) & 1u;
           if (!ptx::mbar_wait(F32 ? &conv[s] : &full[s], ph, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
@@ -389,8 +416,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
                 const uint32_t wa = ws + (uint32_t)a * w_tile_bytes + 32u * k, xb = xs + 32u * k;
-                const uint32_t d = d_tmem + (uint32_t)(a * kTcTileRows);
-                const uint32_t acc_in = (ks > 0 || c > 0 || k > 0) ? 1u : 0u;
+                const uint32_t d = d_tmem + (uint32_t)((a * KG + kg) * acc_stride);
+                const uint32_t acc_in = (!group_start || c > 0 || k > 0) ? 1u : 0u;
                 if constexpr (F32) {
                   ptx::mma_tf32_ss(d, ptx::sw128_kmajor_desc(wa), ptx::sw128_kmajor_desc(xb), idesc, acc_in);
                   ptx::mma_tf32_ss(d, ptx::sw128_kmajor_desc(wa + lo_off), ptx::sw128_kmajor_desc(xb),
@@ -600,13 +627,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int u = a * kTcM + q * 32 + lane;
         const float up = s_up[u], cs = s_cs[u], bp = s_bp[u];
         const uint32_t base = tmem_base + ((uint32_t)(q * 32) << 16) +
-                              (uint32_t)((acc * AT + a) * kTcTileRows);
+                              (uint32_t)((acc * AT + a) * KG * acc_stride);
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           const int c = g * 4 + cc;
           if (c >= nu) break;  // warp-uniform
           float v[32];
           ptx::tmem_ld32(base + (uint32_t)(c * 32), v);
+          if constexpr (F32) {
+            for (int kg = 1; kg < KG; ++kg) {  // the K groups' partial sums, in order
+              float w[32];
+              ptx::tmem_ld32(base + (uint32_t)(kg * acc_stride + c * 32), w);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += w[j];
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float rstd = st[(c * 32 + j) * 2];
@@ -808,7 +843,8 @@ int tc_route_launch(const tide_checkpoint_args *a, float *scores, float2 *row_st
   p.ring_bytes = (uint32_t)(kTcSmemBudget - 1024 - kTcAux);
   p.a_tiles = a_tiles_for(B);
   p.w_rows = w_rows;
-  p.n_acc = n_acc_for(B);
+  // fp32 above H = 1024: TMEM holds K-group accumulators instead of two sets
+  p.n_acc = (dt == TIDE_DTYPE_F32 && a->hidden_dim > kF32OneGroupMaxH) ? 1 : n_acc_for(B);
   p.tmem_cols = 512;
   p.zero = static_cast<uint4 *>(zero);
   p.zero_vec = (int64_t)(zero_bytes / 16);
