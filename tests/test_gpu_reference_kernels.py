@@ -42,7 +42,7 @@ def _router(H, B=128, seed=0):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("N,H", [(1, 2048), (8, 4096), (32, 2048), (128, 4096), (4096, 768),
-                                 (3000, 4096)])
+                                 (3000, 4096), (2048, 8192)])
 def test_router_against_the_reference_kernel(ops, dtype, N, H):
     """Scores of the reference's fused_layernorm_route kernel and of this
     repository's operator, each against the oracle (which pins the oracle on

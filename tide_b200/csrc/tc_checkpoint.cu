@@ -50,7 +50,9 @@
 // ones of the 16-bit case.  Warps 4-15 split each landed stage in place (hi
 // over the loaded values, lo into the stage's second half, x and W' alike)
 // while they take the row statistics; the MMA waits for that instead of the
-// TMA.
+// TMA.  Above H = 1024 the K range is accumulated in several TMEM
+// accumulators (K groups) that the epilogue sums in fp32, since one
+// accumulator over all of K loses about an ulp of its running sum per MMA.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdio.h>
