@@ -212,6 +212,40 @@ int tide_norm_scatter_rows(int dtype, int norm_type, const void *rows, const int
                            const float *norm_bias, float eps, int32_t *error_word,
                            tide_stream_t stream);
 
+/* The elementwise work of a Llama-family decode layer for the live decoder,
+ * each rounding where the HF module it replaces rounds (bf16 or fp16 rows,
+ * weights in the rows' type), rows below the live count only (*n_rows_dev
+ * clamped to [0, n_rows]; n_rows when NULL):
+ * tide_rms_norm:      s = x, or s = to_T(x + delta) written to sum_out (when
+ *                     given); out = to_T(w * to_T(s * rsqrt(mean(s^2) + eps)))
+ *                     -- HF LlamaRMSNorm / Qwen3RMSNorm with an optional fused
+ *                     residual add.  hidden_dim % 8 == 0, <= 8192.
+ * tide_qk_norm_rope:  q [n, hq, 128], k, v [n, hkv, 128]: optional per-head
+ *                     RMSNorm of q and k (Qwen3 q_norm / k_norm; NULL weight =
+ *                     none), the rotary embedding q*cos + rotate_half(q)*sin
+ *                     with cos/sin = to_T(cos/sin(pos * inv_freq[j]) *
+ *                     attention_scaling), then q to q_out and k, v into the
+ *                     slot-addressed caches at pos (*position_dev when given).
+ *                     A slot or position outside the cache writes nothing for
+ *                     that row and sets TIDE_DEVERR_POSITION.
+ * tide_silu_mul:      out = to_T(to_T(silu(gate)) * up), [n, width], width % 8
+ *                     == 0 -- the gated MLP's act_fn(gate_proj(x)) * up_proj(x).
+ * The reference runs the model's own modules for these inside its decode
+ * loop (python/TIDE/runtime.py:266-273). */
+int tide_rms_norm(int dtype, const void *x, const void *delta, void *sum_out, const void *weight,
+                  void *out, int64_t n_rows, const int32_t *n_rows_dev, int64_t hidden_dim,
+                  float eps, tide_stream_t stream);
+int tide_qk_norm_rope(int dtype, const void *q, const void *k, const void *v,
+                      const void *q_norm_weight, const void *k_norm_weight, float eps,
+                      const float *inv_freq, float attention_scaling, int64_t position,
+                      const int32_t *position_dev, const int32_t *slots,
+                      const int32_t *n_rows_dev, int64_t n_rows, int64_t n_q_heads,
+                      int64_t n_kv_heads, int64_t head_dim, void *q_out, void *k_cache,
+                      void *v_cache, int64_t n_slots, int64_t max_len, int32_t *error_word,
+                      tide_stream_t stream);
+int tide_silu_mul(int dtype, const void *gate, const void *up, void *out, int64_t n_rows,
+                  const int32_t *n_rows_dev, int64_t width, tide_stream_t stream);
+
 /* ---- router preparation (once per router) ------------------------------ */
 
 /* From the router's down.weight [B, H] fp32 and the final norm's weight (and

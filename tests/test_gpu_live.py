@@ -368,3 +368,137 @@ def test_norm_scatter_rows_with_a_device_count(dtype, kind):
     ulp = torch.finfo(dtype).eps  # 1 ulp (16-bit), 8 ulp (fp32: another summation order)
     k = 8 if dtype == torch.float32 else 1
     torch.testing.assert_close(got.float(), ref.float(), atol=4 * k * ulp, rtol=k * ulp)
+
+
+def _close16(a: torch.Tensor, b: torch.Tensor) -> bool:
+    """Within 2 ulp everywhere and bit-equal in at least 99 % of the elements:
+    an fp32 sum in another order than torch's moves a statistic by an fp32
+    ulp, which can flip one rounding of a chain of two (x * rstd to 16 bits,
+    then times the weight)."""
+    return _ulp16(a, b) <= 2 and (a == b).float().mean().item() >= 0.99
+
+
+def _ulp16(a: torch.Tensor, b: torch.Tensor) -> int:
+    """Largest distance in units in the last place between two 16-bit tensors."""
+    ia = a.contiguous().view(torch.int16).to(torch.int32)
+    ib = b.contiguous().view(torch.int16).to(torch.int32)
+    ia = torch.where(ia < 0, -(ia & 0x7FFF), ia)
+    ib = torch.where(ib < 0, -(ib & 0x7FFF), ib)
+    return int((ia - ib).abs().max().item()) if ia.numel() else 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_rms_norm_is_the_hf_module(dtype):
+    """tide_rms_norm against the model's RMSNorm module (Qwen3RMSNorm), with
+    and without the fused residual add (_close16), rows past the live count
+    untouched; the residual sum bit-equal."""
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
+
+    from tide_b200 import _native
+
+    ops = _native.ops()
+    n, H, live = 37, 4096, 30
+    mod = Qwen3RMSNorm(H, eps=1e-6).to(DEV, dtype)
+    g = torch.Generator(device=DEV).manual_seed(9)
+    with torch.no_grad():
+        mod.weight.copy_((1 + 0.2 * torch.randn(H, generator=g, device=DEV)).to(dtype))
+        x = (3 * torch.randn(n, H, generator=g, device=DEV)).to(dtype)
+        d = torch.randn(n, H, generator=g, device=DEV).to(dtype)
+        n_dev = torch.tensor([live], dtype=torch.int32, device=DEV)
+        for delta in (None, d):
+            out = torch.full_like(x, 7.0)
+            tot = torch.full_like(x, 7.0) if delta is not None else None
+            ops.rms_norm(x, delta, tot, mod.weight, out, 1e-6, n_dev)
+            s = x if delta is None else x + delta
+            assert _close16(out[:live], mod(s)[:live])
+            assert torch.all(out[live:] == 7.0)
+            if delta is not None:
+                assert torch.equal(tot[:live], s[:live]) and torch.all(tot[live:] == 7.0)
+
+
+@pytest.mark.parametrize("qk_norm", [True, False])
+def test_fused_qk_norm_rope_is_the_hf_modules(qk_norm):
+    """tide_qk_norm_rope against the model's q_norm / k_norm and rotary
+    modules (apply_rotary_pos_emb), with k and v landing in the cache at the
+    rows' slots and the device position."""
+    from transformers.models.qwen3.modeling_qwen3 import apply_rotary_pos_emb
+
+    from tide_b200 import _native
+
+    ops = _native.ops()
+    model = _qwen3_hd128()
+    attn = model.model.layers[1].self_attn
+    rot = model.model.rotary_emb
+    n, hq, hkv, d, n_slots, max_len, pos = 9, 2, 1, 128, 12, 40, 33
+    g = torch.Generator(device=DEV).manual_seed(10)
+    with torch.no_grad():
+        q = torch.randn(n, hq, d, generator=g, device=DEV).to(torch.bfloat16)
+        k = torch.randn(n, hkv, d, generator=g, device=DEV).to(torch.bfloat16)
+        v = torch.randn(n, hkv, d, generator=g, device=DEV).to(torch.bfloat16)
+        for mod in (attn.q_norm, attn.k_norm):
+            mod.weight.copy_((1 + 0.3 * torch.randn(d, generator=g, device=DEV)).to(torch.bfloat16))
+        slots = torch.randperm(n_slots, generator=torch.Generator().manual_seed(2))[:n]
+        slots = slots.to(torch.int32).to(DEV)
+        kc = torch.zeros(n_slots, hkv, max_len, d, dtype=torch.bfloat16, device=DEV)
+        vc = torch.zeros_like(kc)
+        q_out = torch.empty_like(q)
+        err = torch.zeros(1, dtype=torch.int32, device=DEV)
+        ops.qk_norm_rope(q, k, v, attn.q_norm.weight if qk_norm else None,
+                         attn.k_norm.weight if qk_norm else None, float(attn.q_norm.variance_epsilon),
+                         rot.inv_freq.float(), float(rot.attention_scaling), 0,
+                         torch.tensor([pos], dtype=torch.int32, device=DEV), slots, None, q_out, kc,
+                         vc, err)
+        qn = attn.q_norm(q) if qk_norm else q
+        kn = attn.k_norm(k) if qk_norm else k
+        cos, sin = rot(v, torch.full((1, n), pos, dtype=torch.long, device=DEV))
+        q_ref, k_ref = apply_rotary_pos_emb(qn, kn, cos[0], sin[0], unsqueeze_dim=1)
+        assert _close16(q_out, q_ref)
+        assert _close16(kc[slots.long(), :, pos], k_ref)
+        assert torch.equal(vc[slots.long(), :, pos], v)
+        assert int(err.item()) == 0
+        others = torch.ones(n_slots, dtype=torch.bool)
+        others[slots.cpu().long()] = False
+        assert torch.all(kc[others.to(DEV)] == 0) and torch.all(kc[:, :, :pos] == 0)
+
+
+def test_fused_silu_mul_is_the_hf_mlp_gate():
+    from tide_b200 import _native
+
+    ops = _native.ops()
+    g = torch.Generator(device=DEV).manual_seed(11)
+    gate = (2 * torch.randn(33, 1536, generator=g, device=DEV)).to(torch.bfloat16)
+    up = torch.randn(33, 1536, generator=g, device=DEV).to(torch.bfloat16)
+    out = torch.full_like(gate, 7.0)
+    ops.silu_mul(gate, up, out, torch.tensor([20], dtype=torch.int32, device=DEV))
+    ref = torch.nn.functional.silu(gate) * up
+    assert _close16(out[:20], ref[:20]) and torch.all(out[20:] == 7.0)
+
+
+def test_live_decoder_fused_layers_match_the_module_layers(tmp_path):
+    """Four decode steps with the fused layer kernels against the same steps
+    on the model's own modules: the same exits, logits within bf16 noise."""
+    from tide_b200.live import LiveDecoder
+    from tide_b200.scheduler import ExitStats
+
+    model, rt, ids = _decoder_case(tmp_path, B=6)
+    B, S = ids.shape
+    runs = []
+    for fused in (False, True):
+        dec = LiveDecoder(rt, B, S + 6, graph=fused, fused_layers=fused)
+        assert dec.fused == fused
+        st = ExitStats()
+        with torch.no_grad():
+            tok = dec.prefill(ids).argmax(-1)
+            out = []
+            for _ in range(4):
+                lg = dec.step(tok, st)
+                out.append((lg.float().clone(), dec.last_exit_layer.clone()))
+                tok = lg.argmax(-1)
+        dec.read_stats(st)
+        runs.append((out, st))
+    (a, sa), (b, sb) = runs
+    same_exit = [torch.equal(ea, eb) for (_, ea), (_, eb) in zip(a, b)]
+    assert all(same_exit[:2])
+    for (la, ea), (lb, eb) in zip(a[:2], b[:2]):
+        torch.testing.assert_close(la, lb, atol=6e-2, rtol=6e-2)
+    assert sa.total_tokens == sb.total_tokens

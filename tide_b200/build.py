@@ -39,7 +39,7 @@ NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-O3"
                      "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{CSRC}"]
 
 CU_SOURCES = ["capi.cu", "tc_checkpoint.cu", "tc_route_pair.cu", "tc_fused.cu", "move_bulk.cu",
-              "noalloc.cu", "decode_attn.cu"]
+              "noalloc.cu", "decode_attn.cu", "decode_layer.cu"]
 HEADERS = ["common.cuh", "move_bulk.cuh", "simt_kernels.cuh", "tc_checkpoint.cuh", "tc_ptx.cuh"]
 
 

@@ -481,6 +481,89 @@ void kv_append(const at::Tensor &k_new, const at::Tensor &v_new, const std::opti
                                static_cast<int32_t *>(opt_mut(error_word)), cur_stream(k_new)));
 }
 
+void rms_norm(const at::Tensor &x, const std::optional<at::Tensor> &delta,
+              const std::optional<at::Tensor> &sum_out, const at::Tensor &weight,
+              const at::Tensor &out, double eps, const std::optional<at::Tensor> &n_rows_dev) {
+  check_cuda_contig(x, "x");
+  check_cuda_contig(weight, "weight");
+  check_cuda_contig(out, "out");
+  TORCH_CHECK(x.dim() == 2 && out.sizes() == x.sizes(), "x and out must be [n, H]");
+  TORCH_CHECK(weight.numel() == x.size(1) && weight.scalar_type() == x.scalar_type() &&
+              out.scalar_type() == x.scalar_type(), "weight [H] and out in x's dtype");
+  for (const auto *t : {&delta, &sum_out})
+    if (t->has_value() && (*t)->defined()) {
+      check_cuda_contig(**t, "delta/sum_out");
+      TORCH_CHECK((*t)->sizes() == x.sizes() && (*t)->scalar_type() == x.scalar_type(),
+                  "delta and sum_out must be like x");
+    }
+  if (n_rows_dev.has_value() && n_rows_dev->defined())
+    TORCH_CHECK(n_rows_dev->is_cuda() && n_rows_dev->scalar_type() == at::kInt, "n_rows_dev must be int32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  TIDE_CHECK_OK(tide_rms_norm(to_dtype(x.scalar_type(), "rms_norm"), x.data_ptr(), opt_ptr(delta),
+                              opt_mut(sum_out), weight.data_ptr(), out.data_ptr(), x.size(0),
+                              static_cast<const int32_t *>(opt_ptr(n_rows_dev)), x.size(1),
+                              (float)eps, cur_stream(x)));
+}
+
+void qk_norm_rope(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v,
+                  const std::optional<at::Tensor> &q_norm_weight,
+                  const std::optional<at::Tensor> &k_norm_weight, double eps,
+                  const at::Tensor &inv_freq, double attention_scaling, int64_t position,
+                  const std::optional<at::Tensor> &position_dev, const std::optional<at::Tensor> &slots,
+                  const std::optional<at::Tensor> &n_rows_dev, const at::Tensor &q_out,
+                  const at::Tensor &k_cache, const at::Tensor &v_cache,
+                  const std::optional<at::Tensor> &error_word) {
+  for (const auto *t : {&q, &k, &v, &q_out, &k_cache, &v_cache, &inv_freq}) check_cuda_contig(*t, "tensor");
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.sizes() == k.sizes() && q_out.sizes() == q.sizes() &&
+              k.size(0) == q.size(0) && q.size(2) == k.size(2),
+              "q [n, hq, d], k and v [n, hkv, d], q_out like q");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes() && k_cache.size(1) == k.size(1) &&
+              k_cache.size(3) == k.size(2), "caches [slots, hkv, max_len, d]");
+  const auto dt = q.scalar_type();
+  TORCH_CHECK(k.scalar_type() == dt && v.scalar_type() == dt && q_out.scalar_type() == dt &&
+              k_cache.scalar_type() == dt && v_cache.scalar_type() == dt, "one dtype throughout");
+  TORCH_CHECK(inv_freq.scalar_type() == at::kFloat && inv_freq.numel() == q.size(2) / 2,
+              "inv_freq must be fp32 [d/2]");
+  for (const auto *t : {&q_norm_weight, &k_norm_weight})
+    if (t->has_value() && (*t)->defined())
+      TORCH_CHECK((*t)->is_cuda() && (*t)->numel() == q.size(2) && (*t)->scalar_type() == dt,
+                  "q/k norm weights must be [d] in the rows' dtype");
+  const int32_t *sl = nullptr;
+  if (slots.has_value() && slots->defined()) {
+    check_cuda_contig(*slots, "slots");
+    TORCH_CHECK(slots->scalar_type() == at::kInt && slots->numel() >= q.size(0), "slots: int32 per row");
+    sl = slots->data_ptr<int32_t>();
+  }
+  for (const auto *t : {&position_dev, &n_rows_dev, &error_word})
+    if (t->has_value() && (*t)->defined())
+      TORCH_CHECK((*t)->is_cuda() && (*t)->scalar_type() == at::kInt, "device words must be int32");
+  const c10::cuda::CUDAGuard guard(q.device());
+  TIDE_CHECK_OK(tide_qk_norm_rope(
+      to_dtype(dt, "qk_norm_rope"), q.data_ptr(), k.data_ptr(), v.data_ptr(), opt_ptr(q_norm_weight),
+      opt_ptr(k_norm_weight), (float)eps, inv_freq.data_ptr<float>(), (float)attention_scaling,
+      position, static_cast<const int32_t *>(opt_ptr(position_dev)), sl,
+      static_cast<const int32_t *>(opt_ptr(n_rows_dev)), q.size(0), q.size(1), k.size(1), q.size(2),
+      q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.size(0), k_cache.size(2),
+      static_cast<int32_t *>(opt_mut(error_word)), cur_stream(q)));
+}
+
+void silu_mul(const at::Tensor &gate, const at::Tensor &up, const at::Tensor &out,
+              const std::optional<at::Tensor> &n_rows_dev) {
+  check_cuda_contig(gate, "gate");
+  check_cuda_contig(up, "up");
+  check_cuda_contig(out, "out");
+  TORCH_CHECK(gate.dim() == 2 && up.sizes() == gate.sizes() && out.sizes() == gate.sizes() &&
+              up.scalar_type() == gate.scalar_type() && out.scalar_type() == gate.scalar_type(),
+              "gate, up and out: one [n, width] shape and dtype");
+  if (n_rows_dev.has_value() && n_rows_dev->defined())
+    TORCH_CHECK(n_rows_dev->is_cuda() && n_rows_dev->scalar_type() == at::kInt, "n_rows_dev must be int32");
+  const c10::cuda::CUDAGuard guard(gate.device());
+  TIDE_CHECK_OK(tide_silu_mul(to_dtype(gate.scalar_type(), "silu_mul"), gate.data_ptr(), up.data_ptr(),
+                              out.data_ptr(), gate.size(0),
+                              static_cast<const int32_t *>(opt_ptr(n_rows_dev)), gate.size(1),
+                              cur_stream(gate)));
+}
+
 // ---- router fold and fused checkpoint ----------------------------------
 
 std::vector<at::Tensor> router_fold(const at::Tensor &down, const at::Tensor &norm_weight,
@@ -637,6 +720,13 @@ TORCH_LIBRARY(tide, m) {
   m.def("norm_scatter_rows(Tensor rows, Tensor positions, Tensor? n_rows_dev, "
         "Tensor(a!) output_buffer, Tensor norm_weight, Tensor? norm_bias, int norm_type, float eps, "
         "Tensor(b!)? error_word) -> ()");
+  m.def("rms_norm(Tensor x, Tensor? delta, Tensor(a!)? sum_out, Tensor weight, Tensor(b!) out, "
+        "float eps, Tensor? n_rows_dev=None) -> ()");
+  m.def("qk_norm_rope(Tensor q, Tensor k, Tensor v, Tensor? q_norm_weight, Tensor? k_norm_weight, "
+        "float eps, Tensor inv_freq, float attention_scaling, int position, Tensor? position_dev, "
+        "Tensor? slots, Tensor? n_rows_dev, Tensor(a!) q_out, Tensor(b!) k_cache, Tensor(c!) v_cache, "
+        "Tensor(d!)? error_word) -> ()");
+  m.def("silu_mul(Tensor gate, Tensor up, Tensor(a!) out, Tensor? n_rows_dev=None) -> ()");
   m.def("kv_append(Tensor k_new, Tensor v_new, Tensor? slots, Tensor? n_rows_dev, Tensor(a!) k_cache, "
         "Tensor(b!) v_cache, int position, Tensor? position_dev, Tensor(c!)? error_word) -> ()");
   m.def("router_fold(Tensor down, Tensor norm_weight, Tensor? norm_bias, ScalarType fold_dtype) "
@@ -663,6 +753,9 @@ TORCH_LIBRARY_IMPL(tide, CUDA, m) {
   m.impl("decode_attention", &decode_attention);
   m.impl("norm_scatter_rows", &norm_scatter_rows);
   m.impl("kv_append", &kv_append);
+  m.impl("rms_norm", &rms_norm);
+  m.impl("qk_norm_rope", &qk_norm_rope);
+  m.impl("silu_mul", &silu_mul);
   m.impl("router_fold", &router_fold);
   m.impl("checkpoint", &checkpoint);
 }

@@ -164,6 +164,87 @@ class _LlamaFamily:
         return h + layer.mlp(layer.post_attention_layernorm(h))
 
 
+    # ---- the same decode layer on fused kernels (tide_b200/csrc/decode_layer.cu)
+    def fused_decode_ok(self) -> bool:
+        """True when every layer is one the fused kernels reproduce: RMSNorm
+        input / post-attention / final norms, head_dim 128, optional q/k
+        RMSNorm, a rotary embedding with a fixed inv_freq buffer, and a SiLU
+        gated MLP."""
+        rot = self.rotary
+        if getattr(rot, "rope_type", "default") not in ("default", "llama3", "linear") or \
+                not isinstance(getattr(rot, "inv_freq", None), torch.Tensor):
+            return False
+        norms = [self.norm]
+        for layer in self.layers:
+            a, m = layer.self_attn, layer.mlp
+            if getattr(a, "head_dim", 0) != 128 or not all(
+                    hasattr(m, n) for n in ("gate_proj", "up_proj", "down_proj")):
+                return False
+            # nn.SiLU, or transformers' SiLUActivation (F.silu)
+            if type(getattr(m, "act_fn", None)).__name__ not in ("SiLU", "SiLUActivation"):
+                return False
+            norms += [layer.input_layernorm, layer.post_attention_layernorm]
+            if getattr(a, "q_norm", None) is not None:
+                norms += [a.q_norm, a.k_norm]
+        return all(hasattr(n, "variance_epsilon") and isinstance(getattr(n, "weight", None),
+                                                                  torch.Tensor) for n in norms)
+
+    def _inv_freq(self) -> torch.Tensor:
+        """The rotary module's inv_freq as its forward uses it (.float(): a
+        model cast to 16 bits holds the buffer rounded to 16 bits)."""
+        f = getattr(self, "_inv_freq_f32", None)
+        if f is None or f.device != self.rotary.inv_freq.device:
+            f = self._inv_freq_f32 = self.rotary.inv_freq.float().contiguous()
+        return f
+
+    def rms_norm(self, module, h: torch.Tensor, n_live: torch.Tensor,
+                 delta: Optional[torch.Tensor] = None):
+        """module's RMSNorm of h (of h + delta, also returned) for the live
+        rows: (normed, sum or None)."""
+        from tide_b200 import _native
+
+        out = torch.empty_like(h)
+        total = torch.empty_like(h) if delta is not None else None
+        _native.ops().rms_norm(h, delta, total, module.weight, out, float(module.variance_epsilon),
+                               n_live)
+        return out, total
+
+    def decode_layer_fused(self, i: int, h: torch.Tensor, slots: torch.Tensor, n_live: torch.Tensor,
+                           pos: torch.Tensor, length: torch.Tensor, kc: torch.Tensor,
+                           vc: torch.Tensor, err: torch.Tensor) -> torch.Tensor:
+        """decode_layer on fused kernels: the input norm, the q/k norms with the
+        rotary embedding and the cache append, the residual add with the
+        post-attention norm, and the SiLU gate are one kernel each; the
+        projections stay the model's own modules (cuBLAS)."""
+        from tide_b200 import _native
+
+        ops = _native.ops()
+        layer = self.layers[i]
+        attn = layer.self_attn
+        n = h.shape[0]
+        x, _ = self.rms_norm(layer.input_layernorm, h, n_live)
+        q = attn.q_proj(x).view(n, -1, 128)
+        k = attn.k_proj(x).view(n, -1, 128)
+        v = attn.v_proj(x).view(n, -1, 128)
+        qn, kn = getattr(attn, "q_norm", None), getattr(attn, "k_norm", None)
+        q_rot = torch.empty_like(q)
+        ops.qk_norm_rope(q, k, v, qn.weight if qn is not None else None,
+                         kn.weight if kn is not None else None,
+                         float(qn.variance_epsilon) if qn is not None else 0.0,
+                         self._inv_freq(), float(getattr(self.rotary, "attention_scaling", 1.0)),
+                         0, pos, slots, n_live, q_rot, kc, vc, err)
+        o = torch.empty_like(q_rot)
+        ops.decode_attention(q_rot, kc, vc, slots, o, kc.shape[2], float(attn.scaling), err,
+                             n_live, length)
+        x2, h1 = self.rms_norm(layer.post_attention_layernorm, h, n_live,
+                               delta=attn.o_proj(o.view(n, -1)))
+        mlp = layer.mlp
+        g = mlp.gate_proj(x2)
+        act = torch.empty_like(g)
+        ops.silu_mul(g, mlp.up_proj(x2), act, n_live)
+        return h1 + mlp.down_proj(act)
+
+
 class _GPT2Family:
     """GPT-2 blocks (fused c_attn, learned absolute positions)."""
 
@@ -310,7 +391,8 @@ class LiveDecoder:
     it (one launch per step).  Llama-family layers with a head dimension of
     128, bf16 or fp16."""
 
-    def __init__(self, runtime, n_slots: int, max_len: int, graph: bool = False):
+    def __init__(self, runtime, n_slots: int, max_len: int, graph: bool = False,
+                 fused_layers: bool = True):
         from tide_b200.ops import CheckpointRunner
 
         fam = runtime._live_family()
@@ -331,6 +413,9 @@ class LiveDecoder:
         self.runner = CheckpointRunner(p.device)
         self.err = self.runner.error_word
         self.graph = graph
+        # the layers' elementwise work on fused kernels where the model's
+        # modules are ones they reproduce; otherwise the modules themselves
+        self.fused = fused_layers and fam.fused_decode_ok()
         self._bufs = {}
         self.exits_dev = torch.zeros(len(fam.layers), dtype=torch.int64, device=p.device)
         self.remaining_dev = torch.zeros(1, dtype=torch.int64, device=p.device)
@@ -382,8 +467,8 @@ class LiveDecoder:
         b.exit_layer.fill_(-1)
         thr = rt.config.exit_threshold
         for i in range(len(fam.layers)):
-            h = fam.decode_layer(i, h, slots, n_live, self.pos, length, self.k[i], self.v[i],
-                                 self.err)
+            layer_fn = fam.decode_layer_fused if self.fused else fam.decode_layer
+            h = layer_fn(i, h, slots, n_live, self.pos, length, self.k[i], self.v[i], self.err)
             if i not in b.ck:
                 continue
             comp, rows_out, slots_out, exit_pos, counts = b.ck[i]
@@ -399,7 +484,7 @@ class LiveDecoder:
             h, rows, slots, n_live = comp, rows_out, slots_out, counts[0:1]
         # the rows that never exit: the model's last hidden state (its final
         # norm applied, as HF reports it), final-normed once more
-        last = fam.norm(h).contiguous()
+        last = fam.rms_norm(fam.norm, h, n_live)[0] if self.fused else fam.norm(h).contiguous()
         _native.ops().norm_scatter_rows(last, rows, n_live, b.out_buf, norm.weight, norm.bias,
                                         norm.kind, norm.eps, self.err)
         self.remaining_dev += n_live
