@@ -226,8 +226,11 @@ int tide_norm_scatter_rows(int dtype, int norm_type, const void *rows, const int
  *                     with cos/sin = to_T(cos/sin(pos * inv_freq[j]) *
  *                     attention_scaling), then q to q_out and k, v into the
  *                     slot-addressed caches at pos (*position_dev when given).
- *                     A slot or position outside the cache writes nothing for
- *                     that row and sets TIDE_DEVERR_POSITION.
+ *                     rope_positions (optional, int64 per row): each row's own
+ *                     rotary position instead of pos (a prefill, which passes
+ *                     its [n, heads, 1, 128] outputs as the caches, identity
+ *                     slots and pos 0).  A slot or position outside the cache
+ *                     writes nothing for that row and sets TIDE_DEVERR_POSITION.
  * tide_silu_mul:      out = to_T(to_T(silu(gate)) * up), [n, width], width % 8
  *                     == 0 -- the gated MLP's act_fn(gate_proj(x)) * up_proj(x).
  * The reference runs the model's own modules for these inside its decode
@@ -238,8 +241,9 @@ int tide_rms_norm(int dtype, const void *x, const void *delta, void *sum_out, co
 int tide_qk_norm_rope(int dtype, const void *q, const void *k, const void *v,
                       const void *q_norm_weight, const void *k_norm_weight, float eps,
                       const float *inv_freq, float attention_scaling, int64_t position,
-                      const int32_t *position_dev, const int32_t *slots,
-                      const int32_t *n_rows_dev, int64_t n_rows, int64_t n_q_heads,
+                      const int32_t *position_dev, const int64_t *rope_positions,
+                      const int32_t *slots, const int32_t *n_rows_dev, int64_t n_rows,
+                      int64_t n_q_heads,
                       int64_t n_kv_heads, int64_t head_dim, void *q_out, void *k_cache,
                       void *v_cache, int64_t n_slots, int64_t max_len, int32_t *error_word,
                       tide_stream_t stream);

@@ -446,8 +446,8 @@ def test_fused_qk_norm_rope_is_the_hf_modules(qk_norm):
         ops.qk_norm_rope(q, k, v, attn.q_norm.weight if qk_norm else None,
                          attn.k_norm.weight if qk_norm else None, float(attn.q_norm.variance_epsilon),
                          rot.inv_freq.float(), float(rot.attention_scaling), 0,
-                         torch.tensor([pos], dtype=torch.int32, device=DEV), slots, None, q_out, kc,
-                         vc, err)
+                         torch.tensor([pos], dtype=torch.int32, device=DEV), None, slots, None, q_out,
+                         kc, vc, err)
         qn = attn.q_norm(q) if qk_norm else q
         kn = attn.k_norm(k) if qk_norm else k
         cos, sin = rot(v, torch.full((1, n), pos, dtype=torch.long, device=DEV))
@@ -502,3 +502,24 @@ def test_live_decoder_fused_layers_match_the_module_layers(tmp_path):
     for (la, ea), (lb, eb) in zip(a[:2], b[:2]):
         torch.testing.assert_close(la, lb, atol=6e-2, rtol=6e-2)
     assert sa.total_tokens == sb.total_tokens
+
+
+@pytest.mark.parametrize("family", ["llama", "qwen3"])
+def test_live_forward_fused_layers_match_the_module_layers(tmp_path, family):
+    """The live prefill on the fused layer kernels against the same forward on
+    the model's own modules (bf16): the same exits, logits within bf16 noise."""
+    from tide_b200.live import live_forward
+
+    # head_dim 128: Llama at hidden 512 with 4 heads
+    model = llama(dtype=torch.bfloat16, layers=4, hidden=512) if family == "llama" else _qwen3_hd128()
+    H = model.config.hidden_size
+    ids = torch.randint(0, 512, (3, 40), generator=torch.Generator().manual_seed(31)).to(DEV)
+    tuned_routers(tmp_path / "router.pt", model, ids, [1, 2], [0.3, 0.3], 0.6)
+    rt = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.6,
+                                                                       min_layers=0))
+    assert family_of(model).fused_decode_ok()
+    outs = [live_forward(rt, ids, None, fused_layers=f) for f in (False, True)]
+    (oa, sa, ea), (ob, sb, eb) = outs
+    assert torch.equal(ea, eb) and sa.exits_per_layer == sb.exits_per_layer
+    torch.testing.assert_close(ob.float(), oa.float(), atol=5e-2, rtol=5e-2)
+    assert H % 8 == 0

@@ -10,9 +10,12 @@
 //   tide_qk_norm_rope    per head: optional RMSNorm of q and k (Qwen3's
 //                        q_norm / k_norm), the rotary embedding
 //                        q*cos + rotate_half(q)*sin with cos/sin of
-//                        position * inv_freq rounded to T, then q to its
-//                        output and k, v into the slot-addressed cache at the
-//                        decode position (what tide_kv_append does).
+//                        position * inv_freq rounded to T (the decode
+//                        position, or each row's own for a prefill), then q
+//                        to its output and k, v into the slot-addressed cache
+//                        at the decode position (what tide_kv_append does; a
+//                        prefill passes [n, heads, 1, 128] outputs as the
+//                        "cache" with identity slots).
 //   tide_silu_mul        to_T(to_T(silu(gate)) * up): the gated MLP's
 //                        act_fn(gate_proj(x)) * up_proj(x).
 //
@@ -109,7 +112,8 @@ __global__ void __launch_bounds__(256)
     qk_norm_rope_kernel(const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v,
                         const T *__restrict__ q_w, const T *__restrict__ k_w, float eps,
                         const float *__restrict__ inv_freq, float att_scale, int64_t pos_host,
-                        const int32_t *__restrict__ pos_dev, const int32_t *__restrict__ slots,
+                        const int32_t *__restrict__ pos_dev, const int64_t *__restrict__ rope_pos,
+                        const int32_t *__restrict__ slots,
                         const int32_t *__restrict__ n_dev, int64_t n_cap, int hq, int hkv,
                         T *__restrict__ q_out, T *__restrict__ kc, T *__restrict__ vc,
                         int64_t n_slots, int64_t max_len, int32_t *err) {
@@ -146,6 +150,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int e = 0; e < 4; ++e) f[e] = Elem<T>::to_f(e4[e]);
     const T *nw = kind == 0 ? q_w : k_w;
+    const int64_t rot_pos = rope_pos ? rope_pos[row] : pos;  // the row's own position (prefill)
     if (nw) {  // the head's RMSNorm (HF: fp32 statistics, normalised rounded to T, times w)
       float ss = 0.f;
 #pragma unroll
@@ -162,7 +167,7 @@ __global__ void __launch_bounds__(256)
       const float partner = __shfl_xor_sync(0xffffffffu, f[e], 16);
       const float rot = lane < 16 ? -partner : partner;
       const int j = (d0 + e) & (kD / 2 - 1);
-      const float freq = (float)pos * inv_freq[j];
+      const float freq = (float)rot_pos * inv_freq[j];
       const float c = round_t<T>(cosf(freq) * att_scale), s = round_t<T>(sinf(freq) * att_scale);
       o[e] = round_t<T>(round_t<T>(f[e] * c) + round_t<T>(rot * s));
     }
@@ -263,8 +268,9 @@ extern "C" int tide_rms_norm(int dtype, const void *x, const void *delta, void *
 extern "C" int tide_qk_norm_rope(int dtype, const void *q, const void *k, const void *v,
                                  const void *q_norm_weight, const void *k_norm_weight, float eps,
                                  const float *inv_freq, float attention_scaling, int64_t position,
-                                 const int32_t *position_dev, const int32_t *slots,
-                                 const int32_t *n_rows_dev, int64_t n_rows, int64_t n_q_heads,
+                                 const int32_t *position_dev, const int64_t *rope_positions,
+                                 const int32_t *slots, const int32_t *n_rows_dev, int64_t n_rows,
+                                 int64_t n_q_heads,
                                  int64_t n_kv_heads, int64_t head_dim, void *q_out, void *k_cache,
                                  void *v_cache, int64_t n_slots, int64_t max_len,
                                  int32_t *error_word, tide_stream_t stream) {
@@ -288,15 +294,15 @@ extern "C" int tide_qk_norm_rope(int dtype, const void *q, const void *k, const 
         static_cast<const __nv_bfloat16 *>(q), static_cast<const __nv_bfloat16 *>(k),
         static_cast<const __nv_bfloat16 *>(v), static_cast<const __nv_bfloat16 *>(q_norm_weight),
         static_cast<const __nv_bfloat16 *>(k_norm_weight), eps, inv_freq, attention_scaling,
-        position, position_dev, slots, n_rows_dev, n_rows, (int)n_q_heads, (int)n_kv_heads,
-        static_cast<__nv_bfloat16 *>(q_out), static_cast<__nv_bfloat16 *>(k_cache),
+        position, position_dev, rope_positions, slots, n_rows_dev, n_rows, (int)n_q_heads,
+        (int)n_kv_heads, static_cast<__nv_bfloat16 *>(q_out), static_cast<__nv_bfloat16 *>(k_cache),
         static_cast<__nv_bfloat16 *>(v_cache), n_slots, max_len, error_word);
   else
     qk_norm_rope_kernel<__half><<<grid, 256, 0, s>>>(
         static_cast<const __half *>(q), static_cast<const __half *>(k),
         static_cast<const __half *>(v), static_cast<const __half *>(q_norm_weight),
         static_cast<const __half *>(k_norm_weight), eps, inv_freq, attention_scaling, position,
-        position_dev, slots, n_rows_dev, n_rows, (int)n_q_heads, (int)n_kv_heads,
+        position_dev, rope_positions, slots, n_rows_dev, n_rows, (int)n_q_heads, (int)n_kv_heads,
         static_cast<__half *>(q_out), static_cast<__half *>(k_cache),
         static_cast<__half *>(v_cache), n_slots, max_len, error_word);
   return launched("qk_norm_rope");

@@ -509,7 +509,8 @@ void qk_norm_rope(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v,
                   const std::optional<at::Tensor> &q_norm_weight,
                   const std::optional<at::Tensor> &k_norm_weight, double eps,
                   const at::Tensor &inv_freq, double attention_scaling, int64_t position,
-                  const std::optional<at::Tensor> &position_dev, const std::optional<at::Tensor> &slots,
+                  const std::optional<at::Tensor> &position_dev,
+                  const std::optional<at::Tensor> &rope_positions, const std::optional<at::Tensor> &slots,
                   const std::optional<at::Tensor> &n_rows_dev, const at::Tensor &q_out,
                   const at::Tensor &k_cache, const at::Tensor &v_cache,
                   const std::optional<at::Tensor> &error_word) {
@@ -537,11 +538,17 @@ void qk_norm_rope(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v,
   for (const auto *t : {&position_dev, &n_rows_dev, &error_word})
     if (t->has_value() && (*t)->defined())
       TORCH_CHECK((*t)->is_cuda() && (*t)->scalar_type() == at::kInt, "device words must be int32");
+  if (rope_positions.has_value() && rope_positions->defined()) {
+    check_cuda_contig(*rope_positions, "rope_positions");
+    TORCH_CHECK(rope_positions->scalar_type() == at::kLong && rope_positions->numel() >= q.size(0),
+                "rope_positions: int64 per row");
+  }
   const c10::cuda::CUDAGuard guard(q.device());
   TIDE_CHECK_OK(tide_qk_norm_rope(
       to_dtype(dt, "qk_norm_rope"), q.data_ptr(), k.data_ptr(), v.data_ptr(), opt_ptr(q_norm_weight),
       opt_ptr(k_norm_weight), (float)eps, inv_freq.data_ptr<float>(), (float)attention_scaling,
-      position, static_cast<const int32_t *>(opt_ptr(position_dev)), sl,
+      position, static_cast<const int32_t *>(opt_ptr(position_dev)),
+      static_cast<const int64_t *>(opt_ptr(rope_positions)), sl,
       static_cast<const int32_t *>(opt_ptr(n_rows_dev)), q.size(0), q.size(1), k.size(1), q.size(2),
       q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.size(0), k_cache.size(2),
       static_cast<int32_t *>(opt_mut(error_word)), cur_stream(q)));
@@ -724,8 +731,8 @@ TORCH_LIBRARY(tide, m) {
         "float eps, Tensor? n_rows_dev=None) -> ()");
   m.def("qk_norm_rope(Tensor q, Tensor k, Tensor v, Tensor? q_norm_weight, Tensor? k_norm_weight, "
         "float eps, Tensor inv_freq, float attention_scaling, int position, Tensor? position_dev, "
-        "Tensor? slots, Tensor? n_rows_dev, Tensor(a!) q_out, Tensor(b!) k_cache, Tensor(c!) v_cache, "
-        "Tensor(d!)? error_word) -> ()");
+        "Tensor? rope_positions, Tensor? slots, Tensor? n_rows_dev, Tensor(a!) q_out, "
+        "Tensor(b!) k_cache, Tensor(c!) v_cache, Tensor(d!)? error_word) -> ()");
   m.def("silu_mul(Tensor gate, Tensor up, Tensor(a!) out, Tensor? n_rows_dev=None) -> ()");
   m.def("kv_append(Tensor k_new, Tensor v_new, Tensor? slots, Tensor? n_rows_dev, Tensor(a!) k_cache, "
         "Tensor(b!) v_cache, int position, Tensor? position_dev, Tensor(c!)? error_word) -> ()");

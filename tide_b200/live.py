@@ -209,6 +209,42 @@ class _LlamaFamily:
                                n_live)
         return out, total
 
+    def layer_fused(self, i: int, h: torch.Tensor, pos: Optional[torch.Tensor],
+                    seq_pos: torch.Tensor, B: int, S: int) -> torch.Tensor:
+        """layer() of the live prefill on the fused kernels: the input norm,
+        the q/k norms with the rotary embedding at each row's own position,
+        the residual add with the post-attention norm, and the SiLU gate are
+        one kernel each; projections and attention as in layer()."""
+        from tide_b200 import _native
+
+        ops = _native.ops()
+        layer = self.layers[i]
+        attn = layer.self_attn
+        n = h.shape[0]
+        x, _ = self.rms_norm(layer.input_layernorm, h, None)
+        q = attn.q_proj(x).view(n, -1, 128)
+        k = attn.k_proj(x).view(n, -1, 128)
+        v = attn.v_proj(x).view(n, -1, 128)
+        hkv = k.shape[1]
+        qn, kn = getattr(attn, "q_norm", None), getattr(attn, "k_norm", None)
+        q_rot, k_rot = torch.empty_like(q), torch.empty_like(k)
+        # the rows' own outputs serve as a one-position "cache" with identity
+        # slots (v is written onto itself)
+        ident = torch.arange(n, dtype=torch.int32, device=h.device)
+        ops.qk_norm_rope(q, k, v, qn.weight if qn is not None else None,
+                         kn.weight if kn is not None else None,
+                         float(qn.variance_epsilon) if qn is not None else 0.0,
+                         self._inv_freq(), float(getattr(self.rotary, "attention_scaling", 1.0)),
+                         0, None, seq_pos.long().contiguous(), ident, None, q_rot,
+                         k_rot.view(n, hkv, 1, 128), v.view(n, hkv, 1, 128), None)
+        o = _attend(q_rot, k_rot, v, pos, B, S, float(attn.scaling))
+        x2, h1 = self.rms_norm(layer.post_attention_layernorm, h, None, delta=attn.o_proj(o))
+        mlp = layer.mlp
+        g = mlp.gate_proj(x2)
+        act = torch.empty_like(g)
+        ops.silu_mul(g, mlp.up_proj(x2), act, None)
+        return h1 + mlp.down_proj(act)
+
     def decode_layer_fused(self, i: int, h: torch.Tensor, slots: torch.Tensor, n_live: torch.Tensor,
                            pos: torch.Tensor, length: torch.Tensor, kc: torch.Tensor,
                            vc: torch.Tensor, err: torch.Tensor) -> torch.Tensor:
@@ -232,7 +268,7 @@ class _LlamaFamily:
                          kn.weight if kn is not None else None,
                          float(qn.variance_epsilon) if qn is not None else 0.0,
                          self._inv_freq(), float(getattr(self.rotary, "attention_scaling", 1.0)),
-                         0, pos, slots, n_live, q_rot, kc, vc, err)
+                         0, pos, None, slots, n_live, q_rot, kc, vc, err)
         o = torch.empty_like(q_rot)
         ops.decode_attention(q_rot, kc, vc, slots, o, kc.shape[2], float(attn.scaling), err,
                              n_live, length)
@@ -290,11 +326,14 @@ def family_of(model: nn.Module):
 
 @torch.no_grad()
 def live_forward(runtime, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor],
-                 on_checkpoint: Optional[Callable[[int, int], None]] = None):
+                 on_checkpoint: Optional[Callable[[int, int], None]] = None,
+                 fused_layers: bool = True):
     """The live forward of TIDERuntime (see the module docstring): returns
     (out_buf [B*S, H] of final-normed rows at their token positions,
     ExitStats, exit_layer [B*S] int32).  One host read-back of the survivor
-    count per checkpoint (the next layers' shapes depend on it)."""
+    count per checkpoint (the next layers' shapes depend on it).  Llama-
+    family layers of a 16-bit model run on the fused elementwise kernels when
+    they are ones those reproduce (fused_layers=False: the modules)."""
     from tide_b200.scheduler import ExitStats
 
     if attention_mask is not None and not bool(attention_mask.bool().all()):
@@ -316,10 +355,13 @@ def live_forward(runtime, input_ids: torch.Tensor, attention_mask: Optional[torc
     pos_out = [torch.empty(N, dtype=torch.int64, device=dev) for _ in range(2)]
     exit_pos = torch.empty(N, dtype=torch.int64, device=dev)
     counts = torch.zeros(2, dtype=torch.int32, device=dev)
+    fused = fused_layers and isinstance(fam, _LlamaFamily) and \
+        dtype in (torch.bfloat16, torch.float16) and fam.fused_decode_ok()
+    layer_fn = fam.layer_fused if fused else fam.layer
     n_ck = 0
     for i in range(len(fam.layers)):
         seq_pos = seq_all if pos is None else pos % S
-        h = fam.layer(i, h, pos, seq_pos, B, S)
+        h = layer_fn(i, h, pos, seq_pos, B, S)
         if i not in routers:
             continue
         nxt = pos_out[n_ck % 2]
@@ -343,7 +385,7 @@ def live_forward(runtime, input_ids: torch.Tensor, attention_mask: Optional[torc
     if n_rem:
         # as the post-hoc path: the model's last hidden state (its final norm
         # applied, as HF reports it), final-normed once more
-        last = fam.norm(h).contiguous()
+        last = fam.rms_norm(fam.norm, h, None)[0] if fused else fam.norm(h).contiguous()
         if pos is None:
             pos = torch.arange(N, device=dev)
         runtime._runner.norm_scatter(last, pos, out_buf, runtime._norm)
