@@ -107,13 +107,15 @@ NCU_TRAFFIC_CKPT0 = {"rows": 32768, "path": "tc_split", "bytes": (269.5 + 63.3 +
 
 
 def e2e_step_count(requested, h2d_bytes_per_step: int) -> int:
-    """Steps of the e2e region: as requested, else enough for about 2 GB of
-    host-to-device copies (at least 3, at most 200), so that a small
-    workload's region is not a few hundred microseconds of host jitter.  The
-    bytes are those one step actually copies."""
+    """Steps of the e2e region: as requested, else enough for about 8 GB of
+    host-to-device copies (at least 6, at most 200), so that a small
+    workload's region is not a few hundred microseconds of host jitter and
+    the copies of consecutive steps reach their pipelined rate (the first
+    step's load is not overlapped).  The bytes are those one step actually
+    copies."""
     if requested is not None:
         return int(requested)
-    return max(3, min(200, int(2e9 // max(int(h2d_bytes_per_step), 1))))
+    return max(6, min(200, int(8e9 // max(int(h2d_bytes_per_step), 1))))
 
 
 def algorithmic_bytes(n: int, exits: int, h: int, e: int) -> int:
@@ -1166,12 +1168,30 @@ def run_checkpoints(args, world, rank, local) -> None:
     d2h = int(host_out.numel() * host_out.element_size() + n_last * HIDDEN * e
               + host_counts.numel() * 4)
     e2e_steps = e2e_step_count(args.e2e_steps, h2d)
-    e_graph = wl.capture(dev_x)[0]
+    # Two input sets, each with its own step graph: step i+1's host->device
+    # copies run on a copy stream while step i computes and its results go
+    # back (the link is full duplex); a set is refilled only after the graph
+    # that read it has finished.
+    in_sets = [dev_x, [torch.empty_like(x) for x in wl.x]]
+    e_graphs = [wl.capture(in_sets[0])[0], wl.capture(in_sets[1])[0]]
+    s_in = torch.cuda.Stream()
+    loaded = [torch.cuda.Event(), torch.cuda.Event()]
+    released = [torch.cuda.Event(), torch.cuda.Event()]
 
-    def e2e_step():
-        for k in range(len(LAYERS)):
-            dev_x[k][: active[k]].copy_(host_x[k], non_blocking=True)
-        e_graph.replay()
+    def e2e_load(i):
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(released[b])
+            for k in range(len(LAYERS)):
+                in_sets[b][k][: active[k]].copy_(host_x[k], non_blocking=True)
+            loaded[b].record(s_in)
+
+    def e2e_step(i):
+        b = i % 2
+        cur = torch.cuda.current_stream()
+        cur.wait_event(loaded[b])
+        e_graphs[b].replay()
+        released[b].record(cur)
         if gather:
             gather.after_step(wl.counts)
         host_out.copy_(wl.out, non_blocking=True)
@@ -1179,23 +1199,30 @@ def run_checkpoints(args, world, rank, local) -> None:
             host_surv[:n_last].copy_(wl.compact[:n_last], non_blocking=True)
         host_counts.copy_(wl.counts, non_blocking=True)
 
-    e2e_step()  # untimed: the graph's first launch uploads it to the device
+    for i in range(2):  # untimed: each graph's first launch uploads it to the device
+        e2e_load(i)
+        e2e_step(i)
     if gather:
         gather.finish()
     barrier(world)
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record()
-    for _ in range(e2e_steps):
-        e2e_step()
+    s_in.wait_stream(torch.cuda.current_stream())
+    e2e_load(0)
+    for i in range(e2e_steps):
+        if i + 1 < e2e_steps:
+            e2e_load(i + 1)
+        e2e_step(i)
     if gather:
         gather.finish()
+    torch.cuda.current_stream().wait_stream(s_in)
     e_end.record()
     torch.cuda.synchronize()
     e_el = max_over_ranks(world, e_start.elapsed_time(e_end) / 1000.0)
     e2e = {"value": world * rows_per_step * e2e_steps / e_el, "unit": "tokens/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps}
-    del e_graph, step_graph, ck_graphs, host_out, dev_x
+    del e_graphs, in_sets, step_graph, ck_graphs, host_out, dev_x
 
     paths_used = [PATH_NAMES.get(wl.paths[k], wl.paths[k]) for k in range(len(LAYERS))]
     n_launch = sum(launches_per_checkpoint(p) for p in wl.paths.values()) * args.steps

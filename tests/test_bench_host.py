@@ -36,10 +36,10 @@ def test_algorithmic_bytes(bench):
 
 
 def test_e2e_step_count(bench):
-    # the headline sweep copies ~1.6 GB per step: the minimum of 3 steps
-    assert bench.e2e_step_count(None, 32768 * 4096 * 2 * 6) == 3
-    # a 12.6 MB workload: enough steps for ~2 GB of copies
-    assert bench.e2e_step_count(None, 4096 * 768 * 4) == 158
+    # the headline sweep copies ~1.6 GB per step: ~8 GB over 6 steps (the minimum)
+    assert bench.e2e_step_count(None, 32768 * 4096 * 2 * 6) == 6
+    # a 12.6 MB workload: the cap of 200 steps
+    assert bench.e2e_step_count(None, 4096 * 768 * 4) == 200
     assert bench.e2e_step_count(None, 1) == 200
     assert bench.e2e_step_count(5, 1) == 5
     assert bench.e2e_step_count(1, 10 ** 12) == 1
