@@ -174,11 +174,16 @@ class _LlamaFamily:
         if getattr(rot, "rope_type", "default") not in ("default", "llama3", "linear") or \
                 not isinstance(getattr(rot, "inv_freq", None), torch.Tensor):
             return False
+        H = self.embed.embedding_dim
+        if H % 8 or H > 8192:  # tide_rms_norm's row layout
+            return False
         norms = [self.norm]
         for layer in self.layers:
             a, m = layer.self_attn, layer.mlp
             if getattr(a, "head_dim", 0) != 128 or not all(
                     hasattr(m, n) for n in ("gate_proj", "up_proj", "down_proj")):
+                return False
+            if m.gate_proj.out_features % 8:  # tide_silu_mul's vectors
                 return False
             # nn.SiLU, or transformers' SiLUActivation (F.silu)
             if type(getattr(m, "act_fn", None)).__name__ not in ("SiLU", "SiLUActivation"):
