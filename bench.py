@@ -696,7 +696,7 @@ def decode_checkpoints(world: int, rank: int, steps: int = 200) -> dict:
 
 def decode_generate(world: int, rank: int, steps: int = 128, batch: int = 256,
                     ctx: int = 1024) -> dict:
-    """Config 4 at model level: a random-init bf16 Qwen3-8B-architecture
+    """Decode at model level: a random-init bf16 Qwen3-8B-architecture
     model (36 layers, H 4096, 32/8 heads, head_dim 128, MLP 12288, vocab
     151936, QK-norm), a decode batch of 256 sequences per rank whose KV cache
     holds 1024 positions of N(0,1) keys and values, routers at layers
