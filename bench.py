@@ -634,6 +634,10 @@ def engine_prefill(world: int, rank: int, reps: int = 10, warmup: int = 3) -> di
         stats = tdist.global_stats(world, engine.last_stats, layers)
         t_live = timed(lambda: engine(ids, live=True))
         live_stats = tdist.global_stats(world, engine.last_stats, layers)
+        # lm_head on the last position only (what a prefill before decoding
+        # needs), post hoc and live
+        t_keep = timed(lambda: engine(ids, logits_to_keep=1))
+        t_live_keep = timed(lambda: engine(ids, live=True, logits_to_keep=1))
         t_hf = timed(lambda: model(ids).logits)
     tokens = B_all * S * reps
     res.update({"engine_tok_s": tokens / t_engine, "engine_ms_per_call": 1000 * t_engine / reps,
@@ -645,6 +649,10 @@ def engine_prefill(world: int, rank: int, reps: int = 10, warmup: int = 3) -> di
                 "live_mode": "layers after each checkpoint on the active tokens only; exited "
                              "tokens' K/V zero-padded",
                 "live_exit_rate": live_stats.exit_rate,
+                "last_logits_only_tok_s": tokens / t_keep,
+                "live_last_logits_only_tok_s": tokens / t_live_keep,
+                "last_logits_only_mode": "logits_to_keep=1: lm_head on each sequence's last "
+                                         "position only (vocab 128256)",
                 "live_exits_per_layer": {str(k): v for k, v in
                                          sorted(live_stats.exits_per_layer.items())}})
     del engine, model

@@ -237,22 +237,27 @@ def test_score_router_matches_oracle(tmp_path):
 
 
 def test_logits_to_keep(tmp_path):
-    """logits_to_keep = k gives the last k positions of the full logits (the
-    same exit decisions and buffer; lm_head only on the kept rows)."""
+    """logits_to_keep = k: lm_head on the last k positions only.  Against the
+    oracle's post-hoc output rows at those positions through the model's
+    lm_head (bf16 rows: identical where the exit layers agree), and against
+    the full logits' last k positions (bit-identical: the same exit buffer)."""
     model = llama()
-    write_routers(tmp_path / "router.pt", 256, [1, 2], bias=0.8)
+    ids = torch.randint(0, 512, (2, 24), generator=torch.Generator().manual_seed(4)).to(DEV)
+    routers = tuned_routers(tmp_path / "router.pt", model, ids, [1, 2], [0.3, 0.3], 0.7)
     rt = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.7,
                                                                        min_layers=0))
-    ids = torch.randint(0, 512, (2, 24), generator=torch.Generator().manual_seed(4)).to(DEV)
     with torch.no_grad():
         full = rt(ids)
         stats = rt.last_stats
+        ours_exit = rt.last_exit_layer.reshape(2, 24).clone()
         last = rt(ids, logits_to_keep=1)
         last3 = rt(ids, logits_to_keep=3)
+        ref, _, _, _ = oracle_logits(model, rt, ids, routers, 0.7, 0, norm_of(rt._final_norm, "rms"))
     assert last.shape == (2, 1, 512) and last3.shape == (2, 3, 512)
     torch.testing.assert_close(last, full[:, -1:, :], atol=0, rtol=0)
     torch.testing.assert_close(last3, full[:, -3:, :], atol=0, rtol=0)
-    assert rt.last_stats == stats
+    assert rt.last_stats == stats and stats.total_exited > 0
+    torch.testing.assert_close(last3.float(), ref[:, -3:, :].float(), atol=2e-2, rtol=2e-2)
 
 
 def test_threshold_pins(tmp_path):
