@@ -170,14 +170,14 @@ def test_decode_attention_flags_a_slot_outside_the_cache():
     assert torch.all(out[1] == 5.0) and torch.all(out[0] == 0.0) and torch.all(out[2] == 0.0)
 
 
-def _qwen3_hd128():
+def _qwen3_hd128(dtype=torch.bfloat16):
     from transformers import Qwen3Config, Qwen3ForCausalLM
 
     cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
                       num_attention_heads=2, num_key_value_heads=1, head_dim=128,
                       rms_norm_eps=1e-6, max_position_embeddings=256)
     torch.manual_seed(0)
-    return Qwen3ForCausalLM(cfg).to(DEV, torch.bfloat16).eval()
+    return Qwen3ForCausalLM(cfg).to(DEV, dtype).eval()
 
 
 @pytest.mark.parametrize("graph", [False, True])
@@ -523,3 +523,63 @@ def test_live_forward_fused_layers_match_the_module_layers(tmp_path, family):
     assert torch.equal(ea, eb) and sa.exits_per_layer == sb.exits_per_layer
     torch.testing.assert_close(ob.float(), oa.float(), atol=5e-2, rtol=5e-2)
     assert H % 8 == 0
+
+
+def test_live_decoder_when_every_row_exits_at_the_first_checkpoint(tmp_path):
+    """A threshold every score passes: all rows exit at the first checkpoint,
+    the live count drops to 0 and the later layers touch no row (their
+    attention and cache appends are skipped); every row's logits come from
+    that exit, the same as the post-hoc chain's, graph or not."""
+    from tide_b200.live import LiveDecoder
+    from tide_b200.scheduler import ExitStats
+
+    model = _qwen3_hd128()
+    B, S = 5, 10
+    ids = torch.randint(0, 512, (B, S), generator=torch.Generator().manual_seed(41)).to(DEV)
+    tuned_routers(tmp_path / "router.pt", model, ids, [1, 2], [0.3, 0.3], 0.6)
+    rt = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=-1.0,
+                                                                       min_layers=0))
+    for graph in (False, True):
+        dec = LiveDecoder(rt, B, S + 3, graph=graph)
+        st = ExitStats()
+        with torch.no_grad():
+            first = dec.prefill(ids)
+            lg = dec.step(first.argmax(-1), st).float().clone()
+        dec.read_stats(st)
+        assert st.exits_per_layer == {1: B} and st.remaining_tokens == 0
+        assert torch.all(dec.last_exit_layer == 1)
+        for i in range(2, len(dec.k)):  # nothing written above the exit layer
+            assert torch.all(dec.k[i][:, :, S] == 0) and torch.all(dec.v[i][:, :, S] == 0)
+        with torch.no_grad():
+            pre = model(ids, use_cache=True)
+            out = model(first.argmax(-1)[:, None], past_key_values=pre.past_key_values,
+                        use_cache=True, output_hidden_states=True)
+            h1 = out.hidden_states[2][:, -1, :].contiguous()
+            ref = torch.empty_like(h1)
+            rt._runner.norm_scatter(h1, torch.arange(B, device=DEV), ref, rt._norm)
+            ref_logits = rt._lm_head(ref).float()
+        torch.testing.assert_close(lg, ref_logits, atol=6e-2, rtol=6e-2)
+
+
+def test_live_decoder_fp16(tmp_path):
+    """The live decoder on an fp16 model (fused layers, graph) against the same
+    decoder on the model's own modules."""
+    from tide_b200.live import LiveDecoder
+    from tide_b200.scheduler import ExitStats
+
+    model = _qwen3_hd128(torch.float16)
+    B, S = 4, 9
+    ids = torch.randint(0, 512, (B, S), generator=torch.Generator().manual_seed(43)).to(DEV)
+    tuned_routers(tmp_path / "router.pt", model, ids, [1, 2], [0.3, 0.3], 0.6)
+    rt = TIDERuntime(model, tmp_path / "router.pt", config=TIDEConfig(exit_threshold=0.6,
+                                                                       min_layers=0))
+    outs = []
+    for fused in (False, True):
+        dec = LiveDecoder(rt, B, S + 3, graph=fused, fused_layers=fused)
+        assert dec.fused == fused
+        with torch.no_grad():
+            tok = dec.prefill(ids).argmax(-1)
+            outs.append((dec.step(tok, ExitStats()).float().clone(), dec.last_exit_layer.clone()))
+    (la, ea), (lb, eb) = outs
+    assert torch.equal(ea, eb)
+    torch.testing.assert_close(lb, la, atol=2e-2, rtol=2e-2)
