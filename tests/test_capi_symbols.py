@@ -164,3 +164,35 @@ def test_testhooks_library_mirrors_the_product_surface():
     for n in declared_functions():
         assert hasattr(lib, n), n
     assert lib.tide_abi_version() == 1
+
+
+def test_decode_entry_points_reject_bad_arguments_without_a_gpu():
+    """The decode-side entry points (attention, cache append, norm scatter
+    with a device count, the fused layer kernels) validate their arguments
+    before any device call."""
+    lib = _native.lib()
+    ERR_INVALID, ERR_UNSUPPORTED = 1, 2
+    # decode attention: head_dim 64, G = 3, a length past the cache
+    assert lib.tide_decode_attention(2, 16, 16, 16, None, 16, 4, None, 8, 2, 64, 4, 32, 8, None,
+                                     0.1, None, None) == ERR_UNSUPPORTED
+    assert b"head_dim" in lib.tide_last_error()
+    assert lib.tide_decode_attention(2, 16, 16, 16, None, 16, 4, None, 6, 2, 128, 4, 32, 8, None,
+                                     0.1, None, None) == ERR_INVALID
+    assert lib.tide_decode_attention(2, 16, 16, 16, None, 16, 4, None, 8, 2, 128, 4, 32, 33, None,
+                                     0.1, None, None) == ERR_INVALID
+    assert lib.tide_decode_attention(0, 16, 16, 16, None, 16, 4, None, 8, 2, 128, 4, 32, 8, None,
+                                     0.1, None, None) == ERR_UNSUPPORTED  # fp32 caches
+    # cache append: a host position past the cache
+    assert lib.tide_kv_append(2, 16, 16, None, None, 4, 2, 128, 16, 16, 4, 32, 32, None, None,
+                              None) == ERR_INVALID
+    # norm scatter with a device count: bad norm type
+    assert lib.tide_norm_scatter_rows(2, 9, 16, 16, None, 4, 64, 8, 16, 16, None, 1e-5, None,
+                                      None) == ERR_INVALID
+    # fused layer kernels: widths they do not take
+    assert lib.tide_rms_norm(2, 16, None, None, 16, 16, 4, None, 100, 1e-6, None) == ERR_INVALID
+    assert lib.tide_rms_norm(2, 16, None, None, 16, 16, 4, None, 16384, 1e-6, None) == ERR_INVALID
+    assert lib.tide_silu_mul(2, 16, 16, 16, 4, None, 12, None) == ERR_INVALID
+    assert lib.tide_qk_norm_rope(2, 16, 16, 16, None, None, 1e-6, 16, 1.0, 0, None, None, None,
+                                 None, 4, 2, 1, 64, 16, 16, 16, 4, 8, None, None) == ERR_UNSUPPORTED
+    # nothing to do: no rows
+    assert lib.tide_rms_norm(2, None, None, None, None, None, 0, None, 64, 1e-6, None) == 0
