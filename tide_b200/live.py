@@ -417,6 +417,7 @@ class _StepBuffers:
                    for i in checkpoints}
         self.graph = None
         self.logits = None
+        self.threshold = None  # the exit threshold the graph was recorded with
 
 
 class LiveDecoder:
@@ -556,6 +557,7 @@ class LiveDecoder:
         self.exits_dev.zero_()
         self.remaining_dev.zero_()
         b.graph = torch.cuda.CUDAGraph()
+        b.threshold = self.rt.config.exit_threshold
         with torch.cuda.graph(b.graph):
             b.logits = self._body(b)
 
@@ -576,7 +578,10 @@ class LiveDecoder:
             b = self._bufs[B] = _StepBuffers(B, H, self.dtype, self.dev, self._checkpoints())
         b.tokens.copy_(tokens.reshape(B))
         if self.graph:
-            if b.graph is None:
+            # the threshold is a constant of the recorded step: record again
+            # when the engine's changes
+            if b.graph is None or b.threshold != self.rt.config.exit_threshold:
+                b.graph = None
                 self._capture(b)
             b.graph.replay()
             logits = b.logits
