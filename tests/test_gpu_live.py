@@ -583,3 +583,28 @@ def test_live_decoder_fp16(tmp_path):
     (la, ea), (lb, eb) = outs
     assert torch.equal(ea, eb)
     torch.testing.assert_close(lb, la, atol=2e-2, rtol=2e-2)
+
+
+def test_live_decoder_records_again_when_the_threshold_changes(tmp_path):
+    """A graph decoder whose engine's threshold changes between steps records
+    the step again: the steps after the change follow the new threshold, and
+    the exit counts of the steps before it are kept."""
+    from tide_b200.live import LiveDecoder
+    from tide_b200.scheduler import ExitStats
+
+    model, rt, ids = _decoder_case(tmp_path, B=6)
+    B, S = ids.shape
+    dec = LiveDecoder(rt, B, S + 6, graph=True)
+    st = ExitStats()
+    with torch.no_grad():
+        tok = dec.prefill(ids).argmax(-1)
+        tok = dec.step(tok, st).argmax(-1)
+        before = dec.exits_dev.clone()
+        rt.config.exit_threshold = 2.0  # no score passes: no row exits
+        dec.step(tok, st)
+        assert torch.all(dec.last_exit_layer == -1)
+        assert torch.equal(dec.exits_dev, before)
+    dec.read_stats(st)
+    rt.config.exit_threshold = 0.6
+    assert st.total_tokens == 2 * B and st.total_exited == int(before.sum())
+    assert st.remaining_tokens == 2 * B - st.total_exited

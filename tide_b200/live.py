@@ -19,7 +19,14 @@ MLP, which dominate a layer, run on the active rows only.
 
 Supported layer families: Llama-style decoder layers (q/k/v/o projections,
 optional per-head q/k RMSNorm as in Qwen3, rotary embeddings, gated MLP) and
-GPT-2 blocks.  Inputs without padding only.
+GPT-2 blocks.  Inputs without padding only.  For 16-bit Llama-family models
+the layers' elementwise work (RMSNorms with the residual adds, q/k norm +
+rotary, SiLU gate) runs on fused kernels that round where the HF modules
+round (tide_b200/csrc/decode_layer.cu); projections stay the modules' own.
+
+LiveDecoder does the same for decoding: per-row exits whose later layers
+skip the row, a KV cache addressed by slot, and steps free of host reads,
+each one CUDA-graph replay.
 """
 from __future__ import annotations
 
@@ -545,6 +552,7 @@ class LiveDecoder:
         are undone (the position's cache entries, the counters) before the
         capture, which runs nothing."""
         p = self._length
+        counters = (self.exits_dev.clone(), self.remaining_dev.clone())
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(s):
@@ -554,8 +562,8 @@ class LiveDecoder:
             kc[:, :, p].zero_()
             vc[:, :, p].zero_()
         self.length = p
-        self.exits_dev.zero_()
-        self.remaining_dev.zero_()
+        self.exits_dev.copy_(counters[0])
+        self.remaining_dev.copy_(counters[1])
         b.graph = torch.cuda.CUDAGraph()
         b.threshold = self.rt.config.exit_threshold
         with torch.cuda.graph(b.graph):
