@@ -101,9 +101,11 @@ def configure(name: str, rows: int | None = None) -> None:
 
 
 # DRAM bytes (read + write) of checkpoint 0's two kernels (router + mover),
-# 32768 rows x 4096 bf16, from the warm-cache ncu launch list of this
-# benchmark on the split path.
-NCU_TRAFFIC_CKPT0 = {"rows": 32768, "path": "tc_split", "bytes": (269.5 + 63.3 + 221.3 + 209.0) * 1e6}
+# 32768 rows x 4096 bf16, from an ncu capture of those two launches in this
+# benchmark's third warm-up step on the split path, caches left as the
+# previous kernels left them.
+NCU_TRAFFIC_CKPT0 = {"rows": 32768, "path": "tc_split",
+                     "bytes": (269.6 + 58.3 + 219.1 + 209.1) * 1e6}
 
 
 def e2e_step_count(requested, h2d_bytes_per_step: int) -> int:
@@ -1153,7 +1155,7 @@ def run_checkpoints(args, world, rank, local) -> None:
                else None)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic,
-                "traffic_source": "ncu launch list of this workload (warm caches)" if traffic else None,
+                "traffic_source": "ncu capture of checkpoint 0's two kernels in this workload (warm caches)" if traffic else None,
                 "peak_source": "measured" if (ROOT / "MEASURED_PEAKS.json").exists() else "fallback",
                 "kernel": f"checkpoint 0 ({ROWS} rows x {HIDDEN}), every kernel of the call",
                 "per_checkpoint_ms": per_ck, "per_checkpoint_reps": reps,

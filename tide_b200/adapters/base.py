@@ -10,6 +10,16 @@ import torch
 import torch.nn as nn
 
 
+def hidden_of(layer_output) -> torch.Tensor:
+    """The hidden states a decoder layer returned.  Older transformers
+    releases return a tuple whose first element is the hidden states (what
+    the reference's adapters index with `layer_output[0]`); current ones
+    return the tensor itself, where `[0]` would select the first sequence."""
+    if isinstance(layer_output, (tuple, list)):
+        return layer_output[0]
+    return layer_output
+
+
 class BaseAdapter(ABC):
     @abstractmethod
     def get_layers(self, model: nn.Module) -> list[nn.Module]: ...
@@ -45,7 +55,7 @@ class DecoderOnlyAdapter(BaseAdapter):
         return list(model.model.layers)
 
     def get_hidden_state(self, layer_output):
-        return layer_output[0]
+        return hidden_of(layer_output)
 
     def get_final_norm(self, model):
         return model.model.norm

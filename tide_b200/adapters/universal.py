@@ -14,7 +14,7 @@ from typing import Optional
 
 import torch.nn as nn
 
-from tide_b200.adapters.base import BaseAdapter
+from tide_b200.adapters.base import BaseAdapter, hidden_of
 
 logger = logging.getLogger("TIDE")
 
@@ -137,7 +137,7 @@ class UniversalAdapter(BaseAdapter):
         return self._layers
 
     def get_hidden_state(self, layer_output):
-        return layer_output[0]
+        return hidden_of(layer_output)
 
     def get_final_norm(self, model):
         self._ensure(model)
