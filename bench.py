@@ -14,7 +14,9 @@ the six checkpoints.  Inputs (1.1 GiB per step) exceed the 126 MB L2, so no
 explicit flush is needed between steps.  The same run also measures the
 8B-architecture prefill through the engine (random-init Llama-3.1-8B
 architecture, bf16, batch 16 x 2048 split over the ranks): engine(input_ids)
-against the model's own forward, 3 warm-up and 10 timed calls each.
+against the model's own forward, 3 warm-up and 10 timed calls each; and the
+same for a GPT-2-small-architecture model (fp16, LayerNorm, batch 8 x 512,
+routers at layers 4 and 8 exiting ~20 % of the tokens at each).
 
 Inputs: the first CAL_ROWS rows of every checkpoint's tensor and every
 router's weights come from a CPU torch.Generator, so the CPU reference arm
@@ -32,7 +34,7 @@ Other workloads (--workload):
       4, split evenly over the ranks), H in {2048, 4096, 5120, 8192} bf16,
       exit fraction f in {0, 0.1, 0.5, 0.9}; HBM GB/s against the measured
       copy peak for each;
-  llama8b_prefill_engine  the engine prefill measurement alone.
+  llama8b_prefill_engine  the engine prefill measurements alone.
 
 Multi-GPU: one process per GPU under torchrun; every rank processes its own
 batch (weak scaling).  The step's exit counts are all-gathered (NCCL) inside
@@ -551,6 +553,108 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def _tuned_routers(model, ids, layers, fracs, hidden, norm, seed, last_takes_rest=True):
+    """Routers (down/up N(0, 0.02)) at `layers` whose output biases exit the
+    scheduled share of the batch (fracs; with last_takes_rest the last one
+    exits every token still active) on the model's own hidden states for
+    `ids`.  norm = (kind, weight, bias, eps) of the final norm."""
+    from tide_b200 import workloads
+    from tide_b200.router import TokenRouter
+
+    dev = ids.device
+    kind, nw, nb, eps = norm
+    hs = model(ids, output_hidden_states=True, logits_to_keep=1).hidden_states
+    g = torch.Generator().manual_seed(seed)
+    N = ids.numel()
+    exited = torch.zeros(N, dtype=torch.bool, device=dev)
+    routers = {}
+    for L, f in zip(layers, fracs):
+        r = TokenRouter(hidden, 128, up_bias=True)
+        with torch.no_grad():
+            r.down.weight.normal_(0, 0.02, generator=g)
+            r.up.weight.normal_(0, 0.02, generator=g)
+        h = hs[L + 1].reshape(N, -1)
+        z = workloads.prebias_logits_torch(h, kind, nw, nb, eps, r.down.weight.to(dev),
+                                           r.up.weight.to(dev))
+        active = (~exited).nonzero()[:, 0]
+        last = last_takes_rest and L == layers[-1]
+        n_exit = int(active.numel()) if last else int(round(f * N))
+        za = z[active]
+        bias = workloads.bias_for_exit_fraction(za, n_exit / max(1, active.numel()), THRESHOLD)
+        with torch.no_grad():
+            r.up.bias.fill_(bias)
+        exited[active[(za + bias) > workloads.logit(THRESHOLD)]] = True
+        routers[L] = r
+    del hs
+    return routers
+
+
+def _timed_calls(world: int, fn, reps: int, warmup: int) -> float:
+    """Seconds for `reps` calls of fn after `warmup` untimed ones: CUDA
+    events on the current stream, max over ranks."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return max_over_ranks(world, a.elapsed_time(b) / 1000.0)
+
+
+def _engine_measure(world, model, ids, global_tokens, routers, hidden, layers, reps, warmup,
+                    keep_last: bool) -> dict:
+    """engine(ids) post hoc and live (and, with keep_last, with
+    logits_to_keep=1), and the model's own forward, on the same ids;
+    global_tokens = tokens of one call over all ranks."""
+    from tide_b200 import TIDEConfig
+    from tide_b200 import dist as tdist
+    from tide_b200.router import RouterCheckpoint
+    from tide_b200.runtime import TIDERuntime
+
+    tmp = Path(tempfile.mkdtemp(prefix="tide_bench_"))
+    RouterCheckpoint(routers, hidden, 128).save(tmp / "router.pt")
+    engine = TIDERuntime(model, tmp / "router.pt",
+                         config=TIDEConfig(exit_threshold=THRESHOLD, min_layers=0))
+    t_engine = _timed_calls(world, lambda: engine(ids), reps, warmup)
+    stats = tdist.global_stats(world, engine.last_stats, layers)
+    t_live = _timed_calls(world, lambda: engine(ids, live=True), reps, warmup)
+    live_stats = tdist.global_stats(world, engine.last_stats, layers)
+    t_hf = _timed_calls(world, lambda: model(ids).logits, reps, warmup)
+    # the model call the post-hoc engine makes (every layer's hidden states,
+    # one position's logits): the engine's time beyond it is its own
+    t_hs = _timed_calls(world, lambda: model(ids, output_hidden_states=True,
+                                             logits_to_keep=1).hidden_states, reps, warmup)
+    tokens = global_tokens * reps
+    res = {"engine_tok_s": tokens / t_engine, "engine_ms_per_call": 1000 * t_engine / reps,
+           "hf_forward_tok_s": tokens / t_hf, "hf_forward_ms_per_call": 1000 * t_hf / reps,
+           "hf_hidden_states_ms_per_call": 1000 * t_hs / reps,
+           "engine_mode": "post-hoc (every layer runs; the reference's semantics)",
+           "exit_rate": stats.exit_rate,
+           "exits_per_layer": {str(k): v for k, v in sorted(stats.exits_per_layer.items())},
+           "live_tok_s": tokens / t_live, "live_ms_per_call": 1000 * t_live / reps,
+           "live_mode": "layers after each checkpoint on the active tokens only; exited "
+                        "tokens' K/V zero-padded",
+           "live_exit_rate": live_stats.exit_rate,
+           "live_exits_per_layer": {str(k): v for k, v in
+                                    sorted(live_stats.exits_per_layer.items())}}
+    if keep_last:
+        # lm_head on the last position only (what a prefill before decoding
+        # needs), post hoc and live
+        t_keep = _timed_calls(world, lambda: engine(ids, logits_to_keep=1), reps, warmup)
+        t_live_keep = _timed_calls(world, lambda: engine(ids, live=True, logits_to_keep=1),
+                                   reps, warmup)
+        res.update({"last_logits_only_tok_s": tokens / t_keep,
+                    "live_last_logits_only_tok_s": tokens / t_live_keep,
+                    "last_logits_only_mode": "logits_to_keep=1: lm_head on each sequence's last "
+                                             "position only"})
+    del engine
+    return res
+
+
 def engine_prefill(world: int, rank: int, reps: int = 10, warmup: int = 3) -> dict:
     """8B-architecture prefill through the engine: a random-init bf16
     Llama-3.1-8B-architecture model (32 layers, H 4096, 32/8 heads, head_dim
@@ -562,11 +666,7 @@ def engine_prefill(world: int, rank: int, reps: int = 10, warmup: int = 3) -> di
     forward on the same ids."""
     from transformers import LlamaConfig, LlamaForCausalLM
 
-    from tide_b200 import TIDEConfig
     from tide_b200 import dist as tdist
-    from tide_b200 import workloads
-    from tide_b200.router import RouterCheckpoint, TokenRouter
-    from tide_b200.runtime import TIDERuntime
 
     dev = torch.device("cuda")
     layers, fracs = [8, 12, 16, 20, 24, 28], [0.05, 0.10, 0.15, 0.20, 0.20, 0.30]
@@ -590,74 +690,47 @@ def engine_prefill(world: int, rank: int, reps: int = 10, warmup: int = 3) -> di
            "seq_len": S, "batch_per_rank": b1 - b0, "scaling": "strong", "timed_calls": reps,
            "warmup_calls": warmup, "router_layers": layers, "exit_fractions_of_batch": fracs}
     with torch.inference_mode():
-        # routers and biases: exit the scheduled share of the rows still active
-        hs = model(ids, output_hidden_states=True, logits_to_keep=1).hidden_states
-        g = torch.Generator().manual_seed(SEED + 5)
-        N = ids.numel()
-        exited = torch.zeros(N, dtype=torch.bool, device=dev)
-        routers = {}
-        nw = model.model.norm.weight.float()
-        for L, f in zip(layers, fracs):
-            r = TokenRouter(4096, 128, up_bias=True)
-            with torch.no_grad():
-                r.down.weight.normal_(0, 0.02, generator=g)
-                r.up.weight.normal_(0, 0.02, generator=g)
-            h = hs[L + 1].reshape(N, -1)
-            z = workloads.prebias_logits_torch(h, "rms", nw, None, 1e-5, r.down.weight.to(dev),
-                                               r.up.weight.to(dev))
-            active = (~exited).nonzero()[:, 0]
-            n_exit = int(round(f * N)) if L != layers[-1] else int(active.numel())
-            za = z[active]
-            bias = workloads.bias_for_exit_fraction(za, n_exit / max(1, active.numel()), THRESHOLD)
-            with torch.no_grad():
-                r.up.bias.fill_(bias)
-            exited[active[(za + bias) > workloads.logit(THRESHOLD)]] = True
-            routers[L] = r
-        del hs
-        tmp = Path(tempfile.mkdtemp(prefix="tide_bench_"))
-        RouterCheckpoint(routers, 4096, 128).save(tmp / "router.pt")
-        engine = TIDERuntime(model, tmp / "router.pt",
-                             config=TIDEConfig(exit_threshold=THRESHOLD, min_layers=0))
+        routers = _tuned_routers(model, ids, layers, fracs, 4096,
+                                 ("rms", model.model.norm.weight.float(), None, 1e-5), SEED + 5)
+        res.update(_engine_measure(world, model, ids, B_all * S, routers, 4096, layers, reps,
+                                   warmup, keep_last=True))
+    del model
+    torch.cuda.empty_cache()
+    return res
 
-        def timed(fn) -> float:
-            for _ in range(warmup):
-                fn()
-            torch.cuda.synchronize()
-            barrier(world)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            for _ in range(reps):
-                fn()
-            b.record()
-            torch.cuda.synchronize()
-            return max_over_ranks(world, a.elapsed_time(b) / 1000.0)
 
-        t_engine = timed(lambda: engine(ids))
-        stats = tdist.global_stats(world, engine.last_stats, layers)
-        t_live = timed(lambda: engine(ids, live=True))
-        live_stats = tdist.global_stats(world, engine.last_stats, layers)
-        # lm_head on the last position only (what a prefill before decoding
-        # needs), post hoc and live
-        t_keep = timed(lambda: engine(ids, logits_to_keep=1))
-        t_live_keep = timed(lambda: engine(ids, live=True, logits_to_keep=1))
-        t_hf = timed(lambda: model(ids).logits)
-    tokens = B_all * S * reps
-    res.update({"engine_tok_s": tokens / t_engine, "engine_ms_per_call": 1000 * t_engine / reps,
-                "hf_forward_tok_s": tokens / t_hf, "hf_forward_ms_per_call": 1000 * t_hf / reps,
-                "engine_mode": "post-hoc (every layer runs; the reference's semantics)",
-                "exit_rate": stats.exit_rate,
-                "exits_per_layer": {str(k): v for k, v in sorted(stats.exits_per_layer.items())},
-                "live_tok_s": tokens / t_live, "live_ms_per_call": 1000 * t_live / reps,
-                "live_mode": "layers after each checkpoint on the active tokens only; exited "
-                             "tokens' K/V zero-padded",
-                "live_exit_rate": live_stats.exit_rate,
-                "last_logits_only_tok_s": tokens / t_keep,
-                "live_last_logits_only_tok_s": tokens / t_live_keep,
-                "last_logits_only_mode": "logits_to_keep=1: lm_head on each sequence's last "
-                                         "position only (vocab 128256)",
-                "live_exits_per_layer": {str(k): v for k, v in
-                                         sorted(live_stats.exits_per_layer.items())}})
-    del engine, model
+def gpt2_prefill(world: int, rank: int, reps: int = 10, warmup: int = 3) -> dict:
+    """GPT-2-small prefill through the engine: a random-init fp16 GPT-2-small
+    architecture model (12 layers, H 768, 12 heads, MLP 3072, vocab 50257,
+    LayerNorm), routers at layers 4 and 8 whose biases exit about 20 % of
+    the tokens at each, input 8 x 512 uniform random ids (seed 1) split by
+    sequence over the ranks.  Same protocol as the 8B-architecture prefill."""
+    from transformers import GPT2Config, GPT2LMHeadModel
+
+    from tide_b200 import dist as tdist
+
+    dev = torch.device("cuda")
+    layers, fracs = [4, 8], [0.20, 0.16]  # 20 % of the tokens, then 20 % of the rest
+    B_all, S = 8, 512
+    ids_all = torch.randint(0, 50257, (B_all, S), generator=torch.Generator().manual_seed(1))
+    b0, b1 = tdist.shard_range(B_all, world, rank)
+    ids = ids_all[b0:b1].to(dev)
+    cfg = GPT2Config(vocab_size=50257, n_embd=768, n_layer=12, n_head=12, n_inner=3072,
+                     n_positions=1024)
+    torch.manual_seed(SEED)
+    with torch.device(dev):
+        model = GPT2LMHeadModel(cfg).to(torch.float16).eval()
+    res = {"model": "GPT-2-small architecture, random-init fp16", "global_batch": B_all,
+           "seq_len": S, "batch_per_rank": b1 - b0, "scaling": "strong", "timed_calls": reps,
+           "warmup_calls": warmup, "router_layers": layers, "exit_fractions_of_batch": fracs}
+    with torch.inference_mode():
+        ln = model.transformer.ln_f
+        routers = _tuned_routers(model, ids, layers, fracs, 768,
+                                 ("ln", ln.weight.float(), ln.bias.float(), ln.eps), SEED + 6,
+                                 last_takes_rest=False)
+        res.update(_engine_measure(world, model, ids, B_all * S, routers, 768, layers, reps,
+                                   warmup, keep_last=False))
+    del model
     torch.cuda.empty_cache()
     return res
 
@@ -1058,12 +1131,14 @@ def main():
                                   "decode_attention": da}), flush=True)
         elif args.workload == ENGINE_WORKLOAD:
             eng = engine_prefill(world, rank)
+            gpt2 = gpt2_prefill(world, rank)
             if rank == 0:
                 print(json.dumps({"metric": "prefill_tokens_per_s", "value": eng["engine_tok_s"],
                                   "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
                                   "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
                                   "data": "synthetic", "config": {"workload": ENGINE_WORKLOAD},
-                                  "prefill_engine": eng}), flush=True)
+                                  "prefill_engine": eng, "prefill_engine_gpt2": gpt2}),
+                      flush=True)
         else:
             run_checkpoints(args, world, rank, local)
     finally:
@@ -1236,7 +1311,7 @@ def run_checkpoints(args, world, rank, local) -> None:
 
     paths_used = [PATH_NAMES.get(wl.paths[k], wl.paths[k]) for k in range(len(LAYERS))]
     n_launch = sum(launches_per_checkpoint(p) for p in wl.paths.values()) * args.steps
-    engine = decode = decode_gen = None
+    engine = engine_gpt2 = decode = decode_gen = None
     if WORKLOAD == "llama8b_prefill_checkpoints" and args.rows is None:
         del wl
         torch.cuda.empty_cache()
@@ -1246,6 +1321,10 @@ def run_checkpoints(args, world, rank, local) -> None:
                 engine = engine_prefill(world, rank)
             except Exception as exc:  # reported, not fatal: the checkpoint numbers stand
                 engine = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+            try:
+                engine_gpt2 = gpt2_prefill(world, rank)
+            except Exception as exc:
+                engine_gpt2 = {"error": f"{type(exc).__name__}: {exc}"[:400]}
             try:
                 decode_gen = decode_generate(world, rank)
             except Exception as exc:
@@ -1275,6 +1354,7 @@ def run_checkpoints(args, world, rank, local) -> None:
             "gpu_launches": n_launch, "clocks": clocks.summary(),
             "collectives_timed_separately": collectives,
             "prefill_engine": engine,
+            "prefill_engine_gpt2": engine_gpt2,
             "decode_checkpoints": decode,
             "decode_generate": decode_gen,
         }

@@ -103,7 +103,8 @@ def test_live_matches_dense_emulation(tmp_path, dtype):
         torch.testing.assert_close(logits.float(), ref.float(), atol=atol, rtol=atol)
 
 
-@pytest.mark.parametrize("G,L", [(4, 1), (4, 17), (4, 1025), (8, 300), (1, 64), (2, 5000)])
+@pytest.mark.parametrize("G,L", [(4, 1), (4, 17), (4, 1025), (8, 300), (1, 64), (2, 5000),
+                                 (8, 2100), (4, 4166)])
 def test_decode_attention_matches_torch(G, L):
     """tide_decode_attention over slot-addressed caches against an fp32 torch
     softmax attention of the gathered rows (bf16 in and out)."""
