@@ -238,8 +238,9 @@ class TIDERuntime(nn.Module):
                 logits_to_keep: int = 0, live: Optional[bool] = None, **kwargs) -> torch.Tensor:
         """Early-exit forward: logits [B, S, V].  By default the reference's
         post-hoc exit over the model's hidden states (runtime.py:134-192),
-        with one host synchronisation per call (the exit counts, after every
-        kernel is queued).  With live=True (or config.live_compaction) the
+        with one host synchronisation per call (the exit counts, after the
+        checkpoint chain is queued; the lm_head is queued after it and runs
+        while the caller goes on).  With live=True (or config.live_compaction) the
         layers after each checkpoint run only on the tokens still active
         (tide_b200/live.py; logits then differ from the post-hoc ones by
         design, through the exited tokens' zero-padded K/V).  After a call,
@@ -274,9 +275,10 @@ class TIDERuntime(nn.Module):
         if logits_to_keep > 0:
             rows = rows[:, -logits_to_keep:, :]
         if not self._learned_exits():
-            logits = self._lm_head(rows)  # queued before the read-back
+            # the read-back waits for the checkpoint chain only; the lm_head
+            # queued after it then runs while the caller goes on
             self.last_stats = self._read_back(layers, counts, exit_pos, N, (B, S))
-            return logits
+            return self._lm_head(rows)
         self.last_stats = self._read_back(layers, counts, exit_pos, N, (B, S))
         for k, layer in enumerate(layers):
             self._project_exits(out_buf, layer, exit_pos[k][: self._host_counts[2 * k + 1]])
