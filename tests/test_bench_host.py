@@ -1,5 +1,6 @@
 """Host-side pieces of bench.py that need no GPU: the workload table, the
-algorithmic bytes of a checkpoint and the e2e step count."""
+algorithmic bytes of a checkpoint, the e2e step count and the engine
+workloads' router tuning."""
 import importlib.util
 from pathlib import Path
 
@@ -82,3 +83,33 @@ def test_cpu_reference_step_chains_survivors(bench):
     assert t > 0 and 64 <= routed <= 6 * 64
     t2, routed2 = bench.cpu_sweep_step(inp)
     assert routed2 == routed  # deterministic
+
+
+@pytest.mark.parametrize("last_takes_rest", [False, True])
+def test_engine_router_tuning_places_the_exit_schedule(bench, last_takes_rest):
+    """The engine workloads' routers (bench._tuned_routers) exit the scheduled
+    share of the tokens at each checkpoint on the model's own hidden states
+    (here a small GPT-2-architecture model on the CPU, LayerNorm final norm),
+    and with last_takes_rest every token still active at the last one."""
+    from transformers import GPT2Config, GPT2LMHeadModel
+
+    torch.manual_seed(0)
+    m = GPT2LMHeadModel(GPT2Config(vocab_size=101, n_embd=64, n_layer=6, n_head=4,
+                                   n_positions=128)).eval()
+    ids = torch.randint(0, 101, (4, 64), generator=torch.Generator().manual_seed(1))
+    ln = m.transformer.ln_f
+    layers, fracs = [1, 3], [0.25, 0.15]
+    with torch.inference_mode():
+        routers = bench._tuned_routers(m, ids, layers, fracs, 64,
+                                       ("ln", ln.weight.float(), ln.bias.float(), ln.eps), 7,
+                                       last_takes_rest=last_takes_rest)
+        hs = m(ids, output_hidden_states=True).hidden_states
+        N = ids.numel()
+        exited = torch.zeros(N, dtype=torch.bool)
+        for L, f in zip(layers, fracs):
+            h = torch.nn.functional.layer_norm(hs[L + 1].reshape(N, -1).float(), (64,),
+                                               ln.weight, ln.bias, ln.eps)
+            new = (routers[L](h) > bench.THRESHOLD) & ~exited
+            want = int((~exited).sum()) if (last_takes_rest and L == layers[-1]) else round(f * N)
+            assert abs(int(new.sum()) - want) <= 2, (L, int(new.sum()), want)
+            exited |= new
