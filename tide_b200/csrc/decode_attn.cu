@@ -17,17 +17,21 @@
 //
 // Split over the positions (flash decoding): a thread-block cluster of S CTAs
 // per (active row, KV head), CTA s taking the blocks of 128 positions s,
-// s + S, s + 2S, ...  A CTA (128 threads) walks its blocks with a running
-// maximum and sum per query head:
+// s + S, s + 2S, ...  A CTA (eight warps, four at G = 8; warp w owns the
+// positions 16w .. 16w + 15 of a block, 32w .. 32w + 31 with four warps)
+// walks its blocks with a running maximum and sum per query head:
 //   scores   on the tensor cores (mma.sync m16n8k16, 16-bit operands, fp32
 //            accumulators): the G query heads as the rows of A, 8 key rows
-//            as B, four tiles per warp; a key row comes in as four 16-byte
-//            loads by the four lanes that hold it in B;
+//            as B, two (four) tiles per warp; the four lanes that hold a key row
+//            in B read it from shared memory as four 16-byte chunks each;
 //   softmax  one warp per query head: block maximum, rescale factor, the
 //            block's probabilities and their sum;
-//   P V      warp w takes 32 consecutive positions of the block, each lane
-//            four output dimensions of all G heads; a warp reads one 256-byte
-//            value row per position from shared memory.
+//   P V      each lane of warp w: four output dimensions of all G heads over
+//            the warp's positions; a warp reads one 256-byte value row per
+//            position from shared memory.
+// (Eight warps instead of four: the same bytes in flight, the compute
+// between a block's arrival and the next request spread over twice the
+// warps; 3-6 % faster.)
 // The S partial results (running max m_s, sum l_s, unnormalised output a_s)
 // are combined through distributed shared memory: after a cluster barrier
 // CTA r computes its share of the G*128 outputs as
@@ -36,12 +40,15 @@
 // read it.  Exponentials are base 2 on log2(e)-scaled scores.  fp32
 // throughout; output in the cache's 16-bit type.
 //
-// Loads: a block's keys and the query go to registers (16 + 4 loads of 16
-// bytes per lane, all issued before the first is used) and its values to
-// shared memory by one bulk copy (32 KB), so that a block is fetched in one
-// round trip; a CTA's next block is requested after its P V.  The wait for
-// the values is bounded: on expiry the kernel raises TIDE_DEVERR_TIMEOUT and
-// still meets its cluster's barriers.
+// Loads: a block's keys and its values go to shared memory by one bulk copy
+// each (32 KB, two mbarriers, so the scores start when the keys have
+// landed), so that a block is fetched in one round trip; a CTA's next block
+// is requested after its P V.  (Keys loaded to registers by 16-byte loads per
+// lane, and a second value buffer filled while the current block is used,
+// both measured slower.)  After the last block the partial outputs reuse the
+// same shared memory.  The waits are bounded: on expiry the kernel raises
+// TIDE_DEVERR_TIMEOUT, requests nothing more, waits once more for the copies
+// it has outstanding and still meets its cluster's barriers.
 //
 // The active row count and the length may live on the device (a
 // checkpoint's counts, the decode position), so that a decode step needs no
@@ -63,27 +70,29 @@ namespace tide {
 
 namespace dattn {
 constexpr int kD = 128;        // head dimension
-constexpr int kThreads = 128;  // 4 warps
+#ifndef TIDE_DATTN_WARPS
+#define TIDE_DATTN_WARPS 8
+#endif
+// Warps per CTA: eight, except at G = 8, whose larger per-lane accumulators
+// would spill at the register budget of three eight-warp CTAs per SM.
+__host__ __device__ constexpr int warps_for(int G) { return G >= 8 ? 4 : TIDE_DATTN_WARPS; }
 constexpr int kBlock = 128;    // positions per block
+
 constexpr int kMaxSplit = 8;   // CTAs per cluster (portable cluster size)
 #ifndef TIDE_DATTN_MIN_BLOCKS
 #define TIDE_DATTN_MIN_BLOCKS 3
 #endif
-constexpr int kMinBlocks = TIDE_DATTN_MIN_BLOCKS;  // resident CTAs per SM the registers allow
+constexpr int kMinBlocks = TIDE_DATTN_MIN_BLOCKS;  // resident CTAs per SM (64 KB of shared memory each)
+// Grid size the split aims at.  At 256 rows x 8 KV heads x 1024 positions
+// (G = 4, eight warps): 2048 (no split) 198 us with every row active, 114 and
+// 71 us with 128 and 64 of them; 2368 (pairs) 212, 112 and 65 us; the decode
+// step 11.4 against 11.9 ms.
 #ifndef TIDE_DATTN_TARGET_CTAS
-#define TIDE_DATTN_TARGET_CTAS 2368
+#define TIDE_DATTN_TARGET_CTAS 2048
 #endif
-constexpr int64_t kTargetCtas = TIDE_DATTN_TARGET_CTAS;  // grid size the split aims at
+constexpr int64_t kTargetCtas = TIDE_DATTN_TARGET_CTAS;
 constexpr float kLog2e = 1.4426950408889634f;
 }  // namespace dattn
-
-__device__ __forceinline__ uint4 ld_nc16(const void *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
 
 // Tensor-core tile of the scores: D[16 x 8] += A[16 x 16] * B[16 x 8],
 // A = query heads (rows; G <= 8 real, the rest zero), B = 8 key rows,
@@ -106,19 +115,29 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
 }
 
 template <typename T, int G>
-__global__ void __launch_bounds__(dattn::kThreads, dattn::kMinBlocks)
+__global__ void __launch_bounds__(32 * dattn::warps_for(G), dattn::kMinBlocks)
     decode_attention_kernel(const T *__restrict__ q, const T *__restrict__ kc,
                             const T *__restrict__ vc, const int32_t *__restrict__ slots,
                             T *__restrict__ o, int n_rows, const int32_t *__restrict__ n_dev,
                             int hq, int hkv, int64_t n_slots, int64_t max_len, int Lmax,
                             const int32_t *__restrict__ len_dev, float scale, int32_t *err) {
   using namespace dattn;
+  constexpr int kWarps = warps_for(G);
+  constexpr int kThreads = 32 * kWarps;
+  constexpr int kPos = kBlock / kWarps;  // positions of a block per warp (scores and P V)
+  static_assert(kPos % 8 == 0, "whole 8-position score tiles per warp");
   extern __shared__ __align__(128) unsigned char dyn_smem[];
-  T *s_v = reinterpret_cast<T *>(dyn_smem);        // [128 positions][128]: the block's values
+  // [128 positions][128] each: the block's keys, then its values; after the
+  // last block the per-warp partial outputs s_a[kWarps][G][128] (fp32, [0] =
+  // the CTA's) take the same bytes
+  T *s_k = reinterpret_cast<T *>(dyn_smem);
+  T *s_v = s_k + kBlock * kD;
+  float(*s_a)[G][kD] = reinterpret_cast<float(*)[G][kD]>(dyn_smem);
+  static_assert(kWarps * G * kD * sizeof(float) <= 2 * kBlock * kD * sizeof(T),
+                "s_a fits the block");
   __shared__ __align__(16) float s_p[G][kBlock];   // block scores, then probabilities
-  __shared__ __align__(16) float s_a[4][G][kD];    // per-warp partial outputs; [0] = the CTA's
   __shared__ float s_m[G], s_l[G], s_alpha[G];
-  __shared__ __align__(8) uint64_t bar_v;
+  __shared__ __align__(8) uint64_t bar_k, bar_v;
   __shared__ int s_abort;
 
   cg::cluster_group cluster = cg::this_cluster();
@@ -141,6 +160,7 @@ __global__ void __launch_bounds__(dattn::kThreads, dattn::kMinBlocks)
   const T *vb = vc + ((slot * hkv + kvh) * max_len) * kD;
 
   if (tid == 0) {
+    ptx::mbar_init(&bar_k, 1);
     ptx::mbar_init(&bar_v, 1);
     ptx::fence_mbar_init();
     s_abort = 0;
@@ -151,8 +171,11 @@ __global__ void __launch_bounds__(dattn::kThreads, dattn::kMinBlocks)
   }
   __syncthreads();
   const uint64_t pol = l2_evict_first_policy();  // the cache is read once per step
-  auto load_values = [&](int b) {
+  // a block's keys and values: one bulk copy each (thread 0)
+  auto load_block = [&](int b) {
     const uint32_t bytes = (uint32_t)min(kBlock, L - b) * kD * (uint32_t)sizeof(T);
+    ptx::mbar_expect_tx(&bar_k, bytes);
+    ptx::bulk_load(s_k, kb + (int64_t)b * kD, bytes, &bar_k, pol);
     ptx::mbar_expect_tx(&bar_v, bytes);
     ptx::bulk_load(s_v, vb + (int64_t)b * kD, bytes, &bar_v, pol);
   };
@@ -163,26 +186,7 @@ __global__ void __launch_bounds__(dattn::kThreads, dattn::kMinBlocks)
   // fragments use the same dims for row n (query head n < G), so each tile's
   // k order is a permutation shared by both operands.
   const int t4 = lane & 3, n8 = lane >> 2;
-  uint4 kv[4][4];
-  auto load_keys = [&](int b) {
-    const int nb = min(kBlock, L - b);
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int t = warp * 32 + it * 8 + n8;
-      if (t < nb) {
-        const T *kr = kb + (int64_t)(b + t) * kD;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) kv[it][c] = ld_nc16(kr + (c * 4 + t4) * 8);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) kv[it][c] = make_uint4(0, 0, 0, 0);
-      }
-    }
-  };
-  // one round trip for a block: the values by bulk copy, the keys and the
-  // query to registers
-  if (tid == 0 && split * kBlock < L) load_values(split * kBlock);
-  if (split * kBlock < L) load_keys(split * kBlock);
+  if (tid == 0 && split * kBlock < L) load_block(split * kBlock);
   uint4 qf[4];
   if (n8 < G) {
     const T *qr = q + ((int64_t)row * hq + kvh * G + n8) * kD;
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(dattn::kThreads, dattn::kMinBlocks)
   }
   const float qs = scale * kLog2e;
   uint32_t phase = 0;
-  int late_phase = -1;  // the phase of a wait that expired, if any
+  int late_k = -1, late_v = -1;  // the phases of waits that expired, if any
 
   float acc[G][4];
 #pragma unroll
@@ -204,25 +208,34 @@ __global__ void __launch_bounds__(dattn::kThreads, dattn::kMinBlocks)
   // block count: that CTA's partial result is empty)
   for (int b0 = split * kBlock; b0 < L; b0 += S * kBlock) {
     const int nb = min(kBlock, L - b0);
-    // scores: four 16 x 8 tiles per warp, eight k-steps each
+    // the block's keys in shared memory (bounded wait, as for the values)
+    if (!ptx::mbar_wait(&bar_k, phase, &s_abort)) {
+      if (lane == 0) raise_error(err, TIDE_DEVERR_TIMEOUT);
+      s_abort = 1;
+      late_k = (int)phase;
+    }
+    // scores: four 16 x 8 tiles per warp, eight k-steps each; rows at or
+    // past nb hold an earlier block's keys (or nothing) and are masked below
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
+    for (int it = 0; it < kPos / 8; ++it) {
       float d[4] = {0.f, 0.f, 0.f, 0.f};
+      const T *kr = s_k + (warp * kPos + it * 8 + n8) * kD;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        mma_16816<T>(d, qf[c].x, qf[c].y, kv[it][c].x, kv[it][c].y);
-        mma_16816<T>(d, qf[c].z, qf[c].w, kv[it][c].z, kv[it][c].w);
+        const uint4 kc4 = *reinterpret_cast<const uint4 *>(kr + (c * 4 + t4) * 8);
+        mma_16816<T>(d, qf[c].x, qf[c].y, kc4.x, kc4.y);
+        mma_16816<T>(d, qf[c].z, qf[c].w, kc4.z, kc4.w);
       }
       // d[0], d[1]: head n8 at block positions w*32 + it*8 + 2*t4 + {0, 1}
       if (n8 < G) {
-        const int t = warp * 32 + it * 8 + 2 * t4;
+        const int t = warp * kPos + it * 8 + 2 * t4;
         *reinterpret_cast<float2 *>(&s_p[n8][t]) =
             make_float2(t < nb ? d[0] * qs : -INFINITY, t + 1 < nb ? d[1] * qs : -INFINITY);
       }
     }
     __syncthreads();
     // softmax of the block, one warp per query head
-    for (int g = warp; g < G; g += kThreads / 32) {
+    for (int g = warp; g < G; g += kWarps) {
       float v[4], mx = -INFINITY;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -265,10 +278,10 @@ __global__ void __launch_bounds__(dattn::kThreads, dattn::kMinBlocks)
     if (!ptx::mbar_wait(&bar_v, phase, &s_abort)) {
       if (lane == 0) raise_error(err, TIDE_DEVERR_TIMEOUT);
       s_abort = 1;
-      late_phase = (int)phase;
+      late_v = (int)phase;
     }
     phase ^= 1u;
-    const int p0 = warp * 32, p1 = min(nb, p0 + 32);
+    const int p0 = warp * kPos, p1 = min(nb, p0 + kPos);
     for (int t0 = p0; t0 < p1; t0 += 4) {
       float4 pg[G];
 #pragma unroll
@@ -291,26 +304,31 @@ __global__ void __launch_bounds__(dattn::kThreads, dattn::kMinBlocks)
         }
       }
     }
-    __syncthreads();  // s_p, s_alpha and the values are rewritten by the next block
-    if (b0 + S * kBlock < L) {
-      if (tid == 0) load_values(b0 + S * kBlock);
-      load_keys(b0 + S * kBlock);
-    }
+    __syncthreads();  // s_p, s_alpha, the keys and values are rewritten by the next block
+    // (nothing more is requested once a wait has expired: at most one copy
+    // per barrier is ever outstanding)
+    if (tid == 0 && b0 + S * kBlock < L && !s_abort) load_block(b0 + S * kBlock);
   }
 
-  if (late_phase >= 0 && tid == 0) {  // a copy may still be landing: wait for it once more
+  if (tid == 0) {  // after an expired wait a copy may still be landing: wait for it once more
     volatile int none = 0;
-    ptx::mbar_wait(&bar_v, (uint32_t)late_phase, &none);
+    if (late_k >= 0) ptx::mbar_wait(&bar_k, (uint32_t)late_k, &none);
+    if (late_v >= 0) ptx::mbar_wait(&bar_v, (uint32_t)late_v, &none);
   }
-  // this CTA's unnormalised output: sum of the four warps' partials
+  __syncthreads();  // the key and value buffers become s_a
+  // this CTA's unnormalised output: sum of the warps' partials
 #pragma unroll
   for (int g = 0; g < G; ++g)
     *reinterpret_cast<float4 *>(&s_a[warp][g][lane * 4]) =
         make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
   __syncthreads();
+  for (int e = tid; e < G * kD; e += kThreads) {
+    const int g = e / kD, d = e % kD;
+    float sum = s_a[0][g][d];
 #pragma unroll
-  for (int g = 0; g < G; ++g)
-    s_a[0][g][tid] = (s_a[0][g][tid] + s_a[1][g][tid]) + (s_a[2][g][tid] + s_a[3][g][tid]);
+    for (int w = 1; w < kWarps; ++w) sum += s_a[w][g][d];
+    s_a[0][g][d] = sum;
+  }
 
   cluster.sync();  // every CTA's m, l and output are in its shared memory
   constexpr int kOut = G * kD;
@@ -391,18 +409,23 @@ cudaError_t launch_attention(const void *q, const void *k_cache, const void *v_c
                              const int32_t *n_rows_dev, int hq, int hkv, int64_t n_slots,
                              int64_t max_len, int length, const int32_t *length_dev, float scale,
                              int32_t *error_word, int splits, cudaStream_t s) {
-  const size_t dyn = tide::dattn::kBlock * tide::dattn::kD * sizeof(T);
+  const size_t dyn = 2 * tide::dattn::kBlock * tide::dattn::kD * sizeof(T);
   static bool attr_set = false;  // per instantiation: static + dynamic exceed 48 KB at G = 8
   if (!attr_set) {
-    const cudaError_t e = cudaFuncSetAttribute(tide::decode_attention_kernel<T, G>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)dyn);
+    cudaError_t e = cudaFuncSetAttribute(tide::decode_attention_kernel<T, G>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+    if (e != cudaSuccess) return e;
+    // the whole unified L1 / shared array as shared memory: three CTAs of
+    // 64 KB of keys and values each per SM
+    e = cudaFuncSetAttribute(tide::decode_attention_kernel<T, G>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(n_rows * hkv * splits), 1, 1);
-  cfg.blockDim = dim3(tide::dattn::kThreads, 1, 1);
+  cfg.blockDim = dim3(32 * tide::dattn::warps_for(G), 1, 1);
   cfg.dynamicSmemBytes = dyn;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -493,7 +516,9 @@ extern "C" int tide_decode_attention(int dtype, const void *q, const void *k_cac
   }
   // Positions split over a cluster of up to 8 CTAs (at most one per block of
   // 128): as few as keep about kTargetCtas CTAs in the grid, since every
-  // CTA pays a fixed cost (its first round trip, the cluster combine).
+  // CTA pays a fixed cost (its first round trip, the cluster combine).  The
+  // split follows the row capacity (n_rows), not the live count on the
+  // device.
   const int64_t blocks = (length + dattn::kBlock - 1) / dattn::kBlock;
   const int64_t units = n_rows * n_kv_heads;
   int64_t splits = dattn::kTargetCtas > 0 ? (dattn::kTargetCtas + units - 1) / units : blocks;
