@@ -220,7 +220,10 @@ int tide_norm_scatter_rows(int dtype, int norm_type, const void *rows, const int
  *                     given); out = to_T(w * to_T(s * rsqrt(mean(s^2) + eps)))
  *                     -- HF LlamaRMSNorm / Qwen3RMSNorm with an optional fused
  *                     residual add.  hidden_dim % 8 == 0, <= 8192.
- * tide_qk_norm_rope:  q [n, hq, 128], k, v [n, hkv, 128]: optional per-head
+ * tide_qk_norm_rope:  q [n, hq, 128], k, v [n, hkv, 128], rows q_row_stride
+ *                     and kv_row_stride elements apart (0: packed; k and v
+ *                     share a stride, so q, k and v may be column slices of
+ *                     one fused projection's output): optional per-head
  *                     RMSNorm of q and k (Qwen3 q_norm / k_norm; NULL weight =
  *                     none), the rotary embedding q*cos + rotate_half(q)*sin
  *                     with cos/sin = to_T(cos/sin(pos * inv_freq[j]) *
@@ -239,6 +242,7 @@ int tide_rms_norm(int dtype, const void *x, const void *delta, void *sum_out, co
                   void *out, int64_t n_rows, const int32_t *n_rows_dev, int64_t hidden_dim,
                   float eps, tide_stream_t stream);
 int tide_qk_norm_rope(int dtype, const void *q, const void *k, const void *v,
+                      int64_t q_row_stride, int64_t kv_row_stride,
                       const void *q_norm_weight, const void *k_norm_weight, float eps,
                       const float *inv_freq, float attention_scaling, int64_t position,
                       const int32_t *position_dev, const int64_t *rope_positions,

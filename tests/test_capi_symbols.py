@@ -192,7 +192,15 @@ def test_decode_entry_points_reject_bad_arguments_without_a_gpu():
     assert lib.tide_rms_norm(2, 16, None, None, 16, 16, 4, None, 100, 1e-6, None) == ERR_INVALID
     assert lib.tide_rms_norm(2, 16, None, None, 16, 16, 4, None, 16384, 1e-6, None) == ERR_INVALID
     assert lib.tide_silu_mul(2, 16, 16, 16, 4, None, 12, None) == ERR_INVALID
-    assert lib.tide_qk_norm_rope(2, 16, 16, 16, None, None, 1e-6, 16, 1.0, 0, None, None, None,
-                                 None, 4, 2, 1, 64, 16, 16, 16, 4, 8, None, None) == ERR_UNSUPPORTED
+    assert lib.tide_qk_norm_rope(2, 16, 16, 16, 0, 0, None, None, 1e-6, 16, 1.0, 0, None, None,
+                                 None, None, 4, 2, 1, 64, 16, 16, 16, 4, 8, None,
+                                 None) == ERR_UNSUPPORTED
+    # q/k/v row strides that do not cover the heads, or not multiples of 8
+    assert lib.tide_qk_norm_rope(2, 16, 16, 16, 128, 0, None, None, 1e-6, 16, 1.0, 0, None, None,
+                                 None, None, 4, 2, 1, 128, 16, 16, 16, 4, 8, None,
+                                 None) == ERR_INVALID
+    assert lib.tide_qk_norm_rope(2, 16, 16, 16, 0, 132, None, None, 1e-6, 16, 1.0, 0, None, None,
+                                 None, None, 4, 2, 1, 128, 16, 16, 16, 4, 8, None,
+                                 None) == ERR_INVALID
     # nothing to do: no rows
     assert lib.tide_rms_norm(2, None, None, None, None, None, 0, None, 64, 1e-6, None) == 0

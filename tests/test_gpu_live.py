@@ -417,11 +417,13 @@ def test_fused_rms_norm_is_the_hf_module(dtype):
                 assert torch.equal(tot[:live], s[:live]) and torch.all(tot[live:] == 7.0)
 
 
+@pytest.mark.parametrize("packed", [False, True])
 @pytest.mark.parametrize("qk_norm", [True, False])
-def test_fused_qk_norm_rope_is_the_hf_modules(qk_norm):
+def test_fused_qk_norm_rope_is_the_hf_modules(qk_norm, packed):
     """tide_qk_norm_rope against the model's q_norm / k_norm and rotary
     modules (apply_rotary_pos_emb), with k and v landing in the cache at the
-    rows' slots and the device position."""
+    rows' slots and the device position; packed: q, k and v as column slices
+    of one [n, (hq + 2 hkv) * 128] projection output (strided rows)."""
     from transformers.models.qwen3.modeling_qwen3 import apply_rotary_pos_emb
 
     from tide_b200 import _native
@@ -436,13 +438,19 @@ def test_fused_qk_norm_rope_is_the_hf_modules(qk_norm):
         q = torch.randn(n, hq, d, generator=g, device=DEV).to(torch.bfloat16)
         k = torch.randn(n, hkv, d, generator=g, device=DEV).to(torch.bfloat16)
         v = torch.randn(n, hkv, d, generator=g, device=DEV).to(torch.bfloat16)
+        if packed:
+            qkv = torch.cat([q.view(n, -1), k.view(n, -1), v.view(n, -1)], 1)
+            q = qkv[:, :hq * d].view(n, hq, d)
+            k = qkv[:, hq * d:(hq + hkv) * d].view(n, hkv, d)
+            v = qkv[:, (hq + hkv) * d:].view(n, hkv, d)
+            assert not q.is_contiguous() and k.stride(0) == (hq + 2 * hkv) * d
         for mod in (attn.q_norm, attn.k_norm):
             mod.weight.copy_((1 + 0.3 * torch.randn(d, generator=g, device=DEV)).to(torch.bfloat16))
         slots = torch.randperm(n_slots, generator=torch.Generator().manual_seed(2))[:n]
         slots = slots.to(torch.int32).to(DEV)
         kc = torch.zeros(n_slots, hkv, max_len, d, dtype=torch.bfloat16, device=DEV)
         vc = torch.zeros_like(kc)
-        q_out = torch.empty_like(q)
+        q_out = torch.empty(q.shape, dtype=q.dtype, device=DEV)
         err = torch.zeros(1, dtype=torch.int32, device=DEV)
         ops.qk_norm_rope(q, k, v, attn.q_norm.weight if qk_norm else None,
                          attn.k_norm.weight if qk_norm else None, float(attn.q_norm.variance_epsilon),

@@ -54,7 +54,7 @@ PROTOTYPES = {
     "tide_norm_scatter_rows": (C.c_int, [C.c_int, C.c_int, p, p, p, i64, i64, i64, p, p, p, f32,
                                          p, p]),
     "tide_rms_norm": (C.c_int, [C.c_int, p, p, p, p, p, i64, p, i64, f32, p]),
-    "tide_qk_norm_rope": (C.c_int, [C.c_int, p, p, p, p, p, f32, p, f32, i64, p, p, p, p, i64,
+    "tide_qk_norm_rope": (C.c_int, [C.c_int, p, p, p, i64, i64, p, p, f32, p, f32, i64, p, p, p, p, i64,
                                     i64, i64, i64, p, p, p, i64, i64, p, p]),
     "tide_silu_mul": (C.c_int, [C.c_int, p, p, p, i64, p, i64, p]),
     "tide_router_fold": (C.c_int, [C.c_int, p, p, p, i64, i64, p, p, p, p, p]),

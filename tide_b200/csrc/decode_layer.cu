@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(dlayer::kNormThreads)
 template <typename T>
 __global__ void __launch_bounds__(256)
     qk_norm_rope_kernel(const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v,
+                        int64_t q_stride, int64_t kv_stride,
                         const T *__restrict__ q_w, const T *__restrict__ k_w, float eps,
                         const float *__restrict__ inv_freq, float att_scale, int64_t pos_host,
                         const int32_t *__restrict__ pos_dev, const int64_t *__restrict__ rope_pos,
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(256)
       }
       dst = ((slot * hkv + h) * max_len + pos) * kD + d0;
     }
-    const T *src = kind == 0 ? q + (row * hq + h) * kD : (kind == 1 ? k : v) + (row * hkv + h) * kD;
+    const T *src = kind == 0 ? q + row * q_stride + h * kD : (kind == 1 ? k : v) + row * kv_stride + h * kD;
     const uint2 raw = *reinterpret_cast<const uint2 *>(src + d0);
     if (kind == 2) {  // values go to the cache as they are
       *reinterpret_cast<uint2 *>(vc + dst) = raw;
@@ -266,6 +267,7 @@ extern "C" int tide_rms_norm(int dtype, const void *x, const void *delta, void *
 }
 
 extern "C" int tide_qk_norm_rope(int dtype, const void *q, const void *k, const void *v,
+                                 int64_t q_row_stride, int64_t kv_row_stride,
                                  const void *q_norm_weight, const void *k_norm_weight, float eps,
                                  const float *inv_freq, float attention_scaling, int64_t position,
                                  const int32_t *position_dev, const int64_t *rope_positions,
@@ -281,6 +283,12 @@ extern "C" int tide_qk_norm_rope(int dtype, const void *q, const void *k, const 
   if (n_rows < 0 || n_q_heads < 1 || n_kv_heads < 1 || n_slots < 1 || max_len < 1 ||
       (!position_dev && (position < 0 || position >= max_len)) || (!slots && n_rows > n_slots))
     return fail_msg(TIDE_ERR_INVALID, "qk_norm_rope: bad sizes or position");
+  const int64_t q_stride = q_row_stride ? q_row_stride : n_q_heads * head_dim;
+  const int64_t kv_stride = kv_row_stride ? kv_row_stride : n_kv_heads * head_dim;
+  if (q_stride < n_q_heads * head_dim || kv_stride < n_kv_heads * head_dim || q_stride % 8 ||
+      kv_stride % 8)
+    return fail_msg(TIDE_ERR_INVALID,
+                    "qk_norm_rope: row strides must cover the heads and be multiples of 8");
   if (n_rows == 0) return TIDE_OK;
   if (!q || !k || !v || !inv_freq || !q_out || !k_cache || !v_cache)
     return fail_msg(TIDE_ERR_INVALID, "qk_norm_rope: NULL pointer");
@@ -292,7 +300,8 @@ extern "C" int tide_qk_norm_rope(int dtype, const void *q, const void *k, const 
   if (dtype == TIDE_DTYPE_BF16)
     qk_norm_rope_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
         static_cast<const __nv_bfloat16 *>(q), static_cast<const __nv_bfloat16 *>(k),
-        static_cast<const __nv_bfloat16 *>(v), static_cast<const __nv_bfloat16 *>(q_norm_weight),
+        static_cast<const __nv_bfloat16 *>(v), q_stride, kv_stride,
+        static_cast<const __nv_bfloat16 *>(q_norm_weight),
         static_cast<const __nv_bfloat16 *>(k_norm_weight), eps, inv_freq, attention_scaling,
         position, position_dev, rope_positions, slots, n_rows_dev, n_rows, (int)n_q_heads,
         (int)n_kv_heads, static_cast<__nv_bfloat16 *>(q_out), static_cast<__nv_bfloat16 *>(k_cache),
@@ -300,7 +309,7 @@ extern "C" int tide_qk_norm_rope(int dtype, const void *q, const void *k, const 
   else
     qk_norm_rope_kernel<__half><<<grid, 256, 0, s>>>(
         static_cast<const __half *>(q), static_cast<const __half *>(k),
-        static_cast<const __half *>(v), static_cast<const __half *>(q_norm_weight),
+        static_cast<const __half *>(v), q_stride, kv_stride, static_cast<const __half *>(q_norm_weight),
         static_cast<const __half *>(k_norm_weight), eps, inv_freq, attention_scaling, position,
         position_dev, rope_positions, slots, n_rows_dev, n_rows, (int)n_q_heads, (int)n_kv_heads,
         static_cast<__half *>(q_out), static_cast<__half *>(k_cache),

@@ -514,10 +514,16 @@ void qk_norm_rope(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v,
                   const std::optional<at::Tensor> &n_rows_dev, const at::Tensor &q_out,
                   const at::Tensor &k_cache, const at::Tensor &v_cache,
                   const std::optional<at::Tensor> &error_word) {
-  for (const auto *t : {&q, &k, &v, &q_out, &k_cache, &v_cache, &inv_freq}) check_cuda_contig(*t, "tensor");
+  for (const auto *t : {&q_out, &k_cache, &v_cache, &inv_freq}) check_cuda_contig(*t, "tensor");
   TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.sizes() == k.sizes() && q_out.sizes() == q.sizes() &&
               k.size(0) == q.size(0) && q.size(2) == k.size(2),
               "q [n, hq, d], k and v [n, hkv, d], q_out like q");
+  // q, k and v: heads packed within a row; rows may be strided (column
+  // slices of one fused q/k/v projection), k and v with one stride
+  for (const auto *t : {&q, &k, &v})
+    TORCH_CHECK(t->is_cuda() && t->stride(2) == 1 && t->stride(1) == t->size(2),
+                "q, k, v: [n, heads, d] with heads packed in each row");
+  TORCH_CHECK(k.stride(0) == v.stride(0), "k and v must share a row stride");
   TORCH_CHECK(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes() && k_cache.size(1) == k.size(1) &&
               k_cache.size(3) == k.size(2), "caches [slots, hkv, max_len, d]");
   const auto dt = q.scalar_type();
@@ -545,7 +551,8 @@ void qk_norm_rope(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v,
   }
   const c10::cuda::CUDAGuard guard(q.device());
   TIDE_CHECK_OK(tide_qk_norm_rope(
-      to_dtype(dt, "qk_norm_rope"), q.data_ptr(), k.data_ptr(), v.data_ptr(), opt_ptr(q_norm_weight),
+      to_dtype(dt, "qk_norm_rope"), q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0),
+      k.stride(0), opt_ptr(q_norm_weight),
       opt_ptr(k_norm_weight), (float)eps, inv_freq.data_ptr<float>(), (float)attention_scaling,
       position, static_cast<const int32_t *>(opt_ptr(position_dev)),
       static_cast<const int64_t *>(opt_ptr(rope_positions)), sl,
