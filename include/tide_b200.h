@@ -230,10 +230,13 @@ int tide_norm_scatter_rows(int dtype, int norm_type, const void *rows, const int
  *                     attention_scaling), then q to q_out and k, v into the
  *                     slot-addressed caches at pos (*position_dev when given).
  *                     rope_positions (optional, int64 per row): each row's own
- *                     rotary position instead of pos (a prefill, which passes
- *                     its [n, heads, 1, 128] outputs as the caches, identity
- *                     slots and pos 0).  A slot or position outside the cache
- *                     writes nothing for that row and sets TIDE_DEVERR_POSITION.
+ *                     rotary position instead of pos, and q written to
+ *                     q_out[slots[i]] instead of q_out[i] (a prefill, which
+ *                     passes [tokens, heads, 1, 128] buffers as the caches,
+ *                     its rows' token indices as the slots and pos 0, so
+ *                     that q, k and v land at their tokens' places).  A slot
+ *                     or position outside the cache writes nothing for that
+ *                     row and sets TIDE_DEVERR_POSITION.
  * tide_silu_mul:      out = to_T(to_T(silu(gate)) * up), [n, width], width % 8
  *                     == 0 -- the gated MLP's act_fn(gate_proj(x)) * up_proj(x).
  * The reference runs the model's own modules for these inside its decode

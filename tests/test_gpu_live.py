@@ -470,6 +470,50 @@ def test_fused_qk_norm_rope_is_the_hf_modules(qk_norm, packed):
         assert torch.all(kc[others.to(DEV)] == 0) and torch.all(kc[:, :, :pos] == 0)
 
 
+def test_fused_qk_norm_rope_prefill_at_token_places():
+    """A prefill-sized call (2048 rows x 48 heads: eight heads per warp, the
+    cos/sin computed once per row and head group): each row's own rotary
+    position, and q, k, v written at the row's token index (the slots) of
+    [tokens, heads, 1, 128] buffers; tokens no row maps to stay untouched.
+    Against the model's q_norm / k_norm and rotary modules."""
+    from transformers.models.qwen3.modeling_qwen3 import apply_rotary_pos_emb
+
+    from tide_b200 import _native
+
+    ops = _native.ops()
+    model = _qwen3_hd128()
+    attn = model.model.layers[1].self_attn
+    rot = model.model.rotary_emb
+    n, hq, hkv, d, tokens = 2048, 32, 8, 128, 3000
+    g = torch.Generator(device=DEV).manual_seed(12)
+    with torch.no_grad():
+        q = torch.randn(n, hq, d, generator=g, device=DEV).to(torch.bfloat16)
+        k = torch.randn(n, hkv, d, generator=g, device=DEV).to(torch.bfloat16)
+        v = torch.randn(n, hkv, d, generator=g, device=DEV).to(torch.bfloat16)
+        for mod in (attn.q_norm, attn.k_norm):
+            mod.weight.copy_((1 + 0.3 * torch.randn(d, generator=g, device=DEV)).to(torch.bfloat16))
+        place = torch.randperm(tokens, generator=torch.Generator().manual_seed(5))[:n].to(DEV)
+        seq_pos = torch.randint(0, 240, (n,), generator=torch.Generator().manual_seed(6)).to(DEV)
+        q_full = torch.full((tokens, hq, d), 3.0, dtype=torch.bfloat16, device=DEV)
+        k_full = torch.zeros(tokens, hkv, 1, d, dtype=torch.bfloat16, device=DEV)
+        v_full = torch.zeros_like(k_full)
+        err = torch.zeros(1, dtype=torch.int32, device=DEV)
+        ops.qk_norm_rope(q, k, v, attn.q_norm.weight, attn.k_norm.weight,
+                         float(attn.q_norm.variance_epsilon), rot.inv_freq.float(),
+                         float(rot.attention_scaling), 0, None, seq_pos, place.to(torch.int32),
+                         None, q_full, k_full, v_full, err)
+        cos, sin = rot(v, seq_pos[None])
+        q_ref, k_ref = apply_rotary_pos_emb(attn.q_norm(q), attn.k_norm(k), cos[0], sin[0],
+                                            unsqueeze_dim=1)
+        assert int(err.item()) == 0
+        assert _close16(q_full[place], q_ref)
+        assert _close16(k_full[place, :, 0], k_ref)
+        assert torch.equal(v_full[place, :, 0], v)
+        others = torch.ones(tokens, dtype=torch.bool, device=DEV)
+        others[place] = False
+        assert torch.all(q_full[others] == 3.0) and torch.all(k_full[others] == 0)
+
+
 def test_fused_silu_mul_is_the_hf_mlp_gate():
     from tide_b200 import _native
 

@@ -15,7 +15,8 @@
 //                        to its output and k, v into the slot-addressed cache
 //                        at the decode position (what tide_kv_append does; a
 //                        prefill passes [n, heads, 1, 128] outputs as the
-//                        "cache" with identity slots).
+//                        "cache", its rows' token indices as the slots, and
+//                        gets q at those indices too).
 //   tide_silu_mul        to_T(to_T(silu(gate)) * up): the gated MLP's
 //                        act_fn(gate_proj(x)) * up_proj(x).
 //
@@ -104,9 +105,14 @@ __global__ void __launch_bounds__(dlayer::kNormThreads)
   }
 }
 
-// One warp per (row, head) of the q, k and v heads of a row (in that
-// order), head_dim 128: lane l holds dims 4l..4l+3; the rotary partner of a
-// dim (d +- 64) sits 16 lanes away.
+// One warp per (row, group of `group` <= 8 heads) of the row's q, k and v
+// heads (in that order), head_dim 128: lane l holds dims 4l..4l+3; the
+// rotary partner of a dim (d +- 64) sits 16 lanes away.  The rotary cos/sin
+// of a lane's dims depend on the row's position only, so a warp computes
+// them once for its group, and issues the group's loads before using any.
+// A prefill (many rows) takes groups of eight heads, so the cos/sin are
+// computed once per row and eight heads instead of once per head; a decode
+// step (few rows) takes one head per warp, for more warps in flight.
 template <typename T>
 __global__ void __launch_bounds__(256)
     qk_norm_rope_kernel(const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v,
@@ -117,69 +123,103 @@ __global__ void __launch_bounds__(256)
                         const int32_t *__restrict__ slots,
                         const int32_t *__restrict__ n_dev, int64_t n_cap, int hq, int hkv,
                         T *__restrict__ q_out, T *__restrict__ kc, T *__restrict__ vc,
-                        int64_t n_slots, int64_t max_len, int32_t *err) {
+                        int64_t n_slots, int64_t max_len, int group, int32_t *err) {
   constexpr int kD = 128;
+  constexpr int kGroup = 8;  // most heads per warp
   const int lane = threadIdx.x & 31;
   const int heads = hq + 2 * hkv;
+  const int groups = (heads + group - 1) / group;
   const int64_t live = live_rows(n_dev, n_cap);
   const int64_t pos = pos_dev ? (int64_t)__ldg(pos_dev) : pos_host;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
-  for (int64_t wid = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); wid < live * heads;
-       wid += warps) {
-    const int64_t row = wid / heads;
-    const int hh = (int)(wid % heads);
-    const int kind = hh < hq ? 0 : (hh < hq + hkv ? 1 : 2);  // q, k, v
-    const int h = kind == 0 ? hh : (kind == 1 ? hh - hq : hh - hq - hkv);
-    const int d0 = lane * 4;
-    int64_t dst = 0;
-    if (kind != 0) {
-      const int64_t slot = slots ? (int64_t)slots[row] : row;
-      if (slot < 0 || slot >= n_slots || pos < 0 || pos >= max_len) {
-        if (lane == 0) raise_error(err, TIDE_DEVERR_POSITION);
+  const int d0 = lane * 4;
+  for (int64_t wid = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+       wid < live * groups; wid += warps) {
+    const int64_t row = wid / groups;
+    const int h0 = (int)(wid % groups) * group;
+    const int h1 = min(h0 + group, heads);
+    // the row's cache entry, when the group holds k or v heads; a prefill
+    // (rope_pos given) also writes q at the row's slot
+    const int64_t slot = slots ? (int64_t)slots[row] : row;
+    const bool slot_ok = slot >= 0 && slot < n_slots;
+    int64_t cache_row = 0;
+    bool cache_ok = true;
+    if (h1 > hq) {
+      cache_ok = slot_ok && pos >= 0 && pos < max_len;
+      if (!cache_ok && lane == 0) raise_error(err, TIDE_DEVERR_POSITION);
+      cache_row = (slot * hkv) * max_len + pos;  // + h * max_len per head
+    }
+    const bool q_at_slot = rope_pos != nullptr;
+    const bool q_ok = !q_at_slot || slot_ok;
+    if (h0 < hq && !q_ok && lane == 0) raise_error(err, TIDE_DEVERR_POSITION);
+    const int64_t q_row = q_at_slot ? slot : row;
+    // loads of the group's heads, all issued before the first is used
+    uint2 raw[kGroup];
+#pragma unroll
+    for (int i = 0; i < kGroup; ++i) {
+      const int hh = h0 + i;
+      raw[i] = make_uint2(0u, 0u);
+      if (hh >= h1) continue;
+      const T *src = hh < hq ? q + row * q_stride + (int64_t)hh * kD
+                   : (hh < hq + hkv ? k + row * kv_stride + (int64_t)(hh - hq) * kD
+                                    : v + row * kv_stride + (int64_t)(hh - hq - hkv) * kD);
+      raw[i] = *reinterpret_cast<const uint2 *>(src + d0);
+    }
+    // cos / sin of the lane's dims at the row's position (q and k heads only)
+    float cs[4] = {0.f, 0.f, 0.f, 0.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+    if (h0 < hq + hkv) {
+      const int64_t rot_pos = rope_pos ? rope_pos[row] : pos;  // a prefill row's own position
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float freq = (float)rot_pos * inv_freq[(d0 + e) & (kD / 2 - 1)];
+        cs[e] = round_t<T>(cosf(freq) * att_scale);
+        sn[e] = round_t<T>(sinf(freq) * att_scale);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kGroup; ++i) {
+      const int hh = h0 + i;
+      if (hh >= h1) break;
+      const int kind = hh < hq ? 0 : (hh < hq + hkv ? 1 : 2);  // q, k, v
+      const int h = kind == 0 ? hh : (kind == 1 ? hh - hq : hh - hq - hkv);
+      if (kind == 2) {  // values go to the cache as they are
+        if (cache_ok)
+          *reinterpret_cast<uint2 *>(vc + (cache_row + (int64_t)h * max_len) * kD + d0) = raw[i];
         continue;
       }
-      dst = ((slot * hkv + h) * max_len + pos) * kD + d0;
+      if ((kind == 1 && !cache_ok) || (kind == 0 && !q_ok)) continue;
+      const T *e4 = reinterpret_cast<const T *>(&raw[i]);
+      float f[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) f[e] = Elem<T>::to_f(e4[e]);
+      const T *nw = kind == 0 ? q_w : k_w;
+      if (nw) {  // the head's RMSNorm (HF: fp32 statistics, normalised rounded to T, times w)
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ss = fmaf(f[e], f[e], ss);
+        ss = warp_sum(ss);
+        const float rstd = rsqrtf(ss / (float)kD + eps);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          f[e] = round_t<T>(Elem<T>::to_f(nw[d0 + e]) * round_t<T>(f[e] * rstd));
+      }
+      // rotate_half: dims < 64 take -x[d + 64], dims >= 64 take x[d - 64]
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float partner = __shfl_xor_sync(0xffffffffu, f[e], 16);
+        const float rot = lane < 16 ? -partner : partner;
+        o[e] = round_t<T>(round_t<T>(f[e] * cs[e]) + round_t<T>(rot * sn[e]));
+      }
+      uint2 packed;
+      T *p4 = reinterpret_cast<T *>(&packed);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) p4[e] = Elem<T>::from_f(o[e]);
+      if (kind == 0)
+        *reinterpret_cast<uint2 *>(q_out + (q_row * hq + h) * kD + d0) = packed;
+      else
+        *reinterpret_cast<uint2 *>(kc + (cache_row + (int64_t)h * max_len) * kD + d0) = packed;
     }
-    const T *src = kind == 0 ? q + row * q_stride + h * kD : (kind == 1 ? k : v) + row * kv_stride + h * kD;
-    const uint2 raw = *reinterpret_cast<const uint2 *>(src + d0);
-    if (kind == 2) {  // values go to the cache as they are
-      *reinterpret_cast<uint2 *>(vc + dst) = raw;
-      continue;
-    }
-    const T *e4 = reinterpret_cast<const T *>(&raw);
-    float f[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) f[e] = Elem<T>::to_f(e4[e]);
-    const T *nw = kind == 0 ? q_w : k_w;
-    const int64_t rot_pos = rope_pos ? rope_pos[row] : pos;  // the row's own position (prefill)
-    if (nw) {  // the head's RMSNorm (HF: fp32 statistics, normalised rounded to T, times w)
-      float ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) ss = fmaf(f[e], f[e], ss);
-      ss = warp_sum(ss);
-      const float rstd = rsqrtf(ss / (float)kD + eps);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) f[e] = round_t<T>(Elem<T>::to_f(nw[d0 + e]) * round_t<T>(f[e] * rstd));
-    }
-    // rotate_half: dims < 64 take -x[d + 64], dims >= 64 take x[d - 64]
-    float o[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float partner = __shfl_xor_sync(0xffffffffu, f[e], 16);
-      const float rot = lane < 16 ? -partner : partner;
-      const int j = (d0 + e) & (kD / 2 - 1);
-      const float freq = (float)rot_pos * inv_freq[j];
-      const float c = round_t<T>(cosf(freq) * att_scale), s = round_t<T>(sinf(freq) * att_scale);
-      o[e] = round_t<T>(round_t<T>(f[e] * c) + round_t<T>(rot * s));
-    }
-    uint2 packed;
-    T *p4 = reinterpret_cast<T *>(&packed);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) p4[e] = Elem<T>::from_f(o[e]);
-    if (kind == 0)
-      *reinterpret_cast<uint2 *>(q_out + (row * hq + h) * kD + d0) = packed;
-    else
-      *reinterpret_cast<uint2 *>(kc + dst) = packed;
   }
 }
 
@@ -294,7 +334,11 @@ extern "C" int tide_qk_norm_rope(int dtype, const void *q, const void *k, const 
     return fail_msg(TIDE_ERR_INVALID, "qk_norm_rope: NULL pointer");
   if (!aligned16({q, k, v, q_out, k_cache, v_cache}))
     return fail_msg(TIDE_ERR_INVALID, "qk_norm_rope: pointers must be 16-byte aligned");
-  const int64_t warps = n_rows * (n_q_heads + 2 * n_kv_heads);
+  // heads per warp: eight once there are rows enough to fill the GPU with
+  // such groups (a prefill), else one (a decode step)
+  const int64_t heads = n_q_heads + 2 * n_kv_heads;
+  const int group = n_rows * heads >= 148 * 8 * 64 ? 8 : 1;
+  const int64_t warps = n_rows * ((heads + group - 1) / group);
   const unsigned grid = grid_for(warps, 8, 148 * 16);
   cudaStream_t s = (cudaStream_t)stream;
   if (dtype == TIDE_DTYPE_BF16)
@@ -305,7 +349,7 @@ extern "C" int tide_qk_norm_rope(int dtype, const void *q, const void *k, const 
         static_cast<const __nv_bfloat16 *>(k_norm_weight), eps, inv_freq, attention_scaling,
         position, position_dev, rope_positions, slots, n_rows_dev, n_rows, (int)n_q_heads,
         (int)n_kv_heads, static_cast<__nv_bfloat16 *>(q_out), static_cast<__nv_bfloat16 *>(k_cache),
-        static_cast<__nv_bfloat16 *>(v_cache), n_slots, max_len, error_word);
+        static_cast<__nv_bfloat16 *>(v_cache), n_slots, max_len, group, error_word);
   else
     qk_norm_rope_kernel<__half><<<grid, 256, 0, s>>>(
         static_cast<const __half *>(q), static_cast<const __half *>(k),
@@ -313,7 +357,7 @@ extern "C" int tide_qk_norm_rope(int dtype, const void *q, const void *k, const 
         static_cast<const __half *>(k_norm_weight), eps, inv_freq, attention_scaling, position,
         position_dev, rope_positions, slots, n_rows_dev, n_rows, (int)n_q_heads, (int)n_kv_heads,
         static_cast<__half *>(q_out), static_cast<__half *>(k_cache),
-        static_cast<__half *>(v_cache), n_slots, max_len, error_word);
+        static_cast<__half *>(v_cache), n_slots, max_len, group, error_word);
   return launched("qk_norm_rope");
 }
 

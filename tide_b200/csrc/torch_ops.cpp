@@ -515,9 +515,13 @@ void qk_norm_rope(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v,
                   const at::Tensor &k_cache, const at::Tensor &v_cache,
                   const std::optional<at::Tensor> &error_word) {
   for (const auto *t : {&q_out, &k_cache, &v_cache, &inv_freq}) check_cuda_contig(*t, "tensor");
-  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.sizes() == k.sizes() && q_out.sizes() == q.sizes() &&
-              k.size(0) == q.size(0) && q.size(2) == k.size(2),
-              "q [n, hq, d], k and v [n, hkv, d], q_out like q");
+  const bool at_slots = rope_positions.has_value() && rope_positions->defined();
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.sizes() == k.sizes() && k.size(0) == q.size(0) &&
+              q.size(2) == k.size(2), "q [n, hq, d], k and v [n, hkv, d]");
+  TORCH_CHECK(k_cache.dim() == 4, "caches [slots, hkv, max_len, d]");
+  TORCH_CHECK(q_out.dim() == 3 && q_out.size(1) == q.size(1) && q_out.size(2) == q.size(2) &&
+              (at_slots ? q_out.size(0) >= k_cache.size(0) : q_out.size(0) == q.size(0)),
+              "q_out like q, or with rope_positions one row per cache slot");
   // q, k and v: heads packed within a row; rows may be strided (column
   // slices of one fused q/k/v projection), k and v with one stride
   for (const auto *t : {&q, &k, &v})

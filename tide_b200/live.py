@@ -258,19 +258,33 @@ class _LlamaFamily:
         q = attn.q_proj(x).view(n, -1, 128)
         k = attn.k_proj(x).view(n, -1, 128)
         v = attn.v_proj(x).view(n, -1, 128)
-        hkv = k.shape[1]
+        hq, hkv = q.shape[1], k.shape[1]
         qn, kn = getattr(attn, "q_norm", None), getattr(attn, "k_norm", None)
-        q_rot, k_rot = torch.empty_like(q), torch.empty_like(k)
-        # the rows' own outputs serve as a one-position "cache" with identity
-        # slots (v is written onto itself)
-        ident = torch.arange(n, dtype=torch.int32, device=h.device)
+        # q, k and v land at their tokens' places in [B * S] buffers (a one-
+        # position "cache" per token, the tokens' indices as slots): the
+        # exited tokens' keys and values stay zero, their queries are never
+        # read back.  With every token active the rows are the tokens and v
+        # is written onto itself.
+        if pos is None:
+            slots = torch.arange(n, dtype=torch.int32, device=h.device)
+            q_full = torch.empty(n, hq, 128, dtype=q.dtype, device=q.device)
+            k_full = torch.empty(n, hkv, 1, 128, dtype=k.dtype, device=k.device)
+            v_full = v.view(n, hkv, 1, 128)
+        else:
+            slots = pos.to(torch.int32)
+            q_full = torch.empty(B * S, hq, 128, dtype=q.dtype, device=q.device)
+            k_full = torch.zeros(B * S, hkv, 1, 128, dtype=k.dtype, device=k.device)
+            v_full = torch.zeros(B * S, hkv, 1, 128, dtype=v.dtype, device=v.device)
         ops.qk_norm_rope(q, k, v, qn.weight if qn is not None else None,
                          kn.weight if kn is not None else None,
                          float(qn.variance_epsilon) if qn is not None else 0.0,
                          self._inv_freq(), float(getattr(self.rotary, "attention_scaling", 1.0)),
-                         0, None, seq_pos.long().contiguous(), ident, None, q_rot,
-                         k_rot.view(n, hkv, 1, 128), v.view(n, hkv, 1, 128), None)
-        o = _attend(q_rot, k_rot, v, pos, B, S, float(attn.scaling))
+                         0, None, seq_pos.long().contiguous(), slots, None, q_full,
+                         k_full, v_full, None)
+        o = _attend(q_full, k_full.view(-1, hkv, 128), v_full.view(-1, hkv, 128), None, B, S,
+                    float(attn.scaling))
+        if pos is not None:
+            o = o.index_select(0, pos)
         x2, h1 = self.rms_norm(layer.post_attention_layernorm, h, None, delta=attn.o_proj(o))
         mlp = layer.mlp
         g = mlp.gate_proj(x2)
