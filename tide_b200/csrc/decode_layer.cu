@@ -52,8 +52,10 @@ __device__ __forceinline__ int64_t live_rows(const int32_t *n_dev, int64_t n_cap
   return v < 0 ? 0 : (v > n_cap ? n_cap : v);
 }
 
-// One CTA per row (grid-stride), 128 threads, 16-byte vectors.
-template <typename T>
+// One CTA per row (grid-stride), 128 threads, 16-byte vectors, VPT vectors
+// per thread (the row's H / 1024 rounded up to a power of two: the fewer the
+// registers, the more rows in flight per SM).
+template <typename T, int VPT>
 __global__ void __launch_bounds__(dlayer::kNormThreads)
     rms_norm_kernel(const T *__restrict__ x, const T *__restrict__ delta, T *__restrict__ sum_out,
                     const T *__restrict__ w, T *__restrict__ y, int64_t n_cap,
@@ -66,10 +68,10 @@ __global__ void __launch_bounds__(dlayer::kNormThreads)
   for (int64_t row = blockIdx.x; row < live; row += gridDim.x) {
     const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * H);
     const uint4 *dr = delta ? reinterpret_cast<const uint4 *>(delta + row * H) : nullptr;
-    float v[kMaxVecPerThread][8];
+    float v[VPT][8];
     float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxVecPerThread; ++c) {
+    for (int c = 0; c < VPT; ++c) {
       const int i = tid + c * kNormThreads;
       if (i < nv) {
         unpack16<T>(xr[i], v[c]);
@@ -92,7 +94,7 @@ __global__ void __launch_bounds__(dlayer::kNormThreads)
     __syncthreads();  // s_red is rewritten by the next row
     const uint4 *wr = reinterpret_cast<const uint4 *>(w);
 #pragma unroll
-    for (int c = 0; c < kMaxVecPerThread; ++c) {
+    for (int c = 0; c < VPT; ++c) {
       const int i = tid + c * kNormThreads;
       if (i < nv) {
         float wf[8], o[8];
@@ -277,6 +279,22 @@ unsigned grid_for(int64_t work, int64_t per_block, int64_t cap) {
 
 }  // namespace
 
+template <typename T>
+void launch_rms_norm(int vpt, unsigned grid, cudaStream_t s, const void *x, const void *delta,
+                     void *sum_out, const void *weight, void *out, int64_t n_rows,
+                     const int32_t *n_rows_dev, int H, float eps) {
+  const T *xx = static_cast<const T *>(x), *dd = static_cast<const T *>(delta);
+  const T *ww = static_cast<const T *>(weight);
+  T *ss = static_cast<T *>(sum_out), *yy = static_cast<T *>(out);
+  constexpr int kT = tide::dlayer::kNormThreads;
+  switch (vpt) {
+    case 1: tide::rms_norm_kernel<T, 1><<<grid, kT, 0, s>>>(xx, dd, ss, ww, yy, n_rows, n_rows_dev, H, eps); break;
+    case 2: tide::rms_norm_kernel<T, 2><<<grid, kT, 0, s>>>(xx, dd, ss, ww, yy, n_rows, n_rows_dev, H, eps); break;
+    case 4: tide::rms_norm_kernel<T, 4><<<grid, kT, 0, s>>>(xx, dd, ss, ww, yy, n_rows, n_rows_dev, H, eps); break;
+    default: tide::rms_norm_kernel<T, 8><<<grid, kT, 0, s>>>(xx, dd, ss, ww, yy, n_rows, n_rows_dev, H, eps); break;
+  }
+}
+
 extern "C" int tide_rms_norm(int dtype, const void *x, const void *delta, void *sum_out,
                              const void *weight, void *out, int64_t n_rows,
                              const int32_t *n_rows_dev, int64_t hidden_dim, float eps,
@@ -291,18 +309,17 @@ extern "C" int tide_rms_norm(int dtype, const void *x, const void *delta, void *
   if (!x || !weight || !out) return fail_msg(TIDE_ERR_INVALID, "rms_norm: NULL pointer");
   if (!aligned16({x, delta, sum_out, weight, out}))
     return fail_msg(TIDE_ERR_INVALID, "rms_norm: pointers must be 16-byte aligned");
-  const unsigned grid = grid_for(n_rows, 1, 148 * 8);
+  const unsigned grid = grid_for(n_rows, 1, 148 * 16);
   cudaStream_t s = (cudaStream_t)stream;
+  const int64_t nv = hidden_dim / 8;
+  const int vpt = nv <= dlayer::kNormThreads ? 1 : nv <= 2 * dlayer::kNormThreads ? 2
+                : nv <= 4 * dlayer::kNormThreads ? 4 : 8;
   if (dtype == TIDE_DTYPE_BF16)
-    rms_norm_kernel<__nv_bfloat16><<<grid, dlayer::kNormThreads, 0, s>>>(
-        static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(delta),
-        static_cast<__nv_bfloat16 *>(sum_out), static_cast<const __nv_bfloat16 *>(weight),
-        static_cast<__nv_bfloat16 *>(out), n_rows, n_rows_dev, (int)hidden_dim, eps);
+    launch_rms_norm<__nv_bfloat16>(vpt, grid, s, x, delta, sum_out, weight, out, n_rows,
+                                   n_rows_dev, (int)hidden_dim, eps);
   else
-    rms_norm_kernel<__half><<<grid, dlayer::kNormThreads, 0, s>>>(
-        static_cast<const __half *>(x), static_cast<const __half *>(delta),
-        static_cast<__half *>(sum_out), static_cast<const __half *>(weight),
-        static_cast<__half *>(out), n_rows, n_rows_dev, (int)hidden_dim, eps);
+    launch_rms_norm<__half>(vpt, grid, s, x, delta, sum_out, weight, out, n_rows, n_rows_dev,
+                            (int)hidden_dim, eps);
   return launched("rms_norm");
 }
 
