@@ -557,6 +557,28 @@ def test_live_decoder_fused_layers_match_the_module_layers(tmp_path):
     assert sa.total_tokens == sb.total_tokens
 
 
+def test_live_decoder_restacks_changed_projection_weights(tmp_path):
+    """The fused decode layer's stacked q/k/v weights follow the model's: after
+    an in-place change of one layer's k_proj weight, an eager fused step gives
+    what the model's own modules give with the changed weight."""
+    from tide_b200.live import LiveDecoder
+    from tide_b200.scheduler import ExitStats
+
+    model, rt, ids = _decoder_case(tmp_path, B=4)
+    B, S = ids.shape
+    with torch.no_grad():
+        dec0 = LiveDecoder(rt, B, S + 4, graph=False, fused_layers=True)
+        dec0.prefill(ids)
+        dec0.step(ids[:, -1], ExitStats())  # builds the stacked weights
+        model.model.layers[0].self_attn.k_proj.weight.mul_(-0.5)
+        outs = []
+        for fused in (True, False):
+            dec = LiveDecoder(rt, B, S + 4, graph=False, fused_layers=fused)
+            tok = dec.prefill(ids).argmax(-1)
+            outs.append(dec.step(tok, ExitStats()).float().clone())
+    torch.testing.assert_close(outs[0], outs[1], atol=6e-2, rtol=6e-2)
+
+
 @pytest.mark.parametrize("family", ["llama", "qwen3"])
 def test_live_forward_fused_layers_match_the_module_layers(tmp_path, family):
     """The live prefill on the fused layer kernels against the same forward on
