@@ -470,7 +470,8 @@ def test_fused_qk_norm_rope_is_the_hf_modules(qk_norm, packed):
         assert torch.all(kc[others.to(DEV)] == 0) and torch.all(kc[:, :, :pos] == 0)
 
 
-def test_fused_qk_norm_rope_prefill_at_token_places():
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_qk_norm_rope_prefill_at_token_places(dtype):
     """A prefill-sized call (2048 rows x 48 heads: eight heads per warp, the
     cos/sin computed once per row and head group): each row's own rotary
     position, and q, k, v written at the row's token index (the slots) of
@@ -481,21 +482,21 @@ def test_fused_qk_norm_rope_prefill_at_token_places():
     from tide_b200 import _native
 
     ops = _native.ops()
-    model = _qwen3_hd128()
+    model = _qwen3_hd128(dtype)
     attn = model.model.layers[1].self_attn
     rot = model.model.rotary_emb
     n, hq, hkv, d, tokens = 2048, 32, 8, 128, 3000
     g = torch.Generator(device=DEV).manual_seed(12)
     with torch.no_grad():
-        q = torch.randn(n, hq, d, generator=g, device=DEV).to(torch.bfloat16)
-        k = torch.randn(n, hkv, d, generator=g, device=DEV).to(torch.bfloat16)
-        v = torch.randn(n, hkv, d, generator=g, device=DEV).to(torch.bfloat16)
+        q = torch.randn(n, hq, d, generator=g, device=DEV).to(dtype)
+        k = torch.randn(n, hkv, d, generator=g, device=DEV).to(dtype)
+        v = torch.randn(n, hkv, d, generator=g, device=DEV).to(dtype)
         for mod in (attn.q_norm, attn.k_norm):
-            mod.weight.copy_((1 + 0.3 * torch.randn(d, generator=g, device=DEV)).to(torch.bfloat16))
+            mod.weight.copy_((1 + 0.3 * torch.randn(d, generator=g, device=DEV)).to(dtype))
         place = torch.randperm(tokens, generator=torch.Generator().manual_seed(5))[:n].to(DEV)
         seq_pos = torch.randint(0, 240, (n,), generator=torch.Generator().manual_seed(6)).to(DEV)
-        q_full = torch.full((tokens, hq, d), 3.0, dtype=torch.bfloat16, device=DEV)
-        k_full = torch.zeros(tokens, hkv, 1, d, dtype=torch.bfloat16, device=DEV)
+        q_full = torch.full((tokens, hq, d), 3.0, dtype=dtype, device=DEV)
+        k_full = torch.zeros(tokens, hkv, 1, d, dtype=dtype, device=DEV)
         v_full = torch.zeros_like(k_full)
         err = torch.zeros(1, dtype=torch.int32, device=DEV)
         ops.qk_norm_rope(q, k, v, attn.q_norm.weight, attn.k_norm.weight,
